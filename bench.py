@@ -1,0 +1,399 @@
+#!/usr/bin/env python
+"""Benchmark: embeddings/sec of the rembed encoder forward pass on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload bge-base-b256xL128] [--mode bf16|int8_full]
+
+N > 1 runs under torchrun, one process per GPU.  Each rank embeds its own
+batch of the workload (data parallel, no collective on the data path:
+"scaling": "weak"); timing is the max over ranks of CUDA-event time.
+
+One JSON line on rank 0:
+  value     embeddings/s over all ranks, inputs resident in HBM
+            (rg_forward_device), K steps bracketed by barrier + sync;
+  e2e       the same through the public host API (rg_forward: host ids in,
+            host embeddings out, copies inside the timed region);
+  roofline  the dominant kernel (the tcgen05 GEMMs, 4 per layer), timed
+            live with CUDA events around each launch in a second pass;
+  cpu_baseline  the CPU restatement of the reference forward (oracle/) on a
+            bounded sample of the same workload, all host cores;
+  clocks    nvidia-smi samples taken during the timed region.
+``--impl reference`` times only that CPU path, on rank 0, as the
+reference arm.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOADS = {
+    # the headline: bge-base (BERT-base), 256 sequences x 128 tokens, CLS + L2
+    "bge-base-b256xL128": dict(preset="bge-base", nseq=256, lo=128, hi=128),
+    "bge-base-b256xU16-512": dict(preset="bge-base", nseq=256, lo=16, hi=512),
+    "minilm-l6-b32xU8-128": dict(preset="minilm-l6", nseq=32, lo=8, hi=128),
+}
+METRIC = "embeddings/sec at bge-base b256×L128 (fp & int8), 1–8 GPU; tensor-pipe util %"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="bge-base-b256xL128")
+    ap.add_argument("--mode", choices=["bf16", "int8_full"], default="bf16")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target length of the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def make_inputs(wl, seed, n=None):
+    from rembed_b200 import synth
+
+    cfg = synth.preset(wl["preset"])
+    ids, cu = synth.make_batch(cfg, n or wl["nseq"], wl["lo"], wl["hi"], seed=seed)
+    return cfg, ids, cu
+
+
+def gemm_flops_per_token(cfg) -> float:
+    H, I = cfg.hidden_size, cfg.intermediate_size
+    return 2.0 * cfg.num_hidden_layers * (H * 3 * H + H * H + 2 * H * I)
+
+
+# ---------------------------------------------------------------------------
+def cpu_sample(wl, mode: str, target_s: float, nthreads: int):
+    """Time the oracle (CPU restatement of the reference forward) on a bounded
+    sample of the workload: one serial forward per sequence across nthreads
+    threads, as the reference's Embed fans out (rembed.go:309-331)."""
+    import oracle
+    from rembed_b200 import synth
+
+    cfg = synth.preset(wl["preset"])
+    w = synth.make_weights(cfg, seed=0)
+    quant = oracle.QUANT_FULL if mode == "int8_full" else oracle.QUANT_NONE
+    m = oracle.OracleModel(cfg, w, quant)
+    # calibrate on one sequence per thread
+    _, ids, cu = make_inputs(wl, seed=1, n=nthreads)
+    t0 = time.perf_counter()
+    m.embed(ids, cu, nthreads=nthreads)
+    t1 = time.perf_counter() - t0
+    reps = max(1, min(64, int(target_s / max(t1, 1e-3))))
+    n = nthreads * reps
+    _, ids, cu = make_inputs(wl, seed=1, n=n)
+    t0 = time.perf_counter()
+    m.embed(ids, cu, nthreads=nthreads)
+    dt = time.perf_counter() - t0
+    m.close()
+    return {
+        "value": round(n / dt, 3), "unit": "embeddings/s", "cores": nthreads, "kind": "port",
+        "sample": f"{n} sequences of the {wl['preset']} workload (L in [{wl['lo']},{wl['hi']}]), one serial "
+                  f"forward each across {nthreads} threads, {dt:.1f} s; C restatement of the reference "
+                  f"({'full int8' if quant else 'fp32'} path), not the Go binary; CPU: {cpu_model()}",
+    }
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    wl = WORKLOADS[args.workload]
+    import oracle
+    from rembed_b200 import synth
+
+    nth = host_threads()
+    cfg = synth.preset(wl["preset"])
+    w = synth.make_weights(cfg, seed=0)
+    quant = oracle.QUANT_FULL if args.mode == "int8_full" else oracle.QUANT_NONE
+    m = oracle.OracleModel(cfg, w, quant)
+    _, ids, cu = make_inputs(wl, seed=1, n=nth)  # one sequence per thread per step
+    for _ in range(args.warmup):
+        m.embed(ids, cu, nthreads=nth)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        m.embed(ids, cu, nthreads=nth)
+    dt = time.perf_counter() - t0
+    value = nth * args.steps / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "embeddings/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000 * dt / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "s8" if quant else "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "global_batch": wl["nseq"], "seq_len": f"{wl['lo']}-{wl['hi']}",
+                   "parallelism": "cpu threads", "mode": args.mode},
+        "cpu_baseline": {"value": round(value, 3), "unit": "embeddings/s", "cores": nth, "kind": "port",
+                         "sample": f"each step embeds {nth} sequences of the workload, one serial forward per "
+                                   f"sequence per thread; C restatement of the reference forward (Go is not "
+                                   f"installed on this image); CPU: {cpu_model()}"},
+        "e2e": {"value": round(value, 3), "unit": "embeddings/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    m.close()
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clock/throttle samples every 200 ms during the timed region."""
+
+    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"rembed_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+            if self.uuid:
+                cmd += ["-i", self.uuid]
+            self.proc = subprocess.Popen(cmd, stdout=self.fh, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if not self.proc or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in self.path.read_text().splitlines():
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 10:
+                continue
+            try:
+                rows.append({"sm": float(p[2]), "max": float(p[3]), "power": float(p[4]), "active": p[5],
+                             "hw_slowdown": p[6], "hw_thermal_slowdown": p[7], "sw_thermal_slowdown": p[8],
+                             "sw_power_cap": p[9]})
+            except ValueError:
+                continue
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        load = [r for r in rows if r["power"] > 200] or rows
+        reasons = sorted({k for r in load for k in ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                                                      "sw_power_cap") if r[k].lower() == "active"})
+        return {"sm_mhz": float(np.median([r["sm"] for r in load])), "sm_max_mhz": max(r["max"] for r in rows),
+                "reasons": reasons, "samples": len(rows), "samples_under_load": len(load),
+                "power_w_max": max(r["power"] for r in rows)}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def committed_traffic(workload: str, mode: str):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
+    summary (profiles/traffic.json), or None."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text()).get(f"{workload}/{mode}")
+    except (ValueError, OSError):
+        return None
+
+
+def ours(args, rank, world, local_rank):
+    import torch
+
+    from rembed_b200 import synth
+    from rembed_b200.embedder import Embedder
+
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    wl = WORKLOADS[args.workload]
+    cfg = synth.preset(wl["preset"])
+    weights = synth.make_weights(cfg, seed=0)
+    emb = Embedder(cfg, weights, devices=[local_rank], int8_activations=args.mode == "int8_full")
+    del weights
+    _, ids, cu = make_inputs(wl, seed=1000 + rank)
+    nseq, T = len(cu) - 1, int(cu[-1])
+    d_ids = torch.from_numpy(ids).cuda()
+    d_cu = torch.from_numpy(cu).cuda()
+    d_out = torch.empty((nseq, emb.dim), device="cuda", dtype=torch.float32)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        emb.forward_device(d_ids.data_ptr(), d_cu.data_ptr(), cu, d_out.data_ptr(), stream=stream.cuda_stream)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    emb.sync()
+    launches_per_step = emb.last_launches()
+
+    # ---- value: device-resident inputs ----
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(local_rank).uuid)
+        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    except Exception:
+        uuid = None
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(uuid) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    emb.sync()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    clocks = clk.summary()
+    value = world * nseq * args.steps / (ms / 1000.0)
+
+    # ---- e2e: host buffers through the public API ----
+    host_out = np.empty((nseq, emb.dim), dtype=np.float32)
+    for _ in range(2):
+        emb.embed_packed(ids, cu, out=host_out)
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    f0.record(stream)
+    for _ in range(args.steps):
+        emb.embed_packed(ids, cu, out=host_out)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    barrier()
+    e2e_ms = max_over_ranks(max(f0.elapsed_time(f1), 1000.0 * wall))
+    e2e_value = world * nseq * args.steps / (e2e_ms / 1000.0)
+
+    # ---- roofline: per-kernel-class device time, second pass ----
+    emb.profile(True)
+    for _ in range(args.steps):
+        step()
+    stats = emb.profile_stats()
+    emb.profile(False)
+    peaks, peak_src = measured_peaks()
+    g = stats["gemm"]
+    total_ms = sum(v["ms"] for v in stats.values())
+    if args.mode == "int8_full":
+        peak = 2.0 * peaks["bf16_tflops_sustained"]
+        peak_note = f"2x {peak_src} sustained bf16 (dense int8 rate is 2x bf16 on B200)"
+    else:
+        peak = peaks["bf16_tflops_sustained"]
+        peak_note = f"{peak_src} sustained bf16 (kernel timed inside a long forward)"
+    gemm_avg_ms = g["ms"] / max(g["launches"], 1)
+    achieved = (g["flops"] / max(g["launches"], 1)) / (gemm_avg_ms / 1000.0) / 1e12
+    traffic = committed_traffic(args.workload, args.mode)
+    roofline = {
+        "kernel": "tcgen05 GEMM (gemm_kernel), all dense projections",
+        "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+        "frac": round(achieved / peak, 4), "traffic": traffic,
+        "peak_source": peak_note,
+        "algorithmic_per_launch": {"flops": g["flops"] / max(g["launches"], 1),
+                                   "bytes": g["bytes"] / max(g["launches"], 1)},
+        "avg_launch_ms": round(gemm_avg_ms, 4),
+        "share_of_forward": round(g["ms"] / total_ms, 4) if total_ms else None,
+        "kernel_classes": {k: {"ms_per_step": round(v["ms"] / args.steps, 4),
+                               "launches_per_step": v["launches"] // max(args.steps, 1),
+                               "achieved_tflops": round(v["flops"] / (v["ms"] / 1000) / 1e12, 1) if v["ms"] else 0,
+                               "achieved_gbs": round(v["bytes"] / (v["ms"] / 1000) / 1e9, 1) if v["ms"] else 0}
+                           for k, v in stats.items() if v["launches"]},
+    }
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "embeddings/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "s8" if args.mode == "int8_full" else "bf16",
+        "data": "synthetic (seeded random-init weights N(0,0.02) of the named architecture; seeded token ids)",
+        "config": {"workload": args.workload, "global_batch": world * nseq, "per_gpu_batch": nseq,
+                   "seq_len": f"{wl['lo']}-{wl['hi']}", "tokens_per_gpu_step": T, "parallelism": f"dp{world}",
+                   "mode": args.mode,
+                   "l2": "no flush: per-step working set (activations ~0.8 GB + weights) exceeds the 126 MB L2"},
+        "roofline": roofline,
+        "e2e": {"value": round(e2e_value, 2), "unit": "embeddings/s",
+                "h2d_bytes_per_step": int(ids.nbytes + cu.nbytes),
+                "d2h_bytes_per_step": int(host_out.nbytes + 4)},
+        "clocks": clocks,
+        "gpu_launches": int(launches_per_step * args.steps),
+        "gemm_tflops_effective": round(gemm_flops_per_token(cfg) * T * world * args.steps / (ms / 1000) / 1e12, 1),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_sample(wl, args.mode, args.cpu_seconds, host_threads())
+    emb.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank, world)
+        return
+    ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

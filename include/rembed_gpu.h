@@ -1,0 +1,157 @@
+/*
+ * rembed_gpu.h - C ABI of librembed_gpu.so, the B200 (sm_100a) encoder
+ * forward pass for rembed.
+ *
+ * The library replaces the pure-Go kernel layer below rembed's
+ * Model.ForwardWorkers / ForwardTokensWorkers (internal/model/bert.go:657-734)
+ * for a whole batch of sequences at once.  rembed's host keeps Load, the
+ * config derivation, the tokenizers and the Embed / EmbedTokens API; its
+ * per-text forward fan-out (rembed.go:309-331) becomes one rg_forward call.
+ *
+ * Conventions follow the reference's own FFI (python/capi/main.go:9-13):
+ *   - functions return 0 on success and -1 on failure;
+ *   - on failure, if err != NULL, *err receives a malloc'd message that the
+ *     caller releases with rg_free_string (RembedFreeString, main.go:150-155);
+ *   - the caller owns every output buffer; host inputs are borrowed for the
+ *     duration of the call only;
+ *   - a context is safe for concurrent use (the reference Embedder is,
+ *     rembed.go:37-41): calls on one context serialise internally.
+ * Nothing here aborts the process, and there is no CPU fallback: a shape or
+ * mode the CUDA path cannot run is an error.
+ */
+#ifndef REMBED_GPU_H
+#define REMBED_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RG_ABI_VERSION 1
+
+/* Architectures (model.Config.ModelType, config.go:17; dispatch bert.go:316-337). */
+enum {
+    RG_ARCH_BERT = 0, RG_ARCH_DISTILBERT = 1, RG_ARCH_ROBERTA = 2, RG_ARCH_MPNET = 3,
+    RG_ARCH_MODERNBERT = 4, RG_ARCH_QWEN3 = 5, RG_ARCH_GEMMA3 = 6, RG_ARCH_NOMIC = 7
+};
+/* Pooling (Config.Pooling, bert.go:670-679). */
+enum { RG_POOL_MEAN = 0, RG_POOL_CLS = 1, RG_POOL_LASTTOKEN = 2 };
+/* Numeric modes.  RG_MODE_BF16: bf16 tensor-core GEMMs, fp32 accumulate,
+ * fp32 residual stream (replaces the reference's fp32 path).
+ * RG_MODE_INT8_W: weight-only int8, the PackB8 quantiser (WithInt8,
+ * rembed.go:67-69).  RG_MODE_INT8_FULL: int8 weights and per-row int8
+ * activations, the PackB8VNNI scheme (WithInt8Activations, rembed.go:79-81). */
+enum { RG_MODE_BF16 = 0, RG_MODE_INT8_W = 2, RG_MODE_INT8_FULL = 3 };
+/* Host dtypes accepted by rg_upload_weight (safetensors.go:188-209). */
+enum { RG_DTYPE_F32 = 0, RG_DTYPE_F16 = 1, RG_DTYPE_BF16 = 2 };
+/* rg_forward output kinds: pooled (Embed) or per-token hidden states
+ * (EmbedTokens, rembed.go:370-411). */
+enum { RG_OUT_POOLED = 0, RG_OUT_TOKENS = 1 };
+
+/* The Config fields the forward reads (model.Config, config.go:15-78).
+ * Unused fields for an architecture are ignored; zero means "absent". */
+typedef struct rg_model_desc {
+    int arch;                     /* RG_ARCH_* */
+    int hidden_size, num_hidden_layers, num_attention_heads, intermediate_size;
+    int vocab_size, max_position_embeddings;
+    float layer_norm_eps;         /* 0 -> 1e-12 (config.go:228-230) */
+    int pooling;                  /* RG_POOL_* */
+    int normalize;                /* L2-normalise the pooled vector */
+    int pad_token_id, relative_attention_num_buckets;
+    int head_dim, num_key_value_heads;
+    double rope_theta, global_rope_theta, local_rope_theta;
+    int global_attn_every_n_layers, local_attention;
+    int sliding_window, sliding_window_pattern, query_pre_attn_scalar, dense_hidden;
+} rg_model_desc;
+
+typedef struct rg_ctx rg_ctx;
+
+/* Create a context holding one weight replica per listed CUDA device
+ * (data parallel across devices; sequences are sharded, never split).
+ * Replaces model.Load's per-arch loader (bert.go:307-518) minus the
+ * safetensors parsing, which stays with the caller.  mode is RG_MODE_*. */
+int rg_init(const rg_model_desc *desc, const int *devices, int ndev, int mode,
+            rg_ctx **out, char **err);
+
+/* Hand one tensor to the context by its Hugging Face name, exactly as the
+ * reference loader looks it up (bert.go:338-470; prefixes "bert.",
+ * "roberta.", "mpnet.", "distilbert." accepted).  host is read during the
+ * call only.  Shapes are checked against the descriptor. */
+int rg_upload_weight(rg_ctx *ctx, const char *name, int dtype, const int64_t *shape, int ndim,
+                     const void *host, char **err);
+
+/* Once every tensor is uploaded: fuse Q|K|V (bert.go:479-485), quantise
+ * with the reference's own quantisers for the int8 modes (newDense,
+ * bert.go:263-278; PackB8 pack8.go:25-76, PackB8VNNI pack_vnni.go:28-77),
+ * copy to every device.  A non-finite weight under an int8 mode is an
+ * error (pack8.go:43-48). */
+int rg_finalize(rg_ctx *ctx, char **err);
+
+/* Forward a packed batch from HOST memory: ids [cu_seqlens[nseq]] token ids
+ * (int64, as Model.Forward takes them), cu_seqlens [nseq+1] prefix offsets.
+ * RG_OUT_POOLED writes host_out[nseq x out_dim]: pooled, Dense head (Gemma),
+ * L2-normalised when the config says so, then truncated to out_dim and
+ * re-normalised when out_dim < hidden (Matryoshka, rembed.go:441-448).
+ * RG_OUT_TOKENS writes host_out[cu_seqlens[nseq] x hidden], the final hidden
+ * states (out_dim must equal hidden).  Errors, checked before any launch:
+ * empty sequence, sequence longer than the model maximum, token id outside
+ * [0, vocab) (bert.go:742-747, 797-799). */
+int rg_forward(rg_ctx *ctx, const int64_t *ids, const int32_t *cu_seqlens, int nseq, int out_kind,
+               int out_dim, float *host_out, char **err);
+
+/* Forward a packed batch already resident on device `dev_index` (an index
+ * into the rg_init device list): d_ids, d_cu_seqlens and d_out are device
+ * pointers on that device; `stream` is a cudaStream_t (NULL = the context's
+ * own stream for that device).  host_cu_seqlens is the same offsets in host
+ * memory (used for validation and work partitioning, never for ids).  No
+ * synchronisation on return: the result is ready when `stream` reaches this
+ * point.  Ids are validated on the device; a bad id makes the call return
+ * -1 at the next rg_forward_device / rg_sync on this device. */
+int rg_forward_device(rg_ctx *ctx, int dev_index, const int64_t *d_ids, const int32_t *d_cu_seqlens,
+                      const int32_t *host_cu_seqlens, int nseq, int out_kind, int out_dim, float *d_out,
+                      void *stream, char **err);
+
+/* Wait for all work on device `dev_index` and report any deferred error. */
+int rg_sync(rg_ctx *ctx, int dev_index, char **err);
+
+/* Output dimension before truncation (Config.HiddenSize). */
+int rg_hidden(const rg_ctx *ctx);
+/* Numeric mode actually running (replaces Model.Quantized /
+ * QuantizedActivations, bert.go:531-644: there is never a silent fallback,
+ * so this always equals the mode rg_init accepted). */
+int rg_mode_active(const rg_ctx *ctx);
+/* Number of kernel launches the last rg_forward / rg_forward_device issued
+ * on device `dev_index` (for launch accounting in benchmarks). */
+int rg_last_launches(const rg_ctx *ctx, int dev_index);
+
+/* Kernel timing for measurement: when enabled, every launch of a forward on
+ * device `dev_index` is bracketed by CUDA events on its stream.
+ * rg_profile(enable=1) clears the counters; rg_profile_stats synchronises
+ * the device and returns, for one kernel class (RG_KC_*), the summed device
+ * milliseconds, launch count, algorithmic FLOPs and algorithmic bytes since
+ * the last enable.  Off by default (no events recorded). */
+enum { RG_KC_GEMM = 0, RG_KC_ATTENTION = 1, RG_KC_NORM = 2, RG_KC_POOL = 3, RG_KC_QUANT = 4, RG_KC_COUNT = 5 };
+int rg_profile(rg_ctx *ctx, int dev_index, int enable);
+int rg_profile_stats(rg_ctx *ctx, int dev_index, int kernel_class, double *ms, int *launches, double *flops,
+                     double *bytes);
+
+void rg_free(rg_ctx *ctx);
+void rg_free_string(char *s);
+
+/* ---- kernel-level entry points (parity tests, benchmarks) --------------
+ * Device pointers on the current CUDA device; stream = cudaStream_t or NULL.
+ *
+ * rg_dense_bf16: y[M x N] = epilogue(x[M x K] . W[N x K]^T): the dense
+ * projection of applyDense (bert.go:282-301) as one tcgen05 GEMM.
+ * epilogue: 0 = +bias -> bf16 y; 1 = +bias, exact GELU -> bf16 y;
+ * 2 = +bias +residual (fp32) -> fp32 y.  x, W bf16; bias fp32 or NULL.
+ * K must be a multiple of 64, N of 128 (checked). */
+int rg_dense_bf16(const void *x, const void *w, const float *bias, const float *residual, void *y,
+                  int M, int N, int K, int epilogue, void *stream, char **err);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,519 @@
+/*
+ * oracle_model.c - CPU restatement of rembed's per-architecture forward
+ * passes (internal/model) and its batch fan-out (rembed.go).
+ *
+ * TEST INFRASTRUCTURE ONLY: the parity checker for the CUDA path and the
+ * CPU baseline in bench.py.  The product never links or loads it.
+ *
+ * Weights are borrowed float32 tensors named as in the Hugging Face
+ * checkpoints the reference loads (bert.go:338-518).  Dense projections
+ * follow newDense/applyDense (bert.go:263-301): fp32 (k-ordered FMA),
+ * weight-only int8 (PackB8) or full int8 (PackB8VNNI + per-row u8
+ * activations), each followed by a separate bias add.
+ */
+#define _GNU_SOURCE
+#include "oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define MAXW 4096
+#define NAMELEN 160
+
+typedef struct {
+    char name[NAMELEN];
+    const float *data;
+    int64_t numel;
+} wentry;
+
+/* denseWeight (bert.go:32-39) after newDense. */
+typedef struct {
+    int in, out;
+    const float *w;   /* fp32 [out x in] (borrowed or owned via own) */
+    float *own;       /* owned fused buffer, if any */
+    int8_t *q;        /* int8 [out x in] */
+    float *scales;
+    int32_t *colsum;
+    const float *bias;
+    float *own_bias;
+} dense;
+
+typedef struct {
+    dense qkv, attn_out, ffn1, ffn2;
+    const float *attn_ln_g, *attn_ln_b, *out_ln_g, *out_ln_b;
+} bert_layer;
+
+struct or_model {
+    or_config cfg;
+    int quant;
+    wentry w[MAXW];
+    int nw;
+    int finalized;
+    int pos_off;
+    const float *word_emb, *pos_emb, *type_emb, *emb_ln_g, *emb_ln_b, *rel_bias;
+    bert_layer *layers;
+};
+
+static void seterr(char *err, const char *fmt, ...) {
+    if (!err) return;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(err, 256, fmt, ap);
+    va_end(ap);
+}
+
+or_model *or_model_new(const or_config *cfg, int quant) {
+    or_model *m = (or_model *)calloc(1, sizeof(or_model));
+    m->cfg = *cfg;
+    m->quant = quant;
+    if (m->cfg.eps == 0.0f) m->cfg.eps = 1e-12f; /* config.go:228-230 */
+    /* PositionOffset, config.go:84-89 */
+    m->pos_off = (cfg->arch == OR_ARCH_MPNET || cfg->arch == OR_ARCH_ROBERTA) ? cfg->pad_token_id + 1 : 0;
+    return m;
+}
+
+int or_model_set(or_model *m, const char *name, const float *data, int64_t numel) {
+    if (m->nw >= MAXW || strlen(name) >= NAMELEN) return -1;
+    for (int i = 0; i < m->nw; i++)
+        if (strcmp(m->w[i].name, name) == 0) {
+            m->w[i].data = data;
+            m->w[i].numel = numel;
+            return 0;
+        }
+    snprintf(m->w[m->nw].name, NAMELEN, "%s", name);
+    m->w[m->nw].data = data;
+    m->w[m->nw].numel = numel;
+    m->nw++;
+    return 0;
+}
+
+/* Look up name with any of the reference's prefixes (bert.go:338-343). */
+static const float *get_tensor(or_model *m, const char *name, int64_t numel, char *err) {
+    static const char *prefixes[] = {"", "bert.", "roberta.", "mpnet.", "distilbert.", "model."};
+    char full[NAMELEN * 2];
+    for (size_t p = 0; p < sizeof(prefixes) / sizeof(prefixes[0]); p++) {
+        snprintf(full, sizeof(full), "%s%s", prefixes[p], name);
+        for (int i = 0; i < m->nw; i++)
+            if (strcmp(m->w[i].name, full) == 0) {
+                if (numel >= 0 && m->w[i].numel != numel) {
+                    seterr(err, "tensor %s has %lld elements, want %lld", full, (long long)m->w[i].numel,
+                           (long long)numel);
+                    return NULL;
+                }
+                return m->w[i].data;
+            }
+    }
+    seterr(err, "missing tensor %s", name);
+    return NULL;
+}
+
+/* newDense, bert.go:263-278 (quantisation at load, never a silent
+ * fallback here: a non-finite weight under int8 is an error). */
+static int make_dense(dense *d, const float *w, const float *bias, int in, int out, int quant, char *err) {
+    d->in = in;
+    d->out = out;
+    d->w = w;
+    d->bias = bias;
+    if (quant == OR_QUANT_FULL) {
+        d->q = (int8_t *)malloc((size_t)in * out);
+        d->colsum = (int32_t *)malloc(sizeof(int32_t) * out);
+        d->scales = (float *)malloc(sizeof(float) * out);
+        if (or_packb8vnni(w, in, out, d->q, d->colsum, d->scales) != 0) {
+            seterr(err, "PackB8VNNI rejected a [%d x %d] weight (non-finite value or out %% 16 != 0)", out, in);
+            return -1;
+        }
+    } else if (quant == OR_QUANT_WEIGHTS) {
+        d->q = (int8_t *)malloc((size_t)in * out);
+        d->scales = (float *)malloc(sizeof(float) * out);
+        if (or_packb8(w, in, out, d->q, d->scales) != 0) {
+            seterr(err, "PackB8 rejected a [%d x %d] weight (non-finite value or out %% 16 != 0)", out, in);
+            return -1;
+        }
+    }
+    return 0;
+}
+
+static void free_dense(dense *d) {
+    free(d->own);
+    free(d->own_bias);
+    free(d->q);
+    free(d->scales);
+    free(d->colsum);
+}
+
+/* applyDense, bert.go:282-301 */
+static void apply_dense(const dense *d, float *dst, const float *x, int seq, int quant) {
+    if (quant == OR_QUANT_FULL)
+        or_matmul_vnni(dst, x, d->q, d->colsum, d->scales, seq, d->in, d->out);
+    else if (quant == OR_QUANT_WEIGHTS)
+        or_matmul_packed8(dst, x, d->q, d->scales, seq, d->in, d->out);
+    else
+        or_matmul_packed(dst, x, d->w, seq, d->in, d->out);
+    if (d->bias) or_add_bias(dst, d->bias, seq, d->out);
+}
+
+/* BERT / DistilBERT / RoBERTa / MPNet weight binding, bert.go:338-518. */
+static int finalize_bert(or_model *m, char *err) {
+    const or_config *c = &m->cfg;
+    int H = c->hidden, I = c->inter, arch = c->arch;
+    int distil = arch == OR_ARCH_DISTILBERT, mpnet = arch == OR_ARCH_MPNET;
+    if (c->heads <= 0 || H % c->heads != 0) {
+        seterr(err, "hidden_size %d not divisible by num_attention_heads %d", H, c->heads);
+        return -1;
+    }
+    if (!(m->word_emb = get_tensor(m, "embeddings.word_embeddings.weight", (int64_t)c->vocab * H, err))) return -1;
+    if (!(m->pos_emb = get_tensor(m, "embeddings.position_embeddings.weight", (int64_t)c->max_pos * H, err))) return -1;
+    if (!(m->emb_ln_g = get_tensor(m, "embeddings.LayerNorm.weight", H, err))) return -1;
+    if (!(m->emb_ln_b = get_tensor(m, "embeddings.LayerNorm.bias", H, err))) return -1;
+    m->layers = (bert_layer *)calloc(c->layers, sizeof(bert_layer));
+    char nm[NAMELEN];
+#define GET(dst, fmt, n)                                   \
+    do {                                                   \
+        snprintf(nm, sizeof nm, fmt, li);                  \
+        if (!((dst) = get_tensor(m, nm, (n), err))) return -1;   \
+    } while (0)
+    for (int li = 0; li < c->layers; li++) {
+        bert_layer *l = &m->layers[li];
+        const float *qW, *qB, *kW, *kB, *vW, *vB, *oW, *oB, *f1W, *f1B, *f2W, *f2B;
+        if (distil) {
+            GET(qW, "transformer.layer.%d.attention.q_lin.weight", (int64_t)H * H);
+            GET(qB, "transformer.layer.%d.attention.q_lin.bias", H);
+            GET(kW, "transformer.layer.%d.attention.k_lin.weight", (int64_t)H * H);
+            GET(kB, "transformer.layer.%d.attention.k_lin.bias", H);
+            GET(vW, "transformer.layer.%d.attention.v_lin.weight", (int64_t)H * H);
+            GET(vB, "transformer.layer.%d.attention.v_lin.bias", H);
+            GET(oW, "transformer.layer.%d.attention.out_lin.weight", (int64_t)H * H);
+            GET(oB, "transformer.layer.%d.attention.out_lin.bias", H);
+            GET(l->attn_ln_g, "transformer.layer.%d.sa_layer_norm.weight", H);
+            GET(l->attn_ln_b, "transformer.layer.%d.sa_layer_norm.bias", H);
+            GET(f1W, "transformer.layer.%d.ffn.lin1.weight", (int64_t)I * H);
+            GET(f1B, "transformer.layer.%d.ffn.lin1.bias", I);
+            GET(f2W, "transformer.layer.%d.ffn.lin2.weight", (int64_t)H * I);
+            GET(f2B, "transformer.layer.%d.ffn.lin2.bias", H);
+            GET(l->out_ln_g, "transformer.layer.%d.output_layer_norm.weight", H);
+            GET(l->out_ln_b, "transformer.layer.%d.output_layer_norm.bias", H);
+        } else {
+            if (mpnet) {
+                GET(qW, "encoder.layer.%d.attention.attn.q.weight", (int64_t)H * H);
+                GET(qB, "encoder.layer.%d.attention.attn.q.bias", H);
+                GET(kW, "encoder.layer.%d.attention.attn.k.weight", (int64_t)H * H);
+                GET(kB, "encoder.layer.%d.attention.attn.k.bias", H);
+                GET(vW, "encoder.layer.%d.attention.attn.v.weight", (int64_t)H * H);
+                GET(vB, "encoder.layer.%d.attention.attn.v.bias", H);
+                GET(oW, "encoder.layer.%d.attention.attn.o.weight", (int64_t)H * H);
+                GET(oB, "encoder.layer.%d.attention.attn.o.bias", H);
+                GET(l->attn_ln_g, "encoder.layer.%d.attention.LayerNorm.weight", H);
+                GET(l->attn_ln_b, "encoder.layer.%d.attention.LayerNorm.bias", H);
+            } else {
+                GET(qW, "encoder.layer.%d.attention.self.query.weight", (int64_t)H * H);
+                GET(qB, "encoder.layer.%d.attention.self.query.bias", H);
+                GET(kW, "encoder.layer.%d.attention.self.key.weight", (int64_t)H * H);
+                GET(kB, "encoder.layer.%d.attention.self.key.bias", H);
+                GET(vW, "encoder.layer.%d.attention.self.value.weight", (int64_t)H * H);
+                GET(vB, "encoder.layer.%d.attention.self.value.bias", H);
+                GET(oW, "encoder.layer.%d.attention.output.dense.weight", (int64_t)H * H);
+                GET(oB, "encoder.layer.%d.attention.output.dense.bias", H);
+                GET(l->attn_ln_g, "encoder.layer.%d.attention.output.LayerNorm.weight", H);
+                GET(l->attn_ln_b, "encoder.layer.%d.attention.output.LayerNorm.bias", H);
+            }
+            GET(f1W, "encoder.layer.%d.intermediate.dense.weight", (int64_t)I * H);
+            GET(f1B, "encoder.layer.%d.intermediate.dense.bias", I);
+            GET(f2W, "encoder.layer.%d.output.dense.weight", (int64_t)H * I);
+            GET(f2B, "encoder.layer.%d.output.dense.bias", H);
+            GET(l->out_ln_g, "encoder.layer.%d.output.LayerNorm.weight", H);
+            GET(l->out_ln_b, "encoder.layer.%d.output.LayerNorm.bias", H);
+        }
+        /* Fused Q||K||V [3H x H], bert.go:479-485 */
+        float *qkvW = (float *)malloc(sizeof(float) * 3 * (size_t)H * H);
+        float *qkvB = (float *)malloc(sizeof(float) * 3 * (size_t)H);
+        memcpy(qkvW, qW, sizeof(float) * (size_t)H * H);
+        memcpy(qkvW + (size_t)H * H, kW, sizeof(float) * (size_t)H * H);
+        memcpy(qkvW + 2 * (size_t)H * H, vW, sizeof(float) * (size_t)H * H);
+        memcpy(qkvB, qB, sizeof(float) * H);
+        memcpy(qkvB + H, kB, sizeof(float) * H);
+        memcpy(qkvB + 2 * H, vB, sizeof(float) * H);
+        l->qkv.own = qkvW;
+        l->qkv.own_bias = qkvB;
+        if (make_dense(&l->qkv, qkvW, qkvB, H, 3 * H, m->quant, err)) return -1;
+        if (make_dense(&l->attn_out, oW, oB, H, H, m->quant, err)) return -1;
+        if (make_dense(&l->ffn1, f1W, f1B, H, I, m->quant, err)) return -1;
+        if (make_dense(&l->ffn2, f2W, f2B, I, H, m->quant, err)) return -1;
+    }
+#undef GET
+    if (distil) return 0;
+    if (mpnet) {
+        if (!(m->rel_bias = get_tensor(m, "encoder.relative_attention_bias.weight", (int64_t)c->rel_buckets * c->heads, err)))
+            return -1;
+        return 0;
+    }
+    /* token_type_embeddings: any first dimension, row 0 used (bert.go:507-515) */
+    for (int i = 0; i < m->nw; i++) {
+        const char *n = m->w[i].name;
+        const char *s = strstr(n, "embeddings.token_type_embeddings.weight");
+        if (s && m->w[i].numel >= H && m->w[i].numel % H == 0) {
+            m->type_emb = m->w[i].data;
+            return 0;
+        }
+    }
+    seterr(err, "missing tensor embeddings.token_type_embeddings.weight");
+    return -1;
+}
+
+int or_model_finalize(or_model *m, char *err) {
+    int rc;
+    switch (m->cfg.arch) {
+    case OR_ARCH_BERT:
+    case OR_ARCH_DISTILBERT:
+    case OR_ARCH_ROBERTA:
+    case OR_ARCH_MPNET:
+        rc = finalize_bert(m, err);
+        break;
+    default:
+        seterr(err, "oracle: architecture %d not restated", m->cfg.arch);
+        return -1;
+    }
+    if (rc == 0) m->finalized = 1;
+    return rc;
+}
+
+void or_model_free(or_model *m) {
+    if (!m) return;
+    if (m->layers) {
+        for (int i = 0; i < m->cfg.layers; i++) {
+            free_dense(&m->layers[i].qkv);
+            free_dense(&m->layers[i].attn_out);
+            free_dense(&m->layers[i].ffn1);
+            free_dense(&m->layers[i].ffn2);
+        }
+        free(m->layers);
+    }
+    free(m);
+}
+
+static int max_seq_len(const or_model *m) { return m->cfg.max_pos - m->pos_off; } /* config.go:93-95 */
+
+/* encodeWorkers BERT body, bert.go:740-923 (serial: workers = 1). */
+static int encode_bert(or_model *m, const int64_t *ids, int seq, float *x, char *err) {
+    const or_config *c = &m->cfg;
+    int H = c->hidden, heads = c->heads, dh = H / heads, I = c->inter, q = m->quant;
+    float eps = c->eps;
+    for (int i = 0; i < seq; i++) {
+        if (ids[i] < 0 || ids[i] >= c->vocab) {
+            seterr(err, "token id %lld out of vocab range %d", (long long)ids[i], c->vocab);
+            return -1;
+        }
+    }
+    /* Embeddings, bert.go:795-814 */
+    for (int i = 0; i < seq; i++) {
+        float *row = x + (int64_t)i * H;
+        const float *w = m->word_emb + ids[i] * H;
+        const float *p = m->pos_emb + (int64_t)(i + m->pos_off) * H;
+        if (m->type_emb) {
+            for (int j = 0; j < H; j++) row[j] = w[j] + p[j] + m->type_emb[j];
+        } else {
+            for (int j = 0; j < H; j++) row[j] = w[j] + p[j];
+        }
+    }
+    or_layernorm(x, m->emb_ln_g, m->emb_ln_b, seq, H, eps);
+
+    float *bias_delta = NULL;
+    int ndelta = 2 * seq - 1;
+    if (m->rel_bias) { /* bert.go:820-830 */
+        bias_delta = (float *)malloc(sizeof(float) * heads * ndelta);
+        for (int d = -(seq - 1); d <= seq - 1; d++) {
+            int b = or_relpos_bucket(d, c->rel_buckets);
+            for (int h = 0; h < heads; h++) bias_delta[h * ndelta + d + seq - 1] = m->rel_bias[b * heads + h];
+        }
+    }
+    float *qkv = (float *)malloc(sizeof(float) * (size_t)seq * 3 * H);
+    float *ctx = (float *)malloc(sizeof(float) * (size_t)seq * H);
+    float *tmp = (float *)malloc(sizeof(float) * (size_t)seq * H);
+    float *ffh = (float *)malloc(sizeof(float) * (size_t)seq * I);
+    float *sc = (float *)malloc(sizeof(float) * (size_t)seq * seq);
+    float *qh = (float *)malloc(sizeof(float) * (size_t)seq * dh);
+    float *kh = (float *)malloc(sizeof(float) * (size_t)seq * dh);
+    float *vt = (float *)malloc(sizeof(float) * (size_t)seq * dh);
+    float *ch = (float *)malloc(sizeof(float) * (size_t)seq * dh);
+    float scale = (float)(1.0 / sqrt((double)dh));
+
+    for (int li = 0; li < c->layers; li++) {
+        bert_layer *l = &m->layers[li];
+        apply_dense(&l->qkv, qkv, x, seq, q);
+        for (int h = 0; h < heads; h++) { /* bert.go:853-902 */
+            int off = h * dh;
+            for (int i = 0; i < seq; i++) {
+                const float *row = qkv + (int64_t)i * 3 * H;
+                memcpy(qh + (int64_t)i * dh, row + off, sizeof(float) * dh);
+                memcpy(kh + (int64_t)i * dh, row + H + off, sizeof(float) * dh);
+                for (int d = 0; d < dh; d++) vt[(int64_t)d * seq + i] = row[2 * H + off + d];
+            }
+            or_matmul_serial(sc, qh, kh, seq, dh, seq);
+            if (bias_delta) {
+                const float *bd = bias_delta + h * ndelta;
+                for (int i = 0; i < seq; i++) {
+                    float *row = sc + (int64_t)i * seq;
+                    const float *bdi = bd + (seq - 1 - i);
+                    for (int j = 0; j < seq; j++) row[j] = (float)(row[j] * scale) + bdi[j];
+                }
+            } else {
+                for (int i = 0; i < seq * seq; i++) sc[i] *= scale;
+            }
+            or_softmax(sc, seq, seq);
+            or_matmul_serial(ch, sc, vt, seq, seq, dh);
+            for (int i = 0; i < seq; i++) memcpy(ctx + (int64_t)i * H + off, ch + (int64_t)i * dh, sizeof(float) * dh);
+        }
+        apply_dense(&l->attn_out, tmp, ctx, seq, q);
+        or_add(x, tmp, seq * H);
+        or_layernorm(x, l->attn_ln_g, l->attn_ln_b, seq, H, eps);
+        apply_dense(&l->ffn1, ffh, x, seq, q);
+        or_gelu(ffh, seq * I);
+        apply_dense(&l->ffn2, tmp, ffh, seq, q);
+        or_add(x, tmp, seq * H);
+        or_layernorm(x, l->out_ln_g, l->out_ln_b, seq, H, eps);
+    }
+    free(bias_delta);
+    free(qkv);
+    free(ctx);
+    free(tmp);
+    free(ffh);
+    free(sc);
+    free(qh);
+    free(kh);
+    free(vt);
+    free(ch);
+    return 0;
+}
+
+/* ForwardWorkers, bert.go:657-703 */
+int or_forward(or_model *m, const int64_t *ids, int seq, float *pooled, float *tokens, char *err) {
+    const or_config *c = &m->cfg;
+    int H = c->hidden;
+    if (!m->finalized) {
+        seterr(err, "model not finalized");
+        return -1;
+    }
+    if (seq == 0) { /* bert.go:742-747 */
+        seterr(err, "empty token sequence");
+        return -1;
+    }
+    if (seq > max_seq_len(m)) {
+        seterr(err, "sequence length %d exceeds the model's maximum %d", seq, max_seq_len(m));
+        return -1;
+    }
+    float *x = (float *)malloc(sizeof(float) * (size_t)seq * H);
+    int rc;
+    switch (c->arch) {
+    case OR_ARCH_BERT:
+    case OR_ARCH_DISTILBERT:
+    case OR_ARCH_ROBERTA:
+    case OR_ARCH_MPNET:
+        rc = encode_bert(m, ids, seq, x, err);
+        break;
+    default:
+        seterr(err, "oracle: architecture %d not restated", c->arch);
+        rc = -1;
+    }
+    if (rc == 0) {
+        if (tokens) memcpy(tokens, x, sizeof(float) * (size_t)seq * H);
+        if (pooled) {
+            switch (c->pooling) {
+            case OR_POOL_CLS:
+                memcpy(pooled, x, sizeof(float) * H);
+                break;
+            case OR_POOL_LAST:
+                memcpy(pooled, x + (int64_t)(seq - 1) * H, sizeof(float) * H);
+                break;
+            default: /* poolMean, bert.go:692-703 */
+                for (int j = 0; j < H; j++) pooled[j] = 0.0f;
+                for (int i = 0; i < seq; i++)
+                    for (int j = 0; j < H; j++) pooled[j] += x[(int64_t)i * H + j];
+                {
+                    float inv = 1.0f / (float)seq;
+                    for (int j = 0; j < H; j++) pooled[j] *= inv;
+                }
+            }
+            if (c->normalize) or_l2normalize(pooled, H);
+        }
+    }
+    free(x);
+    return rc;
+}
+
+/* ---- batch fan-out, rembed.go:309-331 -------------------------------- */
+typedef struct {
+    or_model *m;
+    const int64_t *ids;
+    const int32_t *cu;
+    int nseq, out_kind, dim;
+    float *out;
+    int next; /* atomic work counter, like ParallelForCap (tensor.go:177-229) */
+    int failed_index;
+    char err[320];
+    pthread_mutex_t mu;
+} batch_job;
+
+static void *batch_worker(void *arg) {
+    batch_job *j = (batch_job *)arg;
+    int H = j->m->cfg.hidden;
+    float *pooled = (float *)malloc(sizeof(float) * H);
+    char err[256];
+    for (;;) {
+        int i = __atomic_fetch_add(&j->next, 1, __ATOMIC_RELAXED);
+        if (i >= j->nseq) break;
+        int s0 = j->cu[i], seq = j->cu[i + 1] - j->cu[i];
+        int rc;
+        if (j->out_kind == 1) {
+            rc = or_forward(j->m, j->ids + s0, seq, NULL, j->out + (int64_t)s0 * H, err);
+        } else {
+            rc = or_forward(j->m, j->ids + s0, seq, pooled, NULL, err);
+            if (rc == 0) {
+                /* truncate, rembed.go:441-448 */
+                if (j->dim < H) or_l2normalize(pooled, j->dim);
+                memcpy(j->out + (int64_t)i * j->dim, pooled, sizeof(float) * j->dim);
+            }
+        }
+        if (rc != 0) {
+            pthread_mutex_lock(&j->mu);
+            if (j->failed_index < 0 || i < j->failed_index) { /* firstError: lowest index */
+                j->failed_index = i;
+                snprintf(j->err, sizeof j->err, "text %d: %.255s", i, err);
+            }
+            pthread_mutex_unlock(&j->mu);
+        }
+    }
+    free(pooled);
+    return NULL;
+}
+
+int or_embed_batch(or_model *m, const int64_t *ids, const int32_t *cu_seqlens, int nseq, int nthreads,
+                   int out_kind, int dim, float *out, char *err) {
+    if (nseq <= 0) return 0;
+    if (dim <= 0 || dim > m->cfg.hidden) dim = m->cfg.hidden;
+    batch_job j;
+    memset(&j, 0, sizeof j);
+    j.m = m;
+    j.ids = ids;
+    j.cu = cu_seqlens;
+    j.nseq = nseq;
+    j.out_kind = out_kind;
+    j.dim = dim;
+    j.out = out;
+    j.failed_index = -1;
+    pthread_mutex_init(&j.mu, NULL);
+    int across = nthreads < nseq ? nthreads : nseq;
+    if (across < 1) across = 1;
+    pthread_t *th = (pthread_t *)malloc(sizeof(pthread_t) * across);
+    for (int t = 0; t < across; t++) pthread_create(&th[t], NULL, batch_worker, &j);
+    for (int t = 0; t < across; t++) pthread_join(th[t], NULL);
+    free(th);
+    pthread_mutex_destroy(&j.mu);
+    if (j.failed_index >= 0) {
+        seterr(err, "%.255s", j.err);
+        return -1;
+    }
+    return 0;
+}

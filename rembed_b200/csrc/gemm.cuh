@@ -1,0 +1,47 @@
+// gemm.cuh - the dense projection of rembed's applyDense
+// (internal/model/bert.go:282-301) as one persistent tcgen05 GEMM with a
+// fused epilogue:  out[M x N] = epi(A[M x K] . W[N x K]^T).
+#pragma once
+
+#include <cuda.h>
+#include <stdint.h>
+
+namespace rg {
+
+enum Epilogue : int {
+    kEpiBias = 0,       // + bias                      -> bf16
+    kEpiBiasGelu = 1,   // + bias, exact (erf) GELU    -> bf16
+    kEpiBiasRes = 2,    // + bias, + fp32 residual     -> fp32
+    kEpiBiasF32 = 3,    // + bias                      -> fp32
+};
+
+struct GemmArgs {
+    int M, N, K;
+    const float* bias;       // [N] or nullptr
+    const float* col_scale;  // [N] or nullptr: int8 weight dequant scale
+    const float* row_scale;  // [M] or nullptr: int8 activation dequant scale
+    const float* residual;   // [M x N] fp32, kEpiBiasRes only
+    void* out;               // [M x ld_out], bf16 or fp32
+    int ld_out;
+    int* status;             // device status word
+};
+
+// Operand element kind of the GEMM.
+enum class GemmKind : int { kBF16 = 0, kS8 = 1 };
+
+// Encode a 2-D K-major tensor map over a row-major [rows x cols] matrix
+// (cols contiguous) with a (128-byte x box_rows) box and 128-byte swizzle.
+// elem_bytes: 2 (bf16) or 1 (int8).  Returns false on failure.
+bool make_kmajor_tmap(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols,
+                      uint64_t row_stride_elems, uint32_t box_rows);
+
+// Launch the GEMM.  tmA covers A [M x K] (box rows 128), tmB covers W
+// [N x K] (box rows = block_n(N)).  Requires K % (128 / elem_bytes) == 0
+// and N % 128 == 0.
+cudaError_t gemm_launch(GemmKind kind, int epi, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                        const GemmArgs& args, int num_sms, cudaStream_t stream);
+
+// Tile width chosen for an output width N (256 where it divides N).
+inline int gemm_block_n(int N) { return (N % 256 == 0) ? 256 : 128; }
+
+}  // namespace rg

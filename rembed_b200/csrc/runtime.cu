@@ -1,0 +1,980 @@
+// runtime.cu - librembed_gpu.so: the C ABI of include/rembed_gpu.h.
+//
+// Host side of the B200 forward pass: weight ingest by Hugging Face name
+// (bert.go:338-518), Q|K|V fusion (bert.go:479-485), the reference's int8
+// quantisers (pack8.go:25-76, pack_vnni.go:28-77), one replica per device,
+// input validation (bert.go:742-747, 797-799), sequence sharding across
+// devices, and the per-layer launch sequence of encodeWorkers
+// (bert.go:839-919) over the packed batch.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/rembed_gpu.h"
+#include "gemm.cuh"
+#include "kernels.cuh"
+#include "sm100.cuh"
+
+using bf16 = __nv_bfloat16;
+
+namespace {
+
+struct Error {
+    std::string msg;
+};
+
+[[noreturn]] void fail(const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    throw Error{buf};
+}
+
+void check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) fail("%s: %s", what, cudaGetErrorString(e));
+}
+
+void set_err(char** err, const std::string& m) {
+    if (err) {
+        *err = static_cast<char*>(malloc(m.size() + 1));
+        if (*err) memcpy(*err, m.c_str(), m.size() + 1);
+    }
+}
+
+struct HostTensor {
+    std::vector<float> data;
+    std::vector<int64_t> shape;
+};
+
+// One dense projection on a device: weights [N x K] (bf16 or int8),
+// optional per-channel dequant scales, bias, and its TMA descriptor.
+struct DevDense {
+    int N = 0, K = 0;
+    void* w = nullptr;
+    float* scale = nullptr;
+    float* bias = nullptr;
+    CUtensorMap tmap;
+};
+
+struct DevLayer {
+    DevDense qkv, o, ffn1, ffn2;
+    float *ln1_g = nullptr, *ln1_b = nullptr, *ln2_g = nullptr, *ln2_b = nullptr;
+};
+
+struct Replica {
+    int device = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    std::vector<void*> allocs;
+    float *word = nullptr, *pos = nullptr, *type0 = nullptr, *emb_g = nullptr, *emb_b = nullptr;
+    std::vector<DevLayer> layers;
+    // workspace
+    int cap_T = 0, cap_seq = 0, cap_out = 0;
+    std::vector<void*> ws;
+    float *x32 = nullptr, *y32 = nullptr;
+    bf16 *xb = nullptr, *qkv = nullptr, *ctx = nullptr, *ffh = nullptr;
+    int8_t *xq = nullptr, *ctxq = nullptr, *ffhq = nullptr;
+    float *xs = nullptr, *ctxs = nullptr, *ffhs = nullptr;
+    int64_t* d_ids = nullptr;
+    int32_t* d_cu = nullptr;
+    float* d_out = nullptr;
+    int* d_status = nullptr;
+    int64_t* h_ids = nullptr;
+    int32_t* h_cu = nullptr;
+    float* h_out = nullptr;
+    int* h_status = nullptr;
+    size_t h_cap_ids = 0, h_cap_cu = 0, h_cap_out = 0;
+    CUtensorMap tm_x, tm_ctx, tm_ffh;
+    int tm_T = -1;
+    int last_launches = 0;
+    const int32_t* h_cu_view = nullptr;  // host copy of the current batch's offsets
+    // kernel timing (rg_profile)
+    bool prof = false;
+    std::vector<cudaEvent_t> ev_pool;
+    size_t ev_used = 0;
+    struct Rec {
+        int cls;
+        size_t e0, e1;
+        double flops, bytes;
+    };
+    std::vector<Rec> pending;
+    double st_ms[RG_KC_COUNT] = {}, st_flops[RG_KC_COUNT] = {}, st_bytes[RG_KC_COUNT] = {};
+    int st_n[RG_KC_COUNT] = {};
+    std::mutex mu;
+};
+
+}  // namespace
+
+struct rg_ctx {
+    rg_model_desc d{};
+    int mode = RG_MODE_BF16;
+    std::vector<int> devices;
+    std::map<std::string, HostTensor> host;
+    std::vector<Replica*> reps;
+    bool finalized = false;
+    std::mutex mu;
+};
+
+namespace {
+
+int max_seq_len(const rg_model_desc& d) {
+    int off = (d.arch == RG_ARCH_MPNET || d.arch == RG_ARCH_ROBERTA) ? d.pad_token_id + 1 : 0;
+    return d.max_position_embeddings - off;
+}
+int pos_offset(const rg_model_desc& d) {
+    return (d.arch == RG_ARCH_MPNET || d.arch == RG_ARCH_ROBERTA) ? d.pad_token_id + 1 : 0;
+}
+
+bool is_bert_family(int a) {
+    return a == RG_ARCH_BERT || a == RG_ARCH_DISTILBERT || a == RG_ARCH_ROBERTA;
+}
+
+// bf16 round-to-nearest-even of a float (NaN kept quiet).
+uint16_t to_bf16_bits(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return static_cast<uint16_t>((u >> 16) | 0x40);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return static_cast<uint16_t>(u >> 16);
+}
+
+bool finite32(float v) { return std::isfinite(v); }
+
+// PackB8 (pack8.go:25-76): float32 scale maxAbs/127, float64 division,
+// round half to even, clamp +-127.
+void quant_packb8(const float* w, int N, int K, int8_t* q, float* scales) {
+    for (int j = 0; j < N; ++j) {
+        const float* row = w + static_cast<size_t>(j) * K;
+        float maxabs = 0.f;
+        for (int p = 0; p < K; ++p) {
+            if (!finite32(row[p])) fail("PackB8: channel %d has a non-finite weight", j);
+            maxabs = std::max(maxabs, std::fabs(row[p]));
+        }
+        float s = maxabs / 127.0f;
+        if (s == 0.f) s = 1.f;
+        scales[j] = s;
+        for (int p = 0; p < K; ++p) {
+            double v = std::nearbyint(static_cast<double>(row[p]) / static_cast<double>(s));
+            v = std::min(127.0, std::max(-127.0, v));
+            q[static_cast<size_t>(j) * K + p] = static_cast<int8_t>(v);
+        }
+    }
+}
+
+// PackB8VNNI (pack_vnni.go:28-77): float64 scale, q = int8(RoundToEven(w/s)),
+// stored dequant scale float32(s).
+void quant_packb8vnni(const float* w, int N, int K, int8_t* q, float* scales) {
+    for (int c = 0; c < N; ++c) {
+        const float* row = w + static_cast<size_t>(c) * K;
+        double maxabs = 0.0;
+        for (int p = 0; p < K; ++p) {
+            if (!finite32(row[p])) fail("PackB8VNNI: weight [%d,%d] is not finite", c, p);
+            maxabs = std::max(maxabs, std::fabs(static_cast<double>(row[p])));
+        }
+        double s = maxabs / 127.0;
+        if (s == 0.0) s = 1.0;
+        scales[c] = static_cast<float>(s);
+        for (int p = 0; p < K; ++p)
+            q[static_cast<size_t>(c) * K + p] =
+                static_cast<int8_t>(static_cast<int32_t>(std::nearbyint(static_cast<double>(row[p]) / s)));
+    }
+}
+
+template <typename T>
+T* dev_alloc(Replica& r, size_t count) {
+    void* p = nullptr;
+    check(cudaMalloc(&p, std::max<size_t>(count, 1) * sizeof(T)), "cudaMalloc");
+    r.allocs.push_back(p);
+    return static_cast<T*>(p);
+}
+
+template <typename T>
+T* dev_upload(Replica& r, const T* host, size_t count) {
+    T* p = dev_alloc<T>(r, count);
+    check(cudaMemcpy(p, host, count * sizeof(T), cudaMemcpyHostToDevice), "cudaMemcpy H2D");
+    return p;
+}
+
+const HostTensor& get_tensor(rg_ctx* c, const std::string& name, std::initializer_list<int64_t> shape) {
+    static const char* prefixes[] = {"", "bert.", "roberta.", "mpnet.", "distilbert.", "model."};
+    for (const char* p : prefixes) {
+        auto it = c->host.find(std::string(p) + name);
+        if (it == c->host.end()) continue;
+        const HostTensor& t = it->second;
+        std::vector<int64_t> want(shape);
+        if (t.shape != want) {
+            std::string got, exp;
+            for (auto v : t.shape) got += std::to_string(v) + ",";
+            for (auto v : want) exp += std::to_string(v) + ",";
+            fail("tensor %s has shape [%s], want [%s]", it->first.c_str(), got.c_str(), exp.c_str());
+        }
+        return t;
+    }
+    fail("missing tensor %s", name.c_str());
+}
+
+// Quantise/convert a [N x K] fp32 weight for `mode` and upload it.
+DevDense make_dense(Replica& r, int mode, const float* w, const float* bias, int N, int K) {
+    DevDense d;
+    d.N = N;
+    d.K = K;
+    const size_t n = static_cast<size_t>(N) * K;
+    if (mode == RG_MODE_BF16) {
+        std::vector<uint16_t> h(n);
+        for (size_t i = 0; i < n; ++i) h[i] = to_bf16_bits(w[i]);
+        d.w = dev_upload(r, h.data(), n);
+        if (!rg::make_kmajor_tmap(&d.tmap, d.w, 2, N, K, K, rg::gemm_block_n(N)))
+            fail("cuTensorMapEncodeTiled failed for a [%d x %d] weight", N, K);
+    } else {
+        std::vector<int8_t> q(n);
+        std::vector<float> s(N);
+        if (mode == RG_MODE_INT8_FULL)
+            quant_packb8vnni(w, N, K, q.data(), s.data());
+        else
+            quant_packb8(w, N, K, q.data(), s.data());
+        d.w = dev_upload(r, q.data(), n);
+        d.scale = dev_upload(r, s.data(), N);
+        if (!rg::make_kmajor_tmap(&d.tmap, d.w, 1, N, K, K, rg::gemm_block_n(N)))
+            fail("cuTensorMapEncodeTiled failed for a [%d x %d] int8 weight", N, K);
+    }
+    if (bias) d.bias = dev_upload(r, bias, N);
+    return d;
+}
+
+void finalize_bert(rg_ctx* c, Replica& r) {
+    const rg_model_desc& d = c->d;
+    const int H = d.hidden_size, I = d.intermediate_size, V = d.vocab_size, P = d.max_position_embeddings;
+    const bool distil = d.arch == RG_ARCH_DISTILBERT;
+    check(cudaSetDevice(r.device), "cudaSetDevice");
+    r.word = dev_upload(r, get_tensor(c, "embeddings.word_embeddings.weight", {V, H}).data.data(), (size_t)V * H);
+    r.pos = dev_upload(r, get_tensor(c, "embeddings.position_embeddings.weight", {P, H}).data.data(), (size_t)P * H);
+    r.emb_g = dev_upload(r, get_tensor(c, "embeddings.LayerNorm.weight", {H}).data.data(), H);
+    r.emb_b = dev_upload(r, get_tensor(c, "embeddings.LayerNorm.bias", {H}).data.data(), H);
+    if (!distil) {
+        // token_type_embeddings: any first dimension, row 0 used (bert.go:507-515)
+        const HostTensor* tt = nullptr;
+        for (const char* p : {"", "bert.", "roberta."}) {
+            auto it = c->host.find(std::string(p) + "embeddings.token_type_embeddings.weight");
+            if (it != c->host.end()) tt = &it->second;
+        }
+        if (!tt) fail("missing tensor embeddings.token_type_embeddings.weight");
+        if (tt->shape.size() != 2 || tt->shape[1] != H || tt->shape[0] < 1)
+            fail("token_type_embeddings has a bad shape");
+        r.type0 = dev_upload(r, tt->data.data(), H);
+    }
+    r.layers.resize(d.num_hidden_layers);
+    for (int li = 0; li < d.num_hidden_layers; ++li) {
+        DevLayer& L = r.layers[li];
+        const std::string p = (distil ? "transformer.layer." : "encoder.layer.") + std::to_string(li) + ".";
+        auto T = [&](const std::string& n, std::initializer_list<int64_t> s) -> const float* {
+            return get_tensor(c, p + n, s).data.data();
+        };
+        const float *qW, *qB, *kW, *kB, *vW, *vB, *oW, *oB, *f1W, *f1B, *f2W, *f2B;
+        if (distil) {
+            qW = T("attention.q_lin.weight", {H, H});
+            qB = T("attention.q_lin.bias", {H});
+            kW = T("attention.k_lin.weight", {H, H});
+            kB = T("attention.k_lin.bias", {H});
+            vW = T("attention.v_lin.weight", {H, H});
+            vB = T("attention.v_lin.bias", {H});
+            oW = T("attention.out_lin.weight", {H, H});
+            oB = T("attention.out_lin.bias", {H});
+            L.ln1_g = dev_upload(r, T("sa_layer_norm.weight", {H}), H);
+            L.ln1_b = dev_upload(r, T("sa_layer_norm.bias", {H}), H);
+            f1W = T("ffn.lin1.weight", {I, H});
+            f1B = T("ffn.lin1.bias", {I});
+            f2W = T("ffn.lin2.weight", {H, I});
+            f2B = T("ffn.lin2.bias", {H});
+            L.ln2_g = dev_upload(r, T("output_layer_norm.weight", {H}), H);
+            L.ln2_b = dev_upload(r, T("output_layer_norm.bias", {H}), H);
+        } else {
+            qW = T("attention.self.query.weight", {H, H});
+            qB = T("attention.self.query.bias", {H});
+            kW = T("attention.self.key.weight", {H, H});
+            kB = T("attention.self.key.bias", {H});
+            vW = T("attention.self.value.weight", {H, H});
+            vB = T("attention.self.value.bias", {H});
+            oW = T("attention.output.dense.weight", {H, H});
+            oB = T("attention.output.dense.bias", {H});
+            L.ln1_g = dev_upload(r, T("attention.output.LayerNorm.weight", {H}), H);
+            L.ln1_b = dev_upload(r, T("attention.output.LayerNorm.bias", {H}), H);
+            f1W = T("intermediate.dense.weight", {I, H});
+            f1B = T("intermediate.dense.bias", {I});
+            f2W = T("output.dense.weight", {H, I});
+            f2B = T("output.dense.bias", {H});
+            L.ln2_g = dev_upload(r, T("output.LayerNorm.weight", {H}), H);
+            L.ln2_b = dev_upload(r, T("output.LayerNorm.bias", {H}), H);
+        }
+        // Q||K||V fused as [3H x H] rows (bert.go:479-485).
+        std::vector<float> qkvW(static_cast<size_t>(3) * H * H), qkvB(3 * H);
+        memcpy(qkvW.data(), qW, sizeof(float) * H * H);
+        memcpy(qkvW.data() + (size_t)H * H, kW, sizeof(float) * H * H);
+        memcpy(qkvW.data() + (size_t)2 * H * H, vW, sizeof(float) * H * H);
+        memcpy(qkvB.data(), qB, sizeof(float) * H);
+        memcpy(qkvB.data() + H, kB, sizeof(float) * H);
+        memcpy(qkvB.data() + 2 * H, vB, sizeof(float) * H);
+        L.qkv = make_dense(r, c->mode, qkvW.data(), qkvB.data(), 3 * H, H);
+        L.o = make_dense(r, c->mode, oW, oB, H, H);
+        L.ffn1 = make_dense(r, c->mode, f1W, f1B, I, H);
+        L.ffn2 = make_dense(r, c->mode, f2W, f2B, H, I);
+    }
+}
+
+void free_workspace(Replica& r) {
+    for (void* p : r.ws) cudaFree(p);
+    r.ws.clear();
+    if (r.h_ids) cudaFreeHost(r.h_ids);
+    if (r.h_cu) cudaFreeHost(r.h_cu);
+    if (r.h_out) cudaFreeHost(r.h_out);
+    r.h_ids = nullptr;
+    r.h_cu = nullptr;
+    r.h_out = nullptr;
+    r.h_cap_ids = r.h_cap_cu = r.h_cap_out = 0;
+    r.cap_T = r.cap_seq = r.cap_out = 0;
+    r.tm_T = -1;
+}
+
+template <typename T>
+T* ws_alloc(Replica& r, size_t count) {
+    void* p = nullptr;
+    check(cudaMalloc(&p, std::max<size_t>(count, 1) * sizeof(T)), "cudaMalloc (workspace)");
+    r.ws.push_back(p);
+    return static_cast<T*>(p);
+}
+
+// Grow the device workspace to hold T tokens / nseq sequences / nout floats.
+void ensure_workspace(rg_ctx* c, Replica& r, int T, int nseq, size_t nout) {
+    const rg_model_desc& d = c->d;
+    const int H = d.hidden_size, I = d.intermediate_size;
+    if (T > r.cap_T || nseq > r.cap_seq || nout > static_cast<size_t>(r.cap_out)) {
+        // Any stream (ours or a caller's) may still read the old buffers.
+        check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+        for (void* p : r.ws) cudaFree(p);
+        r.ws.clear();
+        const int capT = std::max(T, r.cap_T);
+        const int capS = std::max(nseq, r.cap_seq);
+        const size_t capO = std::max<size_t>(nout, r.cap_out);
+        const size_t t = static_cast<size_t>((capT + 255) / 256 * 256);
+        r.x32 = ws_alloc<float>(r, t * H);
+        r.y32 = ws_alloc<float>(r, t * H);
+        r.xb = ws_alloc<bf16>(r, t * H);
+        r.qkv = ws_alloc<bf16>(r, t * 3 * H);
+        r.ctx = ws_alloc<bf16>(r, t * H);
+        r.ffh = ws_alloc<bf16>(r, t * I);
+        if (c->mode == RG_MODE_INT8_FULL) {
+            r.xq = ws_alloc<int8_t>(r, t * H);
+            r.ctxq = ws_alloc<int8_t>(r, t * H);
+            r.ffhq = ws_alloc<int8_t>(r, t * I);
+            r.xs = ws_alloc<float>(r, t);
+            r.ctxs = ws_alloc<float>(r, t);
+            r.ffhs = ws_alloc<float>(r, t);
+        }
+        r.d_ids = ws_alloc<int64_t>(r, t);
+        r.d_cu = ws_alloc<int32_t>(r, capS + 1);
+        r.d_out = ws_alloc<float>(r, capO);
+        r.d_status = ws_alloc<int>(r, 1);
+        r.cap_T = static_cast<int>(t);
+        r.cap_seq = capS;
+        r.cap_out = static_cast<int>(capO);
+        r.tm_T = -1;
+    }
+    if (r.tm_T != T) {
+        const bool s8 = c->mode == RG_MODE_INT8_FULL;
+        const int eb = s8 ? 1 : 2;
+        const void* xa = s8 ? static_cast<const void*>(r.xq) : r.xb;
+        const void* ca = s8 ? static_cast<const void*>(r.ctxq) : r.ctx;
+        const void* fa = s8 ? static_cast<const void*>(r.ffhq) : r.ffh;
+        if (!rg::make_kmajor_tmap(&r.tm_x, xa, eb, T, H, H, 128) ||
+            !rg::make_kmajor_tmap(&r.tm_ctx, ca, eb, T, H, H, 128) ||
+            !rg::make_kmajor_tmap(&r.tm_ffh, fa, eb, T, I, I, 128))
+            fail("cuTensorMapEncodeTiled failed for the activation buffers");
+        r.tm_T = T;
+    }
+}
+
+void ensure_host_staging(Replica& r, size_t nids, size_t ncu, size_t nout) {
+    if (nids > r.h_cap_ids) {
+        if (r.h_ids) cudaFreeHost(r.h_ids);
+        check(cudaMallocHost(&r.h_ids, nids * sizeof(int64_t)), "cudaMallocHost");
+        r.h_cap_ids = nids;
+    }
+    if (ncu > r.h_cap_cu) {
+        if (r.h_cu) cudaFreeHost(r.h_cu);
+        check(cudaMallocHost(&r.h_cu, ncu * sizeof(int32_t)), "cudaMallocHost");
+        r.h_cap_cu = ncu;
+    }
+    if (nout > r.h_cap_out) {
+        if (r.h_out) cudaFreeHost(r.h_out);
+        check(cudaMallocHost(&r.h_out, nout * sizeof(float)), "cudaMallocHost");
+        r.h_cap_out = nout;
+    }
+    if (!r.h_status) check(cudaMallocHost(&r.h_status, sizeof(int)), "cudaMallocHost");
+}
+
+size_t prof_event(Replica& r, cudaStream_t st) {
+    if (r.ev_used == r.ev_pool.size()) {
+        cudaEvent_t e;
+        check(cudaEventCreate(&e), "cudaEventCreate");
+        r.ev_pool.push_back(e);
+    }
+    const size_t i = r.ev_used++;
+    check(cudaEventRecord(r.ev_pool[i], st), "cudaEventRecord");
+    return i;
+}
+
+// Brackets one launch with events when profiling is on.
+struct ProfScope {
+    Replica& r;
+    cudaStream_t st;
+    int cls;
+    double flops, bytes;
+    size_t e0 = 0;
+    ProfScope(Replica& r_, cudaStream_t st_, int cls_, double f, double b) : r(r_), st(st_), cls(cls_), flops(f), bytes(b) {
+        if (r.prof) e0 = prof_event(r, st);
+    }
+    ~ProfScope() {
+        if (r.prof) {
+            const size_t e1 = prof_event(r, st);
+            r.pending.push_back({cls, e0, e1, flops, bytes});
+        }
+    }
+};
+
+void prof_collect(Replica& r) {
+    if (r.pending.empty()) return;
+    check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+    for (const auto& p : r.pending) {
+        float ms = 0.f;
+        check(cudaEventElapsedTime(&ms, r.ev_pool[p.e0], r.ev_pool[p.e1]), "cudaEventElapsedTime");
+        r.st_ms[p.cls] += ms;
+        r.st_flops[p.cls] += p.flops;
+        r.st_bytes[p.cls] += p.bytes;
+        r.st_n[p.cls] += 1;
+    }
+    r.pending.clear();
+    r.ev_used = 0;
+}
+
+void gemm(Replica& r, int mode, const CUtensorMap& tmA, const DevDense& w, int M, int epi, const float* row_scale,
+          const float* residual, void* out, cudaStream_t st, int& launches) {
+    rg::GemmArgs a{};
+    a.M = M;
+    a.N = w.N;
+    a.K = w.K;
+    a.bias = w.bias;
+    a.col_scale = w.scale;
+    a.row_scale = row_scale;
+    a.residual = residual;
+    a.out = out;
+    a.ld_out = w.N;
+    a.status = r.d_status;
+    const rg::GemmKind kind = mode == RG_MODE_INT8_FULL ? rg::GemmKind::kS8 : rg::GemmKind::kBF16;
+    // Algorithmic bytes: A and W read once, output written once (+ fp32
+    // residual read); FLOPs 2*M*N*K.
+    const double eb = kind == rg::GemmKind::kS8 ? 1.0 : 2.0;
+    const double ob = (epi == rg::kEpiBiasRes || epi == rg::kEpiBiasF32) ? 4.0 : 2.0;
+    const double bytes = eb * (double(M) * w.K + double(w.N) * w.K) + ob * double(M) * w.N +
+                         (epi == rg::kEpiBiasRes ? 4.0 * double(M) * w.N : 0.0);
+    ProfScope ps(r, st, RG_KC_GEMM, 2.0 * M * w.N * w.K, bytes);
+    check(rg::gemm_launch(kind, epi, tmA, w.tmap, a, r.num_sms, st), "gemm launch");
+    ++launches;
+}
+
+// The forward over a batch already on the device (ids, cu in r.d_ids /
+// r.d_cu or the caller's buffers).
+void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_t* d_cu, int nseq, int T,
+                       int max_len, int out_kind, int out_dim, float* d_out, cudaStream_t st) {
+    const rg_model_desc& d = c->d;
+    const int H = d.hidden_size, heads = d.num_attention_heads, dh = H / heads;
+    const float eps = d.layer_norm_eps == 0.f ? 1e-12f : d.layer_norm_eps;
+    const int mode = c->mode;
+    const bool s8 = mode == RG_MODE_INT8_FULL;
+    int launches = 0;
+    const double Td = T, Hd = H;
+    double attn_pairs = 0.0;  // sum over sequences of L^2 (bidirectional)
+    for (int i = 0; i < nseq; ++i) {
+        const double L = r.h_cu_view ? (r.h_cu_view[i + 1] - r.h_cu_view[i]) : 0;
+        attn_pairs += L * L;
+    }
+    {
+    ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * (8.0 + 2.0 * 4.0 * Hd + 4.0 * Hd + 2.0 * Hd));
+    check(rg::launch_embed_ln(d_ids, d_cu, nseq, T, r.word, r.pos, r.type0, r.emb_g, r.emb_b, eps, H, d.vocab_size,
+                              pos_offset(d), r.x32, r.xb, s8 ? r.xq : nullptr, s8 ? r.xs : nullptr, r.d_status, st),
+          "embed_ln launch");
+    ++launches;
+    }
+    // attention: QK^T and PV over the allowed (i, j) pairs, 4*dh FLOPs each;
+    // bytes: Q, K, V read once and the context written once (bf16).
+    const double attn_flops = 4.0 * dh * attn_pairs * heads;
+    const double attn_bytes = 2.0 * (3.0 * Td * Hd + Td * Hd);
+    const double ln_bytes = Td * Hd * (4.0 + 4.0 + 2.0 + (s8 ? 1.0 : 0.0));
+    const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
+    for (int li = 0; li < d.num_hidden_layers; ++li) {
+        const DevLayer& L = r.layers[li];
+        gemm(r, mode, r.tm_x, L.qkv, T, rg::kEpiBias, s8 ? r.xs : nullptr, nullptr, r.qkv, st, launches);
+        {
+            ProfScope ps(r, st, RG_KC_ATTENTION, attn_flops, attn_bytes);
+            check(rg::launch_attention(r.qkv, d_cu, nseq, max_len, H, heads, dh, scale, r.ctx, st),
+                  "attention launch");
+            ++launches;
+        }
+        if (s8) {
+            ProfScope ps(r, st, RG_KC_QUANT, 0.0, Td * Hd * 3.0);
+            check(rg::launch_quantize_rows(r.ctx, T, H, r.ctxq, r.ctxs, st), "quantize launch");
+            ++launches;
+        }
+        gemm(r, mode, r.tm_ctx, L.o, T, rg::kEpiBiasRes, s8 ? r.ctxs : nullptr, r.x32, r.y32, st, launches);
+        {
+            ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, ln_bytes);
+            check(rg::launch_ln(r.y32, L.ln1_g, L.ln1_b, eps, T, H, r.x32, r.xb, s8 ? r.xq : nullptr,
+                                s8 ? r.xs : nullptr, st),
+                  "ln launch");
+            ++launches;
+        }
+        gemm(r, mode, r.tm_x, L.ffn1, T, rg::kEpiBiasGelu, s8 ? r.xs : nullptr, nullptr, r.ffh, st, launches);
+        if (s8) {
+            ProfScope ps(r, st, RG_KC_QUANT, 0.0, Td * d.intermediate_size * 3.0);
+            check(rg::launch_quantize_rows(r.ffh, T, d.intermediate_size, r.ffhq, r.ffhs, st), "quantize launch");
+            ++launches;
+        }
+        gemm(r, mode, r.tm_ffh, L.ffn2, T, rg::kEpiBiasRes, s8 ? r.ffhs : nullptr, r.x32, r.y32, st, launches);
+        {
+            ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, ln_bytes);
+            check(rg::launch_ln(r.y32, L.ln2_g, L.ln2_b, eps, T, H, r.x32, r.xb, s8 ? r.xq : nullptr,
+                                s8 ? r.xs : nullptr, st),
+                  "ln launch");
+            ++launches;
+        }
+    }
+    if (out_kind == RG_OUT_POOLED) {
+        const double rows = d.pooling == 0 ? Td : double(nseq);
+        ProfScope ps(r, st, RG_KC_POOL, rows * Hd, 4.0 * (rows * Hd + double(nseq) * out_dim));
+        check(rg::launch_pool(r.x32, d_cu, nseq, H, d.pooling, d.normalize, out_dim, d_out, st), "pool launch");
+        ++launches;
+    } else {
+        check(cudaMemcpyAsync(d_out, r.x32, sizeof(float) * static_cast<size_t>(T) * H, cudaMemcpyDeviceToDevice,
+                              st),
+              "cudaMemcpyAsync D2D");
+    }
+    r.last_launches = launches;
+}
+
+std::string status_message(int s) {
+    std::string m;
+    if (s & rg::kStatusBadToken) m += "token id out of vocab range; ";
+    if (s & rg::kStatusWaitTimeout) m += "a device pipeline wait timed out; ";
+    if (s & rg::kStatusBadShape) m += "inconsistent shape on the device; ";
+    if (m.empty()) m = "device error status " + std::to_string(s);
+    return m;
+}
+
+// Validate a host batch exactly as encodeWorkers does, in sequence order
+// (bert.go:742-747, 797-799); the first failing text is reported.
+void validate_batch(const rg_model_desc& d, const int64_t* ids, const int32_t* cu, int nseq) {
+    if (cu[0] != 0) fail("cu_seqlens[0] must be 0 (got %d)", cu[0]);
+    const int maxlen = max_seq_len(d);
+    for (int i = 0; i < nseq; ++i) {
+        const int len = cu[i + 1] - cu[i];
+        if (len < 0) fail("cu_seqlens must be non-decreasing (text %d)", i);
+        if (len == 0) fail("rembed: text %d: empty token sequence", i);
+        if (len > maxlen) fail("rembed: text %d: sequence length %d exceeds the model's maximum %d", i, len, maxlen);
+        for (int t = cu[i]; t < cu[i + 1]; ++t)
+            if (ids[t] < 0 || ids[t] >= d.vocab_size)
+                fail("rembed: text %d: token id %lld out of vocab range %d", i, static_cast<long long>(ids[t]),
+                     d.vocab_size);
+    }
+}
+
+// Run sequences [s_lo, s_hi) of a host batch on replica r.
+void run_host_shard(rg_ctx* c, Replica& r, const int64_t* ids, const int32_t* cu, int s_lo, int s_hi, int out_kind,
+                    int out_dim, float* host_out) {
+    std::lock_guard<std::mutex> lk(r.mu);
+    check(cudaSetDevice(r.device), "cudaSetDevice");
+    const int nseq = s_hi - s_lo;
+    if (nseq <= 0) return;
+    const int t0 = cu[s_lo], T = cu[s_hi] - t0;
+    const int H = c->d.hidden_size;
+    const size_t nout = out_kind == RG_OUT_POOLED ? static_cast<size_t>(nseq) * out_dim : static_cast<size_t>(T) * H;
+    ensure_workspace(c, r, T, nseq, nout);
+    ensure_host_staging(r, T, nseq + 1, nout);
+    int max_len = 0;
+    for (int i = 0; i <= nseq; ++i) r.h_cu[i] = cu[s_lo + i] - t0;
+    for (int i = 0; i < nseq; ++i) max_len = std::max(max_len, r.h_cu[i + 1] - r.h_cu[i]);
+    memcpy(r.h_ids, ids + t0, sizeof(int64_t) * T);
+    cudaStream_t st = r.stream;
+    check(cudaMemsetAsync(r.d_status, 0, sizeof(int), st), "cudaMemsetAsync");
+    r.h_cu_view = r.h_cu;
+    check(cudaMemcpyAsync(r.d_ids, r.h_ids, sizeof(int64_t) * T, cudaMemcpyHostToDevice, st), "H2D ids");
+    check(cudaMemcpyAsync(r.d_cu, r.h_cu, sizeof(int32_t) * (nseq + 1), cudaMemcpyHostToDevice, st), "H2D cu");
+    forward_on_device(c, r, r.d_ids, r.d_cu, nseq, T, max_len, out_kind, out_dim, r.d_out, st);
+    check(cudaMemcpyAsync(r.h_out, r.d_out, sizeof(float) * nout, cudaMemcpyDeviceToHost, st), "D2H out");
+    check(cudaMemcpyAsync(r.h_status, r.d_status, sizeof(int), cudaMemcpyDeviceToHost, st), "D2H status");
+    check(cudaStreamSynchronize(st), "forward");
+    if (*r.h_status != 0) fail("rembed: %s", status_message(*r.h_status).c_str());
+    float* dst = host_out + (out_kind == RG_OUT_POOLED ? static_cast<size_t>(s_lo) * out_dim
+                                                      : static_cast<size_t>(t0) * H);
+    memcpy(dst, r.h_out, sizeof(float) * nout);
+}
+
+// Contiguous shards with near-equal estimated cost (linear + quadratic
+// attention term), so outputs land in order in the caller's buffer.
+std::vector<int> shard_bounds(const rg_model_desc& d, const int32_t* cu, int nseq, int nrep) {
+    std::vector<double> cost(nseq + 1, 0.0);
+    const double H = d.hidden_size;
+    for (int i = 0; i < nseq; ++i) {
+        const double L = cu[i + 1] - cu[i];
+        cost[i + 1] = cost[i] + L * (12.0 * H * H) + 2.0 * L * L * H;
+    }
+    std::vector<int> b(nrep + 1, nseq);
+    b[0] = 0;
+    int s = 0;
+    for (int k = 1; k < nrep; ++k) {
+        const double target = cost[nseq] * k / nrep;
+        while (s < nseq && cost[s] < target) ++s;
+        b[k] = s;
+    }
+    return b;
+}
+
+}  // namespace
+
+// ===========================================================================
+extern "C" {
+
+int rg_init(const rg_model_desc* desc, const int* devices, int ndev, int mode, rg_ctx** out, char** err) {
+    try {
+        if (!desc || !out) fail("rg_init: null argument");
+        *out = nullptr;
+        const rg_model_desc& d = *desc;
+        if (!is_bert_family(d.arch)) fail("rg_init: architecture %d is not supported by this build", d.arch);
+        if (d.hidden_size <= 0 || d.num_hidden_layers <= 0 || d.num_attention_heads <= 0 ||
+            d.intermediate_size <= 0 || d.vocab_size <= 0 || d.max_position_embeddings <= 0)
+            fail("rg_init: missing or non-positive architecture fields");
+        if (d.hidden_size % d.num_attention_heads != 0)
+            fail("rg_init: hidden_size %d not divisible by num_attention_heads %d", d.hidden_size,
+                 d.num_attention_heads);
+        const int dh = d.hidden_size / d.num_attention_heads;
+        if (dh != 32 && dh != 64) fail("rg_init: head dim %d unsupported (32 or 64)", dh);
+        if (d.hidden_size % 128 != 0 || d.intermediate_size % 128 != 0)
+            fail("rg_init: hidden_size and intermediate_size must be multiples of 128 (got %d, %d)", d.hidden_size,
+                 d.intermediate_size);
+        if (d.pooling < 0 || d.pooling > 2) fail("rg_init: bad pooling %d", d.pooling);
+        if (mode != RG_MODE_BF16 && mode != RG_MODE_INT8_FULL)
+            fail("rg_init: mode %d is not available in this build", mode);
+        if (mode == RG_MODE_INT8_FULL && (d.hidden_size % 128 != 0 || d.intermediate_size % 128 != 0))
+            fail("rg_init: full-int8 needs K multiples of 128");
+        int ndevs = 0;
+        check(cudaGetDeviceCount(&ndevs), "cudaGetDeviceCount");
+        std::vector<int> devs;
+        if (!devices || ndev <= 0) devs.push_back(0);
+        else devs.assign(devices, devices + ndev);
+        for (int dv : devs)
+            if (dv < 0 || dv >= ndevs) fail("rg_init: device %d out of range (%d visible)", dv, ndevs);
+        rg_ctx* c = new rg_ctx();
+        c->d = d;
+        c->mode = mode;
+        c->devices = devs;
+        for (int dv : devs) {
+            Replica* r = new Replica();
+            r->device = dv;
+            c->reps.push_back(r);
+            try {
+                check(cudaSetDevice(dv), "cudaSetDevice");
+                cudaDeviceProp prop;
+                check(cudaGetDeviceProperties(&prop, dv), "cudaGetDeviceProperties");
+                if (prop.major != 10)
+                    fail("rg_init: device %d is sm_%d%d; this library is built for sm_100a", dv, prop.major,
+                         prop.minor);
+                r->num_sms = prop.multiProcessorCount;
+                check(cudaStreamCreateWithFlags(&r->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+            } catch (...) {
+                rg_free(c);
+                throw;
+            }
+        }
+        *out = c;
+        return 0;
+    } catch (const Error& e) {
+        set_err(err, e.msg);
+        return -1;
+    }
+}
+
+int rg_upload_weight(rg_ctx* c, const char* name, int dtype, const int64_t* shape, int ndim, const void* host,
+                     char** err) {
+    try {
+        if (!c || !name || !host || (!shape && ndim > 0)) fail("rg_upload_weight: null argument");
+        std::lock_guard<std::mutex> lk(c->mu);
+        if (c->finalized) fail("rg_upload_weight: context already finalized");
+        HostTensor t;
+        int64_t n = 1;
+        for (int i = 0; i < ndim; ++i) {
+            if (shape[i] < 0) fail("rg_upload_weight: negative dimension in %s", name);
+            t.shape.push_back(shape[i]);
+            n *= shape[i];
+        }
+        t.data.resize(n);
+        if (dtype == RG_DTYPE_F32) {
+            memcpy(t.data.data(), host, sizeof(float) * n);
+        } else if (dtype == RG_DTYPE_BF16) {
+            const uint16_t* s = static_cast<const uint16_t*>(host);
+            for (int64_t i = 0; i < n; ++i) {
+                uint32_t u = static_cast<uint32_t>(s[i]) << 16;
+                memcpy(&t.data[i], &u, 4);
+            }
+        } else if (dtype == RG_DTYPE_F16) {
+            const __half* s = static_cast<const __half*>(host);
+            for (int64_t i = 0; i < n; ++i) t.data[i] = __half2float(s[i]);
+        } else {
+            fail("rg_upload_weight: unknown dtype %d for %s", dtype, name);
+        }
+        c->host[name] = std::move(t);
+        return 0;
+    } catch (const Error& e) {
+        set_err(err, e.msg);
+        return -1;
+    }
+}
+
+int rg_finalize(rg_ctx* c, char** err) {
+    try {
+        if (!c) fail("rg_finalize: null context");
+        std::lock_guard<std::mutex> lk(c->mu);
+        if (c->finalized) return 0;
+        for (Replica* r : c->reps) finalize_bert(c, *r);
+        c->host.clear();
+        c->finalized = true;
+        return 0;
+    } catch (const Error& e) {
+        set_err(err, e.msg);
+        return -1;
+    }
+}
+
+int rg_forward(rg_ctx* c, const int64_t* ids, const int32_t* cu, int nseq, int out_kind, int out_dim,
+               float* host_out, char** err) {
+    try {
+        if (!c) fail("rembed: invalid context");
+        if (!c->finalized) fail("rembed: weights not finalized");
+        if (nseq < 0) fail("rembed: negative text count");
+        if (nseq == 0) return 0;
+        if (!ids || !cu || !host_out) fail("rembed: null buffer");
+        const int H = c->d.hidden_size;
+        if (out_kind == RG_OUT_POOLED) {
+            if (out_dim < 1 || out_dim > H) fail("rembed: WithDim(%d) out of range [1, %d]", out_dim, H);
+        } else if (out_kind == RG_OUT_TOKENS) {
+            if (out_dim != H) fail("rembed: token output needs out_dim == hidden (%d)", H);
+        } else {
+            fail("rembed: bad out_kind %d", out_kind);
+        }
+        validate_batch(c->d, ids, cu, nseq);
+        const int nrep = static_cast<int>(c->reps.size());
+        if (nrep == 1) {
+            run_host_shard(c, *c->reps[0], ids, cu, 0, nseq, out_kind, out_dim, host_out);
+            return 0;
+        }
+        std::vector<int> b = shard_bounds(c->d, cu, nseq, nrep);
+        std::vector<std::string> errs(nrep);
+        std::vector<std::thread> th;
+        for (int k = 0; k < nrep; ++k)
+            th.emplace_back([&, k] {
+                try {
+                    run_host_shard(c, *c->reps[k], ids, cu, b[k], b[k + 1], out_kind, out_dim, host_out);
+                } catch (const Error& e) {
+                    errs[k] = e.msg;
+                }
+            });
+        for (auto& t : th) t.join();
+        for (auto& e : errs)
+            if (!e.empty()) fail("%s", e.c_str());
+        return 0;
+    } catch (const Error& e) {
+        set_err(err, e.msg);
+        return -1;
+    }
+}
+
+int rg_forward_device(rg_ctx* c, int dev_index, const int64_t* d_ids, const int32_t* d_cu, const int32_t* h_cu,
+                      int nseq, int out_kind, int out_dim, float* d_out, void* stream, char** err) {
+    try {
+        if (!c || dev_index < 0 || dev_index >= static_cast<int>(c->reps.size())) fail("rembed: invalid context");
+        if (!c->finalized) fail("rembed: weights not finalized");
+        if (nseq <= 0) return 0;
+        Replica& r = *c->reps[dev_index];
+        std::lock_guard<std::mutex> lk(r.mu);
+        check(cudaSetDevice(r.device), "cudaSetDevice");
+        const int H = c->d.hidden_size;
+        if (out_kind == RG_OUT_POOLED && (out_dim < 1 || out_dim > H))
+            fail("rembed: WithDim(%d) out of range [1, %d]", out_dim, H);
+        if (out_kind == RG_OUT_TOKENS && out_dim != H) fail("rembed: token output needs out_dim == hidden");
+        if (h_cu[0] != 0) fail("cu_seqlens[0] must be 0");
+        int max_len = 0;
+        const int maxlen_model = max_seq_len(c->d);
+        for (int i = 0; i < nseq; ++i) {
+            const int len = h_cu[i + 1] - h_cu[i];
+            if (len <= 0) fail("rembed: text %d: empty token sequence", i);
+            if (len > maxlen_model)
+                fail("rembed: text %d: sequence length %d exceeds the model's maximum %d", i, len, maxlen_model);
+            max_len = std::max(max_len, len);
+        }
+        const int T = h_cu[nseq];
+        const size_t nout = out_kind == RG_OUT_POOLED ? static_cast<size_t>(nseq) * out_dim : static_cast<size_t>(T) * H;
+        ensure_workspace(c, r, T, nseq, nout);
+        cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : r.stream;
+        r.h_cu_view = h_cu;
+        forward_on_device(c, r, d_ids, d_cu, nseq, T, max_len, out_kind, out_dim, d_out, st);
+        r.h_cu_view = nullptr;
+        return 0;
+    } catch (const Error& e) {
+        set_err(err, e.msg);
+        return -1;
+    }
+}
+
+int rg_sync(rg_ctx* c, int dev_index, char** err) {
+    try {
+        if (!c || dev_index < 0 || dev_index >= static_cast<int>(c->reps.size())) fail("rembed: invalid context");
+        Replica& r = *c->reps[dev_index];
+        std::lock_guard<std::mutex> lk(r.mu);
+        check(cudaSetDevice(r.device), "cudaSetDevice");
+        check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+        if (r.d_status) {
+            int s = 0;
+            check(cudaMemcpy(&s, r.d_status, sizeof(int), cudaMemcpyDeviceToHost), "D2H status");
+            if (s != 0) {
+                check(cudaMemset(r.d_status, 0, sizeof(int)), "cudaMemset");
+                fail("rembed: %s", status_message(s).c_str());
+            }
+        }
+        return 0;
+    } catch (const Error& e) {
+        set_err(err, e.msg);
+        return -1;
+    }
+}
+
+int rg_profile(rg_ctx* c, int dev_index, int enable) {
+    if (!c || dev_index < 0 || dev_index >= static_cast<int>(c->reps.size())) return -1;
+    Replica& r = *c->reps[dev_index];
+    std::lock_guard<std::mutex> lk(r.mu);
+    cudaSetDevice(r.device);
+    try {
+        if (!r.pending.empty()) cudaDeviceSynchronize();
+    } catch (...) {
+    }
+    r.pending.clear();
+    r.ev_used = 0;
+    for (int k = 0; k < RG_KC_COUNT; ++k) {
+        r.st_ms[k] = r.st_flops[k] = r.st_bytes[k] = 0.0;
+        r.st_n[k] = 0;
+    }
+    r.prof = enable != 0;
+    return 0;
+}
+
+int rg_profile_stats(rg_ctx* c, int dev_index, int kc, double* ms, int* launches, double* flops, double* bytes) {
+    if (!c || dev_index < 0 || dev_index >= static_cast<int>(c->reps.size()) || kc < 0 || kc >= RG_KC_COUNT)
+        return -1;
+    Replica& r = *c->reps[dev_index];
+    std::lock_guard<std::mutex> lk(r.mu);
+    try {
+        cudaSetDevice(r.device);
+        prof_collect(r);
+    } catch (const Error&) {
+        return -1;
+    }
+    if (ms) *ms = r.st_ms[kc];
+    if (launches) *launches = r.st_n[kc];
+    if (flops) *flops = r.st_flops[kc];
+    if (bytes) *bytes = r.st_bytes[kc];
+    return 0;
+}
+
+int rg_hidden(const rg_ctx* c) { return c ? c->d.hidden_size : 0; }
+int rg_mode_active(const rg_ctx* c) { return c ? c->mode : -1; }
+int rg_last_launches(const rg_ctx* c, int dev_index) {
+    if (!c || dev_index < 0 || dev_index >= static_cast<int>(c->reps.size())) return -1;
+    return c->reps[dev_index]->last_launches;
+}
+
+void rg_free(rg_ctx* c) {
+    if (!c) return;
+    for (Replica* r : c->reps) {
+        cudaSetDevice(r->device);
+        if (r->stream) cudaStreamSynchronize(r->stream);
+        free_workspace(*r);
+        for (cudaEvent_t e : r->ev_pool) cudaEventDestroy(e);
+        for (void* p : r->allocs) cudaFree(p);
+        if (r->h_status) cudaFreeHost(r->h_status);
+        if (r->stream) cudaStreamDestroy(r->stream);
+        delete r;
+    }
+    delete c;
+}
+
+void rg_free_string(char* s) { free(s); }
+
+int rg_dense_bf16(const void* x, const void* w, const float* bias, const float* residual, void* y, int M, int N,
+                  int K, int epilogue, void* stream, char** err) {
+    try {
+        if (M <= 0) return 0;
+        if (K % 64 != 0 || N % 128 != 0) fail("rg_dense_bf16: need K %% 64 == 0 and N %% 128 == 0 (K=%d N=%d)", K, N);
+        if (epilogue < 0 || epilogue > 3) fail("rg_dense_bf16: bad epilogue %d", epilogue);
+        if (epilogue == rg::kEpiBiasRes && !residual) fail("rg_dense_bf16: residual epilogue needs a residual");
+        CUtensorMap ta, tb;
+        if (!rg::make_kmajor_tmap(&ta, x, 2, M, K, K, 128) ||
+            !rg::make_kmajor_tmap(&tb, w, 2, N, K, K, rg::gemm_block_n(N)))
+            fail("rg_dense_bf16: cuTensorMapEncodeTiled failed");
+        int dev = 0;
+        check(cudaGetDevice(&dev), "cudaGetDevice");
+        int sms = 148;
+        check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
+        // One status word per device for this kernel-level entry point.
+        static std::mutex smu;
+        static std::map<int, int*> status_words;
+        int* status = nullptr;
+        {
+            std::lock_guard<std::mutex> lk(smu);
+            auto it = status_words.find(dev);
+            if (it == status_words.end()) {
+                check(cudaMalloc(&status, sizeof(int)), "cudaMalloc");
+                check(cudaMemset(status, 0, sizeof(int)), "cudaMemset");
+                status_words[dev] = status;
+            } else {
+                status = it->second;
+            }
+        }
+        rg::GemmArgs a{};
+        a.M = M;
+        a.N = N;
+        a.K = K;
+        a.bias = bias;
+        a.residual = residual;
+        a.out = y;
+        a.ld_out = N;
+        a.status = status;
+        check(rg::gemm_launch(rg::GemmKind::kBF16, epilogue, ta, tb, a, sms, static_cast<cudaStream_t>(stream)),
+              "gemm launch");
+        return 0;
+    } catch (const Error& e) {
+        set_err(err, e.msg);
+        return -1;
+    }
+}
+
+}  // extern "C"

@@ -1,0 +1,23 @@
+import os
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU")
+
+
+@pytest.fixture(scope="session")
+def cuda():
+    """torch with a visible CUDA device (device memory and streams only)."""
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test run without a visible CUDA device")
+    return torch

@@ -1,0 +1,163 @@
+"""End-to-end parity of the CUDA forward pass against the CPU oracle.
+
+Same seeded weights and token ids on both sides; the CUDA path is reached
+only through the C ABI (rembed_b200.Embedder -> librembed_gpu.so).
+Thresholds (per embedding): bf16 path cosine >= 0.9999 and max-abs <= 2e-3;
+full int8 cosine >= 0.998 against the oracle's own full-int8 path.
+"""
+
+import numpy as np
+import pytest
+
+import oracle
+from rembed_b200 import synth
+from rembed_b200.embedder import Embedder, RembedError
+
+pytestmark = pytest.mark.gpu
+
+COS_BF16, MAXABS_BF16 = 0.9999, 2e-3
+COS_INT8_FULL = 0.998
+
+
+def cosines(a, b):
+    a = a.astype(np.float64)
+    b = b.astype(np.float64)
+    return (a * b).sum(1) / (np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1))
+
+
+def mean_pairwise_cos(e):
+    e = e.astype(np.float64)
+    e = e / np.linalg.norm(e, axis=1, keepdims=True)
+    c = e @ e.T
+    n = len(e)
+    return (c.sum() - np.trace(c)) / (n * (n - 1))
+
+
+class Model:
+    def __init__(self, name, seed=0, quant=oracle.QUANT_NONE, **kw):
+        self.cfg = synth.preset(name)
+        self.w = synth.make_weights(self.cfg, seed=seed)
+        self.gpu = Embedder(self.cfg, self.w, int8_activations=quant == oracle.QUANT_FULL,
+                            int8=quant == oracle.QUANT_WEIGHTS, **kw)
+        self.ref = oracle.OracleModel(self.cfg, self.w, quant)
+
+
+@pytest.fixture(scope="module")
+def tiny(cuda):
+    return Model("tiny-bert")
+
+
+@pytest.fixture(scope="module")
+def minilm(cuda):
+    return Model("minilm-l6")
+
+
+@pytest.fixture(scope="module")
+def bge(cuda):
+    return Model("bge-base")
+
+
+@pytest.mark.parametrize("which,nseq,lo,hi", [("tiny", 9, 1, 200), ("minilm", 16, 8, 128), ("bge", 8, 16, 512)])
+def test_pooled_parity(request, which, nseq, lo, hi):
+    m = request.getfixturevalue(which)
+    ids, cu = synth.make_batch(m.cfg, nseq, lo, hi, seed=11, id_hi=min(m.cfg.vocab_size - 1, 30521))
+    got = m.gpu.embed_packed(ids, cu)
+    want = m.ref.embed(ids, cu)
+    cos = cosines(got, want)
+    maxabs = np.abs(got - want).max(1)
+    assert cos.min() >= COS_BF16, cos
+    assert maxabs.max() <= MAXABS_BF16, maxabs
+    # the check is meaningful only if different texts embed differently
+    assert mean_pairwise_cos(want) < COS_BF16 - 0.01
+
+
+def test_bge_fixed_128(bge):
+    ids, cu = synth.make_batch(bge.cfg, 6, 128, 128, seed=5)
+    got = bge.gpu.embed_packed(ids, cu)
+    want = bge.ref.embed(ids, cu)
+    assert cosines(got, want).min() >= COS_BF16
+    assert np.abs(got - want).max() <= MAXABS_BF16
+
+
+def test_tokens_parity(minilm):
+    ids, cu = synth.make_batch(minilm.cfg, 5, 3, 70, seed=12)
+    seqs = [ids[cu[i]:cu[i + 1]] for i in range(len(cu) - 1)]
+    got = minilm.gpu.embed_tokens(seqs)
+    want = minilm.ref.embed(ids, cu, tokens=True)
+    for i, te in enumerate(got):
+        w = want[cu[i]:cu[i + 1]]
+        assert te.vectors.shape == w.shape
+        assert np.array_equal(te.ids, seqs[i])
+        assert cosines(te.vectors, w).min() >= COS_BF16
+    # EmbedTokens pools to Embed (rembed_test.go:1321-1357): mean pool + L2
+    pooled = np.stack([t.vectors.mean(0) for t in got])
+    pooled /= np.linalg.norm(pooled, axis=1, keepdims=True)
+    assert cosines(pooled, minilm.gpu.embed(seqs)).min() >= 0.99999
+
+
+def test_batch_equals_single_bit_identical(minilm):
+    """Packed varlen batching changes nothing (rembed_test.go:1265-1315)."""
+    ids, cu = synth.make_batch(minilm.cfg, 7, 1, 128, seed=13)
+    batch = minilm.gpu.embed_packed(ids, cu)
+    for i in range(len(cu) - 1):
+        one = minilm.gpu.embed([ids[cu[i]:cu[i + 1]]])
+        assert np.array_equal(one[0], batch[i]), i
+    again = minilm.gpu.embed_packed(ids, cu)
+    assert np.array_equal(again, batch)
+
+
+def test_matryoshka_dim(minilm):
+    ids, cu = synth.make_batch(minilm.cfg, 4, 5, 60, seed=14)
+    full = minilm.gpu.embed_packed(ids, cu)
+    e = Embedder(minilm.cfg, minilm.w, dim=100)
+    assert e.dim == 100
+    short = e.embed_packed(ids, cu)
+    want = full[:, :100] / np.linalg.norm(full[:, :100].astype(np.float64), axis=1, keepdims=True)
+    assert np.abs(short - want).max() <= 1e-6
+    ref = minilm.ref.embed(ids, cu, dim=100)
+    assert cosines(short, ref).min() >= COS_BF16
+    e.close()
+
+
+def test_errors_match_reference_wording(tiny):
+    g = tiny.gpu
+    with pytest.raises(RembedError, match="empty token sequence"):
+        g.embed([[101, 102], []])
+    with pytest.raises(RembedError, match="exceeds the model's maximum"):
+        g.embed([[5] * (tiny.cfg.max_seq_len() + 1)])
+    with pytest.raises(RembedError, match="out of vocab range"):
+        g.embed([[101, tiny.cfg.vocab_size, 102]])
+    with pytest.raises(RembedError, match="out of vocab range"):
+        g.embed([[101, -1, 102]])
+    # the context is still usable after a rejected call
+    assert g.embed([[101, 7, 102]]).shape == (1, tiny.cfg.hidden_size)
+
+
+def test_bad_id_on_device_path_is_reported(tiny, cuda):
+    torch = cuda
+    ids = torch.tensor([101, 5, tiny.cfg.vocab_size + 3, 102], device="cuda", dtype=torch.int64)
+    cu_h = np.array([0, 4], dtype=np.int32)
+    cu = torch.from_numpy(cu_h).cuda()
+    out = torch.empty((1, tiny.cfg.hidden_size), device="cuda")
+    torch.cuda.synchronize()
+    tiny.gpu.forward_device(ids.data_ptr(), cu.data_ptr(), cu_h, out.data_ptr())
+    with pytest.raises(RembedError, match="token id out of vocab range"):
+        tiny.gpu.sync()
+    tiny.gpu.sync()  # status cleared once reported
+
+
+def test_full_int8_parity(minilm_int8):
+    m = minilm_int8
+    assert m.gpu.quantized() and m.gpu.quantized_activations()
+    ids, cu = synth.make_batch(m.cfg, 12, 8, 128, seed=15)
+    got = m.gpu.embed_packed(ids, cu)
+    want = m.ref.embed(ids, cu)
+    assert cosines(got, want).min() >= COS_INT8_FULL
+    # "quant must be active": the int8 result differs from the fp32 oracle
+    fp = oracle.OracleModel(m.cfg, m.w, oracle.QUANT_NONE).embed(ids, cu)
+    assert np.abs(want - fp).max() > 1e-4
+
+
+@pytest.fixture(scope="module")
+def minilm_int8(cuda):
+    return Model("minilm-l6", quant=oracle.QUANT_FULL)
