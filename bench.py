@@ -50,7 +50,7 @@ METRIC = "embeddings/sec at bge-base b256×L128 (fp & int8), 1–8 GPU; tensor-p
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="bge-base-b256xL128")
@@ -263,7 +263,11 @@ def ours(args, rank, world, local_rank):
     d_ids = torch.from_numpy(ids).cuda()
     d_cu = torch.from_numpy(cu).cuda()
     d_out = torch.empty((nseq, emb.dim), device="cuda", dtype=torch.float32)
-    stream = torch.cuda.current_stream()
+    # A dedicated stream: the library launches every kernel of the forward on
+    # it, so CUDA events recorded on it bracket exactly that work.
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    assert stream.cuda_stream != 0
 
     def step():
         emb.forward_device(d_ids.data_ptr(), d_cu.data_ptr(), cu, d_out.data_ptr(), stream=stream.cuda_stream)

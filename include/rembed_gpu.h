@@ -151,6 +151,18 @@ void rg_free_string(char *s);
 int rg_dense_bf16(const void *x, const void *w, const float *bias, const float *residual, void *y,
                   int M, int N, int K, int epilogue, void *stream, char **err);
 
+/* rg_dense_residual_layernorm_bf16: the post-attention / post-FFN sublayer
+ * of the BERT family (applyDense + Add + LayerNorm, bert.go:905-907 and
+ * 916-918):  s = residual + (x . W^T + bias);  out32 = LayerNorm(s; gamma,
+ * beta, eps) in fp32 and outb = bf16(out32).  x [M x K], W [N x K] bf16;
+ * bias, gamma, beta [N] fp32; residual, out32 [M x N] fp32; outb [M x N]
+ * bf16.  The fp32 sum s is scratch in a per-device buffer that the library
+ * allocates on first use and grows as needed.  K % 64 == 0; N a multiple
+ * of 128 up to 2048.  Asynchronous on `stream`. */
+int rg_dense_residual_layernorm_bf16(const void *x, const void *w, const float *bias, const float *residual,
+                                     const float *gamma, const float *beta, float eps, float *out32, void *outb,
+                                     int M, int N, int K, void *stream, char **err);
+
 #ifdef __cplusplus
 }
 #endif

@@ -140,6 +140,15 @@ int pos_offset(const rg_model_desc& d) {
     return (d.arch == RG_ARCH_MPNET || d.arch == RG_ARCH_ROBERTA) ? d.pad_token_id + 1 : 0;
 }
 
+// Row widths the LayerNorm kernels are instantiated for (kernels.cu).
+bool ln_width_ok(int n) {
+    if (n <= 0 || n % 128 != 0) return false;
+    switch (n / 128) {
+    case 1: case 2: case 3: case 4: case 6: case 8: case 12: case 16: return true;
+    default: return false;
+    }
+}
+
 bool is_bert_family(int a) {
     return a == RG_ARCH_BERT || a == RG_ARCH_DISTILBERT || a == RG_ARCH_ROBERTA;
 }
@@ -928,6 +937,69 @@ void rg_free(rg_ctx* c) {
 }
 
 void rg_free_string(char* s) { free(s); }
+
+int rg_dense_residual_layernorm_bf16(const void* x, const void* w, const float* bias, const float* residual,
+                                     const float* gamma, const float* beta, float eps, float* out32, void* outb,
+                                     int M, int N, int K, void* stream, char** err) {
+    try {
+        if (M <= 0) return 0;
+        if (!x || !w || !residual || !gamma || !beta || !out32 || !outb)
+            fail("rg_dense_residual_layernorm_bf16: null buffer");
+        if (K % 64 != 0 || !ln_width_ok(N))
+            fail("rg_dense_residual_layernorm_bf16: unsupported shape (K=%d must be a multiple of 64; N=%d must be "
+                 "one of 128, 256, 384, 512, 768, 1024, 1536, 2048)", K, N);
+        int dev = 0;
+        check(cudaGetDevice(&dev), "cudaGetDevice");
+        int sms = 148;
+        check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        // Per-device scratch: [status word | pad to 256 B | fp32 sum M x N].
+        struct Scratch {
+            float* base = nullptr;
+            size_t floats = 0;
+        };
+        static std::mutex smu;
+        static std::map<int, Scratch> scratch;
+        const size_t need = static_cast<size_t>(M) * N + 64;
+        float* base = nullptr;
+        {
+            std::lock_guard<std::mutex> lk(smu);
+            Scratch& sc = scratch[dev];
+            if (sc.floats < need) {
+                check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+                if (sc.base) check(cudaFree(sc.base), "cudaFree");
+                sc.base = nullptr;
+                sc.floats = 0;
+                check(cudaMalloc(&sc.base, need * sizeof(float)), "cudaMalloc (sublayer scratch)");
+                sc.floats = need;
+            }
+            base = sc.base;
+        }
+        int* status = reinterpret_cast<int*>(base);
+        float* sum = base + 64;
+        check(cudaMemsetAsync(status, 0, sizeof(int), st), "cudaMemsetAsync");
+        CUtensorMap ta, tb;
+        if (!rg::make_kmajor_tmap(&ta, x, 2, M, K, K, 128) ||
+            !rg::make_kmajor_tmap(&tb, w, 2, N, K, K, rg::gemm_block_n(N)))
+            fail("rg_dense_residual_layernorm_bf16: cuTensorMapEncodeTiled failed");
+        rg::GemmArgs a{};
+        a.M = M;
+        a.N = N;
+        a.K = K;
+        a.bias = bias;
+        a.residual = residual;
+        a.out = sum;
+        a.ld_out = N;
+        a.status = status;
+        check(rg::gemm_launch(rg::GemmKind::kBF16, rg::kEpiBiasRes, ta, tb, a, sms, st), "gemm launch");
+        check(rg::launch_ln(sum, gamma, beta, eps, M, N, out32, static_cast<bf16*>(outb), nullptr, nullptr, st),
+              "ln launch");
+        return 0;
+    } catch (const Error& e) {
+        set_err(err, e.msg);
+        return -1;
+    }
+}
 
 int rg_dense_bf16(const void* x, const void* w, const float* bias, const float* residual, void* y, int M, int N,
                   int K, int epilogue, void* stream, char** err) {

@@ -104,6 +104,8 @@ SIGNATURES = {
     "rg_free_string": (None, [ctypes.c_void_p]),
     "rg_dense_bf16": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                      ctypes.c_int, _VP, _ERR]),
+    "rg_dense_residual_layernorm_bf16": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_float, _VP, _VP,
+                                                        ctypes.c_int, ctypes.c_int, ctypes.c_int, _VP, _ERR]),
 }
 
 _lib = None

@@ -65,10 +65,13 @@ def test_pooled_parity(request, which, nseq, lo, hi):
     want = m.ref.embed(ids, cu)
     cos = cosines(got, want)
     maxabs = np.abs(got - want).max(1)
+    print(f"\n[parity] {which}: min cos {cos.min():.7f}, max abs {maxabs.max():.2e}, "
+          f"mean pairwise cos between texts {mean_pairwise_cos(want):.5f}")
     assert cos.min() >= COS_BF16, cos
     assert maxabs.max() <= MAXABS_BF16, maxabs
-    # the check is meaningful only if different texts embed differently
-    assert mean_pairwise_cos(want) < COS_BF16 - 0.01
+    # The check is meaningful only if different texts are much further apart
+    # than the parity threshold allows (random-init CLS pooling is close).
+    assert mean_pairwise_cos(want) < 1 - 10 * (1 - COS_BF16)
 
 
 def test_bge_fixed_128(bge):
@@ -152,6 +155,8 @@ def test_full_int8_parity(minilm_int8):
     ids, cu = synth.make_batch(m.cfg, 12, 8, 128, seed=15)
     got = m.gpu.embed_packed(ids, cu)
     want = m.ref.embed(ids, cu)
+    print(f"\n[parity] minilm full int8: min cos {cosines(got, want).min():.6f}, "
+          f"max abs {np.abs(got - want).max():.2e}")
     assert cosines(got, want).min() >= COS_INT8_FULL
     # "quant must be active": the int8 result differs from the fp32 oracle
     fp = oracle.OracleModel(m.cfg, m.w, oracle.QUANT_NONE).embed(ids, cu)

@@ -64,3 +64,63 @@ def test_dense_rejects_bad_shapes(cuda):
     w = torch.zeros((128, 96), device="cuda", dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="K % 64"):
         run_dense(torch, x, w, None, None, 0)
+
+
+def run_sublayer(torch, x, w, bias, res, gamma, beta, eps, fn="rg_dense_residual_layernorm_bf16"):
+    from rembed_b200.embedder import RembedError, library, take_error
+
+    M, K = x.shape
+    N = w.shape[0]
+    out32 = torch.empty((M, N), device="cuda", dtype=torch.float32)
+    outb = torch.empty((M, N), device="cuda", dtype=torch.bfloat16)
+    err = ctypes.c_char_p()
+    rc = getattr(library(), fn)(
+        ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w.data_ptr()), ctypes.c_void_p(bias.data_ptr()),
+        ctypes.c_void_p(res.data_ptr()), ctypes.c_void_p(gamma.data_ptr()), ctypes.c_void_p(beta.data_ptr()),
+        ctypes.c_float(eps), ctypes.c_void_p(out32.data_ptr()), ctypes.c_void_p(outb.data_ptr()), M, N, K,
+        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), ctypes.byref(err))
+    if rc != 0:
+        raise RembedError(take_error(err))
+    torch.cuda.synchronize()
+    return out32, outb
+
+
+def sublayer_inputs(torch, M, N, K, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.randn((M, K), device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn((N, K), device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+    bias = torch.randn((N,), device="cuda", generator=g) * 0.1
+    res = torch.randn((M, N), device="cuda", generator=g)
+    gamma = 1 + 0.02 * torch.randn((N,), device="cuda", generator=g)
+    beta = 0.02 * torch.randn((N,), device="cuda", generator=g)
+    return x, w, bias, res, gamma, beta
+
+
+def sublayer_reference(x, w, bias, res, gamma, beta, eps):
+    """Add then two-pass LayerNorm in fp32 (tensor.go:383-387, 433-452)."""
+    s = res + (x.float() @ w.float().t() + bias)
+    mean = s.mean(1, keepdim=True)
+    var = ((s - mean) ** 2).mean(1, keepdim=True)
+    return (s - mean) / (var + eps).sqrt() * gamma + beta
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 128, 64), (300, 384, 384), (1000, 768, 768), (257, 768, 3072),
+                                   (64, 1024, 1024)])
+def test_dense_residual_layernorm(cuda, M, N, K):
+    torch = cuda
+    eps = 1e-12
+    args = sublayer_inputs(torch, M, N, K, seed=M + N + K)
+    out32, outb = run_sublayer(torch, *args, eps)
+    ref = sublayer_reference(*args, eps)
+    tol = 2e-4 * (1 + ref.abs()) * math.sqrt(K / 64)
+    assert float(((out32 - ref).abs() - tol).max()) <= 0, float((out32 - ref).abs().max())
+    assert torch.equal(outb, out32.to(torch.bfloat16))
+
+
+def test_dense_residual_layernorm_rejects_bad_width(cuda):
+    torch = cuda
+    from rembed_b200.embedder import RembedError
+
+    args = sublayer_inputs(torch, 4, 640, 64, seed=1)
+    with pytest.raises(RembedError, match="unsupported shape"):
+        run_sublayer(torch, *args, 1e-12)
