@@ -163,6 +163,24 @@ int rg_dense_residual_layernorm_bf16(const void *x, const void *w, const float *
                                      const float *gamma, const float *beta, float eps, float *out32, void *outb,
                                      int M, int N, int K, void *stream, char **err);
 
+/* rg_dense_residual_layernorm_bf16_noalloc: no counterpart in the reference.
+ * The same sublayer as rg_dense_residual_layernorm_bf16, for callers that
+ * must not allocate device memory (code running while a stream is captured
+ * into a CUDA graph, or a host whose memory manager owns all device
+ * allocations).  It calls no allocator: its scratch is a fixed static device
+ * array of RG_NOALLOC_SCRATCH_FLOATS floats (16 MiB) that the library image
+ * holds on every GPU where the library is loaded, until process exit.
+ * Limit: M * N <= RG_NOALLOC_SCRATCH_FLOATS (larger calls fail with an
+ * error naming the limit).  The first call on each device looks up the
+ * array's device address; make that first call before any stream capture.
+ * All calls share the array: calls that overlap on the GPU race; order them
+ * on one stream. */
+#define RG_NOALLOC_SCRATCH_FLOATS ((size_t)4 * 1024 * 1024)
+int rg_dense_residual_layernorm_bf16_noalloc(const void *x, const void *w, const float *bias,
+                                             const float *residual, const float *gamma, const float *beta,
+                                             float eps, float *out32, void *outb, int M, int N, int K,
+                                             void *stream, char **err);
+
 #ifdef __cplusplus
 }
 #endif

@@ -23,7 +23,7 @@ CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "librembed_gpu.so"
 INCLUDE = PKG.parent / "include"
-SOURCES = ["gemm.cu", "kernels.cu", "runtime.cu"]
+SOURCES = ["gemm.cu", "kernels.cu", "runtime.cu", "noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "--expt-relaxed-constexpr", f"-I{INCLUDE}"]

@@ -106,6 +106,9 @@ SIGNATURES = {
                                      ctypes.c_int, _VP, _ERR]),
     "rg_dense_residual_layernorm_bf16": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_float, _VP, _VP,
                                                         ctypes.c_int, ctypes.c_int, ctypes.c_int, _VP, _ERR]),
+    "rg_dense_residual_layernorm_bf16_noalloc": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_float, _VP,
+                                                                _VP, ctypes.c_int, ctypes.c_int, ctypes.c_int, _VP,
+                                                                _ERR]),
 }
 
 _lib = None
