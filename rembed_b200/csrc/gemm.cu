@@ -1,18 +1,25 @@
-// gemm.cu - persistent warp-specialised tcgen05 GEMM for sm_100a.
+// gemm.cu - persistent warp-specialised tcgen05 GEMM for sm_100a on CTA
+// pairs (clusters of 2, tcgen05 cta_group::2).
 //
-// One CTA per SM walks output tiles (128 x BN) in m-major order so that the
-// CTAs in flight share the same A row-blocks through L2.  Roles:
-//   warp 0     TMA producer: A and W k-blocks (128 bytes of K per row,
-//              128-byte swizzle) into a STAGES-deep shared-memory ring;
-//   warp 1     MMA issuer: one thread issues 4 tcgen05.mma per k-block into
-//              one of two TMEM accumulators (2 x BN fp32/s32 columns);
-//   warp 2     TMEM allocator;
-//   warps 4-7  epilogue: tcgen05.ld 32 columns at a time, dequant scales,
-//              bias, GELU or residual, global stores; releases the
-//              accumulator so the next tile's MMAs overlap this epilogue.
+// Each CTA pair walks output tiles of 256 x BN in m-major order (pairs in
+// flight share A row-blocks through L2).  The pair MMA reads 128 rows of A
+// and BN/2 rows of W from each CTA's shared memory and writes each CTA's
+// 128 output rows into that CTA's TMEM, so per SM a k-block moves half the
+// W bytes a single-CTA 128 x BN tile would.  Roles in every CTA:
+//   warp 0      TMA producer: its CTA's A and W k-blocks (128 bytes of K per
+//               row, 128-byte swizzle) into a STAGES-deep ring; both CTAs'
+//               loads complete on the even CTA's barrier;
+//   warp 1      (even CTA only) pair MMA issuer: 4 tcgen05.mma per k-block
+//               into one of two TMEM accumulators, commits that free the
+//               stage in both CTAs and publish finished accumulators;
+//   warp 2      TMEM allocator (pair allocation);
+//   warps 4-11  epilogue: tcgen05.ld 32 columns at a time, transpose through
+//               shared memory, dequant scales, bias, GELU or residual,
+//               coalesced stores; then release the accumulator to the even
+//               CTA so the next tile's MMAs overlap this epilogue.
 // All waits are bounded (sm100.cuh); on a timeout every role stops, the
-// producer drains its in-flight TMA loads, the issuer drains its MMAs, and
-// TMEM is freed before the CTA exits with kStatusWaitTimeout raised.
+// loads and MMAs in flight are drained, and the pair's TMEM is freed before
+// the CTAs exit with kStatusWaitTimeout raised.
 #include <cuda_bf16.h>
 
 #include "gemm.cuh"
@@ -20,24 +27,59 @@
 
 namespace rg {
 
-__device__ __forceinline__ float gelu_erf(float x) {
-    // HF "gelu": 0.5 x (1 + erf(x / sqrt(2))), the function the reference's
-    // geluScalar approximates (tensor.go:499-538).
-    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
-template <int BN, int STAGES, bool S8, int EPI>
-__global__ void __launch_bounds__(256, 1)
+// HF "gelu", 0.5 x (1 + erf(x / sqrt(2))), with erf by Abramowitz & Stegun
+// 7.1.26 (absolute error <= 1.5e-7), the published method the reference's
+// geluScalar uses (tensor.go:499-538); exp(-a^2) through ex2.approx.
+__device__ __forceinline__ float gelu_as(float x) {
+    const float a = fabsf(x) * 0.70710678118654752f;
+    const float t = __fdividef(1.0f, fmaf(0.3275911f, a, 1.0f));
+    float p = fmaf(t, 1.061405429f, -1.453152027f);
+    p = fmaf(p, t, 1.421413741f);
+    p = fmaf(p, t, -0.284496736f);
+    p = fmaf(p, t, 0.254829592f);
+    p *= t;
+    const float e = ex2_approx(-(a * a) * 1.4426950408889634f);
+    const float erf_abs = fmaf(-p, e, 1.0f);
+    const float hx = 0.5f * x;
+    return fmaf(hx, copysignf(erf_abs, x), hx);
+}
+
+constexpr int kEpiWarps = 8;        // two epilogue warps per SM sub-partition
+constexpr int kThreads = 128 + 32 * kEpiWarps;
+constexpr int kStagePitch = 33;     // floats per staged row (conflict-free)
+constexpr int kStageFloats = 32 * kStagePitch;
+
+// Per-CTA shapes of the pair kernel: the tile is 256 x BN, each CTA of the
+// pair holds 128 rows of A and BN/2 rows of W per 128-byte k-block.
+template <int BN>
+struct GemmShape {
+    static constexpr int A_BYTES = 128 * 128;
+    static constexpr int B_BYTES = (BN / 2) * 128;
+    static constexpr int STAGES = BN == 128 ? 7 : 6;
+    static constexpr uint32_t TMEM_COLS = BN == 128 ? 256 : 512;  // 2 accumulators, power of two
+    static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + kEpiWarps * kStageFloats * 4 + 1024 + 256;
+};
+
+template <int BN, bool S8, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
+    using S = GemmShape<BN>;
+    constexpr int STAGES = S::STAGES;
+    constexpr int A_BYTES = S::A_BYTES, B_BYTES = S::B_BYTES;
+    constexpr int K_ELEMS = S8 ? 128 : 64;  // elements per 128-byte k-block
+    constexpr int HALF = BN / 2;            // columns per epilogue warpgroup
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    constexpr int A_BYTES = 128 * 128;
-    constexpr int B_BYTES = BN * 128;
-    constexpr uint32_t TMEM_COLS = 2 * BN;
-    constexpr int K_ELEMS = S8 ? 128 : 64;  // elements per 128-byte k-block
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * A_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+    float* stage_f = reinterpret_cast<float*>(sB + STAGES * B_BYTES);
+    uint64_t* full = reinterpret_cast<uint64_t*>(stage_f + kEpiWarps * kStageFloats);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
@@ -46,7 +88,9 @@ __global__ void __launch_bounds__(256, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m_tiles = (args.M + 127) / 128;
+    const uint32_t rank = cluster_ctarank();  // 0: the CTA that issues the pair MMAs
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int m_tiles = (args.M + 255) / 256;
     const int n_tiles = args.N / BN;
     const int num_tiles = m_tiles * n_tiles;
     const int kblocks = args.K / K_ELEMS;
@@ -58,7 +102,7 @@ __global__ void __launch_bounds__(256, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 128);
+            mbar_init(&tempty[a], 2 * kEpiWarps);  // one arrival per epilogue warp of both CTAs
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -67,20 +111,23 @@ __global__ void __launch_bounds__(256, 1)
         tma_prefetch_desc(&tmB);
     }
     if (warp == 2) {
-        tmem_alloc(tmem_slot, TMEM_COLS);
-        tmem_relinquish();
+        tmem_alloc_pair(tmem_slot, S::TMEM_COLS);
+        tmem_relinquish_pair();
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // shared::cluster addresses of the even CTA's full / tempty barriers.
+    const uint32_t full_lead = mapa_shared(smem_u32(full), 0);
+    const uint32_t tempty_lead = mapa_shared(smem_u32(tempty), 0);
 
     if (warp == 0 && lane == 0) {
-        // ---------------- TMA producer ----------------
+        // ---------------- TMA producer (both CTAs) ----------------
         int stage = 0;
         uint32_t phase = 0;
         uint32_t issued_mask = 0, issued_parity = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        for (int tile = pair; tile < num_tiles; tile += npairs) {
             const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
             bool ok = true;
             for (int kb = 0; kb < kblocks; ++kb) {
@@ -88,9 +135,13 @@ __global__ void __launch_bounds__(256, 1)
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
-                tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * K_ELEMS, m_blk * 128);
-                tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * K_ELEMS, n_blk * BN);
+                // Both CTAs' loads complete on the even CTA's barrier, which
+                // expects the bytes of both.
+                if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (A_BYTES + B_BYTES));
+                tma_load_2d_pair(sA + stage * A_BYTES, &tmA, full_lead + 8 * stage, kb * K_ELEMS,
+                                 m_blk * 256 + rank * 128);
+                tma_load_2d_pair(sB + stage * B_BYTES, &tmB, full_lead + 8 * stage, kb * K_ELEMS,
+                                 n_blk * BN + rank * HALF);
                 issued_mask |= 1u << stage;
                 issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
                 if (++stage == STAGES) {
@@ -100,18 +151,19 @@ __global__ void __launch_bounds__(256, 1)
             }
             if (!ok) break;
         }
-        // Every issued load has landed before the CTA may exit.
-        for (int s = 0; s < STAGES; ++s)
-            if (issued_mask & (1u << s)) mbar_drain(&full[s], (issued_parity >> s) & 1);
-    } else if (warp == 1 && lane == 0) {
-        // ---------------- MMA issuer ----------------
-        constexpr uint32_t idesc = S8 ? idesc_s8(128, BN) : idesc_bf16(128, BN);
+        // The even CTA sees every load of both CTAs land on its barriers.
+        if (rank == 0)
+            for (int s = 0; s < STAGES; ++s)
+                if (issued_mask & (1u << s)) mbar_drain(&full[s], (issued_parity >> s) & 1);
+    } else if (warp == 1 && lane == 0 && rank == 0) {
+        // ---------------- pair MMA issuer (even CTA) ----------------
+        constexpr uint32_t idesc = S8 ? idesc_s8(256, BN) : idesc_bf16(256, BN);
         int stage = 0;
         uint32_t phase = 0;
         int acc = 0;
         uint32_t acc_phase = 0;
         bool issued = false;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        for (int tile = pair; tile < num_tiles; tile += npairs) {
             if (!mbar_wait(&tempty[acc], acc_phase ^ 1, args.status, abort_flag)) break;
             tc_fence_after();
             const uint32_t d = tmem_base + acc * BN;
@@ -128,121 +180,117 @@ __global__ void __launch_bounds__(256, 1)
                 for (int k = 0; k < 4; ++k) {
                     // 32 bytes of K per instruction: +2 in 16-byte units.
                     if constexpr (S8)
-                        umma_s8(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+                        umma_s8_pair(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
                     else
-                        umma_bf16(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+                        umma_bf16_pair(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
                 }
                 issued = true;
-                umma_commit(&empty[stage]);
+                // Free this stage in both CTAs once the MMAs have read it.
+                umma_commit_pair_mc(smem_u32(&empty[stage]), 0x3);
                 if (++stage == STAGES) {
                     stage = 0;
                     phase ^= 1;
                 }
             }
             if (!ok) break;
-            umma_commit(&tfull[acc]);
+            umma_commit_pair_mc(smem_u32(&tfull[acc]), 0x3);
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1;
             }
         }
         if (issued) {
-            umma_commit(drain);
+            umma_commit_pair(smem_u32(drain));
             mbar_drain(drain, 0);
         }
     } else if (warp >= 4) {
-        // ---------------- epilogue ----------------
-        const int quarter = warp - 4;  // TMEM lanes [32*quarter, 32*quarter+32)
+        // ---------------- epilogue (both CTAs, own 128 rows) ----------------
+        // Warp (4 + 4h + q) reads TMEM lanes [32q, 32q + 32) (the lane quarter
+        // its sub-partition may access) and columns [h*HALF, (h+1)*HALF).
+        const int ew = warp - 4;
+        const int quarter = warp & 3;
+        const int half = ew >> 2;
+        float* st = stage_f + ew * kStageFloats;
+        const int tr = lane >> 3;       // transposed: row offset within a 4-row group
+        const int tc = (lane & 7) * 4;  // transposed: first of 4 columns
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        for (int tile = pair; tile < num_tiles; tile += npairs) {
             const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
             if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
             tc_fence_after();
-            const int row = m_blk * 128 + quarter * 32 + lane;
-            const bool live = row < args.M;
-            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
-            const float rs = (args.row_scale && live) ? args.row_scale[row] : 1.0f;
+            const int row_base = m_blk * 256 + static_cast<int>(rank) * 128 + quarter * 32;
+            const int my_row = row_base + lane;
+            const float rs = (args.row_scale && my_row < args.M) ? args.row_scale[my_row] : 1.0f;
+            const uint32_t taddr =
+                tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + half * HALF;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
+            for (int c = 0; c < HALF / 32; ++c) {
                 uint32_t r[32];
                 tmem_ld32(taddr + c * 32, r);
                 tmem_ld_wait();
-                if (!live) continue;
-                const int col0 = n_blk * BN + c * 32;
-                float v[32];
+                // Stage this warp's 32 x 32 fragment (row-per-thread) ...
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
-                    if constexpr (S8)
-                        v[i] = static_cast<float>(static_cast<int32_t>(r[i]));
-                    else
-                        v[i] = __uint_as_float(r[i]);
+                    float v = S8 ? static_cast<float>(static_cast<int32_t>(r[i])) : __uint_as_float(r[i]);
+                    if (args.row_scale) v = v * rs;
+                    st[lane * kStagePitch + i] = v;
                 }
-                if (args.row_scale) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = v[i] * rs;
-                }
-                if (args.col_scale) {
-                    const float4* cs = reinterpret_cast<const float4*>(args.col_scale + col0);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const float4 s = __ldg(cs + i);
-                        v[4 * i + 0] *= s.x;
-                        v[4 * i + 1] *= s.y;
-                        v[4 * i + 2] *= s.z;
-                        v[4 * i + 3] *= s.w;
+                __syncwarp();
+                // ... and read it back 4 consecutive columns per lane, 4 rows
+                // per instruction, so global traffic is whole 128-byte rows.
+                const int col = n_blk * BN + half * HALF + c * 32 + tc;
+                float4 cs = make_float4(1.f, 1.f, 1.f, 1.f), bs = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (args.col_scale) cs = __ldg(reinterpret_cast<const float4*>(args.col_scale + col));
+                if (args.bias) bs = __ldg(reinterpret_cast<const float4*>(args.bias + col));
+#pragma unroll 4
+                for (int it = 0; it < 8; ++it) {
+                    const int rl = it * 4 + tr;
+                    const int row = row_base + rl;
+                    float v0 = st[rl * kStagePitch + tc + 0];
+                    float v1 = st[rl * kStagePitch + tc + 1];
+                    float v2 = st[rl * kStagePitch + tc + 2];
+                    float v3 = st[rl * kStagePitch + tc + 3];
+                    if (row >= args.M) continue;
+                    // (acc * row scale) * column scale + bias: the reference's
+                    // dequant-then-AddBias order (pack_vnni.go:155-173, bert.go:297-300)
+                    v0 = v0 * cs.x + bs.x;
+                    v1 = v1 * cs.y + bs.y;
+                    v2 = v2 * cs.z + bs.z;
+                    v3 = v3 * cs.w + bs.w;
+                    if constexpr (EPI == kEpiBiasGelu) {
+                        v0 = gelu_as(v0);
+                        v1 = gelu_as(v1);
+                        v2 = gelu_as(v2);
+                        v3 = gelu_as(v3);
                     }
-                }
-                if (args.bias) {
-                    const float4* bp = reinterpret_cast<const float4*>(args.bias + col0);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const float4 b = __ldg(bp + i);
-                        v[4 * i + 0] += b.x;
-                        v[4 * i + 1] += b.y;
-                        v[4 * i + 2] += b.z;
-                        v[4 * i + 3] += b.w;
-                    }
-                }
-                if constexpr (EPI == kEpiBiasGelu) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
-                }
-                if constexpr (EPI == kEpiBiasRes || EPI == kEpiBiasF32) {
-                    float* o = reinterpret_cast<float*>(args.out) + static_cast<size_t>(row) * args.ld_out + col0;
-                    if constexpr (EPI == kEpiBiasRes) {
-                        const float4* rp = reinterpret_cast<const float4*>(args.residual +
-                                                                           static_cast<size_t>(row) * args.N + col0);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const float4 x = __ldg(rp + i);
-                            v[4 * i + 0] = x.x + v[4 * i + 0];
-                            v[4 * i + 1] = x.y + v[4 * i + 1];
-                            v[4 * i + 2] = x.z + v[4 * i + 2];
-                            v[4 * i + 3] = x.w + v[4 * i + 3];
+                    const size_t off = static_cast<size_t>(row) * args.ld_out + col;
+                    if constexpr (EPI == kEpiBiasRes || EPI == kEpiBiasF32) {
+                        if constexpr (EPI == kEpiBiasRes) {
+                            const float4 x = __ldg(reinterpret_cast<const float4*>(
+                                args.residual + static_cast<size_t>(row) * args.N + col));
+                            v0 = x.x + v0;
+                            v1 = x.y + v1;
+                            v2 = x.z + v2;
+                            v3 = x.w + v3;
                         }
-                    }
-                    float4* o4 = reinterpret_cast<float4*>(o);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) o4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-                } else {
-                    __nv_bfloat16* o =
-                        reinterpret_cast<__nv_bfloat16*>(args.out) + static_cast<size_t>(row) * args.ld_out + col0;
-                    uint4* o4 = reinterpret_cast<uint4*>(o);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        uint32_t w[4];
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            __nv_bfloat162 p = __floats2bfloat162_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
-                            w[j] = *reinterpret_cast<uint32_t*>(&p);
-                        }
-                        o4[i] = make_uint4(w[0], w[1], w[2], w[3]);
+                        *reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + off) =
+                            make_float4(v0, v1, v2, v3);
+                    } else {
+                        __nv_bfloat162 lo = __floats2bfloat162_rn(v0, v1);
+                        __nv_bfloat162 hi = __floats2bfloat162_rn(v2, v3);
+                        uint2 pk;
+                        pk.x = *reinterpret_cast<uint32_t*>(&lo);
+                        pk.y = *reinterpret_cast<uint32_t*>(&hi);
+                        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(args.out) + off) = pk;
                     }
                 }
+                __syncwarp();
             }
+            // This warp is done with the accumulator: tell the even CTA.
             tc_fence_before();
-            mbar_arrive(&tempty[acc]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty_lead + 8 * acc);
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1;
@@ -250,10 +298,14 @@ __global__ void __launch_bounds__(256, 1)
         }
     }
 
-    __syncthreads();
+    // Teardown: every MMA has completed (the issuer drained them) and every
+    // TMEM read of both CTAs is done before the pair frees its TMEM.
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync();
     if (warp == 2) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, TMEM_COLS);
+        tmem_dealloc_pair(tmem_base, S::TMEM_COLS);
     }
 }
 
@@ -292,11 +344,12 @@ bool make_kmajor_tmap(CUtensorMap* map, const void* base, int elem_bytes, uint64
     return r == CUDA_SUCCESS;
 }
 
-template <int BN, int STAGES, bool S8, int EPI>
+template <int BN, bool S8, int EPI>
 static cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,
                               cudaStream_t stream) {
-    constexpr int smem = STAGES * (128 * 128 + BN * 128) + 1024 + 256;
-    auto kern = gemm_kernel<BN, STAGES, S8, EPI>;
+    constexpr int smem = GemmShape<BN>::SMEM;
+    static_assert(smem <= 232448, "shared memory budget");
+    auto kern = gemm_kernel<BN, S8, EPI>;
     // The shared-memory opt-in is a per-device function attribute.
     static unsigned configured = 0;
     int dev = 0;
@@ -306,36 +359,83 @@ static cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB, co
         if (e != cudaSuccess) return e;
         if (dev < 32) __atomic_fetch_or(&configured, 1u << dev, __ATOMIC_RELEASE);
     }
-    const int tiles = ((args.M + 127) / 128) * (args.N / BN);
-    const int grid = tiles < num_sms ? tiles : num_sms;
-    kern<<<grid, 256, smem, stream>>>(tmA, tmB, args);
+    // One CTA pair per tile slot: as many pairs as can be co-resident.
+    static int max_pairs[32] = {};
+    int pairs = dev < 32 ? __atomic_load_n(&max_pairs[dev], __ATOMIC_ACQUIRE) : 0;
+    if (pairs == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = 2;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = num_sms / 2;
+        }
+        pairs = n;
+        if (dev < 32) __atomic_store_n(&max_pairs[dev], pairs, __ATOMIC_RELEASE);
+    }
+    const int tiles = ((args.M + 255) / 256) * (args.N / BN);
+    const int grid = 2 * (tiles < pairs ? tiles : pairs);
+    kern<<<grid, kThreads, smem, stream>>>(tmA, tmB, args);
     return cudaGetLastError();
 }
 
-template <int BN, int STAGES, bool S8>
+template <int BN, bool S8>
 static cudaError_t dispatch_epi(int epi, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args,
                                 int num_sms, cudaStream_t stream) {
     switch (epi) {
-    case kEpiBias: return launch_one<BN, STAGES, S8, kEpiBias>(tmA, tmB, args, num_sms, stream);
-    case kEpiBiasGelu: return launch_one<BN, STAGES, S8, kEpiBiasGelu>(tmA, tmB, args, num_sms, stream);
-    case kEpiBiasRes: return launch_one<BN, STAGES, S8, kEpiBiasRes>(tmA, tmB, args, num_sms, stream);
-    case kEpiBiasF32: return launch_one<BN, STAGES, S8, kEpiBiasF32>(tmA, tmB, args, num_sms, stream);
+    case kEpiBias: return launch_one<BN, S8, kEpiBias>(tmA, tmB, args, num_sms, stream);
+    case kEpiBiasGelu: return launch_one<BN, S8, kEpiBiasGelu>(tmA, tmB, args, num_sms, stream);
+    case kEpiBiasRes: return launch_one<BN, S8, kEpiBiasRes>(tmA, tmB, args, num_sms, stream);
+    case kEpiBiasF32: return launch_one<BN, S8, kEpiBiasF32>(tmA, tmB, args, num_sms, stream);
     default: return cudaErrorInvalidValue;
     }
 }
 
-cudaError_t gemm_launch(GemmKind kind, int epi, const CUtensorMap& tmA, const CUtensorMap& tmB,
+int gemm_block_n(int M, int N, int num_sms) {
+    // Among the tile widths that divide N, the one with the fewest
+    // (waves x per-tile cost), where a tile costs about BN + 32 columns of
+    // work (the +32 models its fixed epilogue/pipeline overhead).
+    const int m_tiles = (M + 255) / 256;
+    const int pairs = num_sms / 2;
+    int best = 0;
+    long best_cost = 0;
+    for (int bn : {256, 192, 128}) {
+        if (N % bn != 0) continue;
+        const long tiles = static_cast<long>(m_tiles) * (N / bn);
+        const long waves = (tiles + pairs - 1) / pairs;
+        const long cost = waves * (bn + 32);
+        if (best == 0 || cost < best_cost) {
+            best = bn;
+            best_cost = cost;
+        }
+    }
+    return best;
+}
+
+cudaError_t gemm_launch(GemmKind kind, int epi, int block_n, const CUtensorMap& tmA, const CUtensorMap& tmB,
                         const GemmArgs& args, int num_sms, cudaStream_t stream) {
     if (args.M <= 0) return cudaSuccess;
     const int kel = kind == GemmKind::kS8 ? 128 : 64;
-    if (args.N % 128 != 0 || args.K % kel != 0 || args.K <= 0) return cudaErrorInvalidValue;
-    const int bn = gemm_block_n(args.N);
-    if (kind == GemmKind::kBF16) {
-        if (bn == 256) return dispatch_epi<256, 4, false>(epi, tmA, tmB, args, num_sms, stream);
-        return dispatch_epi<128, 6, false>(epi, tmA, tmB, args, num_sms, stream);
+    if (args.K % kel != 0 || args.K <= 0 || block_n <= 0 || args.N % block_n != 0) return cudaErrorInvalidValue;
+    const bool s8 = kind == GemmKind::kS8;
+    switch (block_n) {
+    case 256: return s8 ? dispatch_epi<256, true>(epi, tmA, tmB, args, num_sms, stream)
+                        : dispatch_epi<256, false>(epi, tmA, tmB, args, num_sms, stream);
+    case 192: return s8 ? dispatch_epi<192, true>(epi, tmA, tmB, args, num_sms, stream)
+                        : dispatch_epi<192, false>(epi, tmA, tmB, args, num_sms, stream);
+    case 128: return s8 ? dispatch_epi<128, true>(epi, tmA, tmB, args, num_sms, stream)
+                        : dispatch_epi<128, false>(epi, tmA, tmB, args, num_sms, stream);
+    default: return cudaErrorInvalidValue;
     }
-    if (bn == 256) return dispatch_epi<256, 4, true>(epi, tmA, tmB, args, num_sms, stream);
-    return dispatch_epi<128, 6, true>(epi, tmA, tmB, args, num_sms, stream);
 }
 
 }  // namespace rg

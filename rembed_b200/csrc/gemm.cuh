@@ -35,13 +35,20 @@ enum class GemmKind : int { kBF16 = 0, kS8 = 1 };
 bool make_kmajor_tmap(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols,
                       uint64_t row_stride_elems, uint32_t box_rows);
 
-// Launch the GEMM.  tmA covers A [M x K] (box rows 128), tmB covers W
-// [N x K] (box rows = block_n(N)).  Requires K % (128 / elem_bytes) == 0
-// and N % 128 == 0.
-cudaError_t gemm_launch(GemmKind kind, int epi, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                        const GemmArgs& args, int num_sms, cudaStream_t stream);
+// Output tile width (128, 192 or 256 columns) for an M x N GEMM on num_sms
+// SMs: the width dividing N with the least wave-quantised cost; 0 if none
+// divides N.
+int gemm_block_n(int M, int N, int num_sms);
 
-// Tile width chosen for an output width N (256 where it divides N).
-inline int gemm_block_n(int N) { return (N % 256 == 0) ? 256 : 128; }
+// Rows of W one CTA loads per k-block: each CTA of the pair holds half of a
+// tile's block_n columns.  The tensor map over W must use this box height.
+inline int gemm_w_box_rows(int block_n) { return block_n / 2; }
+
+// Launch the GEMM with tiles of 256 x block_n on CTA pairs.  tmA covers A
+// [M x K] with box rows 128; tmB covers W [N x K] with box rows
+// gemm_w_box_rows(block_n).  Requires K % (128 / elem_bytes) == 0 and
+// N % block_n == 0.
+cudaError_t gemm_launch(GemmKind kind, int epi, int block_n, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                        const GemmArgs& args, int num_sms, cudaStream_t stream);
 
 }  // namespace rg

@@ -125,7 +125,8 @@ extern "C" int rg_dense_residual_layernorm_bf16_noalloc(const void* x, const voi
     if (e != cudaSuccess) return set_err(err, "cudaMemsetAsync: %s", cudaGetErrorString(e));
 
     CUtensorMap ta, tb;
-    if (!rg::make_kmajor_tmap(&ta, x, 2, M, K, K, 128) || !rg::make_kmajor_tmap(&tb, w, 2, N, K, K, rg::gemm_block_n(N)))
+    const int bn = rg::gemm_block_n(M, N, sms);
+    if (!rg::make_kmajor_tmap(&ta, x, 2, M, K, K, 128) || !rg::make_kmajor_tmap(&tb, w, 2, N, K, K, rg::gemm_w_box_rows(bn)))
         return set_err(err, "rg_dense_residual_layernorm_bf16_noalloc: cuTensorMapEncodeTiled failed");
     rg::GemmArgs a{};
     a.M = M;
@@ -136,7 +137,7 @@ extern "C" int rg_dense_residual_layernorm_bf16_noalloc(const void* x, const voi
     a.out = sum;
     a.ld_out = N;
     a.status = status;
-    e = rg::gemm_launch(rg::GemmKind::kBF16, rg::kEpiBiasRes, ta, tb, a, sms, st);
+    e = rg::gemm_launch(rg::GemmKind::kBF16, rg::kEpiBiasRes, bn, ta, tb, a, sms, st);
     if (e != cudaSuccess) return set_err(err, "gemm launch: %s", cudaGetErrorString(e));
     e = rg::launch_ln(sum, gamma, beta, eps, M, N, out32, static_cast<__nv_bfloat16*>(outb), nullptr, nullptr, st);
     if (e != cudaSuccess) return set_err(err, "ln launch: %s", cudaGetErrorString(e));

@@ -68,8 +68,11 @@ struct DevDense {
     void* w = nullptr;
     float* scale = nullptr;
     float* bias = nullptr;
-    CUtensorMap tmap;
+    CUtensorMap tmap[3];  // for tile widths 256, 192, 128 (only widths dividing N are valid)
 };
+
+int bn_index(int bn) { return bn == 256 ? 0 : (bn == 192 ? 1 : 2); }
+constexpr int kBlockWidths[3] = {256, 192, 128};
 
 struct DevLayer {
     DevDense qkv, o, ffn1, ffn2;
@@ -247,8 +250,6 @@ DevDense make_dense(Replica& r, int mode, const float* w, const float* bias, int
         std::vector<uint16_t> h(n);
         for (size_t i = 0; i < n; ++i) h[i] = to_bf16_bits(w[i]);
         d.w = dev_upload(r, h.data(), n);
-        if (!rg::make_kmajor_tmap(&d.tmap, d.w, 2, N, K, K, rg::gemm_block_n(N)))
-            fail("cuTensorMapEncodeTiled failed for a [%d x %d] weight", N, K);
     } else {
         std::vector<int8_t> q(n);
         std::vector<float> s(N);
@@ -258,8 +259,12 @@ DevDense make_dense(Replica& r, int mode, const float* w, const float* bias, int
             quant_packb8(w, N, K, q.data(), s.data());
         d.w = dev_upload(r, q.data(), n);
         d.scale = dev_upload(r, s.data(), N);
-        if (!rg::make_kmajor_tmap(&d.tmap, d.w, 1, N, K, K, rg::gemm_block_n(N)))
-            fail("cuTensorMapEncodeTiled failed for a [%d x %d] int8 weight", N, K);
+    }
+    const int eb = mode == RG_MODE_BF16 ? 2 : 1;
+    for (int i = 0; i < 3; ++i) {
+        if (N % kBlockWidths[i] != 0) continue;
+        if (!rg::make_kmajor_tmap(&d.tmap[i], d.w, eb, N, K, K, rg::gemm_w_box_rows(kBlockWidths[i])))
+            fail("cuTensorMapEncodeTiled failed for a [%d x %d] weight", N, K);
     }
     if (bias) d.bias = dev_upload(r, bias, N);
     return d;
@@ -500,7 +505,9 @@ void gemm(Replica& r, int mode, const CUtensorMap& tmA, const DevDense& w, int M
     const double bytes = eb * (double(M) * w.K + double(w.N) * w.K) + ob * double(M) * w.N +
                          (epi == rg::kEpiBiasRes ? 4.0 * double(M) * w.N : 0.0);
     ProfScope ps(r, st, RG_KC_GEMM, 2.0 * M * w.N * w.K, bytes);
-    check(rg::gemm_launch(kind, epi, tmA, w.tmap, a, r.num_sms, st), "gemm launch");
+    const int bn = rg::gemm_block_n(M, w.N, r.num_sms);
+    if (bn == 0) fail("no GEMM tile width divides N=%d", w.N);
+    check(rg::gemm_launch(kind, epi, bn, tmA, w.tmap[bn_index(bn)], a, r.num_sms, st), "gemm launch");
     ++launches;
 }
 
@@ -979,8 +986,8 @@ int rg_dense_residual_layernorm_bf16(const void* x, const void* w, const float* 
         float* sum = base + 64;
         check(cudaMemsetAsync(status, 0, sizeof(int), st), "cudaMemsetAsync");
         CUtensorMap ta, tb;
-        if (!rg::make_kmajor_tmap(&ta, x, 2, M, K, K, 128) ||
-            !rg::make_kmajor_tmap(&tb, w, 2, N, K, K, rg::gemm_block_n(N)))
+        const int bn = rg::gemm_block_n(M, N, sms);
+        if (!rg::make_kmajor_tmap(&ta, x, 2, M, K, K, 128) || !rg::make_kmajor_tmap(&tb, w, 2, N, K, K, rg::gemm_w_box_rows(bn)))
             fail("rg_dense_residual_layernorm_bf16: cuTensorMapEncodeTiled failed");
         rg::GemmArgs a{};
         a.M = M;
@@ -991,7 +998,7 @@ int rg_dense_residual_layernorm_bf16(const void* x, const void* w, const float* 
         a.out = sum;
         a.ld_out = N;
         a.status = status;
-        check(rg::gemm_launch(rg::GemmKind::kBF16, rg::kEpiBiasRes, ta, tb, a, sms, st), "gemm launch");
+        check(rg::gemm_launch(rg::GemmKind::kBF16, rg::kEpiBiasRes, bn, ta, tb, a, sms, st), "gemm launch");
         check(rg::launch_ln(sum, gamma, beta, eps, M, N, out32, static_cast<bf16*>(outb), nullptr, nullptr, st),
               "ln launch");
         return 0;
@@ -1008,14 +1015,14 @@ int rg_dense_bf16(const void* x, const void* w, const float* bias, const float* 
         if (K % 64 != 0 || N % 128 != 0) fail("rg_dense_bf16: need K %% 64 == 0 and N %% 128 == 0 (K=%d N=%d)", K, N);
         if (epilogue < 0 || epilogue > 3) fail("rg_dense_bf16: bad epilogue %d", epilogue);
         if (epilogue == rg::kEpiBiasRes && !residual) fail("rg_dense_bf16: residual epilogue needs a residual");
-        CUtensorMap ta, tb;
-        if (!rg::make_kmajor_tmap(&ta, x, 2, M, K, K, 128) ||
-            !rg::make_kmajor_tmap(&tb, w, 2, N, K, K, rg::gemm_block_n(N)))
-            fail("rg_dense_bf16: cuTensorMapEncodeTiled failed");
         int dev = 0;
         check(cudaGetDevice(&dev), "cudaGetDevice");
         int sms = 148;
         check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
+        CUtensorMap ta, tb;
+        const int bn = rg::gemm_block_n(M, N, sms);
+        if (!rg::make_kmajor_tmap(&ta, x, 2, M, K, K, 128) || !rg::make_kmajor_tmap(&tb, w, 2, N, K, K, rg::gemm_w_box_rows(bn)))
+            fail("rg_dense_bf16: cuTensorMapEncodeTiled failed");
         // One status word per device for this kernel-level entry point.
         static std::mutex smu;
         static std::map<int, int*> status_words;
@@ -1040,7 +1047,7 @@ int rg_dense_bf16(const void* x, const void* w, const float* bias, const float* 
         a.out = y;
         a.ld_out = N;
         a.status = status;
-        check(rg::gemm_launch(rg::GemmKind::kBF16, epilogue, ta, tb, a, sms, static_cast<cudaStream_t>(stream)),
+        check(rg::gemm_launch(rg::GemmKind::kBF16, epilogue, bn, ta, tb, a, sms, static_cast<cudaStream_t>(stream)),
               "gemm launch");
         return 0;
     } catch (const Error& e) {
