@@ -13,10 +13,10 @@
 //               into one of two TMEM accumulators, commits that free the
 //               stage in both CTAs and publish finished accumulators;
 //   warp 2      TMEM allocator (pair allocation);
-//   warps 4-11  epilogue: tcgen05.ld 32 columns at a time, transpose through
+//   warps 4-19  epilogue: tcgen05.ld 16 columns at a time, transpose through
 //               shared memory, dequant scales, bias, GELU or residual,
-//               coalesced stores; then release the accumulator to the even
-//               CTA so the next tile's MMAs overlap this epilogue.
+//               sector-aligned stores; then release the accumulator to the
+//               even CTA so the next tile's MMAs overlap this epilogue.
 // All waits are bounded (sm100.cuh); on a timeout every role stops, the
 // loads and MMAs in flight are drained, and the pair's TMEM is freed before
 // the CTAs exit with kStatusWaitTimeout raised.
@@ -50,9 +50,10 @@ __device__ __forceinline__ float gelu_as(float x) {
     return fmaf(hx, copysignf(erf_abs, x), hx);
 }
 
-constexpr int kEpiWarps = 8;        // two epilogue warps per SM sub-partition
+constexpr int kEpiWarps = 16;       // four epilogue warps per SM sub-partition
 constexpr int kThreads = 128 + 32 * kEpiWarps;
-constexpr int kStagePitch = 33;     // floats per staged row (conflict-free)
+constexpr int kChunk = 16;          // accumulator columns per TMEM load
+constexpr int kStagePitch = 20;     // floats per staged row: 80-byte rows keep the float4 accesses conflict-free
 constexpr int kStageFloats = 32 * kStagePitch;
 
 // Per-CTA shapes of the pair kernel: the tile is 256 x BN, each CTA of the
@@ -61,7 +62,7 @@ template <int BN>
 struct GemmShape {
     static constexpr int A_BYTES = 128 * 128;
     static constexpr int B_BYTES = (BN / 2) * 128;
-    static constexpr int STAGES = BN == 128 ? 7 : 6;
+    static constexpr int STAGES = BN == 128 ? 7 : (BN == 192 ? 6 : 5);
     static constexpr uint32_t TMEM_COLS = BN == 128 ? 256 : 512;  // 2 accumulators, power of two
     static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + kEpiWarps * kStageFloats * 4 + 1024 + 256;
 };
@@ -73,7 +74,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     constexpr int STAGES = S::STAGES;
     constexpr int A_BYTES = S::A_BYTES, B_BYTES = S::B_BYTES;
     constexpr int K_ELEMS = S8 ? 128 : 64;  // elements per 128-byte k-block
-    constexpr int HALF = BN / 2;            // columns per epilogue warpgroup
+    constexpr int HALF = BN / 2;            // W rows per CTA
+    constexpr int QCOLS = BN / 4;           // accumulator columns per epilogue warp
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -205,80 +207,121 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 4) {
         // ---------------- epilogue (both CTAs, own 128 rows) ----------------
-        // Warp (4 + 4h + q) reads TMEM lanes [32q, 32q + 32) (the lane quarter
-        // its sub-partition may access) and columns [h*HALF, (h+1)*HALF).
+        // Warp (4 + 4g + q) reads TMEM lanes [32q, 32q + 32) (the lane quarter
+        // its sub-partition may access) and accumulator columns
+        // [g*QCOLS, (g+1)*QCOLS), 16 at a time.
         const int ew = warp - 4;
         const int quarter = warp & 3;
-        const int half = ew >> 2;
+        const int cgrp = ew >> 2;
         float* st = stage_f + ew * kStageFloats;
-        const int tr = lane >> 3;       // transposed: row offset within a 4-row group
-        const int tc = (lane & 7) * 4;  // transposed: first of 4 columns
+        // Transposed view of a staged 32 x 16 fragment: lane reads row
+        // (8*it + (lane & 7)), columns 4*(lane >> 3) .. +3, so each quarter
+        // warp touches 8 rows (conflict-free in shared memory) and each row
+        // gets whole 32-byte sectors in global memory.
+        const int tr = lane & 7;
+        const int tc = (lane >> 3) * 4;
+        // The fp32 residual rows this warp will read for tile t, pulled into
+        // L2 one tile ahead so the epilogue's loads hit L2.
+        auto prefetch_residual = [&](int t) {
+            if constexpr (EPI == kEpiBiasRes) {
+                if (t >= num_tiles) return;
+                const int row = (t / n_tiles) * 256 + static_cast<int>(rank) * 128 + quarter * 32 + lane;
+                if (row < args.M)
+                    prefetch_l2_bulk(args.residual + static_cast<size_t>(row) * args.N + (t % n_tiles) * BN +
+                                         cgrp * QCOLS,
+                                     QCOLS * 4);
+            }
+        };
+        prefetch_residual(pair);
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = pair; tile < num_tiles; tile += npairs) {
             const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
             if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
             tc_fence_after();
+            prefetch_residual(tile + npairs);
             const int row_base = m_blk * 256 + static_cast<int>(rank) * 128 + quarter * 32;
-            const int my_row = row_base + lane;
-            const float rs = (args.row_scale && my_row < args.M) ? args.row_scale[my_row] : 1.0f;
+            float rs = 1.0f;
+            if constexpr (S8) {
+                const int my_row = row_base + lane;
+                if (args.row_scale && my_row < args.M) rs = args.row_scale[my_row];
+            }
             const uint32_t taddr =
-                tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + half * HALF;
+                tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + cgrp * QCOLS;
 #pragma unroll 1
-            for (int c = 0; c < HALF / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(taddr + c * 32, r);
-                tmem_ld_wait();
-                // Stage this warp's 32 x 32 fragment (row-per-thread) ...
+            for (int c = 0; c < QCOLS / kChunk; ++c) {
+                const int col = n_blk * BN + cgrp * QCOLS + c * kChunk + tc;
+                float4 res[4];
+                if constexpr (EPI == kEpiBiasRes) {
+                    // residual loads first: in flight while TMEM is read
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    float v = S8 ? static_cast<float>(static_cast<int32_t>(r[i])) : __uint_as_float(r[i]);
-                    if (args.row_scale) v = v * rs;
-                    st[lane * kStagePitch + i] = v;
+                    for (int it = 0; it < 4; ++it) {
+                        const int row = row_base + it * 8 + tr;
+                        res[it] = row < args.M ? __ldg(reinterpret_cast<const float4*>(
+                                                     args.residual + static_cast<size_t>(row) * args.N + col))
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                }
+                uint32_t r[16];
+                tmem_ld16(taddr + c * kChunk, r);
+                tmem_ld_wait();
+                // Stage this warp's 32 x 16 fragment (row-per-thread) ...
+                float4* srow = reinterpret_cast<float4*>(st + lane * kStagePitch);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float4 v;
+                    if constexpr (S8) {
+                        v = make_float4(static_cast<float>(static_cast<int32_t>(r[4 * i])) * rs,
+                                        static_cast<float>(static_cast<int32_t>(r[4 * i + 1])) * rs,
+                                        static_cast<float>(static_cast<int32_t>(r[4 * i + 2])) * rs,
+                                        static_cast<float>(static_cast<int32_t>(r[4 * i + 3])) * rs);
+                    } else {
+                        v = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                        __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+                    }
+                    srow[i] = v;
                 }
                 __syncwarp();
-                // ... and read it back 4 consecutive columns per lane, 4 rows
-                // per instruction, so global traffic is whole 128-byte rows.
-                const int col = n_blk * BN + half * HALF + c * 32 + tc;
                 float4 cs = make_float4(1.f, 1.f, 1.f, 1.f), bs = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (args.col_scale) cs = __ldg(reinterpret_cast<const float4*>(args.col_scale + col));
+                if (S8 && args.col_scale) cs = __ldg(reinterpret_cast<const float4*>(args.col_scale + col));
                 if (args.bias) bs = __ldg(reinterpret_cast<const float4*>(args.bias + col));
-#pragma unroll 4
-                for (int it = 0; it < 8; ++it) {
-                    const int rl = it * 4 + tr;
+                // ... and finish it in the transposed view.
+#pragma unroll
+                for (int it = 0; it < 4; ++it) {
+                    const int rl = it * 8 + tr;
                     const int row = row_base + rl;
-                    float v0 = st[rl * kStagePitch + tc + 0];
-                    float v1 = st[rl * kStagePitch + tc + 1];
-                    float v2 = st[rl * kStagePitch + tc + 2];
-                    float v3 = st[rl * kStagePitch + tc + 3];
+                    float4 v = *reinterpret_cast<const float4*>(st + rl * kStagePitch + tc);
                     if (row >= args.M) continue;
                     // (acc * row scale) * column scale + bias: the reference's
                     // dequant-then-AddBias order (pack_vnni.go:155-173, bert.go:297-300)
-                    v0 = v0 * cs.x + bs.x;
-                    v1 = v1 * cs.y + bs.y;
-                    v2 = v2 * cs.z + bs.z;
-                    v3 = v3 * cs.w + bs.w;
+                    if constexpr (S8) {
+                        v.x = v.x * cs.x;
+                        v.y = v.y * cs.y;
+                        v.z = v.z * cs.z;
+                        v.w = v.w * cs.w;
+                    }
+                    v.x += bs.x;
+                    v.y += bs.y;
+                    v.z += bs.z;
+                    v.w += bs.w;
                     if constexpr (EPI == kEpiBiasGelu) {
-                        v0 = gelu_as(v0);
-                        v1 = gelu_as(v1);
-                        v2 = gelu_as(v2);
-                        v3 = gelu_as(v3);
+                        v.x = gelu_as(v.x);
+                        v.y = gelu_as(v.y);
+                        v.z = gelu_as(v.z);
+                        v.w = gelu_as(v.w);
                     }
                     const size_t off = static_cast<size_t>(row) * args.ld_out + col;
                     if constexpr (EPI == kEpiBiasRes || EPI == kEpiBiasF32) {
                         if constexpr (EPI == kEpiBiasRes) {
-                            const float4 x = __ldg(reinterpret_cast<const float4*>(
-                                args.residual + static_cast<size_t>(row) * args.N + col));
-                            v0 = x.x + v0;
-                            v1 = x.y + v1;
-                            v2 = x.z + v2;
-                            v3 = x.w + v3;
+                            v.x = res[it].x + v.x;
+                            v.y = res[it].y + v.y;
+                            v.z = res[it].z + v.z;
+                            v.w = res[it].w + v.w;
                         }
-                        *reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + off) =
-                            make_float4(v0, v1, v2, v3);
+                        *reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + off) = v;
                     } else {
-                        __nv_bfloat162 lo = __floats2bfloat162_rn(v0, v1);
-                        __nv_bfloat162 hi = __floats2bfloat162_rn(v2, v3);
+                        __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y);
+                        __nv_bfloat162 hi = __floats2bfloat162_rn(v.z, v.w);
                         uint2 pk;
                         pk.x = *reinterpret_cast<uint32_t*>(&lo);
                         pk.y = *reinterpret_cast<uint32_t*>(&hi);

@@ -33,7 +33,7 @@
 #include <cstring>
 #include <mutex>
 
-#include "../../include/rembed_gpu.h"
+#include "rembed_gpu.h"
 #include "gemm.cuh"
 #include "kernels.cuh"
 

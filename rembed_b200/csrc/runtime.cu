@@ -23,7 +23,7 @@
 #include <thread>
 #include <vector>
 
-#include "../../include/rembed_gpu.h"
+#include "rembed_gpu.h"
 #include "gemm.cuh"
 #include "kernels.cuh"
 #include "sm100.cuh"
