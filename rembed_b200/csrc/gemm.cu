@@ -13,9 +13,10 @@
 //               into one of two TMEM accumulators, commits that free the
 //               stage in both CTAs and publish finished accumulators;
 //   warp 2      TMEM allocator (pair allocation);
-//   warps 4-19  epilogue: tcgen05.ld 16 columns at a time, transpose through
-//               shared memory, dequant scales, bias, GELU or residual,
-//               sector-aligned stores; then release the accumulator to the
+//   warps 4-11  epilogue: tcgen05.ld 32 columns at a time (thread = row),
+//               dequant scales, bias, GELU or + residual (TMA-loaded) in
+//               registers, the row into a swizzled staging box, one TMA
+//               store per 32 x 32 box; then release the accumulator to the
 //               even CTA so the next tile's MMAs overlap this epilogue.
 // All waits are bounded (sm100.cuh); on a timeout every role stops, the
 // loads and MMAs in flight are drained, and the pair's TMEM is freed before
@@ -50,11 +51,10 @@ __device__ __forceinline__ float gelu_as(float x) {
     return fmaf(hx, copysignf(erf_abs, x), hx);
 }
 
-constexpr int kEpiWarps = 16;       // four epilogue warps per SM sub-partition
+constexpr int kEpiWarps = 8;        // two epilogue warps per SM sub-partition
 constexpr int kThreads = 128 + 32 * kEpiWarps;
-constexpr int kChunk = 16;          // accumulator columns per TMEM load
-constexpr int kStagePitch = 20;     // floats per staged row: 80-byte rows keep the float4 accesses conflict-free
-constexpr int kStageFloats = 32 * kStagePitch;
+constexpr int kChunk = 32;          // accumulator columns per TMEM load / TMA store box
+constexpr int kStageBytes = 4096;   // one 32 x 32 fp32 (or 32 x 32 bf16, half used) staging box
 
 // Per-CTA shapes of the pair kernel: the tile is 256 x BN, each CTA of the
 // pair holds 128 rows of A and BN/2 rows of W per 128-byte k-block.
@@ -62,30 +62,42 @@ template <int BN>
 struct GemmShape {
     static constexpr int A_BYTES = 128 * 128;
     static constexpr int B_BYTES = (BN / 2) * 128;
-    static constexpr int STAGES = BN == 128 ? 7 : (BN == 192 ? 6 : 5);
+    static constexpr int STAGES = BN == 128 ? 6 : 5;
     static constexpr uint32_t TMEM_COLS = BN == 128 ? 256 : 512;  // 2 accumulators, power of two
-    static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + kEpiWarps * kStageFloats * 4 + 1024 + 256;
+    // mainloop ring + two staging boxes per epilogue warp + barriers
+    static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + kEpiWarps * 2 * kStageBytes + 1024 + 512;
 };
+
+// Byte offset of 16-byte chunk c of row r in a staging box whose rows are
+// row_bytes long, laid out as the TMA swizzle of the store/load map expects
+// (128-byte swizzle for fp32 rows, 64-byte swizzle for bf16 rows): chunk bits
+// [4,7) are XORed with bits [7,10) of the unswizzled offset.
+__device__ __forceinline__ uint32_t swz(int r, int c, int row_bytes) {
+    const uint32_t off = static_cast<uint32_t>(r * row_bytes + c * 16);
+    const uint32_t mask = row_bytes == 128 ? 7u : 3u;
+    return off ^ (((off >> 7) & mask) << 4);
+}
 
 template <int BN, bool S8, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes, GemmArgs args) {
     using S = GemmShape<BN>;
     constexpr int STAGES = S::STAGES;
     constexpr int A_BYTES = S::A_BYTES, B_BYTES = S::B_BYTES;
     constexpr int K_ELEMS = S8 ? 128 : 64;  // elements per 128-byte k-block
-    constexpr int HALF = BN / 2;            // W rows per CTA
-    constexpr int QCOLS = BN / 4;           // accumulator columns per epilogue warp
+    constexpr int HALF = BN / 2;            // W rows per CTA; accumulator columns per epilogue warp
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * A_BYTES;
-    float* stage_f = reinterpret_cast<float*>(sB + STAGES * B_BYTES);
-    uint64_t* full = reinterpret_cast<uint64_t*>(stage_f + kEpiWarps * kStageFloats);
+    uint8_t* stage_base = sB + STAGES * B_BYTES;  // 1024-byte aligned
+    uint64_t* full = reinterpret_cast<uint64_t*>(stage_base + kEpiWarps * 2 * kStageBytes);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
-    uint64_t* drain = tempty + 2;
+    uint64_t* resbar = tempty + 2;  // [kEpiWarps][2]: residual box landed
+    uint64_t* drain = resbar + 2 * kEpiWarps;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -106,11 +118,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_init(&tfull[a], 1);
             mbar_init(&tempty[a], 2 * kEpiWarps);  // one arrival per epilogue warp of both CTAs
         }
+        for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&resbar[i], 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        tma_prefetch_desc(&tmOut);
+        if (EPI == kEpiBiasRes) tma_prefetch_desc(&tmRes);
     }
     if (warp == 2) {
         tmem_alloc_pair(tmem_slot, S::TMEM_COLS);
@@ -207,129 +222,148 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 4) {
         // ---------------- epilogue (both CTAs, own 128 rows) ----------------
-        // Warp (4 + 4g + q) reads TMEM lanes [32q, 32q + 32) (the lane quarter
-        // its sub-partition may access) and accumulator columns
-        // [g*QCOLS, (g+1)*QCOLS), 16 at a time.
+        // Warp (4 + 4h + q) owns TMEM lanes [32q, 32q + 32) (the lane quarter
+        // its sub-partition may access) = 32 output rows, and accumulator
+        // columns [h*HALF, (h+1)*HALF), processed 32 at a time: tcgen05.ld
+        // (thread = row), dequant / bias / GELU / + residual in registers,
+        // the row written into a swizzled staging box, one TMA store per box.
+        // The fp32 residual box arrives by TMA one chunk ahead.
+        constexpr bool F32OUT = EPI == kEpiBiasRes || EPI == kEpiBiasF32;
         const int ew = warp - 4;
         const int quarter = warp & 3;
-        const int cgrp = ew >> 2;
-        float* st = stage_f + ew * kStageFloats;
-        // Transposed view of a staged 32 x 16 fragment: lane reads row
-        // (8*it + (lane & 7)), columns 4*(lane >> 3) .. +3, so each quarter
-        // warp touches 8 rows (conflict-free in shared memory) and each row
-        // gets whole 32-byte sectors in global memory.
-        const int tr = lane & 7;
-        const int tc = (lane >> 3) * 4;
-        // The fp32 residual rows this warp will read for tile t, pulled into
-        // L2 one tile ahead so the epilogue's loads hit L2.
-        auto prefetch_residual = [&](int t) {
+        const int half = ew >> 2;
+        uint8_t* boxes = stage_base + ew * 2 * kStageBytes;
+        uint64_t* rbar = resbar + 2 * ew;
+        uint32_t rphase = 0;   // bit b: parity of the next completion of rbar[b]
+        uint32_t rpending = 0; // bit b: a residual load into buffer b is in flight (lane 0's view)
+        int k = 0;             // running chunk counter of this warp: buffer k & 1
+        constexpr int CHUNKS = HALF / kChunk;
+        // Issue the residual box of chunk c of tile t into buffer b (lane 0).
+        auto load_residual = [&](int t, int c, int b) {
             if constexpr (EPI == kEpiBiasRes) {
                 if (t >= num_tiles) return;
-                const int row = (t / n_tiles) * 256 + static_cast<int>(rank) * 128 + quarter * 32 + lane;
-                if (row < args.M)
-                    prefetch_l2_bulk(args.residual + static_cast<size_t>(row) * args.N + (t % n_tiles) * BN +
-                                         cgrp * QCOLS,
-                                     QCOLS * 4);
+                const int row0 = (t / n_tiles) * 256 + static_cast<int>(rank) * 128 + quarter * 32;
+                const int col0 = (t % n_tiles) * BN + half * HALF + c * kChunk;
+                mbar_arrive_expect_tx(&rbar[b], kStageBytes);
+                tma_load_2d(boxes + b * kStageBytes, &tmRes, &rbar[b], col0, row0);
+                rpending |= 1u << b;
             }
         };
-        prefetch_residual(pair);
+        if (lane == 0) load_residual(pair, 0, 0);
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int tile = pair; tile < num_tiles; tile += npairs) {
+        bool ok = true;
+        for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
             const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
             if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
             tc_fence_after();
-            prefetch_residual(tile + npairs);
-            const int row_base = m_blk * 256 + static_cast<int>(rank) * 128 + quarter * 32;
+            const int row0 = m_blk * 256 + static_cast<int>(rank) * 128 + quarter * 32;
             float rs = 1.0f;
             if constexpr (S8) {
-                const int my_row = row_base + lane;
-                if (args.row_scale && my_row < args.M) rs = args.row_scale[my_row];
+                if (args.row_scale && row0 + lane < args.M) rs = args.row_scale[row0 + lane];
             }
             const uint32_t taddr =
-                tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + cgrp * QCOLS;
+                tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + half * HALF;
 #pragma unroll 1
-            for (int c = 0; c < QCOLS / kChunk; ++c) {
-                const int col = n_blk * BN + cgrp * QCOLS + c * kChunk + tc;
-                float4 res[4];
-                if constexpr (EPI == kEpiBiasRes) {
-                    // residual loads first: in flight while TMEM is read
-#pragma unroll
-                    for (int it = 0; it < 4; ++it) {
-                        const int row = row_base + it * 8 + tr;
-                        res[it] = row < args.M ? __ldg(reinterpret_cast<const float4*>(
-                                                     args.residual + static_cast<size_t>(row) * args.N + col))
-                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int c = 0; c < CHUNKS; ++c, ++k) {
+                const int b = k & 1;
+                uint8_t* box = boxes + b * kStageBytes;
+                const int col0 = n_blk * BN + half * HALF + c * kChunk;
+                if (lane == 0) {
+                    if constexpr (EPI == kEpiBiasRes) {
+                        // The other buffer's store (previous chunk) has read
+                        // its box: it can take the next chunk's residual.
+                        bulk_wait_read<0>();
+                        if (c + 1 < CHUNKS)
+                            load_residual(tile, c + 1, b ^ 1);
+                        else
+                            load_residual(tile + npairs, 0, b ^ 1);
+                    } else {
+                        // This buffer's store (two chunks back) has read its box.
+                        bulk_wait_read<1>();
                     }
                 }
-                uint32_t r[16];
-                tmem_ld16(taddr + c * kChunk, r);
+                __syncwarp();
+                uint32_t r[32];
+                tmem_ld32(taddr + c * kChunk, r);
                 tmem_ld_wait();
-                // Stage this warp's 32 x 16 fragment (row-per-thread) ...
-                float4* srow = reinterpret_cast<float4*>(st + lane * kStagePitch);
+                float v[32];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    float4 v;
-                    if constexpr (S8) {
-                        v = make_float4(static_cast<float>(static_cast<int32_t>(r[4 * i])) * rs,
-                                        static_cast<float>(static_cast<int32_t>(r[4 * i + 1])) * rs,
-                                        static_cast<float>(static_cast<int32_t>(r[4 * i + 2])) * rs,
-                                        static_cast<float>(static_cast<int32_t>(r[4 * i + 3])) * rs);
-                    } else {
-                        v = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
-                                        __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
-                    }
-                    srow[i] = v;
+                for (int i = 0; i < 32; ++i) {
+                    if constexpr (S8)
+                        v[i] = static_cast<float>(static_cast<int32_t>(r[i])) * rs;
+                    else
+                        v[i] = __uint_as_float(r[i]);
                 }
-                __syncwarp();
-                float4 cs = make_float4(1.f, 1.f, 1.f, 1.f), bs = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (S8 && args.col_scale) cs = __ldg(reinterpret_cast<const float4*>(args.col_scale + col));
-                if (args.bias) bs = __ldg(reinterpret_cast<const float4*>(args.bias + col));
-                // ... and finish it in the transposed view.
+                // (acc * row scale) * column scale + bias: the reference's
+                // dequant-then-AddBias order (pack_vnni.go:155-173, bert.go:297-300)
+                if (S8 && args.col_scale) {
+                    const float4* cs = reinterpret_cast<const float4*>(args.col_scale + col0);
 #pragma unroll
-                for (int it = 0; it < 4; ++it) {
-                    const int rl = it * 8 + tr;
-                    const int row = row_base + rl;
-                    float4 v = *reinterpret_cast<const float4*>(st + rl * kStagePitch + tc);
-                    if (row >= args.M) continue;
-                    // (acc * row scale) * column scale + bias: the reference's
-                    // dequant-then-AddBias order (pack_vnni.go:155-173, bert.go:297-300)
-                    if constexpr (S8) {
-                        v.x = v.x * cs.x;
-                        v.y = v.y * cs.y;
-                        v.z = v.z * cs.z;
-                        v.w = v.w * cs.w;
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 q = __ldg(cs + i);
+                        v[4 * i] *= q.x;
+                        v[4 * i + 1] *= q.y;
+                        v[4 * i + 2] *= q.z;
+                        v[4 * i + 3] *= q.w;
                     }
-                    v.x += bs.x;
-                    v.y += bs.y;
-                    v.z += bs.z;
-                    v.w += bs.w;
-                    if constexpr (EPI == kEpiBiasGelu) {
-                        v.x = gelu_as(v.x);
-                        v.y = gelu_as(v.y);
-                        v.z = gelu_as(v.z);
-                        v.w = gelu_as(v.w);
+                }
+                if (args.bias) {
+                    const float4* bp = reinterpret_cast<const float4*>(args.bias + col0);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 q = __ldg(bp + i);
+                        v[4 * i] += q.x;
+                        v[4 * i + 1] += q.y;
+                        v[4 * i + 2] += q.z;
+                        v[4 * i + 3] += q.w;
                     }
-                    const size_t off = static_cast<size_t>(row) * args.ld_out + col;
-                    if constexpr (EPI == kEpiBiasRes || EPI == kEpiBiasF32) {
-                        if constexpr (EPI == kEpiBiasRes) {
-                            v.x = res[it].x + v.x;
-                            v.y = res[it].y + v.y;
-                            v.z = res[it].z + v.z;
-                            v.w = res[it].w + v.w;
+                }
+                if constexpr (EPI == kEpiBiasGelu) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = gelu_as(v[i]);
+                }
+                if constexpr (EPI == kEpiBiasRes) {
+                    if (!mbar_wait(&rbar[b], (rphase >> b) & 1, args.status, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    rphase ^= 1u << b;
+                    rpending &= ~(1u << b);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 x = *reinterpret_cast<const float4*>(box + swz(lane, i, 128));
+                        v[4 * i] = x.x + v[4 * i];
+                        v[4 * i + 1] = x.y + v[4 * i + 1];
+                        v[4 * i + 2] = x.z + v[4 * i + 2];
+                        v[4 * i + 3] = x.w + v[4 * i + 3];
+                    }
+                }
+                if constexpr (F32OUT) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        *reinterpret_cast<float4*>(box + swz(lane, i, 128)) =
+                            make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            __nv_bfloat162 p = __floats2bfloat162_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
+                            w[j] = *reinterpret_cast<uint32_t*>(&p);
                         }
-                        *reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + off) = v;
-                    } else {
-                        __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y);
-                        __nv_bfloat162 hi = __floats2bfloat162_rn(v.z, v.w);
-                        uint2 pk;
-                        pk.x = *reinterpret_cast<uint32_t*>(&lo);
-                        pk.y = *reinterpret_cast<uint32_t*>(&hi);
-                        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(args.out) + off) = pk;
+                        *reinterpret_cast<uint4*>(box + swz(lane, i, 64)) = make_uint4(w[0], w[1], w[2], w[3]);
                     }
                 }
+                fence_proxy_async_smem();
                 __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&tmOut, box, col0, row0);
+                    bulk_commit();
+                }
             }
+            if (!ok) break;
             // This warp is done with the accumulator: tell the even CTA.
             tc_fence_before();
             __syncwarp();
@@ -339,6 +373,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 acc_phase ^= 1;
             }
         }
+        // Every store has read its staging box, and every residual box
+        // requested has landed, before the CTA may exit.
+        if (lane == 0) {
+            bulk_wait_read<0>();
+            for (int b = 0; b < 2; ++b)
+                if (rpending & (1u << b)) mbar_drain(&rbar[b], (rphase >> b) & 1);
+        }
+        __syncwarp();
     }
 
     // Teardown: every MMA has completed (the issuer drained them) and every
@@ -388,8 +430,8 @@ bool make_kmajor_tmap(CUtensorMap* map, const void* base, int elem_bytes, uint64
 }
 
 template <int BN, bool S8, int EPI>
-static cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args, int num_sms,
-                              cudaStream_t stream) {
+static cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmOut,
+                              const CUtensorMap& tmRes, const GemmArgs& args, int num_sms, cudaStream_t stream) {
     constexpr int smem = GemmShape<BN>::SMEM;
     static_assert(smem <= 232448, "shared memory budget");
     auto kern = gemm_kernel<BN, S8, EPI>;
@@ -427,20 +469,39 @@ static cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB, co
     }
     const int tiles = ((args.M + 255) / 256) * (args.N / BN);
     const int grid = 2 * (tiles < pairs ? tiles : pairs);
-    kern<<<grid, kThreads, smem, stream>>>(tmA, tmB, args);
+    kern<<<grid, kThreads, smem, stream>>>(tmA, tmB, tmOut, tmRes, args);
     return cudaGetLastError();
 }
 
 template <int BN, bool S8>
-static cudaError_t dispatch_epi(int epi, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& args,
-                                int num_sms, cudaStream_t stream) {
+static cudaError_t dispatch_epi(int epi, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmOut,
+                                const CUtensorMap& tmRes, const GemmArgs& args, int num_sms, cudaStream_t stream) {
     switch (epi) {
-    case kEpiBias: return launch_one<BN, S8, kEpiBias>(tmA, tmB, args, num_sms, stream);
-    case kEpiBiasGelu: return launch_one<BN, S8, kEpiBiasGelu>(tmA, tmB, args, num_sms, stream);
-    case kEpiBiasRes: return launch_one<BN, S8, kEpiBiasRes>(tmA, tmB, args, num_sms, stream);
-    case kEpiBiasF32: return launch_one<BN, S8, kEpiBiasF32>(tmA, tmB, args, num_sms, stream);
+    case kEpiBias: return launch_one<BN, S8, kEpiBias>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
+    case kEpiBiasGelu: return launch_one<BN, S8, kEpiBiasGelu>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
+    case kEpiBiasRes: return launch_one<BN, S8, kEpiBiasRes>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
+    case kEpiBiasF32: return launch_one<BN, S8, kEpiBiasF32>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
     default: return cudaErrorInvalidValue;
     }
+}
+
+// Output / residual maps: 32 x 32 boxes, rows of 128 bytes (fp32, 128-byte
+// swizzle) or 64 bytes (bf16, 64-byte swizzle), matching swz() above.
+static bool make_epilogue_tmap(CUtensorMap* map, const void* base, bool f32, uint64_t rows, uint64_t cols,
+                               uint64_t ld) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
+    const uint64_t eb = f32 ? 4 : 2;
+    if ((ld * eb) % 16 != 0) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld * eb};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
 }
 
 int gemm_block_n(int M, int N, int num_sms) {
@@ -470,13 +531,22 @@ cudaError_t gemm_launch(GemmKind kind, int epi, int block_n, const CUtensorMap& 
     const int kel = kind == GemmKind::kS8 ? 128 : 64;
     if (args.K % kel != 0 || args.K <= 0 || block_n <= 0 || args.N % block_n != 0) return cudaErrorInvalidValue;
     const bool s8 = kind == GemmKind::kS8;
+    const bool f32out = epi == kEpiBiasRes || epi == kEpiBiasF32;
+    CUtensorMap tmOut, tmRes;
+    if (!make_epilogue_tmap(&tmOut, args.out, f32out, args.M, args.N, args.ld_out)) return cudaErrorInvalidValue;
+    if (epi == kEpiBiasRes) {
+        if (!args.residual || !make_epilogue_tmap(&tmRes, args.residual, true, args.M, args.N, args.N))
+            return cudaErrorInvalidValue;
+    } else {
+        tmRes = tmOut;  // unused
+    }
     switch (block_n) {
-    case 256: return s8 ? dispatch_epi<256, true>(epi, tmA, tmB, args, num_sms, stream)
-                        : dispatch_epi<256, false>(epi, tmA, tmB, args, num_sms, stream);
-    case 192: return s8 ? dispatch_epi<192, true>(epi, tmA, tmB, args, num_sms, stream)
-                        : dispatch_epi<192, false>(epi, tmA, tmB, args, num_sms, stream);
-    case 128: return s8 ? dispatch_epi<128, true>(epi, tmA, tmB, args, num_sms, stream)
-                        : dispatch_epi<128, false>(epi, tmA, tmB, args, num_sms, stream);
+    case 256: return s8 ? dispatch_epi<256, true>(epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream)
+                        : dispatch_epi<256, false>(epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream);
+    case 192: return s8 ? dispatch_epi<192, true>(epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream)
+                        : dispatch_epi<192, false>(epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream);
+    case 128: return s8 ? dispatch_epi<128, true>(epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream)
+                        : dispatch_epi<128, false>(epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream);
     default: return cudaErrorInvalidValue;
     }
 }
