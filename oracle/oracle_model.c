@@ -47,6 +47,16 @@ typedef struct {
     const float *attn_ln_g, *attn_ln_b, *out_ln_g, *out_ln_b;
 } bert_layer;
 
+/* One decoder-style layer (qwen3.go:20-34, modernbert.go:20-28,
+ * gemma3.go:20-38, nomic.go:12-20); unused fields stay NULL. */
+typedef struct {
+    dense q, k, v, qkv, o, gate, up, down, wi, fc11, fc12;
+    const float *in_norm, *q_norm, *k_norm, *post_attn, *pre_ffn, *post_ffn, *mlp_norm;
+    float *own[6]; /* unit-offset copies (Gemma) */
+    const float *n1g, *n1b, *n2g, *n2b;
+    int global;
+} dec_layer;
+
 struct or_model {
     or_config cfg;
     int quant;
@@ -56,6 +66,10 @@ struct or_model {
     int pos_off;
     const float *word_emb, *pos_emb, *type_emb, *emb_ln_g, *emb_ln_b, *rel_bias;
     bert_layer *layers;
+    dec_layer *dl;
+    const float *final_norm;
+    float *final_norm_own, *zero_beta;
+    const float *dense1, *dense2; /* Gemma Dense head [D x H], [H x D] */
 };
 
 static void seterr(char *err, const char *fmt, ...) {
@@ -263,6 +277,123 @@ static int finalize_bert(or_model *m, char *err) {
     return -1;
 }
 
+static float *unit_offset(const float *v, int n) { /* gemma3.go:44-50 */
+    float *o = (float *)malloc(sizeof(float) * n);
+    for (int i = 0; i < n; i++) o[i] = v[i] + 1.0f;
+    return o;
+}
+
+/* qwen3.go:114-183, modernbert.go:33-106, gemma3.go:57-170, nomic.go:22-111 */
+static int finalize_decoder(or_model *m, char *err) {
+    const or_config *c = &m->cfg;
+    int arch = c->arch, H = c->hidden, I = c->inter, q = m->quant;
+    int dh = c->head_dim ? c->head_dim : H / c->heads;
+    int nq = c->heads, nkv = c->kv_heads ? c->kv_heads : c->heads;
+    int qd = nq * dh, kvd = nkv * dh;
+    char nm[NAMELEN];
+    m->dl = (dec_layer *)calloc(c->layers, sizeof(dec_layer));
+    if (arch == OR_ARCH_QWEN3) {
+        if (!(m->word_emb = get_tensor(m, "embed_tokens.weight", (int64_t)c->vocab * H, err))) return -1;
+        if (!(m->final_norm = get_tensor(m, "norm.weight", H, err))) return -1;
+    } else if (arch == OR_ARCH_GEMMA3) {
+        const float *fn;
+        if (!(m->word_emb = get_tensor(m, "embed_tokens.weight", (int64_t)c->vocab * H, err))) return -1;
+        if (!(fn = get_tensor(m, "norm.weight", H, err))) return -1;
+        m->final_norm = m->final_norm_own = unit_offset(fn, H);
+        if (!(m->dense1 = get_tensor(m, "2_Dense.linear.weight", (int64_t)c->dense_hidden * H, err))) return -1;
+        if (!(m->dense2 = get_tensor(m, "3_Dense.linear.weight", (int64_t)H * c->dense_hidden, err))) return -1;
+    } else if (arch == OR_ARCH_MODERNBERT) {
+        if (!(m->word_emb = get_tensor(m, "embeddings.tok_embeddings.weight", (int64_t)c->vocab * H, err))) return -1;
+        if (!(m->emb_ln_g = get_tensor(m, "embeddings.norm.weight", H, err))) return -1;
+        if (!(m->final_norm = get_tensor(m, "final_norm.weight", H, err))) return -1;
+        m->zero_beta = (float *)calloc(H, sizeof(float));
+    } else { /* nomic */
+        if (!(m->word_emb = get_tensor(m, "embeddings.word_embeddings.weight", (int64_t)c->vocab * H, err))) return -1;
+        if (!(m->type_emb = get_tensor(m, "embeddings.token_type_embeddings.weight", 2 * (int64_t)H, err))) return -1;
+        if (!(m->emb_ln_g = get_tensor(m, "emb_ln.weight", H, err))) return -1;
+        if (!(m->emb_ln_b = get_tensor(m, "emb_ln.bias", H, err))) return -1;
+    }
+#define GETL(dst, name, n)                                        \
+    do {                                                          \
+        snprintf(nm, sizeof nm, "%s%d.%s", pre, li, name);        \
+        if (!((dst) = get_tensor(m, nm, (n), err))) return -1;    \
+    } while (0)
+    for (int li = 0; li < c->layers; li++) {
+        dec_layer *l = &m->dl[li];
+        const float *w1, *w2, *w3, *w4;
+        if (arch == OR_ARCH_QWEN3 || arch == OR_ARCH_GEMMA3) {
+            const char *pre = "layers.";
+            const float *in, *qn, *kn, *pa = NULL, *pf = NULL, *pff = NULL, *post = NULL;
+            GETL(in, "input_layernorm.weight", H);
+            GETL(qn, "self_attn.q_norm.weight", dh);
+            GETL(kn, "self_attn.k_norm.weight", dh);
+            if (arch == OR_ARCH_QWEN3) {
+                GETL(post, "post_attention_layernorm.weight", H);
+                l->in_norm = in;
+                l->q_norm = qn;
+                l->k_norm = kn;
+                l->post_attn = post;
+            } else {
+                GETL(pa, "post_attention_layernorm.weight", H);
+                GETL(pf, "pre_feedforward_layernorm.weight", H);
+                GETL(pff, "post_feedforward_layernorm.weight", H);
+                l->in_norm = l->own[0] = unit_offset(in, H);
+                l->q_norm = l->own[1] = unit_offset(qn, dh);
+                l->k_norm = l->own[2] = unit_offset(kn, dh);
+                l->post_attn = l->own[3] = unit_offset(pa, H);
+                l->pre_ffn = l->own[4] = unit_offset(pf, H);
+                l->post_ffn = l->own[5] = unit_offset(pff, H);
+                l->global = (li + 1) % c->sliding_pattern == 0; /* gemma3.go:91 */
+            }
+            GETL(w1, "self_attn.q_proj.weight", (int64_t)qd * H);
+            if (make_dense(&l->q, w1, NULL, H, qd, q, err)) return -1;
+            GETL(w1, "self_attn.k_proj.weight", (int64_t)kvd * H);
+            if (make_dense(&l->k, w1, NULL, H, kvd, q, err)) return -1;
+            GETL(w1, "self_attn.v_proj.weight", (int64_t)kvd * H);
+            if (make_dense(&l->v, w1, NULL, H, kvd, q, err)) return -1;
+            GETL(w1, "self_attn.o_proj.weight", (int64_t)H * qd);
+            if (make_dense(&l->o, w1, NULL, qd, H, q, err)) return -1;
+            GETL(w1, "mlp.gate_proj.weight", (int64_t)I * H);
+            if (make_dense(&l->gate, w1, NULL, H, I, q, err)) return -1;
+            GETL(w1, "mlp.up_proj.weight", (int64_t)I * H);
+            if (make_dense(&l->up, w1, NULL, H, I, q, err)) return -1;
+            GETL(w1, "mlp.down_proj.weight", (int64_t)H * I);
+            if (make_dense(&l->down, w1, NULL, I, H, q, err)) return -1;
+        } else if (arch == OR_ARCH_MODERNBERT) {
+            const char *pre = "layers.";
+            l->global = li % c->global_every == 0; /* modernbert.go:73 */
+            if (li != 0) GETL(l->in_norm, "attn_norm.weight", H);
+            GETL(l->mlp_norm, "mlp_norm.weight", H);
+            GETL(w1, "attn.Wqkv.weight", 3 * (int64_t)H * H);
+            GETL(w2, "attn.Wo.weight", (int64_t)H * H);
+            GETL(w3, "mlp.Wi.weight", 2 * (int64_t)I * H);
+            GETL(w4, "mlp.Wo.weight", (int64_t)H * I);
+            if (make_dense(&l->qkv, w1, NULL, H, 3 * H, q, err)) return -1;
+            if (make_dense(&l->o, w2, NULL, H, H, q, err)) return -1;
+            if (make_dense(&l->wi, w3, NULL, H, 2 * I, q, err)) return -1;
+            if (make_dense(&l->down, w4, NULL, I, H, q, err)) return -1;
+        } else { /* nomic */
+            const char *pre = "encoder.layers.";
+            GETL(l->n1g, "norm1.weight", H);
+            GETL(l->n1b, "norm1.bias", H);
+            GETL(l->n2g, "norm2.weight", H);
+            GETL(l->n2b, "norm2.bias", H);
+            GETL(w1, "attn.Wqkv.weight", 3 * (int64_t)H * H);
+            GETL(w2, "attn.out_proj.weight", (int64_t)H * H);
+            if (make_dense(&l->qkv, w1, NULL, H, 3 * H, q, err)) return -1;
+            if (make_dense(&l->o, w2, NULL, H, H, q, err)) return -1;
+            GETL(w1, "mlp.fc11.weight", (int64_t)I * H);
+            if (make_dense(&l->fc11, w1, NULL, H, I, q, err)) return -1;
+            GETL(w1, "mlp.fc12.weight", (int64_t)I * H);
+            if (make_dense(&l->fc12, w1, NULL, H, I, q, err)) return -1;
+            GETL(w1, "mlp.fc2.weight", (int64_t)H * I);
+            if (make_dense(&l->down, w1, NULL, I, H, q, err)) return -1;
+        }
+    }
+#undef GETL
+    return 0;
+}
+
 int or_model_finalize(or_model *m, char *err) {
     int rc;
     switch (m->cfg.arch) {
@@ -271,6 +402,12 @@ int or_model_finalize(or_model *m, char *err) {
     case OR_ARCH_ROBERTA:
     case OR_ARCH_MPNET:
         rc = finalize_bert(m, err);
+        break;
+    case OR_ARCH_QWEN3:
+    case OR_ARCH_MODERNBERT:
+    case OR_ARCH_GEMMA3:
+    case OR_ARCH_NOMIC:
+        rc = finalize_decoder(m, err);
         break;
     default:
         seterr(err, "oracle: architecture %d not restated", m->cfg.arch);
@@ -282,6 +419,17 @@ int or_model_finalize(or_model *m, char *err) {
 
 void or_model_free(or_model *m) {
     if (!m) return;
+    if (m->dl) {
+        for (int i = 0; i < m->cfg.layers; i++) {
+            dec_layer *l = &m->dl[i];
+            dense *ds[] = {&l->q, &l->k, &l->v, &l->qkv, &l->o, &l->gate, &l->up, &l->down, &l->wi, &l->fc11, &l->fc12};
+            for (size_t j = 0; j < sizeof ds / sizeof ds[0]; j++) free_dense(ds[j]);
+            for (int j = 0; j < 6; j++) free(l->own[j]);
+        }
+        free(m->dl);
+    }
+    free(m->final_norm_own);
+    free(m->zero_beta);
     if (m->layers) {
         for (int i = 0; i < m->cfg.layers; i++) {
             free_dense(&m->layers[i].qkv);
@@ -388,6 +536,300 @@ static int encode_bert(or_model *m, const int64_t *ids, int seq, float *x, char 
     return 0;
 }
 
+/* ropeTable, modernbert.go:108-123: float64 inverse frequencies and trig,
+ * rounded to float32; cos/sin [seq x dh/2]. */
+static void rope_table(float *cs, float *sn, int seq, int dh, double theta) {
+    int half = dh / 2;
+    for (int d = 0; d < half; d++) {
+        double inv = pow(theta, -2.0 * (double)d / (double)dh);
+        for (int p = 0; p < seq; p++) {
+            double ang = (double)p * inv;
+            cs[p * half + d] = (float)cos(ang);
+            sn[p * half + d] = (float)sin(ang);
+        }
+    }
+}
+
+/* applyRoPE, modernbert.go:125-143: rotate_half, products rounded before
+ * the add. x is [seq x dh]. */
+static void apply_rope(float *x, int seq, int dh, const float *cs, const float *sn) {
+    int half = dh / 2;
+    for (int p = 0; p < seq; p++) {
+        float *row = x + (int64_t)p * dh;
+        const float *c = cs + (int64_t)p * half, *s = sn + (int64_t)p * half;
+        for (int d = 0; d < half; d++) {
+            float x1 = row[d], x2 = row[d + half], cc = c[d], ss = s[d];
+            row[d] = (x1 * cc) - (x2 * ss);
+            row[d + half] = (x2 * cc) + (x1 * ss);
+        }
+    }
+}
+
+/* flashAttnCausalHead, qwen3.go:307-390 (block 64, online softmax,
+ * future key blocks skipped). */
+#define FLASH_BLK 64
+static void flash_attn_causal_head(const float *qH, const float *kH, const float *vH, float *out, int seq, int dh,
+                                   float scale, float *sblk, float *acc, float *mrow, float *lrow) {
+    const float neg = -1e30f;
+    for (int q0 = 0; q0 < seq; q0 += FLASH_BLK) {
+        int q1 = q0 + FLASH_BLK < seq ? q0 + FLASH_BLK : seq;
+        int nq = q1 - q0;
+        for (int r = 0; r < nq; r++) {
+            mrow[r] = neg;
+            lrow[r] = 0;
+        }
+        memset(acc, 0, sizeof(float) * (size_t)nq * dh);
+        for (int k0 = 0; k0 < q1; k0 += FLASH_BLK) {
+            int k1 = k0 + FLASH_BLK < q1 ? k0 + FLASH_BLK : q1;
+            int nk = k1 - k0;
+            or_matmul_serial(sblk, qH + (int64_t)q0 * dh, kH + (int64_t)k0 * dh, nq, dh, nk);
+            for (int r = 0; r < nq; r++) {
+                int i = q0 + r;
+                float *srow = sblk + (int64_t)r * nk;
+                float rmax = neg;
+                for (int c = 0; c < nk; c++) {
+                    if (k0 + c > i) {
+                        srow[c] = neg;
+                    } else {
+                        srow[c] *= scale;
+                        if (srow[c] > rmax) rmax = srow[c];
+                    }
+                }
+                if (rmax == neg) continue;
+                float mprev = mrow[r], mnew = mprev;
+                if (rmax > mnew) mnew = rmax;
+                float *ar = acc + (int64_t)r * dh;
+                if (mprev != neg && mnew != mprev) {
+                    float corr = or_expnonpos(mprev - mnew);
+                    lrow[r] *= corr;
+                    for (int d = 0; d < dh; d++) ar[d] *= corr;
+                }
+                float lr = lrow[r];
+                for (int c = 0; c < nk; c++) {
+                    if (k0 + c > i) continue;
+                    float pp = or_expnonpos(srow[c] - mnew);
+                    lr += pp;
+                    const float *vk = vH + (int64_t)(k0 + c) * dh;
+                    for (int d = 0; d < dh; d++) ar[d] += pp * vk[d];
+                }
+                lrow[r] = lr;
+                mrow[r] = mnew;
+            }
+        }
+        for (int r = 0; r < nq; r++) {
+            float inv = 1.0f / lrow[r];
+            for (int d = 0; d < dh; d++) out[(int64_t)(q0 + r) * dh + d] = acc[(int64_t)r * dh + d] * inv;
+        }
+    }
+}
+
+/* Full-score attention of one head with a bidirectional window (the
+ * ModernBERT / Gemma / nomic pattern: MatMulSerial, scale, mask, Softmax,
+ * MatMulSerial). window_kind: 0 none; 1 |i-j| <= w (modernbert.go:268-274);
+ * 2 |i-j| < w (gemma3.go:339-346).  vT is [dh x seq]. */
+static void full_attn_head(const float *qH, const float *kH, const float *vT, float *out, int seq, int dh,
+                           float scale, int window_kind, int w, float *sc) {
+    or_matmul_serial(sc, qH, kH, seq, dh, seq);
+    for (int i = 0; i < seq; i++) {
+        float *row = sc + (int64_t)i * seq;
+        for (int j = 0; j < seq; j++) row[j] *= scale;
+        if (window_kind == 1) {
+            for (int j = 0; j < seq; j++)
+                if (j < i - w || j > i + w) row[j] = -1e30f;
+        } else if (window_kind == 2) {
+            for (int j = 0; j < seq; j++)
+                if (j <= i - w || j >= i + w) row[j] = -1e30f;
+        }
+    }
+    or_softmax(sc, seq, seq);
+    or_matmul_serial(out, sc, vT, seq, seq, dh);
+}
+
+/* encodeQwen3 / encodeModernBERT / encodeGemma3 / encodeNomic
+ * (qwen3.go:395-548, modernbert.go:148-311, gemma3.go:206-384,
+ * nomic.go:113-250). */
+static int encode_decoder(or_model *m, const int64_t *ids, int seq, float *x, char *err) {
+    const or_config *c = &m->cfg;
+    int arch = c->arch, H = c->hidden, I = c->inter, qt = m->quant;
+    int dh = c->head_dim ? c->head_dim : H / c->heads;
+    int nq = c->heads, nkv = c->kv_heads ? c->kv_heads : c->heads, group = nq / nkv, half = dh / 2;
+    int qd = nq * dh, kvd = nkv * dh;
+    float eps = c->eps;
+    for (int i = 0; i < seq; i++)
+        if (ids[i] < 0 || ids[i] >= c->vocab) {
+            seterr(err, "token id %lld out of vocab range %d", (long long)ids[i], c->vocab);
+            return -1;
+        }
+    float *cosG = malloc(sizeof(float) * (size_t)seq * half), *sinG = malloc(sizeof(float) * (size_t)seq * half);
+    float *cosL = malloc(sizeof(float) * (size_t)seq * half), *sinL = malloc(sizeof(float) * (size_t)seq * half);
+    if (arch == OR_ARCH_QWEN3 || arch == OR_ARCH_NOMIC) {
+        rope_table(cosG, sinG, seq, dh, c->rope_theta);
+    } else {
+        rope_table(cosG, sinG, seq, dh, c->global_theta);
+        rope_table(cosL, sinL, seq, dh, c->local_theta);
+    }
+    /* embeddings */
+    if (arch == OR_ARCH_GEMMA3) {
+        float es = (float)sqrt((double)H); /* gemma3.go:264-275 */
+        for (int i = 0; i < seq; i++)
+            for (int j = 0; j < H; j++) x[(int64_t)i * H + j] = m->word_emb[ids[i] * H + j] * es;
+    } else if (arch == OR_ARCH_NOMIC) {
+        for (int i = 0; i < seq; i++)
+            for (int j = 0; j < H; j++) x[(int64_t)i * H + j] = m->word_emb[ids[i] * H + j] + m->type_emb[j];
+        or_layernorm(x, m->emb_ln_g, m->emb_ln_b, seq, H, eps);
+    } else {
+        for (int i = 0; i < seq; i++) memcpy(x + (int64_t)i * H, m->word_emb + ids[i] * H, sizeof(float) * H);
+        if (arch == OR_ARCH_MODERNBERT) or_layernorm(x, m->emb_ln_g, m->zero_beta, seq, H, eps);
+    }
+    size_t S = (size_t)seq;
+    float *normed = malloc(sizeof(float) * S * H);
+    float *qkv = malloc(sizeof(float) * S * (qd + 2 * kvd));
+    float *qb = malloc(sizeof(float) * S * qd), *kb = malloc(sizeof(float) * S * kvd), *vb = malloc(sizeof(float) * S * kvd);
+    float *kHead = malloc(sizeof(float) * (size_t)nkv * S * dh), *vHead = malloc(sizeof(float) * (size_t)nkv * S * dh);
+    float *qH = malloc(sizeof(float) * S * dh), *cH = malloc(sizeof(float) * S * dh);
+    float *ctx = malloc(sizeof(float) * S * qd), *tmp = malloc(sizeof(float) * S * H);
+    float *gb = malloc(sizeof(float) * S * 2 * I), *ub = malloc(sizeof(float) * S * I), *act = malloc(sizeof(float) * S * I);
+    float *sc = malloc(sizeof(float) * S * S);
+    int bq = seq < FLASH_BLK ? seq : FLASH_BLK;
+    float *sblk = malloc(sizeof(float) * bq * bq), *facc = malloc(sizeof(float) * bq * dh);
+    float *mrow = malloc(sizeof(float) * bq), *lrow = malloc(sizeof(float) * bq);
+    float qscale = (float)(1.0 / sqrt((double)dh));
+    if (arch == OR_ARCH_GEMMA3) qscale = (float)(1.0 / sqrt((double)c->query_pre_attn_scalar));
+
+    for (int li = 0; li < c->layers; li++) {
+        dec_layer *l = &m->dl[li];
+        const float *cs = cosG, *sn = sinG;
+        if ((arch == OR_ARCH_MODERNBERT || arch == OR_ARCH_GEMMA3) && !l->global) {
+            cs = cosL;
+            sn = sinL;
+        }
+        if (arch == OR_ARCH_QWEN3 || arch == OR_ARCH_GEMMA3) {
+            memcpy(normed, x, sizeof(float) * S * H);
+            or_rmsnorm(normed, l->in_norm, seq, H, eps);
+            apply_dense(&l->q, qb, normed, seq, qt);
+            apply_dense(&l->k, kb, normed, seq, qt);
+            apply_dense(&l->v, vb, normed, seq, qt);
+            for (int kv = 0; kv < nkv; kv++) {
+                float *kH = kHead + (size_t)kv * S * dh, *vH = vHead + (size_t)kv * S * dh;
+                for (int i = 0; i < seq; i++) {
+                    memcpy(kH + (size_t)i * dh, kb + (size_t)i * kvd + kv * dh, sizeof(float) * dh);
+                    if (arch == OR_ARCH_QWEN3) {
+                        memcpy(vH + (size_t)i * dh, vb + (size_t)i * kvd + kv * dh, sizeof(float) * dh);
+                    } else { /* transposed V [dh x seq] (gemma3.go:292-301) */
+                        for (int d = 0; d < dh; d++) vH[(size_t)d * S + i] = vb[(size_t)i * kvd + kv * dh + d];
+                    }
+                }
+                or_rmsnorm(kH, l->k_norm, seq, dh, eps);
+                apply_rope(kH, seq, dh, cs, sn);
+            }
+            for (int hh = 0; hh < nq; hh++) {
+                for (int i = 0; i < seq; i++) memcpy(qH + (size_t)i * dh, qb + (size_t)i * qd + hh * dh, sizeof(float) * dh);
+                or_rmsnorm(qH, l->q_norm, seq, dh, eps);
+                apply_rope(qH, seq, dh, cs, sn);
+                int kv = hh / group;
+                float *kH = kHead + (size_t)kv * S * dh, *vH = vHead + (size_t)kv * S * dh;
+                if (arch == OR_ARCH_QWEN3)
+                    flash_attn_causal_head(qH, kH, vH, cH, seq, dh, qscale, sblk, facc, mrow, lrow);
+                else
+                    full_attn_head(qH, kH, vH, cH, seq, dh, qscale, l->global ? 0 : 2, c->sliding_window, sc);
+                for (int i = 0; i < seq; i++) memcpy(ctx + (size_t)i * qd + hh * dh, cH + (size_t)i * dh, sizeof(float) * dh);
+            }
+            apply_dense(&l->o, tmp, ctx, seq, qt);
+            if (arch == OR_ARCH_GEMMA3) or_rmsnorm(tmp, l->post_attn, seq, H, eps); /* gemma3.go:357-358 */
+            or_add(x, tmp, seq * H);
+            memcpy(normed, x, sizeof(float) * S * H);
+            or_rmsnorm(normed, arch == OR_ARCH_QWEN3 ? l->post_attn : l->pre_ffn, seq, H, eps);
+            apply_dense(&l->gate, gb, normed, seq, qt);
+            apply_dense(&l->up, ub, normed, seq, qt);
+            for (size_t i = 0; i < S * I; i++) act[i] = gb[i];
+            if (arch == OR_ARCH_QWEN3)
+                or_silu(act, seq * I); /* qwen3.go:530-539 */
+            else
+                or_gelu_tanh(act, seq * I); /* gemma3.go:365-374 */
+            for (size_t i = 0; i < S * I; i++) act[i] *= ub[i];
+            apply_dense(&l->down, tmp, act, seq, qt);
+            if (arch == OR_ARCH_GEMMA3) or_rmsnorm(tmp, l->post_ffn, seq, H, eps);
+            or_add(x, tmp, seq * H);
+        } else { /* ModernBERT (pre-norm) and nomic (post-norm): fused Wqkv */
+            const float *xin = x;
+            if (arch == OR_ARCH_MODERNBERT) {
+                memcpy(normed, x, sizeof(float) * S * H);
+                if (l->in_norm) or_layernorm(normed, l->in_norm, m->zero_beta, seq, H, eps);
+                xin = normed;
+            }
+            apply_dense(&l->qkv, qkv, xin, seq, qt);
+            for (int hh = 0; hh < nq; hh++) {
+                int off = hh * dh;
+                float *kH = kHead, *vT = vHead;
+                for (int i = 0; i < seq; i++) {
+                    const float *row = qkv + (size_t)i * 3 * H;
+                    memcpy(qH + (size_t)i * dh, row + off, sizeof(float) * dh);
+                    memcpy(kH + (size_t)i * dh, row + H + off, sizeof(float) * dh);
+                    for (int d = 0; d < dh; d++) vT[(size_t)d * S + i] = row[2 * H + off + d];
+                }
+                apply_rope(qH, seq, dh, cs, sn);
+                apply_rope(kH, seq, dh, cs, sn);
+                int wk = (arch == OR_ARCH_MODERNBERT && !l->global) ? 1 : 0;
+                full_attn_head(qH, kH, vT, cH, seq, dh, qscale, wk, c->local_attention / 2, sc);
+                for (int i = 0; i < seq; i++) memcpy(ctx + (size_t)i * H + off, cH + (size_t)i * dh, sizeof(float) * dh);
+            }
+            apply_dense(&l->o, tmp, ctx, seq, qt);
+            or_add(x, tmp, seq * H);
+            if (arch == OR_ARCH_NOMIC) {
+                or_layernorm(x, l->n1g, l->n1b, seq, H, eps);
+                apply_dense(&l->fc11, gb, x, seq, qt);
+                apply_dense(&l->fc12, ub, x, seq, qt);
+                for (size_t i = 0; i < S * I; i++) act[i] = ub[i];
+                or_silu(act, seq * I); /* nomic.go:232-242: fc11 * silu(fc12) */
+                for (size_t i = 0; i < S * I; i++) act[i] *= gb[i];
+                apply_dense(&l->down, tmp, act, seq, qt);
+                or_add(x, tmp, seq * H);
+                or_layernorm(x, l->n2g, l->n2b, seq, H, eps);
+            } else {
+                memcpy(normed, x, sizeof(float) * S * H);
+                or_layernorm(normed, l->mlp_norm, m->zero_beta, seq, H, eps);
+                apply_dense(&l->wi, gb, normed, seq, qt);
+                for (int i = 0; i < seq; i++) { /* gelu(value) * gate, modernbert.go:292-301 */
+                    float *dst = act + (size_t)i * I;
+                    memcpy(dst, gb + (size_t)i * 2 * I, sizeof(float) * I);
+                    or_gelu(dst, I);
+                    for (int d = 0; d < I; d++) dst[d] *= gb[(size_t)i * 2 * I + I + d];
+                }
+                apply_dense(&l->down, tmp, act, seq, qt);
+                or_add(x, tmp, seq * H);
+            }
+        }
+    }
+    if (arch == OR_ARCH_QWEN3 || arch == OR_ARCH_GEMMA3)
+        or_rmsnorm(x, m->final_norm, seq, H, eps);
+    else if (arch == OR_ARCH_MODERNBERT)
+        or_layernorm(x, m->final_norm, m->zero_beta, seq, H, eps);
+    free(cosG); free(sinG); free(cosL); free(sinL);
+    free(normed); free(qkv); free(qb); free(kb); free(vb); free(kHead); free(vHead); free(qH); free(cH);
+    free(ctx); free(tmp); free(gb); free(ub); free(act); free(sc); free(sblk); free(facc); free(mrow); free(lrow);
+    return 0;
+}
+
+/* applyGemmaDenseHead, gemma3.go:177-198: two bias-free float32 mat-vecs
+ * with a plain sequential float32 sum. */
+static void gemma_dense_head(const or_model *m, float *pooled) {
+    int H = m->cfg.hidden, D = m->cfg.dense_hidden;
+    float *hid = malloc(sizeof(float) * D);
+    for (int o = 0; o < D; o++) {
+        const float *row = m->dense1 + (size_t)o * H;
+        float acc = 0.0f;
+        for (int i = 0; i < H; i++) acc += row[i] * pooled[i];
+        hid[o] = acc;
+    }
+    for (int o = 0; o < H; o++) {
+        const float *row = m->dense2 + (size_t)o * D;
+        float acc = 0.0f;
+        for (int i = 0; i < D; i++) acc += row[i] * hid[i];
+        pooled[o] = acc;
+    }
+    free(hid);
+}
+
 /* ForwardWorkers, bert.go:657-703 */
 int or_forward(or_model *m, const int64_t *ids, int seq, float *pooled, float *tokens, char *err) {
     const or_config *c = &m->cfg;
@@ -413,6 +855,12 @@ int or_forward(or_model *m, const int64_t *ids, int seq, float *pooled, float *t
     case OR_ARCH_MPNET:
         rc = encode_bert(m, ids, seq, x, err);
         break;
+    case OR_ARCH_QWEN3:
+    case OR_ARCH_MODERNBERT:
+    case OR_ARCH_GEMMA3:
+    case OR_ARCH_NOMIC:
+        rc = encode_decoder(m, ids, seq, x, err);
+        break;
     default:
         seterr(err, "oracle: architecture %d not restated", c->arch);
         rc = -1;
@@ -436,6 +884,7 @@ int or_forward(or_model *m, const int64_t *ids, int seq, float *pooled, float *t
                     for (int j = 0; j < H; j++) pooled[j] *= inv;
                 }
             }
+            if (m->dense1) gemma_dense_head(m, pooled); /* bert.go:682-684 */
             if (c->normalize) or_l2normalize(pooled, H);
         }
     }

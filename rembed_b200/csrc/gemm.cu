@@ -51,6 +51,14 @@ __device__ __forceinline__ float gelu_as(float x) {
     return fmaf(hx, copysignf(erf_abs, x), hx);
 }
 
+// SiLU x * sigmoid(x) (tensor.go:477-481 computes it through a float64 exp).
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+// tanh-approximation GELU (tensor.go:490-497; HF gelu_pytorch_tanh).
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+    const float inner = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+    return 0.5f * x * (1.0f + tanhf(inner));
+}
+
 constexpr int kEpiWarps = 8;        // two epilogue warps per SM sub-partition
 constexpr int kThreads = 128 + 32 * kEpiWarps;
 constexpr int kChunk = 32;          // accumulator columns per TMEM load / TMA store box
@@ -264,18 +272,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             const uint32_t taddr =
                 tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + half * HALF;
+            constexpr bool GLU = EPI >= kEpiGluSilu;
+            constexpr int STEP = GLU ? 2 : 1;  // accumulator chunks per output box
 #pragma unroll 1
-            for (int c = 0; c < CHUNKS; ++c, ++k) {
+            for (int c = 0; c < CHUNKS; c += STEP, ++k) {
                 const int b = k & 1;
                 uint8_t* box = boxes + b * kStageBytes;
-                const int col0 = n_blk * BN + half * HALF + c * kChunk;
+                const int col0 = n_blk * BN + half * HALF + c * kChunk;  // accumulator column
+                const int ocol0 = GLU ? col0 / 2 : col0;                  // output column
                 if (lane == 0) {
                     if constexpr (EPI == kEpiBiasRes) {
                         // The other buffer's store (previous chunk) has read
                         // its box: it can take the next chunk's residual.
                         bulk_wait_read<0>();
-                        if (c + 1 < CHUNKS)
-                            load_residual(tile, c + 1, b ^ 1);
+                        if (c + STEP < CHUNKS)
+                            load_residual(tile, c + STEP, b ^ 1);
                         else
                             load_residual(tile + npairs, 0, b ^ 1);
                     } else {
@@ -295,9 +306,47 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     else
                         v[i] = __uint_as_float(r[i]);
                 }
+                if constexpr (GLU) {
+                    // a = chunk c (activated), b = chunk c + 1 (linear)
+                    uint32_t rb[32];
+                    tmem_ld32(taddr + (c + 1) * kChunk, rb);
+                    tmem_ld_wait();
+                    float w[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        if constexpr (S8)
+                            w[i] = static_cast<float>(static_cast<int32_t>(rb[i])) * rs;
+                        else
+                            w[i] = __uint_as_float(rb[i]);
+                    }
+                    if (S8 && args.col_scale) {
+                        const float4* ca = reinterpret_cast<const float4*>(args.col_scale + col0);
+                        const float4* cb = reinterpret_cast<const float4*>(args.col_scale + col0 + kChunk);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float4 qa = __ldg(ca + i), qb = __ldg(cb + i);
+                            v[4 * i] *= qa.x;
+                            v[4 * i + 1] *= qa.y;
+                            v[4 * i + 2] *= qa.z;
+                            v[4 * i + 3] *= qa.w;
+                            w[4 * i] *= qb.x;
+                            w[4 * i + 1] *= qb.y;
+                            w[4 * i + 2] *= qb.z;
+                            w[4 * i + 3] *= qb.w;
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        float a = v[i];
+                        if constexpr (EPI == kEpiGluSilu) a = silu_f(a);
+                        else if constexpr (EPI == kEpiGluGeluErf) a = gelu_as(a);
+                        else a = gelu_tanh_f(a);
+                        v[i] = a * w[i];
+                    }
+                }
                 // (acc * row scale) * column scale + bias: the reference's
                 // dequant-then-AddBias order (pack_vnni.go:155-173, bert.go:297-300)
-                if (S8 && args.col_scale) {
+                if (!GLU && S8 && args.col_scale) {
                     const float4* cs = reinterpret_cast<const float4*>(args.col_scale + col0);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
@@ -308,7 +357,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         v[4 * i + 3] *= q.w;
                     }
                 }
-                if (args.bias) {
+                if (!GLU && args.bias) {
                     const float4* bp = reinterpret_cast<const float4*>(args.bias + col0);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
@@ -359,7 +408,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    tma_store_2d(&tmOut, box, col0, row0);
+                    tma_store_2d(&tmOut, box, ocol0, row0);
                     bulk_commit();
                 }
             }
@@ -481,6 +530,9 @@ static cudaError_t dispatch_epi(int epi, const CUtensorMap& tmA, const CUtensorM
     case kEpiBiasGelu: return launch_one<BN, S8, kEpiBiasGelu>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
     case kEpiBiasRes: return launch_one<BN, S8, kEpiBiasRes>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
     case kEpiBiasF32: return launch_one<BN, S8, kEpiBiasF32>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
+    case kEpiGluSilu: return launch_one<BN, S8, kEpiGluSilu>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
+    case kEpiGluGeluErf: return launch_one<BN, S8, kEpiGluGeluErf>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
+    case kEpiGluGeluTanh: return launch_one<BN, S8, kEpiGluGeluTanh>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
     default: return cudaErrorInvalidValue;
     }
 }
@@ -504,7 +556,7 @@ static bool make_epilogue_tmap(CUtensorMap* map, const void* base, bool f32, uin
     return r == CUDA_SUCCESS;
 }
 
-int gemm_block_n(int M, int N, int num_sms) {
+int gemm_block_n(int M, int N, int num_sms, bool glu) {
     // Among the tile widths that divide N, the one with the fewest
     // (waves x per-tile cost), where a tile costs about BN + 32 columns of
     // work (the +32 models its fixed epilogue/pipeline overhead).
@@ -513,7 +565,7 @@ int gemm_block_n(int M, int N, int num_sms) {
     int best = 0;
     long best_cost = 0;
     for (int bn : {256, 192, 128}) {
-        if (N % bn != 0) continue;
+        if (N % bn != 0 || (glu && bn == 192)) continue;
         const long tiles = static_cast<long>(m_tiles) * (N / bn);
         const long waves = (tiles + pairs - 1) / pairs;
         const long cost = waves * (bn + 32);
@@ -532,8 +584,12 @@ cudaError_t gemm_launch(GemmKind kind, int epi, int block_n, const CUtensorMap& 
     if (args.K % kel != 0 || args.K <= 0 || block_n <= 0 || args.N % block_n != 0) return cudaErrorInvalidValue;
     const bool s8 = kind == GemmKind::kS8;
     const bool f32out = epi == kEpiBiasRes || epi == kEpiBiasF32;
+    const bool glu = epi_is_glu(epi);
+    // GLU tiles pair 32-column chunks inside each epilogue warp's columns.
+    if (glu && (block_n == 192 || args.N % 64 != 0)) return cudaErrorInvalidValue;
     CUtensorMap tmOut, tmRes;
-    if (!make_epilogue_tmap(&tmOut, args.out, f32out, args.M, args.N, args.ld_out)) return cudaErrorInvalidValue;
+    if (!make_epilogue_tmap(&tmOut, args.out, f32out, args.M, glu ? args.N / 2 : args.N, args.ld_out))
+        return cudaErrorInvalidValue;
     if (epi == kEpiBiasRes) {
         if (!args.residual || !make_epilogue_tmap(&tmRes, args.residual, true, args.M, args.N, args.N))
             return cudaErrorInvalidValue;

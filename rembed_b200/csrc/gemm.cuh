@@ -11,9 +11,16 @@ namespace rg {
 enum Epilogue : int {
     kEpiBias = 0,       // + bias                      -> bf16
     kEpiBiasGelu = 1,   // + bias, exact (erf) GELU    -> bf16
-    kEpiBiasRes = 2,    // + bias, + fp32 residual     -> fp32
+    kEpiBiasRes = 2,    // + bias, + fp32 residual     -> fp32 (out may alias the residual)
     kEpiBiasF32 = 3,    // + bias                      -> fp32
+    // Gated linear units over W rows interleaved in blocks of 32: block 2j
+    // is the activated operand a, block 2j+1 the linear operand b of the
+    // same 32 output columns; out[M x N/2] = act(a) * b -> bf16.
+    kEpiGluSilu = 4,      // silu(a) * b   (qwen3.go:530-539, nomic.go:232-242)
+    kEpiGluGeluErf = 5,   // gelu(a) * b   (modernbert.go:292-301)
+    kEpiGluGeluTanh = 6,  // gelu_tanh(a) * b (gemma3.go:365-374)
 };
+inline bool epi_is_glu(int epi) { return epi >= kEpiGluSilu; }
 
 struct GemmArgs {
     int M, N, K;
@@ -38,7 +45,7 @@ bool make_kmajor_tmap(CUtensorMap* map, const void* base, int elem_bytes, uint64
 // Output tile width (128, 192 or 256 columns) for an M x N GEMM on num_sms
 // SMs: the width dividing N with the least wave-quantised cost; 0 if none
 // divides N.
-int gemm_block_n(int M, int N, int num_sms);
+int gemm_block_n(int M, int N, int num_sms, bool glu = false);
 
 // Rows of W one CTA loads per k-block: each CTA of the pair holds half of a
 // tile's block_n columns.  The tensor map over W must use this box height.

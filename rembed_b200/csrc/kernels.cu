@@ -26,47 +26,72 @@ __device__ __forceinline__ float warp_max(float v) {
 
 // Row i of a warp-per-row kernel holds H = 128*NV floats: lane owns the
 // float4 chunks lane + 32*c, c < NV (coalesced 512-byte segments).
-template <int NV>
-__device__ __forceinline__ void ln_finish(float (&v)[NV][4], const float* g, const float* b, float eps, int H,
-                                          float* x32_row, __nv_bfloat16* xb_row, int8_t* xq_row, float* xq_scale,
-                                          int lane) {
-    float s = 0.f;
+//
+// Normalise the row in registers (LayerNorm, tensor.go:433-452: two-pass
+// mean / biased variance; or RMSNorm, tensor.go:459-471: mean square) with
+// gain g and bias b (LayerNorm only; nullptr = zero; g nullptr = identity),
+// then write any of:
+// fp32 row, bf16 row, int8 row + scale (QuantizeRowU8 without the +128
+// offset, pack_vnni.go:85-117).
+template <int NV, bool RMS>
+__device__ __forceinline__ void norm_finish(float (&v)[NV][4], const float* g, const float* b, float eps, int H,
+                                            float* out32, __nv_bfloat16* outb, int8_t* outq, float* outqs,
+                                            int lane) {
+    float mean = 0.f, inv = 1.f;
+    if (!g) {
+        // identity (ModernBERT's layer-0 attention norm): only the stores
+    } else if constexpr (RMS) {
+        float q = 0.f;
 #pragma unroll
-    for (int c = 0; c < NV; ++c) s += (v[c][0] + v[c][1]) + (v[c][2] + v[c][3]);
-    const float mean = warp_sum(s) / static_cast<float>(H);
-    float q = 0.f;
+        for (int c = 0; c < NV; ++c)
 #pragma unroll
-    for (int c = 0; c < NV; ++c)
+            for (int e = 0; e < 4; ++e) q += v[c][e] * v[c][e];
+        inv = 1.0f / sqrtf(warp_sum(q) / static_cast<float>(H) + eps);
+    } else {
+        float s = 0.f;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const float d = v[c][e] - mean;
-            q += d * d;
-        }
-    const float var = warp_sum(q) / static_cast<float>(H);
-    const float inv = 1.0f / sqrtf(var + eps);
+        for (int c = 0; c < NV; ++c) s += (v[c][0] + v[c][1]) + (v[c][2] + v[c][3]);
+        mean = warp_sum(s) / static_cast<float>(H);
+        float q = 0.f;
+#pragma unroll
+        for (int c = 0; c < NV; ++c)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float d = v[c][e] - mean;
+                q += d * d;
+            }
+        inv = 1.0f / sqrtf(warp_sum(q) / static_cast<float>(H) + eps);
+    }
     float amax = 0.f;
 #pragma unroll
     for (int c = 0; c < NV; ++c) {
         const int j = (lane + 32 * c) * 4;
-        const float4 gg = __ldg(reinterpret_cast<const float4*>(g + j));
-        const float4 bb = __ldg(reinterpret_cast<const float4*>(b + j));
-        v[c][0] = (v[c][0] - mean) * inv * gg.x + bb.x;
-        v[c][1] = (v[c][1] - mean) * inv * gg.y + bb.y;
-        v[c][2] = (v[c][2] - mean) * inv * gg.z + bb.z;
-        v[c][3] = (v[c][3] - mean) * inv * gg.w + bb.w;
-        reinterpret_cast<float4*>(x32_row + j)[0] = make_float4(v[c][0], v[c][1], v[c][2], v[c][3]);
-        __nv_bfloat162 lo = __floats2bfloat162_rn(v[c][0], v[c][1]);
-        __nv_bfloat162 hi = __floats2bfloat162_rn(v[c][2], v[c][3]);
-        uint2 pk;
-        pk.x = *reinterpret_cast<uint32_t*>(&lo);
-        pk.y = *reinterpret_cast<uint32_t*>(&hi);
-        reinterpret_cast<uint2*>(xb_row + j)[0] = pk;
+        const float4 gg = g ? __ldg(reinterpret_cast<const float4*>(g + j)) : make_float4(1.f, 1.f, 1.f, 1.f);
+        float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (!RMS && b) bb = __ldg(reinterpret_cast<const float4*>(b + j));
+        if constexpr (RMS) {
+            v[c][0] = v[c][0] * inv * gg.x;
+            v[c][1] = v[c][1] * inv * gg.y;
+            v[c][2] = v[c][2] * inv * gg.z;
+            v[c][3] = v[c][3] * inv * gg.w;
+        } else {
+            v[c][0] = (v[c][0] - mean) * inv * gg.x + bb.x;
+            v[c][1] = (v[c][1] - mean) * inv * gg.y + bb.y;
+            v[c][2] = (v[c][2] - mean) * inv * gg.z + bb.z;
+            v[c][3] = (v[c][3] - mean) * inv * gg.w + bb.w;
+        }
+        if (out32) reinterpret_cast<float4*>(out32 + j)[0] = make_float4(v[c][0], v[c][1], v[c][2], v[c][3]);
+        if (outb) {
+            __nv_bfloat162 lo = __floats2bfloat162_rn(v[c][0], v[c][1]);
+            __nv_bfloat162 hi = __floats2bfloat162_rn(v[c][2], v[c][3]);
+            uint2 pk;
+            pk.x = *reinterpret_cast<uint32_t*>(&lo);
+            pk.y = *reinterpret_cast<uint32_t*>(&hi);
+            reinterpret_cast<uint2*>(outb + j)[0] = pk;
+        }
         amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[c][0]), fabsf(v[c][1])), fmaxf(fabsf(v[c][2]), fabsf(v[c][3]))));
     }
-    if (xq_row) {
-        // QuantizeRowU8 (pack_vnni.go:85-117) without the +128 offset:
-        // float32 scale = maxAbs/127 (1 for a zero row), float32 reciprocal,
-        // round-half-even, clamp to the int8 range.
+    if (outq) {
         amax = warp_max(amax);
         float scale = amax / 127.0f;
         if (scale == 0.0f) scale = 1.0f;
@@ -79,81 +104,149 @@ __device__ __forceinline__ void ln_finish(float (&v)[NV][4], const float* g, con
             o.y = (signed char)max(-128, min(127, __float2int_rn(v[c][1] * rinv)));
             o.z = (signed char)max(-128, min(127, __float2int_rn(v[c][2] * rinv)));
             o.w = (signed char)max(-128, min(127, __float2int_rn(v[c][3] * rinv)));
-            reinterpret_cast<char4*>(xq_row + j)[0] = o;
+            reinterpret_cast<char4*>(outq + j)[0] = o;
         }
-        if (lane == 0) *xq_scale = scale;
+        if (lane == 0) *outqs = scale;
     }
 }
 
 template <int NV>
-__global__ void __launch_bounds__(256) embed_ln_kernel(const int64_t* __restrict__ ids, const int32_t* __restrict__ cu,
-                                                      int nseq, int T, const float* __restrict__ word,
-                                                      const float* __restrict__ pos, const float* __restrict__ type0,
-                                                      const float* __restrict__ g, const float* __restrict__ b,
-                                                      float eps, int H, int vocab, int pos_off, float* x32,
-                                                      __nv_bfloat16* xb, int8_t* xq, float* xq_scale, int* status) {
-    const int lane = threadIdx.x & 31;
-    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (t >= T) return;
-    // Sequence of token t: the last s with cu[s] <= t.
-    int lo = 0, hi = nseq - 1;
+__device__ __forceinline__ void store_row(const float (&v)[NV][4], float* out32, __nv_bfloat16* outb, int lane) {
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+        const int j = (lane + 32 * c) * 4;
+        if (out32) reinterpret_cast<float4*>(out32 + j)[0] = make_float4(v[c][0], v[c][1], v[c][2], v[c][3]);
+        if (outb) {
+            __nv_bfloat162 lo = __floats2bfloat162_rn(v[c][0], v[c][1]);
+            __nv_bfloat162 hi = __floats2bfloat162_rn(v[c][2], v[c][3]);
+            uint2 pk;
+            pk.x = *reinterpret_cast<uint32_t*>(&lo);
+            pk.y = *reinterpret_cast<uint32_t*>(&hi);
+            reinterpret_cast<uint2*>(outb + j)[0] = pk;
+        }
+    }
+}
+
+__device__ __forceinline__ int seq_of_token(const int32_t* __restrict__ cu, int nseq, int t) {
+    int lo = 0, hi = nseq - 1;  // the last s with cu[s] <= t
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
         if (__ldg(cu + mid) <= t) lo = mid;
         else hi = mid - 1;
     }
-    const int p = t - __ldg(cu + lo) + pos_off;
-    int64_t id = __ldg(ids + t);
-    const bool bad = id < 0 || id >= vocab;
+    return lo;
+}
+
+template <int NV>
+__global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= p.T) return;
+    const int H = p.H;
+    int64_t id = __ldg(p.ids + t);
+    const bool bad = id < 0 || id >= p.vocab;
     if (bad) {
-        if (lane == 0) atomicOr(status, kStatusBadToken);
+        if (lane == 0) atomicOr(p.status, kStatusBadToken);
         id = 0;
     }
-    const float* w = word + id * H;
-    const float* pr = pos + static_cast<int64_t>(p) * H;
+    const float* w = p.word + id * H;
+    const float* pr = nullptr;
+    if (p.pos) {
+        const int s = seq_of_token(p.cu, p.nseq, t);
+        pr = p.pos + static_cast<int64_t>(t - __ldg(p.cu + s) + p.pos_off) * H;
+    }
     float v[NV][4];
 #pragma unroll
     for (int c = 0; c < NV; ++c) {
         const int j = (lane + 32 * c) * 4;
         const float4 a = __ldg(reinterpret_cast<const float4*>(w + j));
-        const float4 q = __ldg(reinterpret_cast<const float4*>(pr + j));
-        // (word + pos) + type, the reference's summation order.
-        v[c][0] = a.x + q.x;
-        v[c][1] = a.y + q.y;
-        v[c][2] = a.z + q.z;
-        v[c][3] = a.w + q.w;
-        if (type0) {
-            const float4 ty = __ldg(reinterpret_cast<const float4*>(type0 + j));
+        v[c][0] = a.x;
+        v[c][1] = a.y;
+        v[c][2] = a.z;
+        v[c][3] = a.w;
+        if (pr) {  // (word + pos) + type, the reference's summation order
+            const float4 q = __ldg(reinterpret_cast<const float4*>(pr + j));
+            v[c][0] += q.x;
+            v[c][1] += q.y;
+            v[c][2] += q.z;
+            v[c][3] += q.w;
+        }
+        if (p.type0) {
+            const float4 ty = __ldg(reinterpret_cast<const float4*>(p.type0 + j));
             v[c][0] += ty.x;
             v[c][1] += ty.y;
             v[c][2] += ty.z;
             v[c][3] += ty.w;
         }
+        if (p.scale != 1.0f) {  // Gemma's sqrt(H) (gemma3.go:264-275)
+            v[c][0] *= p.scale;
+            v[c][1] *= p.scale;
+            v[c][2] *= p.scale;
+            v[c][3] *= p.scale;
+        }
         if (bad) v[c][0] = v[c][1] = v[c][2] = v[c][3] = 0.f;
     }
-    ln_finish<NV>(v, g, b, eps, H, x32 + static_cast<int64_t>(t) * H, xb + static_cast<int64_t>(t) * H,
-                  xq ? xq + static_cast<int64_t>(t) * H : nullptr, xq_scale ? xq_scale + t : nullptr, lane);
+    float* x32 = p.x32 + static_cast<int64_t>(t) * H;
+    __nv_bfloat16* xb = p.xb ? p.xb + static_cast<int64_t>(t) * H : nullptr;
+    if (p.g)
+        norm_finish<NV, false>(v, p.g, p.b, p.eps, H, x32, xb, p.xq ? p.xq + static_cast<int64_t>(t) * H : nullptr,
+                               p.xq_scale ? p.xq_scale + t : nullptr, lane);
+    else
+        store_row<NV>(v, x32, xb, lane);
 }
 
-template <int NV>
-__global__ void __launch_bounds__(256) ln_kernel(const float* __restrict__ y32, const float* __restrict__ g,
-                                                const float* __restrict__ b, float eps, int T, int H, float* x32,
-                                                __nv_bfloat16* xb, int8_t* xq, float* xq_scale) {
+template <int NV, bool RMS>
+__global__ void __launch_bounds__(256) norm_kernel(NormParams p) {
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (t >= T) return;
-    const float* y = y32 + static_cast<int64_t>(t) * H;
+    if (t >= p.T) return;
+    const int64_t off = static_cast<int64_t>(t) * p.H;
     float v[NV][4];
 #pragma unroll
     for (int c = 0; c < NV; ++c) {
-        const float4 a = __ldg(reinterpret_cast<const float4*>(y + (lane + 32 * c) * 4));
+        const float4 a = __ldg(reinterpret_cast<const float4*>(p.in + off + (lane + 32 * c) * 4));
         v[c][0] = a.x;
         v[c][1] = a.y;
         v[c][2] = a.z;
         v[c][3] = a.w;
     }
-    ln_finish<NV>(v, g, b, eps, H, x32 + static_cast<int64_t>(t) * H, xb + static_cast<int64_t>(t) * H,
-                  xq ? xq + static_cast<int64_t>(t) * H : nullptr, xq_scale ? xq_scale + t : nullptr, lane);
+    norm_finish<NV, RMS>(v, p.g, p.b, p.eps, p.H, p.out32 ? p.out32 + off : nullptr, p.outb ? p.outb + off : nullptr,
+                         p.outq ? p.outq + off : nullptr, p.outqs ? p.outqs + t : nullptr, lane);
+}
+
+// x32 += RMSNorm(o32; g): Gemma's post-attention / post-FFN norm of the
+// sublayer output before the residual add (gemma3.go:357-358, 376).
+template <int NV>
+__global__ void __launch_bounds__(256) add_rmsnorm_kernel(float* __restrict__ x32, const float* __restrict__ o32,
+                                                         const float* __restrict__ g, float eps, int T, int H) {
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= T) return;
+    const int64_t off = static_cast<int64_t>(t) * H;
+    float v[NV][4];
+    float q = 0.f;
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(o32 + off + (lane + 32 * c) * 4));
+        v[c][0] = a.x;
+        v[c][1] = a.y;
+        v[c][2] = a.z;
+        v[c][3] = a.w;
+        q += (a.x * a.x + a.y * a.y) + (a.z * a.z + a.w * a.w);
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(q) / static_cast<float>(H) + eps);
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+        const int j = (lane + 32 * c) * 4;
+        const float4 gg = __ldg(reinterpret_cast<const float4*>(g + j));
+        float4* xp = reinterpret_cast<float4*>(x32 + off + j);
+        float4 x = *xp;
+        x.x += v[c][0] * inv * gg.x;
+        x.y += v[c][1] * inv * gg.y;
+        x.z += v[c][2] * inv * gg.z;
+        x.w += v[c][3] * inv * gg.w;
+        *xp = x;
+    }
 }
 
 #define RG_NV_DISPATCH(H, CALL)           \
@@ -169,24 +262,145 @@ __global__ void __launch_bounds__(256) ln_kernel(const float* __restrict__ y32, 
     default: return cudaErrorInvalidValue; \
     }
 
-cudaError_t launch_embed_ln(const int64_t* ids, const int32_t* cu, int nseq, int T, const float* word,
-                            const float* pos, const float* type0, const float* g, const float* b, float eps,
-                            int H, int vocab, int pos_off, float* x32, __nv_bfloat16* xb, int8_t* xq,
-                            float* xq_scale, int* status, cudaStream_t st) {
-    if (T <= 0) return cudaSuccess;
-    if (H % 128 != 0) return cudaErrorInvalidValue;
-    const int grid = (T + 7) / 8;
-    RG_NV_DISPATCH(H, (embed_ln_kernel<NV><<<grid, 256, 0, st>>>(ids, cu, nseq, T, word, pos, type0, g, b, eps, H,
-                                                                vocab, pos_off, x32, xb, xq, xq_scale, status)));
+cudaError_t launch_embed(const EmbedParams& p, cudaStream_t st) {
+    if (p.T <= 0) return cudaSuccess;
+    if (p.H % 128 != 0) return cudaErrorInvalidValue;
+    const int grid = (p.T + 7) / 8;
+    RG_NV_DISPATCH(p.H, (embed_kernel<NV><<<grid, 256, 0, st>>>(p)));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_norm(const NormParams& p, bool rms, cudaStream_t st) {
+    if (p.T <= 0) return cudaSuccess;
+    if (p.H % 128 != 0) return cudaErrorInvalidValue;
+    const int grid = (p.T + 7) / 8;
+    if (rms) {
+        RG_NV_DISPATCH(p.H, (norm_kernel<NV, true><<<grid, 256, 0, st>>>(p)));
+    } else {
+        RG_NV_DISPATCH(p.H, (norm_kernel<NV, false><<<grid, 256, 0, st>>>(p)));
+    }
     return cudaGetLastError();
 }
 
 cudaError_t launch_ln(const float* y32, const float* g, const float* b, float eps, int T, int H, float* x32,
                       __nv_bfloat16* xb, int8_t* xq, float* xq_scale, cudaStream_t st) {
+    NormParams p{};
+    p.in = y32;
+    p.g = g;
+    p.b = b;
+    p.eps = eps;
+    p.T = T;
+    p.H = H;
+    p.out32 = x32;
+    p.outb = xb;
+    p.outq = xq;
+    p.outqs = xq_scale;
+    return launch_norm(p, false, st);
+}
+
+cudaError_t launch_add_rmsnorm(float* x32, const float* o32, const float* g, float eps, int T, int H, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if (H % 128 != 0) return cudaErrorInvalidValue;
     const int grid = (T + 7) / 8;
-    RG_NV_DISPATCH(H, (ln_kernel<NV><<<grid, 256, 0, st>>>(y32, g, b, eps, T, H, x32, xb, xq, xq_scale)));
+    RG_NV_DISPATCH(H, (add_rmsnorm_kernel<NV><<<grid, 256, 0, st>>>(x32, o32, g, eps, T, H)));
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// QK-norm + RoPE in place on the q and k heads of the fused qkv buffer: one
+// warp per (token, head).  Lane holds elements d = lane + 32k; with dh >= 64
+// the rotate-half partner d + dh/2 is in the same lane.  RMSNorm over dh with
+// the q or k gain (qwen3.go:485-508, gemma3.go:303-330), then the rotation
+// at the token's position in its sequence (modernbert.go:125-143: products
+// rounded before the add/sub).
+template <int DH>
+__global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkRopeParams p) {
+    constexpr int E = DH / 32, HALF = DH / 2;
+    const int lane = threadIdx.x & 31;
+    const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int heads = p.nq + p.nkv;
+    if (item >= p.T * heads) return;
+    const int t = item / heads, h = item % heads;
+    const bool is_q = h < p.nq;
+    __nv_bfloat16* row = p.qkv + static_cast<int64_t>(t) * p.ld + (is_q ? h * DH : p.nq * DH + (h - p.nq) * DH);
+    float v[E];
+#pragma unroll
+    for (int k = 0; k < E; ++k) v[k] = __bfloat162float(row[lane + 32 * k]);
+    const float* g = is_q ? p.q_norm : p.k_norm;
+    if (g) {
+        float q = 0.f;
+#pragma unroll
+        for (int k = 0; k < E; ++k) q += v[k] * v[k];
+        const float inv = 1.0f / sqrtf(warp_sum(q) / static_cast<float>(DH) + p.eps);
+#pragma unroll
+        for (int k = 0; k < E; ++k) v[k] = v[k] * inv * __ldg(g + lane + 32 * k);
+    }
+    if (p.cos) {
+        const int s = seq_of_token(p.cu, p.nseq, t);
+        const int pos = t - __ldg(p.cu + s);
+        const float* cs = p.cos + static_cast<int64_t>(pos) * HALF;
+        const float* sn = p.sin + static_cast<int64_t>(pos) * HALF;
+#pragma unroll
+        for (int k = 0; k < E / 2; ++k) {
+            const int d = lane + 32 * k;
+            const float x1 = v[k], x2 = v[k + E / 2];
+            const float cc = __ldg(cs + d), ss = __ldg(sn + d);
+            v[k] = __fsub_rn(__fmul_rn(x1, cc), __fmul_rn(x2, ss));
+            v[k + E / 2] = __fadd_rn(__fmul_rn(x2, cc), __fmul_rn(x1, ss));
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < E; ++k) row[lane + 32 * k] = __float2bfloat16(v[k]);
+}
+
+cudaError_t launch_qk_norm_rope(const QkRopeParams& p, int head_dim, cudaStream_t st) {
+    if (p.T <= 0) return cudaSuccess;
+    const long items = static_cast<long>(p.T) * (p.nq + p.nkv);
+    const int grid = static_cast<int>((items + 7) / 8);
+    switch (head_dim) {
+    case 64: qk_norm_rope_kernel<64><<<grid, 256, 0, st>>>(p); break;
+    case 128: qk_norm_rope_kernel<128><<<grid, 256, 0, st>>>(p); break;
+    case 256: qk_norm_rope_kernel<256><<<grid, 256, 0, st>>>(p); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Small fp32 GEMM for the Dense head (gemma3.go:177-198, never quantised):
+// out[M x N] = x[M x K] . W[N x K]^T, 32 x 32 output tiles, K in steps of 32.
+__global__ void __launch_bounds__(256) dense_f32_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                       float* __restrict__ out, int M, int N, int K) {
+    __shared__ float xs[32][33];
+    __shared__ float ws[32][33];
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
+    const int m0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k0 = 0; k0 < K; k0 += 32) {
+        for (int r = ty; r < 32; r += 8) {
+            xs[r][tx] = (m0 + r < M && k0 + tx < K) ? x[static_cast<int64_t>(m0 + r) * K + k0 + tx] : 0.f;
+            ws[r][tx] = (n0 + r < N && k0 + tx < K) ? w[static_cast<int64_t>(n0 + r) * K + k0 + tx] : 0.f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < 32; ++k) {
+            const float b = ws[tx][k];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[i] = fmaf(xs[ty + 8 * i][k], b, acc[i]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int m = m0 + ty + 8 * i, n = n0 + tx;
+        if (m < M && n < N) out[static_cast<int64_t>(m) * N + n] = acc[i];
+    }
+}
+
+cudaError_t launch_dense_f32(const float* x, const float* w, float* out, int M, int N, int K, cudaStream_t st) {
+    if (M <= 0) return cudaSuccess;
+    const dim3 grid((N + 31) / 32, (M + 31) / 32);
+    dense_f32_kernel<<<grid, 256, 0, st>>>(x, w, out, M, N, K);
     return cudaGetLastError();
 }
 
@@ -270,92 +484,128 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&p);
 }
 
-template <int D>
-__device__ __forceinline__ void load_tile64(__nv_bfloat16* s, const __nv_bfloat16* g, int r0, int L, int ld) {
+template <int D, int ROWS>
+__device__ __forceinline__ void load_tile(__nv_bfloat16* s, const __nv_bfloat16* g, int r0, int L, int ld) {
     constexpr int LDS = D + 8;
     constexpr int CPR = D / 8;  // 16-byte chunks per row
-    for (int i = threadIdx.x; i < 64 * CPR; i += 128) {
+    for (int i = threadIdx.x; i < ROWS * CPR; i += 128) {
         const int r = i / CPR, c = i % CPR;
         const int gr = r0 + r;
-        const bool ok = gr < L;
+        const bool ok = gr >= 0 && gr < L;
         const __nv_bfloat16* src = g + static_cast<int64_t>(ok ? gr : 0) * ld + c * 8;
         cp_async16(s + r * LDS + c * 8, src, ok);
     }
 }
 
-template <int D>
-__global__ void __launch_bounds__(128) attention_kernel(const __nv_bfloat16* __restrict__ qkv,
-                                                       const int32_t* __restrict__ cu, int H, float scale_log2,
-                                                       __nv_bfloat16* __restrict__ ctx) {
+// CTA = (64 query rows, query head, sequence); 4 warps x 16 rows; key
+// blocks of BKV rows.  Q (D <= 128: in registers; D = 256: re-read from
+// shared memory per k-step), S = Q K^T and O += P V on bf16 mma.sync with
+// fp32 accumulators, online softmax in the exp2 domain.
+template <int D, bool PLAIN>
+__global__ void __launch_bounds__(128) attention_kernel(AttnParams p) {
+    constexpr int BKV = D == 256 ? 32 : 64;
     constexpr int LDS = D + 8;
-    constexpr int KS = D / 16;   // k-steps over the head dim
-    constexpr int DT = D / 8;    // n-tiles of the output
-    __shared__ __align__(16) __nv_bfloat16 sQ[64 * LDS];
-    __shared__ __align__(16) __nv_bfloat16 sK[64 * LDS];
-    __shared__ __align__(16) __nv_bfloat16 sV[64 * LDS];
+    constexpr int KS = D / 16;     // k-steps over the head dim
+    constexpr int DT = D / 8;      // n-tiles of the output
+    constexpr int NT = BKV / 8;    // n-tiles of S
+    constexpr bool QREG = D <= 128;
+    extern __shared__ __align__(16) uint8_t attn_smem[];
+    __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(attn_smem);
+    __nv_bfloat16* sK = sQ + 64 * LDS;
+    __nv_bfloat16* sV = sK + BKV * LDS;
 
     const int s = blockIdx.z, h = blockIdx.y;
-    const int s0 = __ldg(cu + s), L = __ldg(cu + s + 1) - s0;
+    const int s0 = __ldg(p.cu + s), L = __ldg(p.cu + s + 1) - s0;
     const int q0 = blockIdx.x * 64;
     if (q0 >= L) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ld = 3 * H;
-    const __nv_bfloat16* Qg = qkv + static_cast<int64_t>(s0) * ld + h * D;
-    const __nv_bfloat16* Kg = Qg + H;
-    const __nv_bfloat16* Vg = Qg + 2 * H;
+    const int hk = h / p.group;
+    const __nv_bfloat16* Qg = p.q + static_cast<int64_t>(s0) * p.ldq + h * D;
+    const __nv_bfloat16* Kg = p.k + static_cast<int64_t>(s0) * p.ldk + hk * D;
+    const __nv_bfloat16* Vg = p.v + static_cast<int64_t>(s0) * p.ldv + hk * D;
 
-    load_tile64<D>(sQ, Qg, q0, L, ld);
+    load_tile<D, 64>(sQ, Qg, q0, L, p.ldq);
     cp_async_commit_wait();
     __syncthreads();
 
-    uint32_t qf[KS][4];
+    uint32_t qf[QREG ? KS : 1][4];
+    if constexpr (QREG) {
 #pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {
-        const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int c = ks * 16 + (lane >> 4) * 8;
-        ldsm_x4(qf[ks], sQ + r * LDS + c);
+        for (int ks = 0; ks < KS; ++ks) {
+            const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+            const int c = ks * 16 + (lane >> 4) * 8;
+            ldsm_x4(qf[ks], sQ + r * LDS + c);
+        }
     }
 
     float o[DT][4];
 #pragma unroll
     for (int i = 0; i < DT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float m0 = -1e30f, m1 = -1e30f, l0 = 0.f, l1 = 0.f;
+    const int qi0 = q0 + warp * 16 + (lane >> 2);  // this thread's first query row (second: +8)
 
-    const int nkv = (L + 63) / 64;
-    for (int kb = 0; kb < nkv; ++kb) {
+    // Key range any row of this block may see: j - i in [lo, hi].
+    const int jmin = max(0, q0 + p.rel_lo);
+    const int jmax = min(L - 1, q0 + 63 + p.rel_hi);
+    const int kb0 = jmin / BKV, kb1 = jmax / BKV;
+    for (int kb = kb0; kb <= kb1; ++kb) {
         __syncthreads();  // previous tile fully consumed
-        load_tile64<D>(sK, Kg, kb * 64, L, ld);
-        load_tile64<D>(sV, Vg, kb * 64, L, ld);
+        load_tile<D, BKV>(sK, Kg, kb * BKV, L, p.ldk);
+        load_tile<D, BKV>(sV, Vg, kb * BKV, L, p.ldv);
         cp_async_commit_wait();
         __syncthreads();
 
-        float sc[8][4];
+        float sc[NT][4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
+        for (int i = 0; i < NT; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
+            uint32_t a[4];
+            if constexpr (QREG) {
+                a[0] = qf[ks][0];
+                a[1] = qf[ks][1];
+                a[2] = qf[ks][2];
+                a[3] = qf[ks][3];
+            } else {
+                const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+                const int c = ks * 16 + (lane >> 4) * 8;
+                ldsm_x4(a, sQ + r * LDS + c);
+            }
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < NT / 2; ++j) {
                 uint32_t b[4];
                 const int r = 16 * j + (lane & 7) + (lane >> 4) * 8;
                 const int c = ks * 16 + ((lane >> 3) & 1) * 8;
                 ldsm_x4(b, sK + r * LDS + c);
-                mma_bf16_16816(sc[2 * j], qf[ks], b[0], b[1]);
-                mma_bf16_16816(sc[2 * j + 1], qf[ks], b[2], b[3]);
+                mma_bf16_16816(sc[2 * j], a, b[0], b[1]);
+                mma_bf16_16816(sc[2 * j + 1], a, b[2], b[3]);
             }
         }
-        // scale into the exp2 domain, mask keys past the sequence end
+        // scale (+ relative bias), mask, into the exp2 domain
         float tm0 = -1e30f, tm1 = -1e30f;
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
+        for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int col = kb * 64 + nt * 8 + (lane & 3) * 2 + e;
-                const bool ok = col < L;
-                sc[nt][e] = ok ? sc[nt][e] * scale_log2 : -1e30f;
-                sc[nt][2 + e] = ok ? sc[nt][2 + e] * scale_log2 : -1e30f;
-                tm0 = fmaxf(tm0, sc[nt][e]);
-                tm1 = fmaxf(tm1, sc[nt][2 + e]);
+            for (int e = 0; e < 4; ++e) {
+                const int qi = qi0 + (e >> 1) * 8;
+                const int j = kb * BKV + nt * 8 + (lane & 3) * 2 + (e & 1);
+                const int rel = j - qi;
+                // PLAIN: no window and no bias, only the sequence end masks keys
+                const bool ok = PLAIN ? j < L : (j < L && rel >= p.rel_lo && rel <= p.rel_hi);
+                float x = sc[nt][e];
+                if (!PLAIN && p.bias) {
+                    // bias[h][rel + bias_off]: scores * scale + bias (bert.go:876-889)
+                    const int bi = min(max(rel + p.bias_off, 0), 2 * p.bias_off);
+                    x = (x * p.scale + __ldg(p.bias + static_cast<int64_t>(h) * (2 * p.bias_off + 1) + bi)) *
+                        1.4426950408889634f;
+                } else {
+                    x = x * p.scale_log2;
+                }
+                sc[nt][e] = ok ? x : -1e30f;
+                if (e < 2)
+                    tm0 = fmaxf(tm0, sc[nt][e]);
+                else
+                    tm1 = fmaxf(tm1, sc[nt][e]);
             }
         }
         tm0 = fmaxf(tm0, __shfl_xor_sync(0xffffffffu, tm0, 1));
@@ -375,19 +625,22 @@ __global__ void __launch_bounds__(128) attention_kernel(const __nv_bfloat16* __r
             o[i][2] *= c1;
             o[i][3] *= c1;
         }
-        uint32_t pf[4][4];
+        uint32_t pf[NT / 2][4];
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-            const float p0 = exp2f(sc[nt][0] - m0), p1 = exp2f(sc[nt][1] - m0);
-            const float p2 = exp2f(sc[nt][2] - m1), p3 = exp2f(sc[nt][3] - m1);
+        for (int nt = 0; nt < NT; ++nt) {
+            // a fully masked row keeps m = -1e30: its probabilities are 0
+            const float p0 = sc[nt][0] > -1e29f ? exp2f(sc[nt][0] - m0) : 0.f;
+            const float p1 = sc[nt][1] > -1e29f ? exp2f(sc[nt][1] - m0) : 0.f;
+            const float p2 = sc[nt][2] > -1e29f ? exp2f(sc[nt][2] - m1) : 0.f;
+            const float p3 = sc[nt][3] > -1e29f ? exp2f(sc[nt][3] - m1) : 0.f;
             l0 += p0 + p1;
             l1 += p2 + p3;
             pf[nt >> 1][(nt & 1) * 2 + 0] = pack_bf16(p0, p1);
             pf[nt >> 1][(nt & 1) * 2 + 1] = pack_bf16(p2, p3);
         }
-        // O += P V over the 4 key sub-blocks of 16
+        // O += P V over the key sub-blocks of 16
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < NT / 2; ++j) {
             const uint32_t a[4] = {pf[j][0], pf[j][1], pf[j][2], pf[j][3]};
 #pragma unroll
             for (int i = 0; i < DT / 2; ++i) {
@@ -404,32 +657,53 @@ __global__ void __launch_bounds__(128) attention_kernel(const __nv_bfloat16* __r
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-    const float i0 = 1.0f / l0, i1 = 1.0f / l1;
-    const int r0 = q0 + warp * 16 + (lane >> 2);
-    __nv_bfloat16* out = ctx + static_cast<int64_t>(s0) * H + h * D + (lane & 3) * 2;
+    const float i0 = l0 > 0.f ? 1.0f / l0 : 0.f, i1 = l1 > 0.f ? 1.0f / l1 : 0.f;
+    __nv_bfloat16* out = p.out + static_cast<int64_t>(s0) * p.ldo + h * D + (lane & 3) * 2;
 #pragma unroll
     for (int i = 0; i < DT; ++i) {
-        if (r0 < L)
-            *reinterpret_cast<uint32_t*>(out + static_cast<int64_t>(r0) * H + i * 8) =
+        if (qi0 < L)
+            *reinterpret_cast<uint32_t*>(out + static_cast<int64_t>(qi0) * p.ldo + i * 8) =
                 pack_bf16(o[i][0] * i0, o[i][1] * i0);
-        if (r0 + 8 < L)
-            *reinterpret_cast<uint32_t*>(out + static_cast<int64_t>(r0 + 8) * H + i * 8) =
+        if (qi0 + 8 < L)
+            *reinterpret_cast<uint32_t*>(out + static_cast<int64_t>(qi0 + 8) * p.ldo + i * 8) =
                 pack_bf16(o[i][2] * i1, o[i][3] * i1);
     }
 }
 
-cudaError_t launch_attention(const __nv_bfloat16* qkv, const int32_t* cu, int nseq, int max_len, int H, int heads,
-                             int head_dim, float scale, __nv_bfloat16* ctx, cudaStream_t st) {
-    if (nseq <= 0) return cudaSuccess;
+template <int D, bool PLAIN>
+static cudaError_t launch_attention_dp(const AttnParams& p, int nseq, int max_len, int heads, cudaStream_t st) {
+    constexpr int BKV = D == 256 ? 32 : 64;
+    constexpr int smem = (64 + 2 * BKV) * (D + 8) * 2;
+    static unsigned configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (smem > 48 * 1024 && (dev >= 32 || !(__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & (1u << dev)))) {
+        cudaError_t e =
+            cudaFuncSetAttribute(attention_kernel<D, PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        if (dev < 32) __atomic_fetch_or(&configured, 1u << dev, __ATOMIC_RELEASE);
+    }
     const dim3 grid((max_len + 63) / 64, heads, nseq);
-    const float sl2 = scale * 1.4426950408889634f;
-    if (head_dim == 64)
-        attention_kernel<64><<<grid, 128, 0, st>>>(qkv, cu, H, sl2, ctx);
-    else if (head_dim == 32)
-        attention_kernel<32><<<grid, 128, 0, st>>>(qkv, cu, H, sl2, ctx);
-    else
-        return cudaErrorInvalidValue;
+    attention_kernel<D, PLAIN><<<grid, 128, smem, st>>>(p);
     return cudaGetLastError();
+}
+
+template <int D>
+static cudaError_t launch_attention_d(const AttnParams& p, int nseq, int max_len, int heads, cudaStream_t st) {
+    const bool plain = !p.bias && p.rel_lo <= -max_len && p.rel_hi >= max_len;
+    return plain ? launch_attention_dp<D, true>(p, nseq, max_len, heads, st)
+                 : launch_attention_dp<D, false>(p, nseq, max_len, heads, st);
+}
+
+cudaError_t launch_attention(const AttnParams& p, int nseq, int max_len, int heads, int head_dim, cudaStream_t st) {
+    if (nseq <= 0) return cudaSuccess;
+    switch (head_dim) {
+    case 32: return launch_attention_d<32>(p, nseq, max_len, heads, st);
+    case 64: return launch_attention_d<64>(p, nseq, max_len, heads, st);
+    case 128: return launch_attention_d<128>(p, nseq, max_len, heads, st);
+    case 256: return launch_attention_d<256>(p, nseq, max_len, heads, st);
+    default: return cudaErrorInvalidValue;
+    }
 }
 
 // ---------------------------------------------------------------------------

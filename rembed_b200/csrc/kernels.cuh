@@ -7,31 +7,89 @@
 
 namespace rg {
 
-// Per-token embedding sum + LayerNorm (bert.go:795-814):
-//   x = LN(word[id] + pos[p + pos_off] (+ type[0]))
-// writes fp32 x32 and its bf16 copy xb; p is the token's index inside its
-// sequence (cu_seqlens).  A token id outside [0, vocab) raises
-// kStatusBadToken and writes zeros (never reads out of bounds).
-cudaError_t launch_embed_ln(const int64_t* ids, const int32_t* cu, int nseq, int T, const float* word,
-                            const float* pos, const float* type0, const float* g, const float* b, float eps,
-                            int H, int vocab, int pos_off, float* x32, __nv_bfloat16* xb, int8_t* xq,
-                            float* xq_scale, int* status, cudaStream_t st);
+// Embedding rows (bert.go:795-814, qwen3.go:457-462, modernbert.go:204-211,
+// gemma3.go:264-275, nomic.go:164-176): x = word[id] (+ pos[p + pos_off])
+// (+ type0), times scale, then LayerNorm(g, b) when g is set; p is the
+// token's index in its sequence.  Writes fp32 x32 and, if set, bf16 xb and
+// the int8 row (xq, xq_scale).  An id outside [0, vocab) raises
+// kStatusBadToken and yields zeros (never an out-of-bounds read).
+struct EmbedParams {
+    const int64_t* ids;
+    const int32_t* cu;
+    int nseq, T, H, vocab, pos_off;
+    const float *word, *pos, *type0;
+    float scale;
+    const float *g, *b;
+    float eps;
+    float* x32;
+    __nv_bfloat16* xb;
+    int8_t* xq;
+    float* xq_scale;
+    int* status;
+};
+cudaError_t launch_embed(const EmbedParams& p, cudaStream_t st);
 
-// LayerNorm of y32 rows (tensor.go:433-452) -> x32 (fp32) and xb (bf16);
-// optionally also the per-row int8 quantisation of the fp32 result (xq,
-// xq_scale) for the full-int8 mode (QuantizeRowU8, pack_vnni.go:85-117).
+// Row normalisation of in [T x H]: LayerNorm (g, b; b nullptr = zero) or
+// RMSNorm (g); g nullptr = identity.  Outputs (each optional): out32 (may alias in), outb (bf16),
+// outq + outqs (int8 row quantisation).
+struct NormParams {
+    const float* in;
+    const float *g, *b;
+    float eps;
+    int T, H;
+    float* out32;
+    __nv_bfloat16* outb;
+    int8_t* outq;
+    float* outqs;
+};
+cudaError_t launch_norm(const NormParams& p, bool rms, cudaStream_t st);
 cudaError_t launch_ln(const float* y32, const float* g, const float* b, float eps, int T, int H, float* x32,
                       __nv_bfloat16* xb, int8_t* xq, float* xq_scale, cudaStream_t st);
+// x32 += RMSNorm(o32; g)  (Gemma's post-sublayer norms).
+cudaError_t launch_add_rmsnorm(float* x32, const float* o32, const float* g, float eps, int T, int H, cudaStream_t st);
+
+// QK-norm (optional) + RoPE (optional) in place on the q heads [0, nq) and
+// k heads of the fused qkv buffer [T x ld] (q at column 0, k at nq*dh).
+// cos/sin are [positions x dh/2] tables.  head_dim 64, 128 or 256.
+struct QkRopeParams {
+    __nv_bfloat16* qkv;
+    int ld, T, nq, nkv;
+    const float *q_norm, *k_norm;
+    float eps;
+    const float *cos, *sin;
+    const int32_t* cu;
+    int nseq;
+};
+cudaError_t launch_qk_norm_rope(const QkRopeParams& p, int head_dim, cudaStream_t st);
+
+// out[M x N] = x[M x K] . W[N x K]^T in fp32 (the Gemma Dense head).
+cudaError_t launch_dense_f32(const float* x, const float* w, float* out, int M, int N, int K, cudaStream_t st);
 
 // Per-row symmetric int8 quantisation of a bf16 [T x K] matrix
 // (QuantizeRowU8 with the +128 offset removed: q in [-128, 127]).
 cudaError_t launch_quantize_rows(const __nv_bfloat16* x, int T, int K, int8_t* q, float* scale, cudaStream_t st);
 
-// Bidirectional varlen attention over the fused qkv buffer [T x 3H]
-// (bert.go:853-902): per sequence and head, softmax(Q K^T * scale) V.
-// Writes ctx [T x H] bf16.  head_dim 32 or 64.
-cudaError_t launch_attention(const __nv_bfloat16* qkv, const int32_t* cu, int nseq, int max_len, int H,
-                             int heads, int head_dim, float scale, __nv_bfloat16* ctx, cudaStream_t st);
+// Varlen attention (bert.go:853-902, qwen3.go:307-390, modernbert.go:239-281,
+// gemma3.go:303-354): per sequence and query head h (key/value head
+// h / group), out = softmax(Q K^T * scale [+ bias(j - i)]) V over the keys j
+// with rel_lo <= j - i <= rel_hi (causal: rel_hi = 0; symmetric window w:
+// rel_lo = -w, rel_hi = w; unbounded: +-2^30).  Q, K, V, out are token-major
+// bf16 with row strides ldq/ldk/ldv/ldo; head h's columns start at h*D.
+// bias, if set, is [heads x (2*bias_off + 1)] indexed by j - i + bias_off
+// (MPNet's bucketed relative-position bias, added after the scale).
+struct AttnParams {
+    const __nv_bfloat16 *q, *k, *v;
+    int ldq, ldk, ldv;
+    const int32_t* cu;
+    int group;
+    float scale, scale_log2;
+    int rel_lo, rel_hi;
+    const float* bias;
+    int bias_off;
+    __nv_bfloat16* out;
+    int ldo;
+};
+cudaError_t launch_attention(const AttnParams& p, int nseq, int max_len, int heads, int head_dim, cudaStream_t st);
 
 // Pooling + L2 + Matryoshka truncation (bert.go:657-703, rembed.go:441-448):
 // out[nseq x dim].

@@ -74,9 +74,18 @@ struct DevDense {
 int bn_index(int bn) { return bn == 256 ? 0 : (bn == 192 ? 1 : 2); }
 constexpr int kBlockWidths[3] = {256, 192, 128};
 
+// One layer on a device.  BERT family / nomic (post-norm): ln1/ln2 after
+// the residual adds.  Qwen3 / ModernBERT / Gemma3 (pre-norm): attn_norm
+// before QKV (nullptr: identity, ModernBERT layer 0), ffn_norm before the
+// FFN, post_attn / post_ffn on the sublayer outputs (Gemma), q_norm /
+// k_norm (QK-norm).  ffn1 is a GLU GEMM (rows interleaved by 32) where the
+// architecture gates.
 struct DevLayer {
     DevDense qkv, o, ffn1, ffn2;
     float *ln1_g = nullptr, *ln1_b = nullptr, *ln2_g = nullptr, *ln2_b = nullptr;
+    float *attn_norm = nullptr, *ffn_norm = nullptr, *post_attn = nullptr, *post_ffn = nullptr;
+    float *q_norm = nullptr, *k_norm = nullptr;
+    bool global = true;
 };
 
 struct Replica {
@@ -85,6 +94,12 @@ struct Replica {
     cudaStream_t stream = nullptr;
     std::vector<void*> allocs;
     float *word = nullptr, *pos = nullptr, *type0 = nullptr, *emb_g = nullptr, *emb_b = nullptr;
+    float* rel_bias = nullptr;  // MPNet: [heads x (2*rel_bias_off + 1)] by j - i
+    int rel_bias_off = 0;
+    float emb_scale = 1.0f;     // Gemma: sqrt(H)
+    float *final_norm = nullptr, *zero_beta = nullptr;
+    float *cos_g = nullptr, *sin_g = nullptr, *cos_l = nullptr, *sin_l = nullptr;  // RoPE [positions x dh/2]
+    float *dense1 = nullptr, *dense2 = nullptr;  // Gemma Dense head, fp32
     std::vector<DevLayer> layers;
     // workspace
     int cap_T = 0, cap_seq = 0, cap_out = 0;
@@ -93,6 +108,8 @@ struct Replica {
     bf16 *xb = nullptr, *qkv = nullptr, *ctx = nullptr, *ffh = nullptr;
     int8_t *xq = nullptr, *ctxq = nullptr, *ffhq = nullptr;
     float *xs = nullptr, *ctxs = nullptr, *ffhs = nullptr;
+    float *pool32 = nullptr, *head_hid = nullptr, *head_out = nullptr;  // Gemma Dense head
+    int32_t* iota = nullptr;                                            // [0, 1, ..., cap_seq]
     int64_t* d_ids = nullptr;
     int32_t* d_cu = nullptr;
     float* d_out = nullptr;
@@ -153,7 +170,44 @@ bool ln_width_ok(int n) {
 }
 
 bool is_bert_family(int a) {
-    return a == RG_ARCH_BERT || a == RG_ARCH_DISTILBERT || a == RG_ARCH_ROBERTA;
+    return a == RG_ARCH_BERT || a == RG_ARCH_DISTILBERT || a == RG_ARCH_ROBERTA || a == RG_ARCH_MPNET;
+}
+// Pre-norm stacks: norm before each sublayer, residual added raw.
+bool is_prenorm(int a) { return a == RG_ARCH_QWEN3 || a == RG_ARCH_MODERNBERT || a == RG_ARCH_GEMMA3; }
+bool has_rope(int a) { return a == RG_ARCH_QWEN3 || a == RG_ARCH_MODERNBERT || a == RG_ARCH_GEMMA3 || a == RG_ARCH_NOMIC; }
+bool is_glu(int a) { return a == RG_ARCH_QWEN3 || a == RG_ARCH_MODERNBERT || a == RG_ARCH_GEMMA3 || a == RG_ARCH_NOMIC; }
+
+struct Dims {
+    int H, I, nq, nkv, dh, qd, kvd, nqkv;
+};
+Dims dims(const rg_model_desc& d) {
+    Dims m{};
+    m.H = d.hidden_size;
+    m.I = d.intermediate_size;
+    m.nq = d.num_attention_heads;
+    m.dh = d.head_dim > 0 ? d.head_dim : d.hidden_size / d.num_attention_heads;
+    m.nkv = (d.arch == RG_ARCH_QWEN3 || d.arch == RG_ARCH_GEMMA3) ? d.num_key_value_heads : m.nq;
+    m.qd = m.nq * m.dh;
+    m.kvd = m.nkv * m.dh;
+    m.nqkv = m.qd + 2 * m.kvd;
+    return m;
+}
+
+// relPosBucket (bert.go:126-150): MPNet's bucket of a relative position
+// (memory j - context i), HF's relative_position_bucket with max distance 128.
+int rel_pos_bucket(int rel, int num_buckets) {
+    int n = -rel;
+    const int half = num_buckets / 2;
+    int ret = 0;
+    if (n < 0) {
+        ret = half;
+        n = -n;
+    }
+    const int max_exact = half / 2;
+    if (n < max_exact) return ret + n;
+    const int v = max_exact + static_cast<int>(std::log(static_cast<double>(n) / max_exact) /
+                                               std::log(128.0 / max_exact) * static_cast<double>(half - max_exact));
+    return ret + std::min(v, half - 1);
 }
 
 // bf16 round-to-nearest-even of a float (NaN kept quiet).
@@ -274,12 +328,27 @@ void finalize_bert(rg_ctx* c, Replica& r) {
     const rg_model_desc& d = c->d;
     const int H = d.hidden_size, I = d.intermediate_size, V = d.vocab_size, P = d.max_position_embeddings;
     const bool distil = d.arch == RG_ARCH_DISTILBERT;
+    const bool mpnet = d.arch == RG_ARCH_MPNET;
     check(cudaSetDevice(r.device), "cudaSetDevice");
     r.word = dev_upload(r, get_tensor(c, "embeddings.word_embeddings.weight", {V, H}).data.data(), (size_t)V * H);
     r.pos = dev_upload(r, get_tensor(c, "embeddings.position_embeddings.weight", {P, H}).data.data(), (size_t)P * H);
     r.emb_g = dev_upload(r, get_tensor(c, "embeddings.LayerNorm.weight", {H}).data.data(), H);
     r.emb_b = dev_upload(r, get_tensor(c, "embeddings.LayerNorm.bias", {H}).data.data(), H);
-    if (!distil) {
+    if (mpnet) {
+        // One shared bucketed bias table [buckets x heads] (bert.go:495-505),
+        // expanded to [heads x (2*maxlen - 1)] by j - i (bert.go:820-830).
+        const int nb = d.relative_attention_num_buckets, heads = d.num_attention_heads;
+        const float* rb = get_tensor(c, "encoder.relative_attention_bias.weight", {nb, heads}).data.data();
+        const int maxlen = max_seq_len(d);
+        const int nd = 2 * maxlen - 1;
+        std::vector<float> delta(static_cast<size_t>(heads) * nd);
+        for (int dd = -(maxlen - 1); dd <= maxlen - 1; ++dd) {
+            const int b = rel_pos_bucket(dd, nb);
+            for (int h = 0; h < heads; ++h) delta[static_cast<size_t>(h) * nd + dd + maxlen - 1] = rb[b * heads + h];
+        }
+        r.rel_bias = dev_upload(r, delta.data(), delta.size());
+        r.rel_bias_off = maxlen - 1;
+    } else if (!distil) {
         // token_type_embeddings: any first dimension, row 0 used (bert.go:507-515)
         const HostTensor* tt = nullptr;
         for (const char* p : {"", "bert.", "roberta."}) {
@@ -316,6 +385,23 @@ void finalize_bert(rg_ctx* c, Replica& r) {
             f2B = T("ffn.lin2.bias", {H});
             L.ln2_g = dev_upload(r, T("output_layer_norm.weight", {H}), H);
             L.ln2_b = dev_upload(r, T("output_layer_norm.bias", {H}), H);
+        } else if (mpnet) {
+            qW = T("attention.attn.q.weight", {H, H});
+            qB = T("attention.attn.q.bias", {H});
+            kW = T("attention.attn.k.weight", {H, H});
+            kB = T("attention.attn.k.bias", {H});
+            vW = T("attention.attn.v.weight", {H, H});
+            vB = T("attention.attn.v.bias", {H});
+            oW = T("attention.attn.o.weight", {H, H});
+            oB = T("attention.attn.o.bias", {H});
+            L.ln1_g = dev_upload(r, T("attention.LayerNorm.weight", {H}), H);
+            L.ln1_b = dev_upload(r, T("attention.LayerNorm.bias", {H}), H);
+            f1W = T("intermediate.dense.weight", {I, H});
+            f1B = T("intermediate.dense.bias", {I});
+            f2W = T("output.dense.weight", {H, I});
+            f2B = T("output.dense.bias", {H});
+            L.ln2_g = dev_upload(r, T("output.LayerNorm.weight", {H}), H);
+            L.ln2_b = dev_upload(r, T("output.LayerNorm.bias", {H}), H);
         } else {
             qW = T("attention.self.query.weight", {H, H});
             qB = T("attention.self.query.bias", {H});
@@ -349,6 +435,147 @@ void finalize_bert(rg_ctx* c, Replica& r) {
     }
 }
 
+// GLU weight for the fused gate/up GEMM: rows interleaved in blocks of 32,
+// block 2j = act[32j, 32j+32), block 2j+1 = lin[32j, 32j+32).
+std::vector<float> interleave_glu(const float* act, const float* lin, int I, int K) {
+    std::vector<float> w(static_cast<size_t>(2) * I * K);
+    for (int b = 0; b < I / 32; ++b) {
+        memcpy(&w[(static_cast<size_t>(2 * b) * 32) * K], act + static_cast<size_t>(b) * 32 * K, sizeof(float) * 32 * K);
+        memcpy(&w[(static_cast<size_t>(2 * b + 1) * 32) * K], lin + static_cast<size_t>(b) * 32 * K,
+               sizeof(float) * 32 * K);
+    }
+    return w;
+}
+
+std::vector<float> concat_rows(std::initializer_list<std::pair<const float*, size_t>> parts) {
+    std::vector<float> w;
+    for (const auto& p : parts) w.insert(w.end(), p.first, p.first + p.second);
+    return w;
+}
+
+// ropeTable (modernbert.go:108-123): float64 inverse frequencies and trig,
+// rounded to float32, for positions [0, npos).
+void rope_tables(Replica& r, int npos, int dh, double theta, float** cosp, float** sinp) {
+    const int half = dh / 2;
+    std::vector<float> cs(static_cast<size_t>(npos) * half), sn(static_cast<size_t>(npos) * half);
+    for (int d = 0; d < half; ++d) {
+        const double inv = std::pow(theta, -2.0 * d / dh);
+        for (int p = 0; p < npos; ++p) {
+            const double ang = static_cast<double>(p) * inv;
+            cs[static_cast<size_t>(p) * half + d] = static_cast<float>(std::cos(ang));
+            sn[static_cast<size_t>(p) * half + d] = static_cast<float>(std::sin(ang));
+        }
+    }
+    *cosp = dev_upload(r, cs.data(), cs.size());
+    *sinp = dev_upload(r, sn.data(), sn.size());
+}
+
+std::vector<float> unit_offset(const float* v, int n) {  // gemma3.go:44-50
+    std::vector<float> o(v, v + n);
+    for (float& x : o) x += 1.0f;
+    return o;
+}
+
+// Qwen3 (qwen3.go:114-183), Gemma3 (gemma3.go:57-170), ModernBERT
+// (modernbert.go:33-106), nomic (nomic.go:22-111): weights by HF name.
+void finalize_decoder(rg_ctx* c, Replica& r) {
+    const rg_model_desc& d = c->d;
+    const Dims m = dims(d);
+    const int H = m.H, I = m.I, V = d.vocab_size, dh = m.dh;
+    const int arch = d.arch;
+    check(cudaSetDevice(r.device), "cudaSetDevice");
+    auto G = [&](const std::string& n, std::initializer_list<int64_t> sh) -> const float* {
+        return get_tensor(c, n, sh).data.data();
+    };
+    auto up = [&](const float* h, size_t n) { return dev_upload(r, h, n); };
+    const int npos = d.max_position_embeddings;
+    if (arch == RG_ARCH_QWEN3 || arch == RG_ARCH_GEMMA3) {
+        r.word = up(G("embed_tokens.weight", {V, H}), static_cast<size_t>(V) * H);
+        if (arch == RG_ARCH_QWEN3) {
+            r.final_norm = up(G("norm.weight", {H}), H);
+            rope_tables(r, npos, dh, d.rope_theta, &r.cos_g, &r.sin_g);
+        } else {
+            r.final_norm = up(unit_offset(G("norm.weight", {H}), H).data(), H);
+            r.emb_scale = static_cast<float>(std::sqrt(static_cast<double>(H)));
+            rope_tables(r, npos, dh, d.global_rope_theta, &r.cos_g, &r.sin_g);
+            rope_tables(r, npos, dh, d.local_rope_theta, &r.cos_l, &r.sin_l);
+            const int D = d.dense_hidden;
+            r.dense1 = up(G("2_Dense.linear.weight", {D, H}), static_cast<size_t>(D) * H);
+            r.dense2 = up(G("3_Dense.linear.weight", {H, D}), static_cast<size_t>(H) * D);
+        }
+    } else if (arch == RG_ARCH_MODERNBERT) {
+        r.word = up(G("embeddings.tok_embeddings.weight", {V, H}), static_cast<size_t>(V) * H);
+        r.emb_g = up(G("embeddings.norm.weight", {H}), H);
+        r.final_norm = up(G("final_norm.weight", {H}), H);
+        std::vector<float> z(H, 0.0f);
+        r.zero_beta = up(z.data(), H);
+        rope_tables(r, npos, dh, d.global_rope_theta, &r.cos_g, &r.sin_g);
+        rope_tables(r, npos, dh, d.local_rope_theta, &r.cos_l, &r.sin_l);
+    } else {  // nomic
+        r.word = up(G("embeddings.word_embeddings.weight", {V, H}), static_cast<size_t>(V) * H);
+        r.type0 = up(G("embeddings.token_type_embeddings.weight", {2, H}), H);
+        r.emb_g = up(G("emb_ln.weight", {H}), H);
+        r.emb_b = up(G("emb_ln.bias", {H}), H);
+        rope_tables(r, npos, dh, d.rope_theta, &r.cos_g, &r.sin_g);
+    }
+    r.layers.resize(d.num_hidden_layers);
+    for (int li = 0; li < d.num_hidden_layers; ++li) {
+        DevLayer& L = r.layers[li];
+        if (arch == RG_ARCH_QWEN3 || arch == RG_ARCH_GEMMA3) {
+            const std::string p = "layers." + std::to_string(li) + ".";
+            auto norm = [&](const std::string& n, int len) {
+                const float* v = G(p + n, {len});
+                return arch == RG_ARCH_GEMMA3 ? up(unit_offset(v, len).data(), len) : up(v, len);
+            };
+            L.attn_norm = norm("input_layernorm.weight", H);
+            L.q_norm = norm("self_attn.q_norm.weight", dh);
+            L.k_norm = norm("self_attn.k_norm.weight", dh);
+            if (arch == RG_ARCH_QWEN3) {
+                L.ffn_norm = norm("post_attention_layernorm.weight", H);
+            } else {
+                L.post_attn = norm("post_attention_layernorm.weight", H);
+                L.ffn_norm = norm("pre_feedforward_layernorm.weight", H);
+                L.post_ffn = norm("post_feedforward_layernorm.weight", H);
+                L.global = (li + 1) % d.sliding_window_pattern == 0;  // gemma3.go:91
+            }
+            const size_t qn = static_cast<size_t>(m.qd) * H, kn = static_cast<size_t>(m.kvd) * H;
+            std::vector<float> wqkv = concat_rows({{G(p + "self_attn.q_proj.weight", {m.qd, H}), qn},
+                                                   {G(p + "self_attn.k_proj.weight", {m.kvd, H}), kn},
+                                                   {G(p + "self_attn.v_proj.weight", {m.kvd, H}), kn}});
+            L.qkv = make_dense(r, c->mode, wqkv.data(), nullptr, m.nqkv, H);
+            L.o = make_dense(r, c->mode, G(p + "self_attn.o_proj.weight", {H, m.qd}), nullptr, H, m.qd);
+            std::vector<float> wgu = interleave_glu(G(p + "mlp.gate_proj.weight", {I, H}),
+                                                    G(p + "mlp.up_proj.weight", {I, H}), I, H);
+            L.ffn1 = make_dense(r, c->mode, wgu.data(), nullptr, 2 * I, H);
+            L.ffn2 = make_dense(r, c->mode, G(p + "mlp.down_proj.weight", {H, I}), nullptr, H, I);
+        } else if (arch == RG_ARCH_MODERNBERT) {
+            const std::string p = "layers." + std::to_string(li) + ".";
+            L.global = li % d.global_attn_every_n_layers == 0;  // modernbert.go:73
+            if (li != 0) L.attn_norm = up(G(p + "attn_norm.weight", {H}), H);
+            L.ffn_norm = up(G(p + "mlp_norm.weight", {H}), H);
+            L.qkv = make_dense(r, c->mode, G(p + "attn.Wqkv.weight", {3 * H, H}), nullptr, 3 * H, H);
+            L.o = make_dense(r, c->mode, G(p + "attn.Wo.weight", {H, H}), nullptr, H, H);
+            const float* wi = G(p + "mlp.Wi.weight", {2 * I, H});  // value rows [0, I), gate rows [I, 2I)
+            std::vector<float> wgu = interleave_glu(wi, wi + static_cast<size_t>(I) * H, I, H);
+            L.ffn1 = make_dense(r, c->mode, wgu.data(), nullptr, 2 * I, H);
+            L.ffn2 = make_dense(r, c->mode, G(p + "mlp.Wo.weight", {H, I}), nullptr, H, I);
+        } else {  // nomic
+            const std::string p = "encoder.layers." + std::to_string(li) + ".";
+            L.ln1_g = up(G(p + "norm1.weight", {H}), H);
+            L.ln1_b = up(G(p + "norm1.bias", {H}), H);
+            L.ln2_g = up(G(p + "norm2.weight", {H}), H);
+            L.ln2_b = up(G(p + "norm2.bias", {H}), H);
+            L.qkv = make_dense(r, c->mode, G(p + "attn.Wqkv.weight", {3 * H, H}), nullptr, 3 * H, H);
+            L.o = make_dense(r, c->mode, G(p + "attn.out_proj.weight", {H, H}), nullptr, H, H);
+            // fc11 * silu(fc12): the activated operand is fc12 (nomic.go:232-242)
+            std::vector<float> wgu = interleave_glu(G(p + "mlp.fc12.weight", {I, H}), G(p + "mlp.fc11.weight", {I, H}),
+                                                    I, H);
+            L.ffn1 = make_dense(r, c->mode, wgu.data(), nullptr, 2 * I, H);
+            L.ffn2 = make_dense(r, c->mode, G(p + "mlp.fc2.weight", {H, I}), nullptr, H, I);
+        }
+    }
+}
+
 void free_workspace(Replica& r) {
     for (void* p : r.ws) cudaFree(p);
     r.ws.clear();
@@ -374,7 +601,8 @@ T* ws_alloc(Replica& r, size_t count) {
 // Grow the device workspace to hold T tokens / nseq sequences / nout floats.
 void ensure_workspace(rg_ctx* c, Replica& r, int T, int nseq, size_t nout) {
     const rg_model_desc& d = c->d;
-    const int H = d.hidden_size, I = d.intermediate_size;
+    const Dims m = dims(d);
+    const int H = m.H, I = m.I;
     if (T > r.cap_T || nseq > r.cap_seq || nout > static_cast<size_t>(r.cap_out)) {
         // Any stream (ours or a caller's) may still read the old buffers.
         check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
@@ -387,12 +615,21 @@ void ensure_workspace(rg_ctx* c, Replica& r, int T, int nseq, size_t nout) {
         r.x32 = ws_alloc<float>(r, t * H);
         r.y32 = ws_alloc<float>(r, t * H);
         r.xb = ws_alloc<bf16>(r, t * H);
-        r.qkv = ws_alloc<bf16>(r, t * 3 * H);
-        r.ctx = ws_alloc<bf16>(r, t * H);
+        r.qkv = ws_alloc<bf16>(r, t * m.nqkv);
+        r.ctx = ws_alloc<bf16>(r, t * m.qd);
         r.ffh = ws_alloc<bf16>(r, t * I);
+        if (r.dense1) {
+            r.pool32 = ws_alloc<float>(r, static_cast<size_t>(capS) * H);
+            r.head_hid = ws_alloc<float>(r, static_cast<size_t>(capS) * d.dense_hidden);
+            r.head_out = ws_alloc<float>(r, static_cast<size_t>(capS) * H);
+            r.iota = ws_alloc<int32_t>(r, capS + 1);
+            std::vector<int32_t> io(capS + 1);
+            for (int i = 0; i <= capS; ++i) io[i] = i;
+            check(cudaMemcpy(r.iota, io.data(), sizeof(int32_t) * (capS + 1), cudaMemcpyHostToDevice), "H2D iota");
+        }
         if (c->mode == RG_MODE_INT8_FULL) {
             r.xq = ws_alloc<int8_t>(r, t * H);
-            r.ctxq = ws_alloc<int8_t>(r, t * H);
+            r.ctxq = ws_alloc<int8_t>(r, t * m.qd);
             r.ffhq = ws_alloc<int8_t>(r, t * I);
             r.xs = ws_alloc<float>(r, t);
             r.ctxs = ws_alloc<float>(r, t);
@@ -414,7 +651,7 @@ void ensure_workspace(rg_ctx* c, Replica& r, int T, int nseq, size_t nout) {
         const void* ca = s8 ? static_cast<const void*>(r.ctxq) : r.ctx;
         const void* fa = s8 ? static_cast<const void*>(r.ffhq) : r.ffh;
         if (!rg::make_kmajor_tmap(&r.tm_x, xa, eb, T, H, H, 128) ||
-            !rg::make_kmajor_tmap(&r.tm_ctx, ca, eb, T, H, H, 128) ||
+            !rg::make_kmajor_tmap(&r.tm_ctx, ca, eb, T, m.qd, m.qd, 128) ||
             !rg::make_kmajor_tmap(&r.tm_ffh, fa, eb, T, I, I, 128))
             fail("cuTensorMapEncodeTiled failed for the activation buffers");
         r.tm_T = T;
@@ -495,93 +732,233 @@ void gemm(Replica& r, int mode, const CUtensorMap& tmA, const DevDense& w, int M
     a.row_scale = row_scale;
     a.residual = residual;
     a.out = out;
-    a.ld_out = w.N;
+    a.ld_out = rg::epi_is_glu(epi) ? w.N / 2 : w.N;
     a.status = r.d_status;
     const rg::GemmKind kind = mode == RG_MODE_INT8_FULL ? rg::GemmKind::kS8 : rg::GemmKind::kBF16;
     // Algorithmic bytes: A and W read once, output written once (+ fp32
     // residual read); FLOPs 2*M*N*K.
     const double eb = kind == rg::GemmKind::kS8 ? 1.0 : 2.0;
-    const double ob = (epi == rg::kEpiBiasRes || epi == rg::kEpiBiasF32) ? 4.0 : 2.0;
+    const double ob = (epi == rg::kEpiBiasRes || epi == rg::kEpiBiasF32) ? 4.0 : (rg::epi_is_glu(epi) ? 1.0 : 2.0);
     const double bytes = eb * (double(M) * w.K + double(w.N) * w.K) + ob * double(M) * w.N +
                          (epi == rg::kEpiBiasRes ? 4.0 * double(M) * w.N : 0.0);
     ProfScope ps(r, st, RG_KC_GEMM, 2.0 * M * w.N * w.K, bytes);
-    const int bn = rg::gemm_block_n(M, w.N, r.num_sms);
+    const int bn = rg::gemm_block_n(M, w.N, r.num_sms, rg::epi_is_glu(epi));
     if (bn == 0) fail("no GEMM tile width divides N=%d", w.N);
     check(rg::gemm_launch(kind, epi, bn, tmA, w.tmap[bn_index(bn)], a, r.num_sms, st), "gemm launch");
     ++launches;
 }
 
+// Allowed key offsets j - i of a layer's attention (see AttnParams).
+void layer_window(const rg_model_desc& d, const DevLayer& L, int* lo, int* hi) {
+    *lo = -(1 << 30);
+    *hi = 1 << 30;
+    if (d.arch == RG_ARCH_QWEN3) {
+        *hi = 0;  // causal (qwen3.go:319-390)
+    } else if (d.arch == RG_ARCH_MODERNBERT && !L.global) {
+        *lo = -(d.local_attention / 2);  // |i - j| <= LocalAttention/2 (modernbert.go:268-274)
+        *hi = d.local_attention / 2;
+    } else if (d.arch == RG_ARCH_GEMMA3 && !L.global) {
+        *lo = -(d.sliding_window - 1);  // |i - j| < SlidingWindow (gemma3.go:339-346)
+        *hi = d.sliding_window - 1;
+    }
+}
+
+// Number of (i, j) pairs in [0, L)^2 with lo <= j - i <= hi (lo <= 0 <= hi),
+// summed over the batch: sum over offsets d of (L - |d|).
+double attn_pairs(const int32_t* cu, int nseq, int lo, int hi) {
+    double n = 0.0;
+    if (!cu) return n;
+    for (int s = 0; s < nseq; ++s) {
+        const double L = cu[s + 1] - cu[s];
+        if (L <= 0) continue;
+        const double a = std::min<double>(-static_cast<double>(lo), L - 1), b = std::min<double>(hi, L - 1);
+        auto S = [&](double k) { return (k + 1) * L - k * (k + 1) / 2; };  // sum_{d=0..k} (L - d)
+        n += S(a) + S(b) - L;
+    }
+    return n;
+}
+
 // The forward over a batch already on the device (ids, cu in r.d_ids /
-// r.d_cu or the caller's buffers).
+// r.d_cu or the caller's buffers): encodeWorkers and its per-arch variants
+// (bert.go:740-923, qwen3.go:395-548, modernbert.go:148-311,
+// gemma3.go:206-384, nomic.go:113-250), then ForwardWorkers' pooling, Dense
+// head and L2 (bert.go:657-703).
 void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_t* d_cu, int nseq, int T,
                        int max_len, int out_kind, int out_dim, float* d_out, cudaStream_t st) {
     const rg_model_desc& d = c->d;
-    const int H = d.hidden_size, heads = d.num_attention_heads, dh = H / heads;
+    const Dims m = dims(d);
+    const int H = m.H, I = m.I, dh = m.dh, arch = d.arch;
     const float eps = d.layer_norm_eps == 0.f ? 1e-12f : d.layer_norm_eps;
     const int mode = c->mode;
     const bool s8 = mode == RG_MODE_INT8_FULL;
+    const bool pre = is_prenorm(arch);
     int launches = 0;
     const double Td = T, Hd = H;
-    double attn_pairs = 0.0;  // sum over sequences of L^2 (bidirectional)
-    for (int i = 0; i < nseq; ++i) {
-        const double L = r.h_cu_view ? (r.h_cu_view[i + 1] - r.h_cu_view[i]) : 0;
-        attn_pairs += L * L;
-    }
+    const double row_bytes = Td * Hd * (4.0 + 4.0 + 2.0 + (s8 ? 1.0 : 0.0));
+
+    // ---- embeddings
     {
-    ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * (8.0 + 2.0 * 4.0 * Hd + 4.0 * Hd + 2.0 * Hd));
-    check(rg::launch_embed_ln(d_ids, d_cu, nseq, T, r.word, r.pos, r.type0, r.emb_g, r.emb_b, eps, H, d.vocab_size,
-                              pos_offset(d), r.x32, r.xb, s8 ? r.xq : nullptr, s8 ? r.xs : nullptr, r.d_status, st),
-          "embed_ln launch");
-    ++launches;
+        ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * (8.0 + 4.0 * Hd * 2 + 6.0 * Hd));
+        rg::EmbedParams e{};
+        e.ids = d_ids;
+        e.cu = d_cu;
+        e.nseq = nseq;
+        e.T = T;
+        e.H = H;
+        e.vocab = d.vocab_size;
+        e.pos_off = pos_offset(d);
+        e.word = r.word;
+        e.pos = r.pos;
+        e.type0 = r.type0;
+        e.scale = r.emb_scale;
+        e.g = r.emb_g;
+        e.b = arch == RG_ARCH_MODERNBERT ? r.zero_beta : r.emb_b;
+        e.eps = eps;
+        e.x32 = r.x32;
+        e.xb = pre ? nullptr : r.xb;  // pre-norm stacks normalise before the first GEMM
+        e.xq = (!pre && s8) ? r.xq : nullptr;
+        e.xq_scale = (!pre && s8) ? r.xs : nullptr;
+        e.status = r.d_status;
+        check(rg::launch_embed(e, st), "embed launch");
+        ++launches;
     }
-    // attention: QK^T and PV over the allowed (i, j) pairs, 4*dh FLOPs each;
-    // bytes: Q, K, V read once and the context written once (bf16).
-    const double attn_flops = 4.0 * dh * attn_pairs * heads;
-    const double attn_bytes = 2.0 * (3.0 * Td * Hd + Td * Hd);
-    const double ln_bytes = Td * Hd * (4.0 + 4.0 + 2.0 + (s8 ? 1.0 : 0.0));
-    const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
+    // Norm of x32 into the next GEMM's A operand (bf16, or int8 + scales).
+    auto norm_into_a = [&](const float* g, const float* b, bool rms) {
+        ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * Hd * (4.0 + 2.0 + (s8 ? 1.0 : 0.0)));
+        rg::NormParams p{};
+        p.in = r.x32;
+        p.g = g;
+        p.b = b;
+        p.eps = eps;
+        p.T = T;
+        p.H = H;
+        p.outb = r.xb;
+        p.outq = s8 ? r.xq : nullptr;
+        p.outqs = s8 ? r.xs : nullptr;
+        check(rg::launch_norm(p, rms, st), "norm launch");  // g nullptr: identity
+        ++launches;
+    };
+    auto post_norm = [&](const float* g, const float* b) {  // y32 -> LN -> x32 (+ A operand)
+        ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, row_bytes);
+        check(rg::launch_ln(r.y32, g, b, eps, T, H, r.x32, r.xb, s8 ? r.xq : nullptr, s8 ? r.xs : nullptr, st),
+              "ln launch");
+        ++launches;
+    };
+    auto quantize = [&](const bf16* x, int K, int8_t* q, float* sc) {
+        ProfScope ps(r, st, RG_KC_QUANT, 0.0, Td * K * 3.0);
+        check(rg::launch_quantize_rows(x, T, K, q, sc, st), "quantize launch");
+        ++launches;
+    };
+    const float scale = static_cast<float>(
+        1.0 / std::sqrt(static_cast<double>(arch == RG_ARCH_GEMMA3 ? d.query_pre_attn_scalar : dh)));
+    const int glu_epi = arch == RG_ARCH_MODERNBERT ? rg::kEpiGluGeluErf
+                        : arch == RG_ARCH_GEMMA3   ? rg::kEpiGluGeluTanh
+                                                   : rg::kEpiGluSilu;
+
     for (int li = 0; li < d.num_hidden_layers; ++li) {
         const DevLayer& L = r.layers[li];
+        // ---- attention sublayer
+        if (pre) norm_into_a(L.attn_norm, arch == RG_ARCH_MODERNBERT ? r.zero_beta : nullptr, arch != RG_ARCH_MODERNBERT);
         gemm(r, mode, r.tm_x, L.qkv, T, rg::kEpiBias, s8 ? r.xs : nullptr, nullptr, r.qkv, st, launches);
+        if (has_rope(arch)) {
+            ProfScope ps(r, st, RG_KC_NORM, 0.0, Td * (m.qd + m.kvd) * 4.0);
+            rg::QkRopeParams q{};
+            q.qkv = r.qkv;
+            q.ld = m.nqkv;
+            q.T = T;
+            q.nq = m.nq;
+            q.nkv = m.nkv;
+            q.q_norm = L.q_norm;
+            q.k_norm = L.k_norm;
+            q.eps = eps;
+            q.cos = L.global ? r.cos_g : r.cos_l;
+            q.sin = L.global ? r.sin_g : r.sin_l;
+            q.cu = d_cu;
+            q.nseq = nseq;
+            check(rg::launch_qk_norm_rope(q, dh, st), "qk norm/rope launch");
+            ++launches;
+        }
         {
-            ProfScope ps(r, st, RG_KC_ATTENTION, attn_flops, attn_bytes);
-            check(rg::launch_attention(r.qkv, d_cu, nseq, max_len, H, heads, dh, scale, r.ctx, st),
-                  "attention launch");
+            int lo, hi;
+            layer_window(d, L, &lo, &hi);
+            const double pairs = attn_pairs(r.h_cu_view, nseq, lo, hi);
+            ProfScope ps(r, st, RG_KC_ATTENTION, 4.0 * dh * pairs * m.nq,
+                         2.0 * Td * (2.0 * m.qd + 2.0 * m.kvd));
+            rg::AttnParams ap{};
+            ap.q = r.qkv;
+            ap.k = r.qkv + m.qd;
+            ap.v = r.qkv + m.qd + m.kvd;
+            ap.ldq = ap.ldk = ap.ldv = m.nqkv;
+            ap.cu = d_cu;
+            ap.group = m.nq / m.nkv;
+            ap.scale = scale;
+            ap.scale_log2 = scale * 1.4426950408889634f;
+            ap.rel_lo = lo;
+            ap.rel_hi = hi;
+            ap.bias = r.rel_bias;
+            ap.bias_off = r.rel_bias_off;
+            ap.out = r.ctx;
+            ap.ldo = m.qd;
+            check(rg::launch_attention(ap, nseq, max_len, m.nq, dh, st), "attention launch");
             ++launches;
         }
-        if (s8) {
-            ProfScope ps(r, st, RG_KC_QUANT, 0.0, Td * Hd * 3.0);
-            check(rg::launch_quantize_rows(r.ctx, T, H, r.ctxq, r.ctxs, st), "quantize launch");
+        if (s8) quantize(r.ctx, m.qd, r.ctxq, r.ctxs);
+        if (!pre) {
+            gemm(r, mode, r.tm_ctx, L.o, T, rg::kEpiBiasRes, s8 ? r.ctxs : nullptr, r.x32, r.y32, st, launches);
+            post_norm(L.ln1_g, L.ln1_b);
+        } else if (arch == RG_ARCH_GEMMA3) {
+            gemm(r, mode, r.tm_ctx, L.o, T, rg::kEpiBiasF32, s8 ? r.ctxs : nullptr, nullptr, r.y32, st, launches);
+            ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * Hd * 12.0);
+            check(rg::launch_add_rmsnorm(r.x32, r.y32, L.post_attn, eps, T, H, st), "add_rmsnorm launch");
             ++launches;
+        } else {  // residual added in place on x32
+            gemm(r, mode, r.tm_ctx, L.o, T, rg::kEpiBiasRes, s8 ? r.ctxs : nullptr, r.x32, r.x32, st, launches);
         }
-        gemm(r, mode, r.tm_ctx, L.o, T, rg::kEpiBiasRes, s8 ? r.ctxs : nullptr, r.x32, r.y32, st, launches);
-        {
-            ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, ln_bytes);
-            check(rg::launch_ln(r.y32, L.ln1_g, L.ln1_b, eps, T, H, r.x32, r.xb, s8 ? r.xq : nullptr,
-                                s8 ? r.xs : nullptr, st),
-                  "ln launch");
+        // ---- FFN sublayer
+        if (pre) norm_into_a(L.ffn_norm, arch == RG_ARCH_MODERNBERT ? r.zero_beta : nullptr, arch != RG_ARCH_MODERNBERT);
+        gemm(r, mode, r.tm_x, L.ffn1, T, is_glu(arch) ? glu_epi : rg::kEpiBiasGelu, s8 ? r.xs : nullptr, nullptr,
+             r.ffh, st, launches);
+        if (s8) quantize(r.ffh, I, r.ffhq, r.ffhs);
+        if (!pre) {
+            gemm(r, mode, r.tm_ffh, L.ffn2, T, rg::kEpiBiasRes, s8 ? r.ffhs : nullptr, r.x32, r.y32, st, launches);
+            post_norm(L.ln2_g, L.ln2_b);
+        } else if (arch == RG_ARCH_GEMMA3) {
+            gemm(r, mode, r.tm_ffh, L.ffn2, T, rg::kEpiBiasF32, s8 ? r.ffhs : nullptr, nullptr, r.y32, st, launches);
+            ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * Hd * 12.0);
+            check(rg::launch_add_rmsnorm(r.x32, r.y32, L.post_ffn, eps, T, H, st), "add_rmsnorm launch");
             ++launches;
+        } else {
+            gemm(r, mode, r.tm_ffh, L.ffn2, T, rg::kEpiBiasRes, s8 ? r.ffhs : nullptr, r.x32, r.x32, st, launches);
         }
-        gemm(r, mode, r.tm_x, L.ffn1, T, rg::kEpiBiasGelu, s8 ? r.xs : nullptr, nullptr, r.ffh, st, launches);
-        if (s8) {
-            ProfScope ps(r, st, RG_KC_QUANT, 0.0, Td * d.intermediate_size * 3.0);
-            check(rg::launch_quantize_rows(r.ffh, T, d.intermediate_size, r.ffhq, r.ffhs, st), "quantize launch");
-            ++launches;
-        }
-        gemm(r, mode, r.tm_ffh, L.ffn2, T, rg::kEpiBiasRes, s8 ? r.ffhs : nullptr, r.x32, r.y32, st, launches);
-        {
-            ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, ln_bytes);
-            check(rg::launch_ln(r.y32, L.ln2_g, L.ln2_b, eps, T, H, r.x32, r.xb, s8 ? r.xq : nullptr,
-                                s8 ? r.xs : nullptr, st),
-                  "ln launch");
-            ++launches;
-        }
+    }
+    if (r.final_norm) {  // qwen3.go:544, gemma3.go:380, modernbert.go:307
+        ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * Hd * 8.0);
+        rg::NormParams p{};
+        p.in = r.x32;
+        p.g = r.final_norm;
+        p.b = arch == RG_ARCH_MODERNBERT ? r.zero_beta : nullptr;
+        p.eps = eps;
+        p.T = T;
+        p.H = H;
+        p.out32 = r.x32;
+        check(rg::launch_norm(p, arch != RG_ARCH_MODERNBERT, st), "final norm launch");
+        ++launches;
     }
     if (out_kind == RG_OUT_POOLED) {
         const double rows = d.pooling == 0 ? Td : double(nseq);
         ProfScope ps(r, st, RG_KC_POOL, rows * Hd, 4.0 * (rows * Hd + double(nseq) * out_dim));
-        check(rg::launch_pool(r.x32, d_cu, nseq, H, d.pooling, d.normalize, out_dim, d_out, st), "pool launch");
-        ++launches;
+        if (r.dense1) {
+            // pool, Dense head H -> D -> H (fp32), then L2 and truncate (gemma3.go:177-198)
+            const int D = d.dense_hidden;
+            check(rg::launch_pool(r.x32, d_cu, nseq, H, d.pooling, 0, H, r.pool32, st), "pool launch");
+            check(rg::launch_dense_f32(r.pool32, r.dense1, r.head_hid, nseq, D, H, st), "dense launch");
+            check(rg::launch_dense_f32(r.head_hid, r.dense2, r.head_out, nseq, H, D, st), "dense launch");
+            check(rg::launch_pool(r.head_out, r.iota, nseq, H, 1, d.normalize, out_dim, d_out, st), "l2 launch");
+            launches += 4;
+        } else {
+            check(rg::launch_pool(r.x32, d_cu, nseq, H, d.pooling, d.normalize, out_dim, d_out, st), "pool launch");
+            ++launches;
+        }
     } else {
         check(cudaMemcpyAsync(d_out, r.x32, sizeof(float) * static_cast<size_t>(T) * H, cudaMemcpyDeviceToDevice,
                               st),
@@ -677,19 +1054,37 @@ int rg_init(const rg_model_desc* desc, const int* devices, int ndev, int mode, r
         if (!desc || !out) fail("rg_init: null argument");
         *out = nullptr;
         const rg_model_desc& d = *desc;
-        if (!is_bert_family(d.arch)) fail("rg_init: architecture %d is not supported by this build", d.arch);
+        if (d.arch < RG_ARCH_BERT || d.arch > RG_ARCH_NOMIC) fail("rg_init: unknown architecture %d", d.arch);
         if (d.hidden_size <= 0 || d.num_hidden_layers <= 0 || d.num_attention_heads <= 0 ||
             d.intermediate_size <= 0 || d.vocab_size <= 0 || d.max_position_embeddings <= 0)
             fail("rg_init: missing or non-positive architecture fields");
         if (d.hidden_size % d.num_attention_heads != 0)
             fail("rg_init: hidden_size %d not divisible by num_attention_heads %d", d.hidden_size,
                  d.num_attention_heads);
-        const int dh = d.hidden_size / d.num_attention_heads;
-        if (dh != 32 && dh != 64) fail("rg_init: head dim %d unsupported (32 or 64)", dh);
+        const Dims dm = dims(d);
+        const int dh = dm.dh;
+        if (dh != 32 && dh != 64 && dh != 128 && dh != 256)
+            fail("rg_init: head dim %d unsupported (32, 64, 128 or 256)", dh);
+        if (has_rope(d.arch) && dh == 32) fail("rg_init: RoPE needs head dim >= 64");
+        if (dm.nkv <= 0 || dm.nq % dm.nkv != 0)
+            fail("rg_init: num_attention_heads %d not divisible by num_key_value_heads %d", dm.nq, dm.nkv);
+        if (d.arch == RG_ARCH_MODERNBERT && (d.global_attn_every_n_layers < 1 || d.local_attention < 2))
+            fail("rg_init: modernbert needs global_attn_every_n_layers >= 1 and local_attention >= 2");
+        if (d.arch == RG_ARCH_GEMMA3 &&
+            (d.sliding_window < 1 || d.sliding_window_pattern < 1 || d.query_pre_attn_scalar < 1 || d.dense_hidden < 1))
+            fail("rg_init: gemma3 needs sliding_window, sliding_window_pattern, query_pre_attn_scalar, dense_hidden");
+        if (is_glu(d.arch) && (d.intermediate_size % 64 != 0))
+            fail("rg_init: gated FFN needs intermediate_size %% 64 == 0 (got %d)", d.intermediate_size);
+        if (dm.nqkv % 128 != 0 || dm.qd % 64 != 0)
+            fail("rg_init: fused q/k/v width %d must be a multiple of 128", dm.nqkv);
         if (d.hidden_size % 128 != 0 || d.intermediate_size % 128 != 0)
             fail("rg_init: hidden_size and intermediate_size must be multiples of 128 (got %d, %d)", d.hidden_size,
                  d.intermediate_size);
         if (d.pooling < 0 || d.pooling > 2) fail("rg_init: bad pooling %d", d.pooling);
+        if (d.arch == RG_ARCH_MPNET && d.relative_attention_num_buckets < 2)
+            fail("rg_init: mpnet needs relative_attention_num_buckets >= 2");
+        if (max_seq_len(d) <= 0) fail("rg_init: no usable positions (max_position_embeddings %d, offset %d)",
+                                      d.max_position_embeddings, pos_offset(d));
         if (mode != RG_MODE_BF16 && mode != RG_MODE_INT8_FULL)
             fail("rg_init: mode %d is not available in this build", mode);
         if (mode == RG_MODE_INT8_FULL && (d.hidden_size % 128 != 0 || d.intermediate_size % 128 != 0))
@@ -772,7 +1167,12 @@ int rg_finalize(rg_ctx* c, char** err) {
         if (!c) fail("rg_finalize: null context");
         std::lock_guard<std::mutex> lk(c->mu);
         if (c->finalized) return 0;
-        for (Replica* r : c->reps) finalize_bert(c, *r);
+        for (Replica* r : c->reps) {
+            if (is_bert_family(c->d.arch))
+                finalize_bert(c, *r);
+            else
+                finalize_decoder(c, *r);
+        }
         c->host.clear();
         c->finalized = true;
         return 0;

@@ -40,7 +40,80 @@ PRESETS = {
     "bge-base": lambda: _bert("synthetic/bge-base-en-v1.5", 768, 12, 12, 3072, "cls"),
     # A tiny BERT for fast unit tests (same code path, small dims).
     "tiny-bert": lambda: _bert("synthetic/tiny-bert", 128, 2, 2, 512, "mean", vocab=4096, max_pos=256),
+    # The other BERT-path encoders (bert.go:338-518), small dims.
+    "tiny-distilbert": lambda: _variant("distilbert", "synthetic/tiny-distilbert"),
+    "tiny-roberta": lambda: _variant("roberta", "synthetic/tiny-roberta", pad_token_id=1, max_pos=258),
+    "tiny-mpnet": lambda: _variant("mpnet", "synthetic/tiny-mpnet", pad_token_id=1, max_pos=258,
+                                   relative_attention_num_buckets=32),
+    # all-mpnet-base-v2 architecture (12 layers, hidden 768, 12 x 64, FFN 3072, mean pool).
+    "mpnet-base": lambda: _variant("mpnet", "synthetic/all-mpnet-base-v2", H=768, L=12, heads=12, I=3072,
+                                   vocab=30527, pad_token_id=1, max_pos=514, relative_attention_num_buckets=32,
+                                   eps=1e-5),
 }
+
+
+def _qwen3(name, H, L, nq, nkv, dh, I, vocab, max_pos):
+    return Config(name=name, model_type="qwen3", hidden_size=H, num_hidden_layers=L, num_attention_heads=nq,
+                  num_key_value_heads=nkv, head_dim=dh, intermediate_size=I, vocab_size=vocab,
+                  max_position_embeddings=max_pos, layer_norm_eps=1e-6, rope_theta=1e6, pooling="lasttoken",
+                  normalize=True)
+
+
+def _modernbert(name, H, L, heads, I, vocab, max_pos, local_attention):
+    return Config(name=name, model_type="modernbert", hidden_size=H, num_hidden_layers=L,
+                  num_attention_heads=heads, intermediate_size=I, vocab_size=vocab,
+                  max_position_embeddings=max_pos, layer_norm_eps=1e-5, global_attn_every_n_layers=3,
+                  local_attention=local_attention, global_rope_theta=160000.0, local_rope_theta=10000.0,
+                  pooling="mean", normalize=True)
+
+
+def _gemma3(name, H, L, nq, nkv, dh, I, vocab, max_pos, window, pattern, dense):
+    return Config(name=name, model_type="gemma3", hidden_size=H, num_hidden_layers=L, num_attention_heads=nq,
+                  num_key_value_heads=nkv, head_dim=dh, intermediate_size=I, vocab_size=vocab,
+                  max_position_embeddings=max_pos, layer_norm_eps=1e-6, sliding_window=window,
+                  sliding_window_pattern=pattern, query_pre_attn_scalar=dh, global_rope_theta=1e6,
+                  local_rope_theta=1e4, dense_hidden=dense, pooling="mean", normalize=True, tokenizer="gemma")
+
+
+def _nomic(name, H, L, heads, I, vocab, max_pos):
+    return Config(name=name, model_type="nomic_bert", hidden_size=H, num_hidden_layers=L,
+                  num_attention_heads=heads, head_dim=H // heads, intermediate_size=I, vocab_size=vocab,
+                  max_position_embeddings=max_pos, layer_norm_eps=1e-12, rope_theta=1000.0, pooling="mean",
+                  normalize=True)
+
+
+PRESETS.update({
+    # Qwen3-Embedding-0.6B: causal decoder, 28 layers, hidden 1024, 16 q / 8 kv heads x 128,
+    # SwiGLU 3072, RMSNorm 1e-6, RoPE 1e6, last-token pooling.
+    "qwen3-0.6b": lambda: _qwen3("synthetic/Qwen3-Embedding-0.6B", 1024, 28, 16, 8, 128, 3072, 151669, 32768),
+    "tiny-qwen3": lambda: _qwen3("synthetic/tiny-qwen3", 256, 2, 4, 2, 64, 512, 2048, 1024),
+    # ModernBERT-base: 22 layers, hidden 768, 12 x 64, GeGLU 1152, global every 3rd layer
+    # (RoPE 160000), local window 128 (RoPE 10000).
+    "modernbert-base": lambda: _modernbert("synthetic/ModernBERT-base", 768, 22, 12, 1152, 50368, 8192, 128),
+    "tiny-modernbert": lambda: _modernbert("synthetic/tiny-modernbert", 128, 4, 2, 256, 2048, 1024, 16),
+    # EmbeddingGemma-300m: 24 layers, hidden 768, 3 q / 1 kv head x 256, GeGLU-tanh 1152,
+    # alternating local (effective window 257) / global, Dense head 768->3072->768.
+    "embeddinggemma-300m": lambda: _gemma3("synthetic/embeddinggemma-300m", 768, 24, 3, 1, 256, 1152, 262144,
+                                           2048, 257, 2, 3072),
+    "tiny-gemma3": lambda: _gemma3("synthetic/tiny-gemma3", 128, 4, 2, 1, 64, 256, 2048, 512, 9, 2, 256),
+    # nomic-embed-text-v1.5: post-norm, RoPE 1000, SwiGLU fc11 * silu(fc12).
+    "nomic-embed-v1.5": lambda: _nomic("synthetic/nomic-embed-text-v1.5", 768, 12, 12, 3072, 30528, 2048),
+    "tiny-nomic": lambda: _nomic("synthetic/tiny-nomic", 128, 2, 2, 256, 2048, 512),
+})
+
+# Families whose token ids are not framed by CLS/SEP in the synthetic batches.
+UNFRAMED = {"qwen3", "modernbert", "gemma3"}
+
+
+def _variant(model_type, name, H=128, L=2, heads=2, I=512, vocab=4096, max_pos=256, eps=1e-12, **kw):
+    c = _bert(name, H, L, heads, I, "mean", vocab=vocab, max_pos=max_pos)
+    c.model_type = model_type
+    c.layer_norm_eps = eps
+    if model_type == "roberta":
+        c.type_vocab_size = 1
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c
 
 
 def preset(name: str) -> Config:
@@ -48,36 +121,120 @@ def preset(name: str) -> Config:
 
 
 def _bert_shapes(cfg: Config) -> dict[str, tuple]:
+    """HF tensor names of the BERT-path encoders (bert.go:381-470, 495-515)."""
     H, I = cfg.hidden_size, cfg.intermediate_size
+    mt = cfg.model_type
+    pre = {"roberta": "roberta.", "mpnet": "mpnet.", "distilbert": "distilbert."}.get(mt, "")
     s: dict[str, tuple] = {
-        "embeddings.word_embeddings.weight": (cfg.vocab_size, H),
-        "embeddings.position_embeddings.weight": (cfg.max_position_embeddings, H),
-        "embeddings.token_type_embeddings.weight": (cfg.type_vocab_size, H),
-        "embeddings.LayerNorm.weight": (H,),
-        "embeddings.LayerNorm.bias": (H,),
+        pre + "embeddings.word_embeddings.weight": (cfg.vocab_size, H),
+        pre + "embeddings.position_embeddings.weight": (cfg.max_position_embeddings, H),
+        pre + "embeddings.LayerNorm.weight": (H,),
+        pre + "embeddings.LayerNorm.bias": (H,),
     }
+    if mt not in ("distilbert", "mpnet"):
+        s[pre + "embeddings.token_type_embeddings.weight"] = (cfg.type_vocab_size, H)
+    if mt == "mpnet":
+        s[pre + "encoder.relative_attention_bias.weight"] = (cfg.relative_attention_num_buckets,
+                                                             cfg.num_attention_heads)
     for i in range(cfg.num_hidden_layers):
-        p = f"encoder.layer.{i}."
-        for nm in ("query", "key", "value"):
-            s[p + f"attention.self.{nm}.weight"] = (H, H)
-            s[p + f"attention.self.{nm}.bias"] = (H,)
-        s[p + "attention.output.dense.weight"] = (H, H)
-        s[p + "attention.output.dense.bias"] = (H,)
-        s[p + "attention.output.LayerNorm.weight"] = (H,)
-        s[p + "attention.output.LayerNorm.bias"] = (H,)
-        s[p + "intermediate.dense.weight"] = (I, H)
-        s[p + "intermediate.dense.bias"] = (I,)
-        s[p + "output.dense.weight"] = (H, I)
-        s[p + "output.dense.bias"] = (H,)
-        s[p + "output.LayerNorm.weight"] = (H,)
-        s[p + "output.LayerNorm.bias"] = (H,)
+        if mt == "distilbert":
+            p = f"{pre}transformer.layer.{i}."
+            attn = {"q_lin": "attention.q_lin", "k_lin": "attention.k_lin", "v_lin": "attention.v_lin",
+                    "out": "attention.out_lin"}
+            names = [(attn["q_lin"], (H, H)), (attn["k_lin"], (H, H)), (attn["v_lin"], (H, H)),
+                     (attn["out"], (H, H)), ("ffn.lin1", (I, H)), ("ffn.lin2", (H, I))]
+            norms = ["sa_layer_norm", "output_layer_norm"]
+        else:
+            p = f"{pre}encoder.layer.{i}."
+            if mt == "mpnet":
+                qkvo = ["attention.attn.q", "attention.attn.k", "attention.attn.v", "attention.attn.o"]
+                norms = ["attention.LayerNorm", "output.LayerNorm"]
+            else:
+                qkvo = ["attention.self.query", "attention.self.key", "attention.self.value",
+                        "attention.output.dense"]
+                norms = ["attention.output.LayerNorm", "output.LayerNorm"]
+            names = [(qkvo[0], (H, H)), (qkvo[1], (H, H)), (qkvo[2], (H, H)), (qkvo[3], (H, H)),
+                     ("intermediate.dense", (I, H)), ("output.dense", (H, I))]
+        for nm, shp in names:
+            s[p + nm + ".weight"] = shp
+            s[p + nm + ".bias"] = (shp[0],)
+        for nm in norms:
+            s[p + nm + ".weight"] = (H,)
+            s[p + nm + ".bias"] = (H,)
+    return s
+
+
+def _decoder_shapes(cfg: Config) -> dict[str, tuple]:
+    """HF tensor names of the Qwen3 / Gemma3 / ModernBERT / nomic loaders
+    (qwen3.go:87-110, gemma3.go:103-170, modernbert.go:55-103, nomic.go:36-110)."""
+    H, I, mt = cfg.hidden_size, cfg.intermediate_size, cfg.model_type
+    dh = cfg.attn_head_dim
+    nq, nkv = cfg.num_attention_heads, (cfg.num_key_value_heads or cfg.num_attention_heads)
+    s: dict[str, tuple] = {}
+    if mt in ("qwen3", "gemma3"):
+        s["embed_tokens.weight"] = (cfg.vocab_size, H)
+        s["norm.weight"] = (H,)
+        for i in range(cfg.num_hidden_layers):
+            p = f"layers.{i}."
+            s[p + "input_layernorm.weight"] = (H,)
+            s[p + "post_attention_layernorm.weight"] = (H,)
+            if mt == "gemma3":
+                s[p + "pre_feedforward_layernorm.weight"] = (H,)
+                s[p + "post_feedforward_layernorm.weight"] = (H,)
+            s[p + "self_attn.q_proj.weight"] = (nq * dh, H)
+            s[p + "self_attn.k_proj.weight"] = (nkv * dh, H)
+            s[p + "self_attn.v_proj.weight"] = (nkv * dh, H)
+            s[p + "self_attn.o_proj.weight"] = (H, nq * dh)
+            s[p + "self_attn.q_norm.weight"] = (dh,)
+            s[p + "self_attn.k_norm.weight"] = (dh,)
+            s[p + "mlp.gate_proj.weight"] = (I, H)
+            s[p + "mlp.up_proj.weight"] = (I, H)
+            s[p + "mlp.down_proj.weight"] = (H, I)
+        if mt == "gemma3":
+            s["2_Dense.linear.weight"] = (cfg.dense_hidden, H)
+            s["3_Dense.linear.weight"] = (H, cfg.dense_hidden)
+    elif mt == "modernbert":
+        s["embeddings.tok_embeddings.weight"] = (cfg.vocab_size, H)
+        s["embeddings.norm.weight"] = (H,)
+        s["final_norm.weight"] = (H,)
+        for i in range(cfg.num_hidden_layers):
+            p = f"layers.{i}."
+            if i != 0:
+                s[p + "attn_norm.weight"] = (H,)
+            s[p + "attn.Wqkv.weight"] = (3 * H, H)
+            s[p + "attn.Wo.weight"] = (H, H)
+            s[p + "mlp_norm.weight"] = (H,)
+            s[p + "mlp.Wi.weight"] = (2 * I, H)
+            s[p + "mlp.Wo.weight"] = (H, I)
+    else:  # nomic_bert
+        s["embeddings.word_embeddings.weight"] = (cfg.vocab_size, H)
+        s["embeddings.token_type_embeddings.weight"] = (2, H)
+        s["emb_ln.weight"] = (H,)
+        s["emb_ln.bias"] = (H,)
+        for i in range(cfg.num_hidden_layers):
+            p = f"encoder.layers.{i}."
+            s[p + "attn.Wqkv.weight"] = (3 * H, H)
+            s[p + "attn.out_proj.weight"] = (H, H)
+            s[p + "mlp.fc11.weight"] = (I, H)
+            s[p + "mlp.fc12.weight"] = (I, H)
+            s[p + "mlp.fc2.weight"] = (H, I)
+            for n in ("norm1", "norm2"):
+                s[p + n + ".weight"] = (H,)
+                s[p + n + ".bias"] = (H,)
     return s
 
 
 def tensor_shapes(cfg: Config) -> dict[str, tuple]:
-    if cfg.model_type in ("", "bert"):
+    if cfg.model_type in ("", "bert", "distilbert", "roberta", "mpnet"):
         return _bert_shapes(cfg)
+    if cfg.model_type in ("qwen3", "gemma3", "modernbert", "nomic_bert"):
+        return _decoder_shapes(cfg)
     raise NotImplementedError(f"synthetic weights for model_type {cfg.model_type!r}")
+
+
+def _is_gain(name: str) -> bool:
+    return name.endswith(("LayerNorm.weight", "norm.weight", "_norm.weight", "layer_norm.weight", "layernorm.weight",
+                          "emb_ln.weight", "norm1.weight", "norm2.weight"))
 
 
 def make_weights(cfg: Config, seed: int = 0, std: float = 0.02) -> dict[str, np.ndarray]:
@@ -87,8 +244,14 @@ def make_weights(cfg: Config, seed: int = 0, std: float = 0.02) -> dict[str, np.
     for name, shape in tensor_shapes(cfg).items():
         w = rng.standard_normal(shape, dtype=np.float32)
         w *= np.float32(std)
-        if name.endswith("LayerNorm.weight") or name.endswith("norm.weight") or name.endswith("_norm.weight"):
+        # Norm gains are 1 + N(0, std), except Gemma's, whose stored weights
+        # are the offset from 1 (the loader adds it: gemma3.go:44-50).
+        if _is_gain(name) and cfg.model_type != "gemma3":
             w += np.float32(1.0)
+        if cfg.model_type == "qwen3":
+            # bf16 checkpoint widened to float32 (safetensors.go:188-209)
+            w = (w.view(np.uint32) + np.uint32(0x7FFF) + ((w.view(np.uint32) >> 16) & 1)) & np.uint32(0xFFFF0000)
+            w = w.view(np.float32)
         out[name] = np.ascontiguousarray(w)
     return out
 
@@ -102,6 +265,9 @@ def make_batch(cfg: Config, nseq: int, lo: int, hi: int, seed: int = 1,
     is CLS + ids uniform in [id_lo, id_hi] + SEP, the layout a WordPiece
     tokenizer produces for BERT-family models.
     """
+    if cfg.model_type in UNFRAMED:
+        framed = False
+        id_lo = 0 if id_lo == 1000 else id_lo
     rng = np.random.default_rng(seed)
     hi = min(hi, cfg.max_seq_len())
     lens = rng.integers(lo, hi + 1, size=nseq) if hi > lo else np.full(nseq, lo)

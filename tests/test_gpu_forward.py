@@ -166,3 +166,30 @@ def test_full_int8_parity(minilm_int8):
 @pytest.fixture(scope="module")
 def minilm_int8(cuda):
     return Model("minilm-l6", quant=oracle.QUANT_FULL)
+
+
+@pytest.mark.parametrize("name,nseq,lo,hi", [("tiny-distilbert", 7, 1, 200), ("tiny-roberta", 7, 1, 256),
+                                             ("tiny-mpnet", 9, 1, 256), ("mpnet-base", 6, 16, 384)])
+def test_bert_path_variants(cuda, name, nseq, lo, hi):
+    """DistilBERT names, RoBERTa's position offset and MPNet's relative
+    attention bias (bert.go:338-518, 820-830, 876-889) on the same kernels."""
+    m = Model(name)
+    ids, cu = synth.make_batch(m.cfg, nseq, lo, hi, seed=21, id_lo=5, id_hi=m.cfg.vocab_size - 1, cls_id=0, sep_id=2)
+    got = m.gpu.embed_packed(ids, cu)
+    want = m.ref.embed(ids, cu)
+    cos = cosines(got, want)
+    print(f"\n[parity] {name}: min cos {cos.min():.7f}, max abs {np.abs(got - want).max():.2e}")
+    assert cos.min() >= COS_BF16
+    assert np.abs(got - want).max() <= MAXABS_BF16
+    m.gpu.close()
+
+
+def test_full_int8_parity_bge(cuda):
+    m = Model("bge-base", quant=oracle.QUANT_FULL)
+    ids, cu = synth.make_batch(m.cfg, 6, 16, 256, seed=16)
+    got = m.gpu.embed_packed(ids, cu)
+    want = m.ref.embed(ids, cu)
+    cos = cosines(got, want)
+    print(f"\n[parity] bge full int8: min cos {cos.min():.6f}, max abs {np.abs(got - want).max():.2e}")
+    assert cos.min() >= COS_INT8_FULL
+    m.gpu.close()
