@@ -2,7 +2,7 @@
 """Benchmark: embeddings/sec of the rembed encoder forward pass on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload bge-base-b256xL128] [--mode bf16|int8_full]
+                    [--workload bge-base-b256xL128] [--mode f16|bf16|int8_w|int8_full]
 
 N > 1 runs under torchrun, one process per GPU.  Each rank embeds its own
 batch of the workload (data parallel, no collective on the data path:
@@ -45,6 +45,13 @@ WORKLOADS = {
     "minilm-l6-b32xU8-128": dict(preset="minilm-l6", nseq=32, lo=8, hi=128),
 }
 METRIC = "embeddings/sec at bge-base b256×L128 (fp & int8), 1–8 GPU; tensor-pipe util %"
+# mode -> (Embedder keyword arguments, oracle quantisation name, dtype the path computes in)
+MODES = {
+    "f16": ({"fp16": True}, "QUANT_NONE", "f16"),
+    "bf16": ({"fp16": False}, "QUANT_NONE", "bf16"),
+    "int8_w": ({"int8": True}, "QUANT_WEIGHTS", "s8 weights x f16"),
+    "int8_full": ({"int8_activations": True}, "QUANT_FULL", "s8"),
+}
 
 
 def parse():
@@ -54,7 +61,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="bge-base-b256xL128")
-    ap.add_argument("--mode", choices=["bf16", "int8_full"], default="bf16")
+    ap.add_argument("--mode", choices=list(MODES), default="f16")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target length of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -90,6 +97,9 @@ def gemm_flops_per_token(cfg) -> float:
     return 2.0 * cfg.num_hidden_layers * (H * 3 * H + H * H + 2 * H * I)
 
 
+ORACLE_PATH = {"f16": "fp32", "bf16": "fp32", "int8_w": "weight-int8", "int8_full": "full int8"}
+
+
 # ---------------------------------------------------------------------------
 def cpu_sample(wl, mode: str, target_s: float, nthreads: int):
     """Time the oracle (CPU restatement of the reference forward) on a bounded
@@ -100,7 +110,7 @@ def cpu_sample(wl, mode: str, target_s: float, nthreads: int):
 
     cfg = synth.preset(wl["preset"])
     w = synth.make_weights(cfg, seed=0)
-    quant = oracle.QUANT_FULL if mode == "int8_full" else oracle.QUANT_NONE
+    quant = getattr(oracle, MODES[mode][1])
     m = oracle.OracleModel(cfg, w, quant)
     # calibrate on one sequence per thread
     _, ids, cu = make_inputs(wl, seed=1, n=nthreads)
@@ -118,7 +128,7 @@ def cpu_sample(wl, mode: str, target_s: float, nthreads: int):
         "value": round(n / dt, 3), "unit": "embeddings/s", "cores": nthreads, "kind": "port",
         "sample": f"{n} sequences of the {wl['preset']} workload (L in [{wl['lo']},{wl['hi']}]), one serial "
                   f"forward each across {nthreads} threads, {dt:.1f} s; C restatement of the reference "
-                  f"({'full int8' if quant else 'fp32'} path), not the Go binary; CPU: {cpu_model()}",
+                  f"({ORACLE_PATH[mode]} path), not the Go binary; CPU: {cpu_model()}",
     }
 
 
@@ -132,7 +142,7 @@ def reference_arm(args, rank, world):
     nth = host_threads()
     cfg = synth.preset(wl["preset"])
     w = synth.make_weights(cfg, seed=0)
-    quant = oracle.QUANT_FULL if args.mode == "int8_full" else oracle.QUANT_NONE
+    quant = getattr(oracle, MODES[args.mode][1])
     m = oracle.OracleModel(cfg, w, quant)
     _, ids, cu = make_inputs(wl, seed=1, n=nth)  # one sequence per thread per step
     for _ in range(args.warmup):
@@ -146,7 +156,8 @@ def reference_arm(args, rank, world):
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "embeddings/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1000 * dt / args.steps, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "s8" if quant else "f32", "data": "synthetic",
+        "vs_baseline": None, "dtype": {"QUANT_NONE": "f32", "QUANT_WEIGHTS": "s8 weights x f32",
+                                       "QUANT_FULL": "u8 x s8"}[MODES[args.mode][1]], "data": "synthetic",
         "config": {"workload": args.workload, "global_batch": wl["nseq"], "seq_len": f"{wl['lo']}-{wl['hi']}",
                    "parallelism": "cpu threads", "mode": args.mode},
         "cpu_baseline": {"value": round(value, 3), "unit": "embeddings/s", "cores": nth, "kind": "port",
@@ -256,7 +267,7 @@ def ours(args, rank, world, local_rank):
     wl = WORKLOADS[args.workload]
     cfg = synth.preset(wl["preset"])
     weights = synth.make_weights(cfg, seed=0)
-    emb = Embedder(cfg, weights, devices=[local_rank], int8_activations=args.mode == "int8_full")
+    emb = Embedder(cfg, weights, devices=[local_rank], **MODES[args.mode][0])
     del weights
     _, ids, cu = make_inputs(wl, seed=1000 + rank)
     nseq, T = len(cu) - 1, int(cu[-1])
@@ -341,7 +352,8 @@ def ours(args, rank, world, local_rank):
         peak_note = f"2x {peak_src} sustained bf16 (dense int8 rate is 2x bf16 on B200)"
     else:
         peak = peaks["bf16_tflops_sustained"]
-        peak_note = f"{peak_src} sustained bf16 (kernel timed inside a long forward)"
+        peak_note = (f"{peak_src} sustained bf16 (kernel timed inside a long forward; fp16 and bf16 share "
+                     f"the kind::f16 tensor rate)")
     gemm_avg_ms = g["ms"] / max(g["launches"], 1)
     achieved = (g["flops"] / max(g["launches"], 1)) / (gemm_avg_ms / 1000.0) / 1e12
     traffic = committed_traffic(args.workload, args.mode)
@@ -364,7 +376,7 @@ def ours(args, rank, world, local_rank):
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "embeddings/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "s8" if args.mode == "int8_full" else "bf16",
+        "scaling": "weak", "vs_baseline": None, "dtype": MODES[args.mode][2],
         "data": "synthetic (seeded random-init weights N(0,0.02) of the named architecture; seeded token ids)",
         "config": {"workload": args.workload, "global_batch": world * nseq, "per_gpu_batch": nseq,
                    "seq_len": f"{wl['lo']}-{wl['hi']}", "tokens_per_gpu_step": T, "parallelism": f"dp{world}",

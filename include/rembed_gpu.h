@@ -39,11 +39,14 @@ enum {
 /* Pooling (Config.Pooling, bert.go:670-679). */
 enum { RG_POOL_MEAN = 0, RG_POOL_CLS = 1, RG_POOL_LASTTOKEN = 2 };
 /* Numeric modes.  RG_MODE_BF16: bf16 tensor-core GEMMs, fp32 accumulate,
- * fp32 residual stream (replaces the reference's fp32 path).
- * RG_MODE_INT8_W: weight-only int8, the PackB8 quantiser (WithInt8,
- * rembed.go:67-69).  RG_MODE_INT8_FULL: int8 weights and per-row int8
- * activations, the PackB8VNNI scheme (WithInt8Activations, rembed.go:79-81). */
-enum { RG_MODE_BF16 = 0, RG_MODE_INT8_W = 2, RG_MODE_INT8_FULL = 3 };
+ * fp32 residual stream (replaces the reference's fp32 path).  RG_MODE_F16:
+ * the same with fp16 operands (8x finer rounding; weights must fit the fp16
+ * range).  RG_MODE_INT8_W: weight-only int8, the PackB8 quantiser
+ * (WithInt8, rembed.go:67-69): int8 weights in HBM, widened to fp16 inside
+ * the GEMM mainloop, fp16 activations.  RG_MODE_INT8_FULL: int8 weights and
+ * per-row int8 activations, the PackB8VNNI scheme (WithInt8Activations,
+ * rembed.go:79-81). */
+enum { RG_MODE_BF16 = 0, RG_MODE_F16 = 1, RG_MODE_INT8_W = 2, RG_MODE_INT8_FULL = 3 };
 /* Host dtypes accepted by rg_upload_weight (safetensors.go:188-209). */
 enum { RG_DTYPE_F32 = 0, RG_DTYPE_F16 = 1, RG_DTYPE_BF16 = 2 };
 /* rg_forward output kinds: pooled (Embed) or per-token hidden states

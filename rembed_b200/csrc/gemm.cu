@@ -1,450 +1,17 @@
-// gemm.cu - persistent warp-specialised tcgen05 GEMM for sm_100a on CTA
-// pairs (clusters of 2, tcgen05 cta_group::2).
-//
-// Each CTA pair walks output tiles of 256 x BN in m-major order (pairs in
-// flight share A row-blocks through L2).  The pair MMA reads 128 rows of A
-// and BN/2 rows of W from each CTA's shared memory and writes each CTA's
-// 128 output rows into that CTA's TMEM, so per SM a k-block moves half the
-// W bytes a single-CTA 128 x BN tile would.  Roles in every CTA:
-//   warp 0      TMA producer: its CTA's A and W k-blocks (128 bytes of K per
-//               row, 128-byte swizzle) into a STAGES-deep ring; both CTAs'
-//               loads complete on the even CTA's barrier;
-//   warp 1      (even CTA only) pair MMA issuer: 4 tcgen05.mma per k-block
-//               into one of two TMEM accumulators, commits that free the
-//               stage in both CTAs and publish finished accumulators;
-//   warp 2      TMEM allocator (pair allocation);
-//   warps 4-11  epilogue: tcgen05.ld 32 columns at a time (thread = row),
-//               dequant scales, bias, GELU or + residual (TMA-loaded) in
-//               registers, the row into a swizzled staging box, one TMA
-//               store per 32 x 32 box; then release the accumulator to the
-//               even CTA so the next tile's MMAs overlap this epilogue.
-// All waits are bounded (sm100.cuh); on a timeout every role stops, the
-// loads and MMAs in flight are drained, and the pair's TMEM is freed before
-// the CTAs exit with kStatusWaitTimeout raised.
-#include <cuda_bf16.h>
+// gemm.cu - host side of the tcgen05 GEMM: tensor maps, tile-width choice
+// and the launch switch over operand kinds (kernel in gemm_impl.cuh, one
+// translation unit per kind).
+#include <cuda.h>
+#include <cuda_runtime.h>
 
 #include "gemm.cuh"
-#include "sm100.cuh"
 
 namespace rg {
 
-__device__ __forceinline__ float ex2_approx(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
-// HF "gelu", 0.5 x (1 + erf(x / sqrt(2))), with erf by Abramowitz & Stegun
-// 7.1.26 (absolute error <= 1.5e-7), the published method the reference's
-// geluScalar uses (tensor.go:499-538); exp(-a^2) through ex2.approx.
-__device__ __forceinline__ float gelu_as(float x) {
-    const float a = fabsf(x) * 0.70710678118654752f;
-    const float t = __fdividef(1.0f, fmaf(0.3275911f, a, 1.0f));
-    float p = fmaf(t, 1.061405429f, -1.453152027f);
-    p = fmaf(p, t, 1.421413741f);
-    p = fmaf(p, t, -0.284496736f);
-    p = fmaf(p, t, 0.254829592f);
-    p *= t;
-    const float e = ex2_approx(-(a * a) * 1.4426950408889634f);
-    const float erf_abs = fmaf(-p, e, 1.0f);
-    const float hx = 0.5f * x;
-    return fmaf(hx, copysignf(erf_abs, x), hx);
-}
-
-// SiLU x * sigmoid(x) (tensor.go:477-481 computes it through a float64 exp).
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
-// tanh-approximation GELU (tensor.go:490-497; HF gelu_pytorch_tanh).
-__device__ __forceinline__ float gelu_tanh_f(float x) {
-    const float inner = 0.7978845608028654f * (x + 0.044715f * x * x * x);
-    return 0.5f * x * (1.0f + tanhf(inner));
-}
-
-constexpr int kEpiWarps = 8;        // two epilogue warps per SM sub-partition
-constexpr int kThreads = 128 + 32 * kEpiWarps;
-constexpr int kChunk = 32;          // accumulator columns per TMEM load / TMA store box
-constexpr int kStageBytes = 4096;   // one 32 x 32 fp32 (or 32 x 32 bf16, half used) staging box
-
-// Per-CTA shapes of the pair kernel: the tile is 256 x BN, each CTA of the
-// pair holds 128 rows of A and BN/2 rows of W per 128-byte k-block.
-template <int BN>
-struct GemmShape {
-    static constexpr int A_BYTES = 128 * 128;
-    static constexpr int B_BYTES = (BN / 2) * 128;
-    static constexpr int STAGES = BN == 128 ? 6 : 5;
-    static constexpr uint32_t TMEM_COLS = BN == 128 ? 256 : 512;  // 2 accumulators, power of two
-    // mainloop ring + two staging boxes per epilogue warp + barriers
-    static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + kEpiWarps * 2 * kStageBytes + 1024 + 512;
-};
-
-// Byte offset of 16-byte chunk c of row r in a staging box whose rows are
-// row_bytes long, laid out as the TMA swizzle of the store/load map expects
-// (128-byte swizzle for fp32 rows, 64-byte swizzle for bf16 rows): chunk bits
-// [4,7) are XORed with bits [7,10) of the unswizzled offset.
-__device__ __forceinline__ uint32_t swz(int r, int c, int row_bytes) {
-    const uint32_t off = static_cast<uint32_t>(r * row_bytes + c * 16);
-    const uint32_t mask = row_bytes == 128 ? 7u : 3u;
-    return off ^ (((off >> 7) & mask) << 4);
-}
-
-template <int BN, bool S8, int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes, GemmArgs args) {
-    using S = GemmShape<BN>;
-    constexpr int STAGES = S::STAGES;
-    constexpr int A_BYTES = S::A_BYTES, B_BYTES = S::B_BYTES;
-    constexpr int K_ELEMS = S8 ? 128 : 64;  // elements per 128-byte k-block
-    constexpr int HALF = BN / 2;            // W rows per CTA; accumulator columns per epilogue warp
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sA = smem;
-    uint8_t* sB = smem + STAGES * A_BYTES;
-    uint8_t* stage_base = sB + STAGES * B_BYTES;  // 1024-byte aligned
-    uint64_t* full = reinterpret_cast<uint64_t*>(stage_base + kEpiWarps * 2 * kStageBytes);
-    uint64_t* empty = full + STAGES;
-    uint64_t* tfull = empty + STAGES;
-    uint64_t* tempty = tfull + 2;
-    uint64_t* resbar = tempty + 2;  // [kEpiWarps][2]: residual box landed
-    uint64_t* drain = resbar + 2 * kEpiWarps;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t rank = cluster_ctarank();  // 0: the CTA that issues the pair MMAs
-    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-    const int m_tiles = (args.M + 255) / 256;
-    const int n_tiles = args.N / BN;
-    const int num_tiles = m_tiles * n_tiles;
-    const int kblocks = args.K / K_ELEMS;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
-        }
-        for (int a = 0; a < 2; ++a) {
-            mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 2 * kEpiWarps);  // one arrival per epilogue warp of both CTAs
-        }
-        for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&resbar[i], 1);
-        mbar_init(drain, 1);
-        *abort_flag = 0;
-        fence_mbar_init();
-        tma_prefetch_desc(&tmA);
-        tma_prefetch_desc(&tmB);
-        tma_prefetch_desc(&tmOut);
-        if (EPI == kEpiBiasRes) tma_prefetch_desc(&tmRes);
-    }
-    if (warp == 2) {
-        tmem_alloc_pair(tmem_slot, S::TMEM_COLS);
-        tmem_relinquish_pair();
-    }
-    tc_fence_before();
-    cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
-    tc_fence_after();
-    const uint32_t tmem_base = *tmem_slot;
-    // shared::cluster addresses of the even CTA's full / tempty barriers.
-    const uint32_t full_lead = mapa_shared(smem_u32(full), 0);
-    const uint32_t tempty_lead = mapa_shared(smem_u32(tempty), 0);
-
-    if (warp == 0 && lane == 0) {
-        // ---------------- TMA producer (both CTAs) ----------------
-        int stage = 0;
-        uint32_t phase = 0;
-        uint32_t issued_mask = 0, issued_parity = 0;
-        for (int tile = pair; tile < num_tiles; tile += npairs) {
-            const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
-            bool ok = true;
-            for (int kb = 0; kb < kblocks; ++kb) {
-                if (!mbar_wait(&empty[stage], phase ^ 1, args.status, abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                // Both CTAs' loads complete on the even CTA's barrier, which
-                // expects the bytes of both.
-                if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (A_BYTES + B_BYTES));
-                tma_load_2d_pair(sA + stage * A_BYTES, &tmA, full_lead + 8 * stage, kb * K_ELEMS,
-                                 m_blk * 256 + rank * 128);
-                tma_load_2d_pair(sB + stage * B_BYTES, &tmB, full_lead + 8 * stage, kb * K_ELEMS,
-                                 n_blk * BN + rank * HALF);
-                issued_mask |= 1u << stage;
-                issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-                if (++stage == STAGES) {
-                    stage = 0;
-                    phase ^= 1;
-                }
-            }
-            if (!ok) break;
-        }
-        // The even CTA sees every load of both CTAs land on its barriers.
-        if (rank == 0)
-            for (int s = 0; s < STAGES; ++s)
-                if (issued_mask & (1u << s)) mbar_drain(&full[s], (issued_parity >> s) & 1);
-    } else if (warp == 1 && lane == 0 && rank == 0) {
-        // ---------------- pair MMA issuer (even CTA) ----------------
-        constexpr uint32_t idesc = S8 ? idesc_s8(256, BN) : idesc_bf16(256, BN);
-        int stage = 0;
-        uint32_t phase = 0;
-        int acc = 0;
-        uint32_t acc_phase = 0;
-        bool issued = false;
-        for (int tile = pair; tile < num_tiles; tile += npairs) {
-            if (!mbar_wait(&tempty[acc], acc_phase ^ 1, args.status, abort_flag)) break;
-            tc_fence_after();
-            const uint32_t d = tmem_base + acc * BN;
-            bool ok = true;
-            for (int kb = 0; kb < kblocks; ++kb) {
-                if (!mbar_wait(&full[stage], phase, args.status, abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint64_t ad = sdesc_k128(smem_u32(sA + stage * A_BYTES));
-                const uint64_t bd = sdesc_k128(smem_u32(sB + stage * B_BYTES));
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    // 32 bytes of K per instruction: +2 in 16-byte units.
-                    if constexpr (S8)
-                        umma_s8_pair(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
-                    else
-                        umma_bf16_pair(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
-                }
-                issued = true;
-                // Free this stage in both CTAs once the MMAs have read it.
-                umma_commit_pair_mc(smem_u32(&empty[stage]), 0x3);
-                if (++stage == STAGES) {
-                    stage = 0;
-                    phase ^= 1;
-                }
-            }
-            if (!ok) break;
-            umma_commit_pair_mc(smem_u32(&tfull[acc]), 0x3);
-            if (++acc == 2) {
-                acc = 0;
-                acc_phase ^= 1;
-            }
-        }
-        if (issued) {
-            umma_commit_pair(smem_u32(drain));
-            mbar_drain(drain, 0);
-        }
-    } else if (warp >= 4) {
-        // ---------------- epilogue (both CTAs, own 128 rows) ----------------
-        // Warp (4 + 4h + q) owns TMEM lanes [32q, 32q + 32) (the lane quarter
-        // its sub-partition may access) = 32 output rows, and accumulator
-        // columns [h*HALF, (h+1)*HALF), processed 32 at a time: tcgen05.ld
-        // (thread = row), dequant / bias / GELU / + residual in registers,
-        // the row written into a swizzled staging box, one TMA store per box.
-        // The fp32 residual box arrives by TMA one chunk ahead.
-        constexpr bool F32OUT = EPI == kEpiBiasRes || EPI == kEpiBiasF32;
-        const int ew = warp - 4;
-        const int quarter = warp & 3;
-        const int half = ew >> 2;
-        uint8_t* boxes = stage_base + ew * 2 * kStageBytes;
-        uint64_t* rbar = resbar + 2 * ew;
-        uint32_t rphase = 0;   // bit b: parity of the next completion of rbar[b]
-        uint32_t rpending = 0; // bit b: a residual load into buffer b is in flight (lane 0's view)
-        int k = 0;             // running chunk counter of this warp: buffer k & 1
-        constexpr int CHUNKS = HALF / kChunk;
-        // Issue the residual box of chunk c of tile t into buffer b (lane 0).
-        auto load_residual = [&](int t, int c, int b) {
-            if constexpr (EPI == kEpiBiasRes) {
-                if (t >= num_tiles) return;
-                const int row0 = (t / n_tiles) * 256 + static_cast<int>(rank) * 128 + quarter * 32;
-                const int col0 = (t % n_tiles) * BN + half * HALF + c * kChunk;
-                mbar_arrive_expect_tx(&rbar[b], kStageBytes);
-                tma_load_2d(boxes + b * kStageBytes, &tmRes, &rbar[b], col0, row0);
-                rpending |= 1u << b;
-            }
-        };
-        if (lane == 0) load_residual(pair, 0, 0);
-        int acc = 0;
-        uint32_t acc_phase = 0;
-        bool ok = true;
-        for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-            const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
-            if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
-            tc_fence_after();
-            const int row0 = m_blk * 256 + static_cast<int>(rank) * 128 + quarter * 32;
-            float rs = 1.0f;
-            if constexpr (S8) {
-                if (args.row_scale && row0 + lane < args.M) rs = args.row_scale[row0 + lane];
-            }
-            const uint32_t taddr =
-                tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + half * HALF;
-            constexpr bool GLU = EPI >= kEpiGluSilu;
-            constexpr int STEP = GLU ? 2 : 1;  // accumulator chunks per output box
-#pragma unroll 1
-            for (int c = 0; c < CHUNKS; c += STEP, ++k) {
-                const int b = k & 1;
-                uint8_t* box = boxes + b * kStageBytes;
-                const int col0 = n_blk * BN + half * HALF + c * kChunk;  // accumulator column
-                const int ocol0 = GLU ? col0 / 2 : col0;                  // output column
-                if (lane == 0) {
-                    if constexpr (EPI == kEpiBiasRes) {
-                        // The other buffer's store (previous chunk) has read
-                        // its box: it can take the next chunk's residual.
-                        bulk_wait_read<0>();
-                        if (c + STEP < CHUNKS)
-                            load_residual(tile, c + STEP, b ^ 1);
-                        else
-                            load_residual(tile + npairs, 0, b ^ 1);
-                    } else {
-                        // This buffer's store (two chunks back) has read its box.
-                        bulk_wait_read<1>();
-                    }
-                }
-                __syncwarp();
-                uint32_t r[32];
-                tmem_ld32(taddr + c * kChunk, r);
-                tmem_ld_wait();
-                float v[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    if constexpr (S8)
-                        v[i] = static_cast<float>(static_cast<int32_t>(r[i])) * rs;
-                    else
-                        v[i] = __uint_as_float(r[i]);
-                }
-                if constexpr (GLU) {
-                    // a = chunk c (activated), b = chunk c + 1 (linear)
-                    uint32_t rb[32];
-                    tmem_ld32(taddr + (c + 1) * kChunk, rb);
-                    tmem_ld_wait();
-                    float w[32];
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        if constexpr (S8)
-                            w[i] = static_cast<float>(static_cast<int32_t>(rb[i])) * rs;
-                        else
-                            w[i] = __uint_as_float(rb[i]);
-                    }
-                    if (S8 && args.col_scale) {
-                        const float4* ca = reinterpret_cast<const float4*>(args.col_scale + col0);
-                        const float4* cb = reinterpret_cast<const float4*>(args.col_scale + col0 + kChunk);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const float4 qa = __ldg(ca + i), qb = __ldg(cb + i);
-                            v[4 * i] *= qa.x;
-                            v[4 * i + 1] *= qa.y;
-                            v[4 * i + 2] *= qa.z;
-                            v[4 * i + 3] *= qa.w;
-                            w[4 * i] *= qb.x;
-                            w[4 * i + 1] *= qb.y;
-                            w[4 * i + 2] *= qb.z;
-                            w[4 * i + 3] *= qb.w;
-                        }
-                    }
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        float a = v[i];
-                        if constexpr (EPI == kEpiGluSilu) a = silu_f(a);
-                        else if constexpr (EPI == kEpiGluGeluErf) a = gelu_as(a);
-                        else a = gelu_tanh_f(a);
-                        v[i] = a * w[i];
-                    }
-                }
-                // (acc * row scale) * column scale + bias: the reference's
-                // dequant-then-AddBias order (pack_vnni.go:155-173, bert.go:297-300)
-                if (!GLU && S8 && args.col_scale) {
-                    const float4* cs = reinterpret_cast<const float4*>(args.col_scale + col0);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const float4 q = __ldg(cs + i);
-                        v[4 * i] *= q.x;
-                        v[4 * i + 1] *= q.y;
-                        v[4 * i + 2] *= q.z;
-                        v[4 * i + 3] *= q.w;
-                    }
-                }
-                if (!GLU && args.bias) {
-                    const float4* bp = reinterpret_cast<const float4*>(args.bias + col0);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const float4 q = __ldg(bp + i);
-                        v[4 * i] += q.x;
-                        v[4 * i + 1] += q.y;
-                        v[4 * i + 2] += q.z;
-                        v[4 * i + 3] += q.w;
-                    }
-                }
-                if constexpr (EPI == kEpiBiasGelu) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = gelu_as(v[i]);
-                }
-                if constexpr (EPI == kEpiBiasRes) {
-                    if (!mbar_wait(&rbar[b], (rphase >> b) & 1, args.status, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    rphase ^= 1u << b;
-                    rpending &= ~(1u << b);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const float4 x = *reinterpret_cast<const float4*>(box + swz(lane, i, 128));
-                        v[4 * i] = x.x + v[4 * i];
-                        v[4 * i + 1] = x.y + v[4 * i + 1];
-                        v[4 * i + 2] = x.z + v[4 * i + 2];
-                        v[4 * i + 3] = x.w + v[4 * i + 3];
-                    }
-                }
-                if constexpr (F32OUT) {
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        *reinterpret_cast<float4*>(box + swz(lane, i, 128)) =
-                            make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        uint32_t w[4];
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            __nv_bfloat162 p = __floats2bfloat162_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
-                            w[j] = *reinterpret_cast<uint32_t*>(&p);
-                        }
-                        *reinterpret_cast<uint4*>(box + swz(lane, i, 64)) = make_uint4(w[0], w[1], w[2], w[3]);
-                    }
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    tma_store_2d(&tmOut, box, ocol0, row0);
-                    bulk_commit();
-                }
-            }
-            if (!ok) break;
-            // This warp is done with the accumulator: tell the even CTA.
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(tempty_lead + 8 * acc);
-            if (++acc == 2) {
-                acc = 0;
-                acc_phase ^= 1;
-            }
-        }
-        // Every store has read its staging box, and every residual box
-        // requested has landed, before the CTA may exit.
-        if (lane == 0) {
-            bulk_wait_read<0>();
-            for (int b = 0; b < 2; ++b)
-                if (rpending & (1u << b)) mbar_drain(&rbar[b], (rphase >> b) & 1);
-        }
-        __syncwarp();
-    }
-
-    // Teardown: every MMA has completed (the issuer drained them) and every
-    // TMEM read of both CTAs is done before the pair frees its TMEM.
-    __syncwarp();
-    tc_fence_before();
-    cluster_sync();
-    if (warp == 2) {
-        tc_fence_after();
-        tmem_dealloc_pair(tmem_base, S::TMEM_COLS);
-    }
-}
-
-// ---------------------------------------------------------------------------
-// Host side.
+template <int KIND>
+cudaError_t dispatch_kind(int block_n, int epi, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                          const CUtensorMap& tmOut, const CUtensorMap& tmRes, const GemmArgs& args, int num_sms,
+                          cudaStream_t stream);
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -478,69 +45,24 @@ bool make_kmajor_tmap(CUtensorMap* map, const void* base, int elem_bytes, uint64
     return r == CUDA_SUCCESS;
 }
 
-template <int BN, bool S8, int EPI>
-static cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmOut,
-                              const CUtensorMap& tmRes, const GemmArgs& args, int num_sms, cudaStream_t stream) {
-    constexpr int smem = GemmShape<BN>::SMEM;
-    static_assert(smem <= 232448, "shared memory budget");
-    auto kern = gemm_kernel<BN, S8, EPI>;
-    // The shared-memory opt-in is a per-device function attribute.
-    static unsigned configured = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 32 || !(__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & (1u << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        if (dev < 32) __atomic_fetch_or(&configured, 1u << dev, __ATOMIC_RELEASE);
-    }
-    // One CTA pair per tile slot: as many pairs as can be co-resident.
-    static int max_pairs[32] = {};
-    int pairs = dev < 32 ? __atomic_load_n(&max_pairs[dev], __ATOMIC_ACQUIRE) : 0;
-    if (pairs == 0) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
-        cfg.blockDim = dim3(kThreads, 1, 1);
-        cfg.dynamicSmemBytes = smem;
-        cudaLaunchAttribute attr;
-        attr.id = cudaLaunchAttributeClusterDimension;
-        attr.val.clusterDim.x = 2;
-        attr.val.clusterDim.y = 1;
-        attr.val.clusterDim.z = 1;
-        cfg.attrs = &attr;
-        cfg.numAttrs = 1;
-        int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
-            cudaGetLastError();
-            n = num_sms / 2;
-        }
-        pairs = n;
-        if (dev < 32) __atomic_store_n(&max_pairs[dev], pairs, __ATOMIC_RELEASE);
-    }
-    const int tiles = ((args.M + 255) / 256) * (args.N / BN);
-    const int grid = 2 * (tiles < pairs ? tiles : pairs);
-    kern<<<grid, kThreads, smem, stream>>>(tmA, tmB, tmOut, tmRes, args);
-    return cudaGetLastError();
-}
-
-template <int BN, bool S8>
-static cudaError_t dispatch_epi(int epi, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmOut,
-                                const CUtensorMap& tmRes, const GemmArgs& args, int num_sms, cudaStream_t stream) {
-    switch (epi) {
-    case kEpiBias: return launch_one<BN, S8, kEpiBias>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case kEpiBiasGelu: return launch_one<BN, S8, kEpiBiasGelu>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case kEpiBiasRes: return launch_one<BN, S8, kEpiBiasRes>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case kEpiBiasF32: return launch_one<BN, S8, kEpiBiasF32>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case kEpiGluSilu: return launch_one<BN, S8, kEpiGluSilu>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case kEpiGluGeluErf: return launch_one<BN, S8, kEpiGluGeluErf>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case kEpiGluGeluTanh: return launch_one<BN, S8, kEpiGluGeluTanh>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    default: return cudaErrorInvalidValue;
-    }
+bool make_w8_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) != 0 || cols % 16 != 0) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
 }
 
 // Output / residual maps: 32 x 32 boxes, rows of 128 bytes (fp32, 128-byte
-// swizzle) or 64 bytes (bf16, 64-byte swizzle), matching swz() above.
-static bool make_epilogue_tmap(CUtensorMap* map, const void* base, bool f32, uint64_t rows, uint64_t cols,
-                               uint64_t ld) {
+// swizzle) or 64 bytes (16-bit, 64-byte swizzle), matching the kernel's
+// staging-box layout (swz in gemm_impl.cuh).
+static bool make_epilogue_tmap(CUtensorMap* map, const void* base, bool f32, bool f16, uint64_t rows,
+                               uint64_t cols, uint64_t ld) {
     EncodeTiledFn fn = encode_fn();
     if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
     const uint64_t eb = f32 ? 4 : 2;
@@ -549,7 +71,9 @@ static bool make_epilogue_tmap(CUtensorMap* map, const void* base, bool f32, uin
     cuuint64_t strides[1] = {ld * eb};
     cuuint32_t box[2] = {32, 32};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+    const CUtensorMapDataType dt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : (f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+    CUresult r = fn(map, dt, 2,
                     const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -582,27 +106,25 @@ cudaError_t gemm_launch(GemmKind kind, int epi, int block_n, const CUtensorMap& 
     if (args.M <= 0) return cudaSuccess;
     const int kel = kind == GemmKind::kS8 ? 128 : 64;
     if (args.K % kel != 0 || args.K <= 0 || block_n <= 0 || args.N % block_n != 0) return cudaErrorInvalidValue;
-    const bool s8 = kind == GemmKind::kS8;
     const bool f32out = epi == kEpiBiasRes || epi == kEpiBiasF32;
+    const bool f16out = kind == GemmKind::kF16 || kind == GemmKind::kW8;
     const bool glu = epi_is_glu(epi);
     // GLU tiles pair 32-column chunks inside each epilogue warp's columns.
     if (glu && (block_n == 192 || args.N % 64 != 0)) return cudaErrorInvalidValue;
     CUtensorMap tmOut, tmRes;
-    if (!make_epilogue_tmap(&tmOut, args.out, f32out, args.M, glu ? args.N / 2 : args.N, args.ld_out))
+    if (!make_epilogue_tmap(&tmOut, args.out, f32out, f16out, args.M, glu ? args.N / 2 : args.N, args.ld_out))
         return cudaErrorInvalidValue;
     if (epi == kEpiBiasRes) {
-        if (!args.residual || !make_epilogue_tmap(&tmRes, args.residual, true, args.M, args.N, args.N))
+        if (!args.residual || !make_epilogue_tmap(&tmRes, args.residual, true, false, args.M, args.N, args.N))
             return cudaErrorInvalidValue;
     } else {
         tmRes = tmOut;  // unused
     }
-    switch (block_n) {
-    case 256: return s8 ? dispatch_epi<256, true>(epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream)
-                        : dispatch_epi<256, false>(epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case 192: return s8 ? dispatch_epi<192, true>(epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream)
-                        : dispatch_epi<192, false>(epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case 128: return s8 ? dispatch_epi<128, true>(epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream)
-                        : dispatch_epi<128, false>(epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream);
+    switch (kind) {
+    case GemmKind::kBF16: return dispatch_kind<0>(block_n, epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream);
+    case GemmKind::kS8: return dispatch_kind<1>(block_n, epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream);
+    case GemmKind::kF16: return dispatch_kind<2>(block_n, epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream);
+    case GemmKind::kW8: return dispatch_kind<3>(block_n, epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -28,19 +28,27 @@ struct GemmArgs {
     const float* col_scale;  // [N] or nullptr: int8 weight dequant scale
     const float* row_scale;  // [M] or nullptr: int8 activation dequant scale
     const float* residual;   // [M x N] fp32, kEpiBiasRes only
-    void* out;               // [M x ld_out], bf16 or fp32
+    void* out;               // [M x ld_out], 16-bit (bf16 / fp16 by kind) or fp32
     int ld_out;
     int* status;             // device status word
 };
 
 // Operand element kind of the GEMM.
-enum class GemmKind : int { kBF16 = 0, kS8 = 1 };
+//   kBF16: bf16 A and W, bf16 output.
+//   kS8:   int8 A (row scales) and int8 W (column scales), bf16 output.
+//   kF16:  fp16 A and W, fp16 output.
+//   kW8:   fp16 A, int8 W (column scales) widened to fp16 in shared memory
+//          inside the mainloop, fp16 output.
+enum class GemmKind : int { kBF16 = 0, kS8 = 1, kF16 = 2, kW8 = 3 };
 
 // Encode a 2-D K-major tensor map over a row-major [rows x cols] matrix
 // (cols contiguous) with a (128-byte x box_rows) box and 128-byte swizzle.
 // elem_bytes: 2 (bf16) or 1 (int8).  Returns false on failure.
 bool make_kmajor_tmap(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols,
                       uint64_t row_stride_elems, uint32_t box_rows);
+// Tensor map over an int8 weight [rows x cols] for GemmKind::kW8: boxes of
+// 64 bytes of K x box_rows, unswizzled.
+bool make_w8_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
 
 // Output tile width (128, 192 or 256 columns) for an M x N GEMM on num_sms
 // SMs: the width dividing N with the least wave-quantised cost; 0 if none
@@ -53,8 +61,8 @@ inline int gemm_w_box_rows(int block_n) { return block_n / 2; }
 
 // Launch the GEMM with tiles of 256 x block_n on CTA pairs.  tmA covers A
 // [M x K] with box rows 128; tmB covers W [N x K] with box rows
-// gemm_w_box_rows(block_n).  Requires K % (128 / elem_bytes) == 0 and
-// N % block_n == 0.
+// gemm_w_box_rows(block_n) (make_w8_tmap for kW8).  Requires K a multiple of
+// 64 (128 for kS8) and N % block_n == 0.
 cudaError_t gemm_launch(GemmKind kind, int epi, int block_n, const CUtensorMap& tmA, const CUtensorMap& tmB,
                         const GemmArgs& args, int num_sms, cudaStream_t stream);
 

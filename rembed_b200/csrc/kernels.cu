@@ -9,6 +9,7 @@
 #include <stdint.h>
 
 #include "kernels.cuh"
+#include "act16.cuh"
 #include "sm100.cuh"
 
 namespace rg {
@@ -33,10 +34,10 @@ __device__ __forceinline__ float warp_max(float v) {
 // then write any of:
 // fp32 row, bf16 row, int8 row + scale (QuantizeRowU8 without the +128
 // offset, pack_vnni.go:85-117).
-template <int NV, bool RMS>
-__device__ __forceinline__ void norm_finish(float (&v)[NV][4], const float* g, const float* b, float eps, int H,
-                                            float* out32, __nv_bfloat16* outb, int8_t* outq, float* outqs,
-                                            int lane) {
+// Returns true (in every lane) if an fp16 output overflowed or was NaN.
+template <int NV, bool RMS, bool F16>
+__device__ __forceinline__ bool norm_finish(float (&v)[NV][4], const float* g, const float* b, float eps, int H,
+                                            float* out32, uint16_t* outb, int8_t* outq, float* outqs, int lane) {
     float mean = 0.f, inv = 1.f;
     if (!g) {
         // identity (ModernBERT's layer-0 attention norm): only the stores
@@ -81,14 +82,9 @@ __device__ __forceinline__ void norm_finish(float (&v)[NV][4], const float* g, c
             v[c][3] = (v[c][3] - mean) * inv * gg.w + bb.w;
         }
         if (out32) reinterpret_cast<float4*>(out32 + j)[0] = make_float4(v[c][0], v[c][1], v[c][2], v[c][3]);
-        if (outb) {
-            __nv_bfloat162 lo = __floats2bfloat162_rn(v[c][0], v[c][1]);
-            __nv_bfloat162 hi = __floats2bfloat162_rn(v[c][2], v[c][3]);
-            uint2 pk;
-            pk.x = *reinterpret_cast<uint32_t*>(&lo);
-            pk.y = *reinterpret_cast<uint32_t*>(&hi);
-            reinterpret_cast<uint2*>(outb + j)[0] = pk;
-        }
+        if (outb)
+            reinterpret_cast<uint2*>(outb + j)[0] =
+                make_uint2(pack2<F16>(v[c][0], v[c][1]), pack2<F16>(v[c][2], v[c][3]));
         amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[c][0]), fabsf(v[c][1])), fmaxf(fabsf(v[c][2]), fabsf(v[c][3]))));
     }
     if (outq) {
@@ -108,23 +104,24 @@ __device__ __forceinline__ void norm_finish(float (&v)[NV][4], const float* g, c
         }
         if (lane == 0) *outqs = scale;
     }
+    if constexpr (F16) return outb && __any_sync(0xffffffffu, !(amax <= 65504.0f));
+    return false;
 }
 
-template <int NV>
-__device__ __forceinline__ void store_row(const float (&v)[NV][4], float* out32, __nv_bfloat16* outb, int lane) {
+template <int NV, bool F16>
+__device__ __forceinline__ bool store_row(const float (&v)[NV][4], float* out32, uint16_t* outb, int lane) {
+    float amax = 0.f;
 #pragma unroll
     for (int c = 0; c < NV; ++c) {
         const int j = (lane + 32 * c) * 4;
         if (out32) reinterpret_cast<float4*>(out32 + j)[0] = make_float4(v[c][0], v[c][1], v[c][2], v[c][3]);
-        if (outb) {
-            __nv_bfloat162 lo = __floats2bfloat162_rn(v[c][0], v[c][1]);
-            __nv_bfloat162 hi = __floats2bfloat162_rn(v[c][2], v[c][3]);
-            uint2 pk;
-            pk.x = *reinterpret_cast<uint32_t*>(&lo);
-            pk.y = *reinterpret_cast<uint32_t*>(&hi);
-            reinterpret_cast<uint2*>(outb + j)[0] = pk;
-        }
+        if (outb)
+            reinterpret_cast<uint2*>(outb + j)[0] =
+                make_uint2(pack2<F16>(v[c][0], v[c][1]), pack2<F16>(v[c][2], v[c][3]));
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[c][0]), fabsf(v[c][1])), fmaxf(fabsf(v[c][2]), fabsf(v[c][3]))));
     }
+    if constexpr (F16) return outb && __any_sync(0xffffffffu, !(amax <= 65504.0f));
+    return false;
 }
 
 __device__ __forceinline__ int seq_of_token(const int32_t* __restrict__ cu, int nseq, int t) {
@@ -137,7 +134,7 @@ __device__ __forceinline__ int seq_of_token(const int32_t* __restrict__ cu, int 
     return lo;
 }
 
-template <int NV>
+template <int NV, bool F16>
 __global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -187,15 +184,18 @@ __global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
         if (bad) v[c][0] = v[c][1] = v[c][2] = v[c][3] = 0.f;
     }
     float* x32 = p.x32 + static_cast<int64_t>(t) * H;
-    __nv_bfloat16* xb = p.xb ? p.xb + static_cast<int64_t>(t) * H : nullptr;
+    uint16_t* xb = p.xb ? p.xb + static_cast<int64_t>(t) * H : nullptr;
+    bool overflow;
     if (p.g)
-        norm_finish<NV, false>(v, p.g, p.b, p.eps, H, x32, xb, p.xq ? p.xq + static_cast<int64_t>(t) * H : nullptr,
-                               p.xq_scale ? p.xq_scale + t : nullptr, lane);
+        overflow = norm_finish<NV, false, F16>(v, p.g, p.b, p.eps, H, x32, xb,
+                                               p.xq ? p.xq + static_cast<int64_t>(t) * H : nullptr,
+                                               p.xq_scale ? p.xq_scale + t : nullptr, lane);
     else
-        store_row<NV>(v, x32, xb, lane);
+        overflow = store_row<NV, F16>(v, x32, xb, lane);
+    if (overflow && lane == 0) atomicOr(p.status, kStatusF16Overflow);
 }
 
-template <int NV, bool RMS>
+template <int NV, bool RMS, bool F16>
 __global__ void __launch_bounds__(256) norm_kernel(NormParams p) {
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -210,8 +210,9 @@ __global__ void __launch_bounds__(256) norm_kernel(NormParams p) {
         v[c][2] = a.z;
         v[c][3] = a.w;
     }
-    norm_finish<NV, RMS>(v, p.g, p.b, p.eps, p.H, p.out32 ? p.out32 + off : nullptr, p.outb ? p.outb + off : nullptr,
+    const bool overflow = norm_finish<NV, RMS, F16>(v, p.g, p.b, p.eps, p.H, p.out32 ? p.out32 + off : nullptr, p.outb ? p.outb + off : nullptr,
                          p.outq ? p.outq + off : nullptr, p.outqs ? p.outqs + t : nullptr, lane);
+    if (overflow && p.status && lane == 0) atomicOr(p.status, kStatusF16Overflow);
 }
 
 // x32 += RMSNorm(o32; g): Gemma's post-attention / post-FFN norm of the
@@ -266,7 +267,11 @@ cudaError_t launch_embed(const EmbedParams& p, cudaStream_t st) {
     if (p.T <= 0) return cudaSuccess;
     if (p.H % 128 != 0) return cudaErrorInvalidValue;
     const int grid = (p.T + 7) / 8;
-    RG_NV_DISPATCH(p.H, (embed_kernel<NV><<<grid, 256, 0, st>>>(p)));
+    if (p.f16) {
+        RG_NV_DISPATCH(p.H, (embed_kernel<NV, true><<<grid, 256, 0, st>>>(p)));
+    } else {
+        RG_NV_DISPATCH(p.H, (embed_kernel<NV, false><<<grid, 256, 0, st>>>(p)));
+    }
     return cudaGetLastError();
 }
 
@@ -274,17 +279,23 @@ cudaError_t launch_norm(const NormParams& p, bool rms, cudaStream_t st) {
     if (p.T <= 0) return cudaSuccess;
     if (p.H % 128 != 0) return cudaErrorInvalidValue;
     const int grid = (p.T + 7) / 8;
-    if (rms) {
-        RG_NV_DISPATCH(p.H, (norm_kernel<NV, true><<<grid, 256, 0, st>>>(p)));
+    if (rms && p.f16) {
+        RG_NV_DISPATCH(p.H, (norm_kernel<NV, true, true><<<grid, 256, 0, st>>>(p)));
+    } else if (rms) {
+        RG_NV_DISPATCH(p.H, (norm_kernel<NV, true, false><<<grid, 256, 0, st>>>(p)));
+    } else if (p.f16) {
+        RG_NV_DISPATCH(p.H, (norm_kernel<NV, false, true><<<grid, 256, 0, st>>>(p)));
     } else {
-        RG_NV_DISPATCH(p.H, (norm_kernel<NV, false><<<grid, 256, 0, st>>>(p)));
+        RG_NV_DISPATCH(p.H, (norm_kernel<NV, false, false><<<grid, 256, 0, st>>>(p)));
     }
     return cudaGetLastError();
 }
 
 cudaError_t launch_ln(const float* y32, const float* g, const float* b, float eps, int T, int H, float* x32,
-                      __nv_bfloat16* xb, int8_t* xq, float* xq_scale, cudaStream_t st) {
+                      uint16_t* xb, bool f16, int8_t* xq, float* xq_scale, cudaStream_t st, int* status) {
     NormParams p{};
+    p.f16 = f16;
+    p.status = status;
     p.in = y32;
     p.g = g;
     p.b = b;
@@ -313,7 +324,7 @@ cudaError_t launch_add_rmsnorm(float* x32, const float* o32, const float* g, flo
 // the q or k gain (qwen3.go:485-508, gemma3.go:303-330), then the rotation
 // at the token's position in its sequence (modernbert.go:125-143: products
 // rounded before the add/sub).
-template <int DH>
+template <int DH, bool F16>
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkRopeParams p) {
     constexpr int E = DH / 32, HALF = DH / 2;
     const int lane = threadIdx.x & 31;
@@ -322,10 +333,10 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkRopeParams p) {
     if (item >= p.T * heads) return;
     const int t = item / heads, h = item % heads;
     const bool is_q = h < p.nq;
-    __nv_bfloat16* row = p.qkv + static_cast<int64_t>(t) * p.ld + (is_q ? h * DH : p.nq * DH + (h - p.nq) * DH);
+    uint16_t* row = p.qkv + static_cast<int64_t>(t) * p.ld + (is_q ? h * DH : p.nq * DH + (h - p.nq) * DH);
     float v[E];
 #pragma unroll
-    for (int k = 0; k < E; ++k) v[k] = __bfloat162float(row[lane + 32 * k]);
+    for (int k = 0; k < E; ++k) v[k] = to_f32<F16>(row[lane + 32 * k]);
     const float* g = is_q ? p.q_norm : p.k_norm;
     if (g) {
         float q = 0.f;
@@ -349,8 +360,15 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkRopeParams p) {
             v[k + E / 2] = __fadd_rn(__fmul_rn(x2, cc), __fmul_rn(x1, ss));
         }
     }
+    float amax = 0.f;
 #pragma unroll
-    for (int k = 0; k < E; ++k) row[lane + 32 * k] = __float2bfloat16(v[k]);
+    for (int k = 0; k < E; ++k) {
+        row[lane + 32 * k] = from_f32<F16>(v[k]);
+        amax = fmaxf(amax, fabsf(v[k]));
+    }
+    if constexpr (F16)
+        if (__any_sync(0xffffffffu, !(amax <= 65504.0f)) && lane == 0 && p.status)
+            atomicOr(p.status, kStatusF16Overflow);
 }
 
 cudaError_t launch_qk_norm_rope(const QkRopeParams& p, int head_dim, cudaStream_t st) {
@@ -358,9 +376,18 @@ cudaError_t launch_qk_norm_rope(const QkRopeParams& p, int head_dim, cudaStream_
     const long items = static_cast<long>(p.T) * (p.nq + p.nkv);
     const int grid = static_cast<int>((items + 7) / 8);
     switch (head_dim) {
-    case 64: qk_norm_rope_kernel<64><<<grid, 256, 0, st>>>(p); break;
-    case 128: qk_norm_rope_kernel<128><<<grid, 256, 0, st>>>(p); break;
-    case 256: qk_norm_rope_kernel<256><<<grid, 256, 0, st>>>(p); break;
+    case 64:
+        if (p.f16) qk_norm_rope_kernel<64, true><<<grid, 256, 0, st>>>(p);
+        else qk_norm_rope_kernel<64, false><<<grid, 256, 0, st>>>(p);
+        break;
+    case 128:
+        if (p.f16) qk_norm_rope_kernel<128, true><<<grid, 256, 0, st>>>(p);
+        else qk_norm_rope_kernel<128, false><<<grid, 256, 0, st>>>(p);
+        break;
+    case 256:
+        if (p.f16) qk_norm_rope_kernel<256, true><<<grid, 256, 0, st>>>(p);
+        else qk_norm_rope_kernel<256, false><<<grid, 256, 0, st>>>(p);
+        break;
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
@@ -455,12 +482,20 @@ cudaError_t launch_quantize_rows(const __nv_bfloat16* x, int T, int K, int8_t* q
 // key/value tiles of 64 rows; S = Q K^T and O += P V on bf16 mma.sync with
 // fp32 accumulators; online softmax in the exp2 domain.  Rows of the
 // shared tiles are padded by 16 bytes so ldmatrix is conflict-free.
-__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+template <bool F16>
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    if constexpr (F16)
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -479,20 +514,15 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool vali
 __device__ __forceinline__ void cp_async_commit_wait() {
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-    __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&p);
-}
-
 template <int D, int ROWS>
-__device__ __forceinline__ void load_tile(__nv_bfloat16* s, const __nv_bfloat16* g, int r0, int L, int ld) {
+__device__ __forceinline__ void load_tile(uint16_t* s, const uint16_t* g, int r0, int L, int ld) {
     constexpr int LDS = D + 8;
     constexpr int CPR = D / 8;  // 16-byte chunks per row
     for (int i = threadIdx.x; i < ROWS * CPR; i += 128) {
         const int r = i / CPR, c = i % CPR;
         const int gr = r0 + r;
         const bool ok = gr >= 0 && gr < L;
-        const __nv_bfloat16* src = g + static_cast<int64_t>(ok ? gr : 0) * ld + c * 8;
+        const uint16_t* src = g + static_cast<int64_t>(ok ? gr : 0) * ld + c * 8;
         cp_async16(s + r * LDS + c * 8, src, ok);
     }
 }
@@ -501,7 +531,7 @@ __device__ __forceinline__ void load_tile(__nv_bfloat16* s, const __nv_bfloat16*
 // blocks of BKV rows.  Q (D <= 128: in registers; D = 256: re-read from
 // shared memory per k-step), S = Q K^T and O += P V on bf16 mma.sync with
 // fp32 accumulators, online softmax in the exp2 domain.
-template <int D, bool PLAIN>
+template <int D, bool PLAIN, bool F16>
 __global__ void __launch_bounds__(128) attention_kernel(AttnParams p) {
     constexpr int BKV = D == 256 ? 32 : 64;
     constexpr int LDS = D + 8;
@@ -510,9 +540,9 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnParams p) {
     constexpr int NT = BKV / 8;    // n-tiles of S
     constexpr bool QREG = D <= 128;
     extern __shared__ __align__(16) uint8_t attn_smem[];
-    __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(attn_smem);
-    __nv_bfloat16* sK = sQ + 64 * LDS;
-    __nv_bfloat16* sV = sK + BKV * LDS;
+    uint16_t* sQ = reinterpret_cast<uint16_t*>(attn_smem);
+    uint16_t* sK = sQ + 64 * LDS;
+    uint16_t* sV = sK + BKV * LDS;
 
     const int s = blockIdx.z, h = blockIdx.y;
     const int s0 = __ldg(p.cu + s), L = __ldg(p.cu + s + 1) - s0;
@@ -520,9 +550,9 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnParams p) {
     if (q0 >= L) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int hk = h / p.group;
-    const __nv_bfloat16* Qg = p.q + static_cast<int64_t>(s0) * p.ldq + h * D;
-    const __nv_bfloat16* Kg = p.k + static_cast<int64_t>(s0) * p.ldk + hk * D;
-    const __nv_bfloat16* Vg = p.v + static_cast<int64_t>(s0) * p.ldv + hk * D;
+    const uint16_t* Qg = p.q + static_cast<int64_t>(s0) * p.ldq + h * D;
+    const uint16_t* Kg = p.k + static_cast<int64_t>(s0) * p.ldk + hk * D;
+    const uint16_t* Vg = p.v + static_cast<int64_t>(s0) * p.ldv + hk * D;
 
     load_tile<D, 64>(sQ, Qg, q0, L, p.ldq);
     cp_async_commit_wait();
@@ -577,8 +607,8 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnParams p) {
                 const int r = 16 * j + (lane & 7) + (lane >> 4) * 8;
                 const int c = ks * 16 + ((lane >> 3) & 1) * 8;
                 ldsm_x4(b, sK + r * LDS + c);
-                mma_bf16_16816(sc[2 * j], a, b[0], b[1]);
-                mma_bf16_16816(sc[2 * j + 1], a, b[2], b[3]);
+                mma_16816<F16>(sc[2 * j], a, b[0], b[1]);
+                mma_16816<F16>(sc[2 * j + 1], a, b[2], b[3]);
             }
         }
         // scale (+ relative bias), mask, into the exp2 domain
@@ -635,8 +665,8 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnParams p) {
             const float p3 = sc[nt][3] > -1e29f ? exp2f(sc[nt][3] - m1) : 0.f;
             l0 += p0 + p1;
             l1 += p2 + p3;
-            pf[nt >> 1][(nt & 1) * 2 + 0] = pack_bf16(p0, p1);
-            pf[nt >> 1][(nt & 1) * 2 + 1] = pack_bf16(p2, p3);
+            pf[nt >> 1][(nt & 1) * 2 + 0] = pack2<F16>(p0, p1);
+            pf[nt >> 1][(nt & 1) * 2 + 1] = pack2<F16>(p2, p3);
         }
         // O += P V over the key sub-blocks of 16
 #pragma unroll
@@ -648,8 +678,8 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnParams p) {
                 const int r = 16 * j + (lane & 7) + ((lane >> 3) & 1) * 8;
                 const int c = 16 * i + (lane >> 4) * 8;
                 ldsm_x4_t(b, sV + r * LDS + c);
-                mma_bf16_16816(o[2 * i], a, b[0], b[1]);
-                mma_bf16_16816(o[2 * i + 1], a, b[2], b[3]);
+                mma_16816<F16>(o[2 * i], a, b[0], b[1]);
+                mma_16816<F16>(o[2 * i + 1], a, b[2], b[3]);
             }
         }
     }
@@ -658,19 +688,19 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnParams p) {
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
     const float i0 = l0 > 0.f ? 1.0f / l0 : 0.f, i1 = l1 > 0.f ? 1.0f / l1 : 0.f;
-    __nv_bfloat16* out = p.out + static_cast<int64_t>(s0) * p.ldo + h * D + (lane & 3) * 2;
+    uint16_t* out = p.out + static_cast<int64_t>(s0) * p.ldo + h * D + (lane & 3) * 2;
 #pragma unroll
     for (int i = 0; i < DT; ++i) {
         if (qi0 < L)
             *reinterpret_cast<uint32_t*>(out + static_cast<int64_t>(qi0) * p.ldo + i * 8) =
-                pack_bf16(o[i][0] * i0, o[i][1] * i0);
+                pack2<F16>(o[i][0] * i0, o[i][1] * i0);
         if (qi0 + 8 < L)
             *reinterpret_cast<uint32_t*>(out + static_cast<int64_t>(qi0 + 8) * p.ldo + i * 8) =
-                pack_bf16(o[i][2] * i1, o[i][3] * i1);
+                pack2<F16>(o[i][2] * i1, o[i][3] * i1);
     }
 }
 
-template <int D, bool PLAIN>
+template <int D, bool PLAIN, bool F16>
 static cudaError_t launch_attention_dp(const AttnParams& p, int nseq, int max_len, int heads, cudaStream_t st) {
     constexpr int BKV = D == 256 ? 32 : 64;
     constexpr int smem = (64 + 2 * BKV) * (D + 8) * 2;
@@ -679,20 +709,23 @@ static cudaError_t launch_attention_dp(const AttnParams& p, int nseq, int max_le
     cudaGetDevice(&dev);
     if (smem > 48 * 1024 && (dev >= 32 || !(__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & (1u << dev)))) {
         cudaError_t e =
-            cudaFuncSetAttribute(attention_kernel<D, PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            cudaFuncSetAttribute(attention_kernel<D, PLAIN, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         if (dev < 32) __atomic_fetch_or(&configured, 1u << dev, __ATOMIC_RELEASE);
     }
     const dim3 grid((max_len + 63) / 64, heads, nseq);
-    attention_kernel<D, PLAIN><<<grid, 128, smem, st>>>(p);
+    attention_kernel<D, PLAIN, F16><<<grid, 128, smem, st>>>(p);
     return cudaGetLastError();
 }
 
 template <int D>
 static cudaError_t launch_attention_d(const AttnParams& p, int nseq, int max_len, int heads, cudaStream_t st) {
     const bool plain = !p.bias && p.rel_lo <= -max_len && p.rel_hi >= max_len;
-    return plain ? launch_attention_dp<D, true>(p, nseq, max_len, heads, st)
-                 : launch_attention_dp<D, false>(p, nseq, max_len, heads, st);
+    if (p.f16)
+        return plain ? launch_attention_dp<D, true, true>(p, nseq, max_len, heads, st)
+                     : launch_attention_dp<D, false, true>(p, nseq, max_len, heads, st);
+    return plain ? launch_attention_dp<D, true, false>(p, nseq, max_len, heads, st)
+                 : launch_attention_dp<D, false, false>(p, nseq, max_len, heads, st);
 }
 
 cudaError_t launch_attention(const AttnParams& p, int nseq, int max_len, int heads, int head_dim, cudaStream_t st) {

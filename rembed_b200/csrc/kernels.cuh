@@ -10,9 +10,10 @@ namespace rg {
 // Embedding rows (bert.go:795-814, qwen3.go:457-462, modernbert.go:204-211,
 // gemma3.go:264-275, nomic.go:164-176): x = word[id] (+ pos[p + pos_off])
 // (+ type0), times scale, then LayerNorm(g, b) when g is set; p is the
-// token's index in its sequence.  Writes fp32 x32 and, if set, bf16 xb and
-// the int8 row (xq, xq_scale).  An id outside [0, vocab) raises
-// kStatusBadToken and yields zeros (never an out-of-bounds read).
+// token's index in its sequence.  Writes fp32 x32 and, if set, the 16-bit
+// row xb (fp16 if f16, else bf16) and the int8 row (xq, xq_scale).  An id
+// outside [0, vocab) raises kStatusBadToken and yields zeros (never an
+// out-of-bounds read).
 struct EmbedParams {
     const int64_t* ids;
     const int32_t* cu;
@@ -22,7 +23,8 @@ struct EmbedParams {
     const float *g, *b;
     float eps;
     float* x32;
-    __nv_bfloat16* xb;
+    uint16_t* xb;
+    bool f16;
     int8_t* xq;
     float* xq_scale;
     int* status;
@@ -30,21 +32,25 @@ struct EmbedParams {
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t st);
 
 // Row normalisation of in [T x H]: LayerNorm (g, b; b nullptr = zero) or
-// RMSNorm (g); g nullptr = identity.  Outputs (each optional): out32 (may alias in), outb (bf16),
-// outq + outqs (int8 row quantisation).
+// RMSNorm (g); g nullptr = identity.  Outputs (each optional): out32 (may
+// alias in), outb (16-bit: fp16 if f16, else bf16), outq + outqs (int8 row
+// quantisation).
 struct NormParams {
     const float* in;
     const float *g, *b;
     float eps;
     int T, H;
     float* out32;
-    __nv_bfloat16* outb;
+    uint16_t* outb;
+    bool f16;
     int8_t* outq;
     float* outqs;
+    int* status;  // optional: kStatusF16Overflow if an fp16 output overflows
 };
 cudaError_t launch_norm(const NormParams& p, bool rms, cudaStream_t st);
 cudaError_t launch_ln(const float* y32, const float* g, const float* b, float eps, int T, int H, float* x32,
-                      __nv_bfloat16* xb, int8_t* xq, float* xq_scale, cudaStream_t st);
+                      uint16_t* xb, bool f16, int8_t* xq, float* xq_scale, cudaStream_t st,
+                      int* status = nullptr);
 // x32 += RMSNorm(o32; g)  (Gemma's post-sublayer norms).
 cudaError_t launch_add_rmsnorm(float* x32, const float* o32, const float* g, float eps, int T, int H, cudaStream_t st);
 
@@ -52,13 +58,15 @@ cudaError_t launch_add_rmsnorm(float* x32, const float* o32, const float* g, flo
 // k heads of the fused qkv buffer [T x ld] (q at column 0, k at nq*dh).
 // cos/sin are [positions x dh/2] tables.  head_dim 64, 128 or 256.
 struct QkRopeParams {
-    __nv_bfloat16* qkv;
+    uint16_t* qkv;  // 16-bit: fp16 if f16, else bf16
+    bool f16;
     int ld, T, nq, nkv;
     const float *q_norm, *k_norm;
     float eps;
     const float *cos, *sin;
     const int32_t* cu;
     int nseq;
+    int* status;  // optional: kStatusF16Overflow
 };
 cudaError_t launch_qk_norm_rope(const QkRopeParams& p, int head_dim, cudaStream_t st);
 
@@ -74,11 +82,12 @@ cudaError_t launch_quantize_rows(const __nv_bfloat16* x, int T, int K, int8_t* q
 // h / group), out = softmax(Q K^T * scale [+ bias(j - i)]) V over the keys j
 // with rel_lo <= j - i <= rel_hi (causal: rel_hi = 0; symmetric window w:
 // rel_lo = -w, rel_hi = w; unbounded: +-2^30).  Q, K, V, out are token-major
-// bf16 with row strides ldq/ldk/ldv/ldo; head h's columns start at h*D.
+// 16-bit rows with strides ldq/ldk/ldv/ldo; head h's columns start at h*D.
 // bias, if set, is [heads x (2*bias_off + 1)] indexed by j - i + bias_off
 // (MPNet's bucketed relative-position bias, added after the scale).
 struct AttnParams {
-    const __nv_bfloat16 *q, *k, *v;
+    const uint16_t *q, *k, *v;  // 16-bit: fp16 if f16, else bf16
+    bool f16;
     int ldq, ldk, ldv;
     const int32_t* cu;
     int group;
@@ -86,7 +95,7 @@ struct AttnParams {
     int rel_lo, rel_hi;
     const float* bias;
     int bias_off;
-    __nv_bfloat16* out;
+    uint16_t* out;
     int ldo;
 };
 cudaError_t launch_attention(const AttnParams& p, int nseq, int max_len, int heads, int head_dim, cudaStream_t st);

@@ -139,7 +139,7 @@ extern "C" int rg_dense_residual_layernorm_bf16_noalloc(const void* x, const voi
     a.status = status;
     e = rg::gemm_launch(rg::GemmKind::kBF16, rg::kEpiBiasRes, bn, ta, tb, a, sms, st);
     if (e != cudaSuccess) return set_err(err, "gemm launch: %s", cudaGetErrorString(e));
-    e = rg::launch_ln(sum, gamma, beta, eps, M, N, out32, static_cast<__nv_bfloat16*>(outb), nullptr, nullptr, st);
+    e = rg::launch_ln(sum, gamma, beta, eps, M, N, out32, static_cast<uint16_t*>(outb), false, nullptr, nullptr, st);
     if (e != cudaSuccess) return set_err(err, "ln launch: %s", cudaGetErrorString(e));
     return 0;
 }

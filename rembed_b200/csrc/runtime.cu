@@ -28,7 +28,7 @@
 #include "kernels.cuh"
 #include "sm100.cuh"
 
-using bf16 = __nv_bfloat16;
+using act16 = uint16_t;  // 16-bit activation words: bf16 or fp16 by mode
 
 namespace {
 
@@ -105,7 +105,7 @@ struct Replica {
     int cap_T = 0, cap_seq = 0, cap_out = 0;
     std::vector<void*> ws;
     float *x32 = nullptr, *y32 = nullptr;
-    bf16 *xb = nullptr, *qkv = nullptr, *ctx = nullptr, *ffh = nullptr;
+    act16 *xb = nullptr, *qkv = nullptr, *ctx = nullptr, *ffh = nullptr;
     int8_t *xq = nullptr, *ctxq = nullptr, *ffhq = nullptr;
     float *xs = nullptr, *ctxs = nullptr, *ffhs = nullptr;
     float *pool32 = nullptr, *head_hid = nullptr, *head_out = nullptr;  // Gemma Dense head
@@ -219,6 +219,39 @@ uint16_t to_bf16_bits(float f) {
     return static_cast<uint16_t>(u >> 16);
 }
 
+// fp16 round-to-nearest-even of a float; false if it overflows the fp16
+// range (|f| rounds above 65504) or is not finite.
+bool to_f16_bits(float f, uint16_t* out) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    const uint32_t sign = (u >> 16) & 0x8000u;
+    const uint32_t a = u & 0x7fffffffu;
+    if (a >= 0x7f800000u) return false;
+    const int e = static_cast<int>(a >> 23) - 127;  // unbiased exponent
+    if (e < -25) {                                  // below half the smallest subnormal
+        *out = static_cast<uint16_t>(sign);
+        return true;
+    }
+    uint32_t mant = (a & 0x7fffffu) | 0x800000u;  // 24-bit significand
+    int shift;                                     // bits dropped from the 24-bit significand
+    uint32_t base;                                 // exponent field of the result, pre-rounding
+    if (e < -14) {  // subnormal result q * 2^-24 with q = mant * 2^(e + 1)
+        shift = -e - 1;
+        base = 0;
+    } else {
+        shift = 13;
+        base = static_cast<uint32_t>(e + 15) << 10;
+        mant &= 0x7fffffu;  // drop the implicit bit: it lives in the exponent field
+    }
+    uint32_t q = mant >> shift;
+    const uint32_t rem = mant & ((1u << shift) - 1u), halfway = 1u << (shift - 1);
+    if (rem > halfway || (rem == halfway && (q & 1u))) ++q;  // carries into the exponent field as needed
+    const uint32_t h = base + q;
+    if (h >= 0x7c00u) return false;
+    *out = static_cast<uint16_t>(sign | h);
+    return true;
+}
+
 bool finite32(float v) { return std::isfinite(v); }
 
 // PackB8 (pack8.go:25-76): float32 scale maxAbs/127, float64 division,
@@ -304,6 +337,13 @@ DevDense make_dense(Replica& r, int mode, const float* w, const float* bias, int
         std::vector<uint16_t> h(n);
         for (size_t i = 0; i < n; ++i) h[i] = to_bf16_bits(w[i]);
         d.w = dev_upload(r, h.data(), n);
+    } else if (mode == RG_MODE_F16) {
+        std::vector<uint16_t> h(n);
+        for (size_t i = 0; i < n; ++i)
+            if (!to_f16_bits(w[i], &h[i]))
+                fail("f16 mode: weight [%zu, %zu] = %g is outside the fp16 range", i / K, i % K,
+                     static_cast<double>(w[i]));
+        d.w = dev_upload(r, h.data(), n);
     } else {
         std::vector<int8_t> q(n);
         std::vector<float> s(N);
@@ -314,11 +354,13 @@ DevDense make_dense(Replica& r, int mode, const float* w, const float* bias, int
         d.w = dev_upload(r, q.data(), n);
         d.scale = dev_upload(r, s.data(), N);
     }
-    const int eb = mode == RG_MODE_BF16 ? 2 : 1;
+    const int eb = (mode == RG_MODE_BF16 || mode == RG_MODE_F16) ? 2 : 1;
     for (int i = 0; i < 3; ++i) {
         if (N % kBlockWidths[i] != 0) continue;
-        if (!rg::make_kmajor_tmap(&d.tmap[i], d.w, eb, N, K, K, rg::gemm_w_box_rows(kBlockWidths[i])))
-            fail("cuTensorMapEncodeTiled failed for a [%d x %d] weight", N, K);
+        const uint32_t box_rows = rg::gemm_w_box_rows(kBlockWidths[i]);
+        const bool ok = mode == RG_MODE_INT8_W ? rg::make_w8_tmap(&d.tmap[i], d.w, N, K, box_rows)
+                                               : rg::make_kmajor_tmap(&d.tmap[i], d.w, eb, N, K, K, box_rows);
+        if (!ok) fail("cuTensorMapEncodeTiled failed for a [%d x %d] weight", N, K);
     }
     if (bias) d.bias = dev_upload(r, bias, N);
     return d;
@@ -614,10 +656,10 @@ void ensure_workspace(rg_ctx* c, Replica& r, int T, int nseq, size_t nout) {
         const size_t t = static_cast<size_t>((capT + 255) / 256 * 256);
         r.x32 = ws_alloc<float>(r, t * H);
         r.y32 = ws_alloc<float>(r, t * H);
-        r.xb = ws_alloc<bf16>(r, t * H);
-        r.qkv = ws_alloc<bf16>(r, t * m.nqkv);
-        r.ctx = ws_alloc<bf16>(r, t * m.qd);
-        r.ffh = ws_alloc<bf16>(r, t * I);
+        r.xb = ws_alloc<act16>(r, t * H);
+        r.qkv = ws_alloc<act16>(r, t * m.nqkv);
+        r.ctx = ws_alloc<act16>(r, t * m.qd);
+        r.ffh = ws_alloc<act16>(r, t * I);
         if (r.dense1) {
             r.pool32 = ws_alloc<float>(r, static_cast<size_t>(capS) * H);
             r.head_hid = ws_alloc<float>(r, static_cast<size_t>(capS) * d.dense_hidden);
@@ -734,7 +776,10 @@ void gemm(Replica& r, int mode, const CUtensorMap& tmA, const DevDense& w, int M
     a.out = out;
     a.ld_out = rg::epi_is_glu(epi) ? w.N / 2 : w.N;
     a.status = r.d_status;
-    const rg::GemmKind kind = mode == RG_MODE_INT8_FULL ? rg::GemmKind::kS8 : rg::GemmKind::kBF16;
+    const rg::GemmKind kind = mode == RG_MODE_INT8_FULL ? rg::GemmKind::kS8
+                              : mode == RG_MODE_F16     ? rg::GemmKind::kF16
+                              : mode == RG_MODE_INT8_W  ? rg::GemmKind::kW8
+                                                        : rg::GemmKind::kBF16;
     // Algorithmic bytes: A and W read once, output written once (+ fp32
     // residual read); FLOPs 2*M*N*K.
     const double eb = kind == rg::GemmKind::kS8 ? 1.0 : 2.0;
@@ -791,6 +836,7 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
     const float eps = d.layer_norm_eps == 0.f ? 1e-12f : d.layer_norm_eps;
     const int mode = c->mode;
     const bool s8 = mode == RG_MODE_INT8_FULL;
+    const bool f16 = mode == RG_MODE_F16 || mode == RG_MODE_INT8_W;  // fp16 activations, else bf16
     const bool pre = is_prenorm(arch);
     int launches = 0;
     const double Td = T, Hd = H;
@@ -816,6 +862,7 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         e.eps = eps;
         e.x32 = r.x32;
         e.xb = pre ? nullptr : r.xb;  // pre-norm stacks normalise before the first GEMM
+        e.f16 = f16;
         e.xq = (!pre && s8) ? r.xq : nullptr;
         e.xq_scale = (!pre && s8) ? r.xs : nullptr;
         e.status = r.d_status;
@@ -833,6 +880,8 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         p.T = T;
         p.H = H;
         p.outb = r.xb;
+        p.f16 = f16;
+        p.status = r.d_status;
         p.outq = s8 ? r.xq : nullptr;
         p.outqs = s8 ? r.xs : nullptr;
         check(rg::launch_norm(p, rms, st), "norm launch");  // g nullptr: identity
@@ -840,13 +889,15 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
     };
     auto post_norm = [&](const float* g, const float* b) {  // y32 -> LN -> x32 (+ A operand)
         ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, row_bytes);
-        check(rg::launch_ln(r.y32, g, b, eps, T, H, r.x32, r.xb, s8 ? r.xq : nullptr, s8 ? r.xs : nullptr, st),
+        check(rg::launch_ln(r.y32, g, b, eps, T, H, r.x32, r.xb, f16, s8 ? r.xq : nullptr, s8 ? r.xs : nullptr, st,
+                            r.d_status),
               "ln launch");
         ++launches;
     };
-    auto quantize = [&](const bf16* x, int K, int8_t* q, float* sc) {
+    auto quantize = [&](const act16* x, int K, int8_t* q, float* sc) {  // bf16 rows (full-int8 mode)
         ProfScope ps(r, st, RG_KC_QUANT, 0.0, Td * K * 3.0);
-        check(rg::launch_quantize_rows(x, T, K, q, sc, st), "quantize launch");
+        check(rg::launch_quantize_rows(reinterpret_cast<const __nv_bfloat16*>(x), T, K, q, sc, st),
+              "quantize launch");
         ++launches;
     };
     const float scale = static_cast<float>(
@@ -864,6 +915,8 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
             ProfScope ps(r, st, RG_KC_NORM, 0.0, Td * (m.qd + m.kvd) * 4.0);
             rg::QkRopeParams q{};
             q.qkv = r.qkv;
+            q.f16 = f16;
+            q.status = r.d_status;
             q.ld = m.nqkv;
             q.T = T;
             q.nq = m.nq;
@@ -889,6 +942,7 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
             ap.k = r.qkv + m.qd;
             ap.v = r.qkv + m.qd + m.kvd;
             ap.ldq = ap.ldk = ap.ldv = m.nqkv;
+            ap.f16 = f16;
             ap.cu = d_cu;
             ap.group = m.nq / m.nkv;
             ap.scale = scale;
@@ -972,6 +1026,7 @@ std::string status_message(int s) {
     if (s & rg::kStatusBadToken) m += "token id out of vocab range; ";
     if (s & rg::kStatusWaitTimeout) m += "a device pipeline wait timed out; ";
     if (s & rg::kStatusBadShape) m += "inconsistent shape on the device; ";
+    if (s & rg::kStatusF16Overflow) m += "an activation overflowed the fp16 range (use the bf16 mode); ";
     if (m.empty()) m = "device error status " + std::to_string(s);
     return m;
 }
@@ -1085,9 +1140,10 @@ int rg_init(const rg_model_desc* desc, const int* devices, int ndev, int mode, r
             fail("rg_init: mpnet needs relative_attention_num_buckets >= 2");
         if (max_seq_len(d) <= 0) fail("rg_init: no usable positions (max_position_embeddings %d, offset %d)",
                                       d.max_position_embeddings, pos_offset(d));
-        if (mode != RG_MODE_BF16 && mode != RG_MODE_INT8_FULL)
+        if (mode != RG_MODE_BF16 && mode != RG_MODE_F16 && mode != RG_MODE_INT8_W && mode != RG_MODE_INT8_FULL)
             fail("rg_init: mode %d is not available in this build", mode);
-        if (mode == RG_MODE_INT8_FULL && (d.hidden_size % 128 != 0 || d.intermediate_size % 128 != 0))
+        if (mode == RG_MODE_INT8_FULL && (d.hidden_size % 128 != 0 || d.intermediate_size % 128 != 0 ||
+                                          dims(d).qd % 128 != 0))
             fail("rg_init: full-int8 needs K multiples of 128");
         int ndevs = 0;
         check(cudaGetDeviceCount(&ndevs), "cudaGetDeviceCount");
@@ -1399,7 +1455,7 @@ int rg_dense_residual_layernorm_bf16(const void* x, const void* w, const float* 
         a.ld_out = N;
         a.status = status;
         check(rg::gemm_launch(rg::GemmKind::kBF16, rg::kEpiBiasRes, bn, ta, tb, a, sms, st), "gemm launch");
-        check(rg::launch_ln(sum, gamma, beta, eps, M, N, out32, static_cast<bf16*>(outb), nullptr, nullptr, st),
+        check(rg::launch_ln(sum, gamma, beta, eps, M, N, out32, static_cast<act16*>(outb), false, nullptr, nullptr, st),
               "ln launch");
         return 0;
     } catch (const Error& e) {

@@ -20,6 +20,7 @@ enum : int {
     kStatusWaitTimeout = 1,   // an mbarrier wait gave up
     kStatusBadToken = 2,      // a token id outside [0, vocab)
     kStatusBadShape = 4,      // a launch saw an inconsistent shape
+    kStatusF16Overflow = 8,   // an fp16 activation overflowed (or was NaN)
 };
 
 constexpr long long kWaitLimitCycles = 2000000000LL;  // ~1 s at 1.9 GHz
@@ -176,6 +177,10 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 // [24,29) M>>4.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+// kind::f16 with fp16 A and B (format 0 at bits [7,10) and [10,13)).
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 __host__ __device__ constexpr uint32_t idesc_s8(int M, int N) {
     return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);

@@ -33,7 +33,7 @@ from .config import Config
 
 __all__ = ["Embedder", "RembedError", "TokenEmbeddings", "load", "library"]
 
-RG_MODE_BF16, RG_MODE_INT8_W, RG_MODE_INT8_FULL = 0, 2, 3
+RG_MODE_BF16, RG_MODE_F16, RG_MODE_INT8_W, RG_MODE_INT8_FULL = 0, 1, 2, 3
 RG_DTYPE_F32, RG_DTYPE_F16, RG_DTYPE_BF16 = 0, 1, 2
 RG_OUT_POOLED, RG_OUT_TOKENS = 0, 1
 
@@ -178,11 +178,16 @@ class Embedder:
     """
 
     def __init__(self, config: Config, weights: dict, *, int8: bool = False, int8_activations: bool = False,
-                 dim: int = 0, devices: Sequence[int] = (0,)):
+                 dim: int = 0, devices: Sequence[int] = (0,), fp16: bool = True):
         self._lib = library()
         self._ctx = None
         self.config = config.validate(config.name or "config")
-        mode = RG_MODE_INT8_FULL if int8_activations else (RG_MODE_INT8_W if int8 else RG_MODE_BF16)
+        # WithInt8Activations implies WithInt8 (rembed.go:79-81).  The
+        # unquantised path runs fp16 tensor-core operands by default (closest
+        # to the reference's fp32; an fp16 overflow is reported, never
+        # silently turned into inf); fp16=False selects bf16 operands.
+        mode = (RG_MODE_INT8_FULL if int8_activations else RG_MODE_INT8_W if int8
+                else RG_MODE_F16 if fp16 else RG_MODE_BF16)
         H = config.hidden_size
         if dim and not (1 <= dim <= H):
             raise RembedError(f"rembed: WithDim({dim}) out of range [1, {H}]")
@@ -320,7 +325,7 @@ class Embedder:
 
 
 def load(ref: str | os.PathLike, *, int8: bool = False, int8_activations: bool = False, dim: int = 0,
-         devices: Sequence[int] = (0,)) -> Embedder:
+         devices: Sequence[int] = (0,), fp16: bool = True) -> Embedder:
     """rembed.Load over a converted model directory (manifest.json +
     model.safetensors).  Hub download and HF-config derivation stay with the
     reference host."""
@@ -329,4 +334,5 @@ def load(ref: str | os.PathLike, *, int8: bool = False, int8_activations: bool =
     p = Path(ref)
     cfg = Config.load(p / "manifest.json")
     weights = read_safetensors(p / "model.safetensors")
-    return Embedder(cfg, weights, int8=int8, int8_activations=int8_activations, dim=dim, devices=devices)
+    return Embedder(cfg, weights, int8=int8, int8_activations=int8_activations, dim=dim, devices=devices,
+                    fp16=fp16)

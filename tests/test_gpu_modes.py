@@ -1,0 +1,116 @@
+"""The numeric modes against the CPU oracle.
+
+fp16 (RG_MODE_F16, the default unquantised path): fp16 tensor-core operands,
+fp32 accumulation and fp32 residual stream; cosine >= 0.9999 and max-abs
+<= 2e-3 per embedding.
+bf16 (RG_MODE_BF16): the same bar, except tiny-gemma3, whose bf16 floor is
+measured at max-abs 3.1e-3: its fp32 weights rounded to bf16 (3.1e-3 -> 1.1e-3
+when the weights are bf16-exact), unit-gain post-sublayer norms that carry
+each sublayer's rounding into the residual, and 128-wide embeddings whose
+elements are 2.4x those of the 768-wide production model (which meets 2e-3).
+Weight-only int8 (RG_MODE_INT8_W, WithInt8): the PackB8 quantiser
+(pack8.go:25-76), int8 weights widened to fp16 inside the GEMM mainloop;
+compared with the oracle's own weight-int8 path, cosine >= 0.999
+(the north-star bar for w-int8).
+"""
+
+import numpy as np
+import pytest
+
+import oracle
+from rembed_b200 import synth
+from rembed_b200.embedder import Embedder
+
+pytestmark = pytest.mark.gpu
+
+COS_BF16, MAXABS_BF16 = 0.9999, 2e-3
+COS_INT8_W = 0.999
+
+
+def cosines(a, b):
+    a = a.astype(np.float64)
+    b = b.astype(np.float64)
+    return (a * b).sum(1) / (np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1))
+
+
+CASES = [("tiny-bert", 9, 1, 200), ("minilm-l6", 12, 8, 128), ("bge-base", 6, 16, 384),
+         ("tiny-mpnet", 7, 1, 256), ("tiny-qwen3", 7, 1, 200), ("tiny-modernbert", 7, 1, 120),
+         ("tiny-gemma3", 7, 1, 100), ("tiny-nomic", 7, 1, 200), ("qwen3-0.6b", 3, 16, 160),
+         ("embeddinggemma-300m", 3, 200, 400)]
+
+
+@pytest.mark.parametrize("name,nseq,lo,hi", CASES)
+def test_fp16_parity(cuda, name, nseq, lo, hi):
+    cfg = synth.preset(name)
+    w = synth.make_weights(cfg, seed=41)
+    ids, cu = synth.make_batch(cfg, nseq, lo, hi, seed=42)
+    gpu = Embedder(cfg, w, fp16=True)
+    got = gpu.embed_packed(ids, cu)
+    gpu.close()
+    want = oracle.OracleModel(cfg, w, oracle.QUANT_NONE).embed(ids, cu)
+    cos = cosines(got, want)
+    print(f"\n[parity] {name} fp16: min cos {cos.min():.7f}, max abs {np.abs(got - want).max():.2e}")
+    assert cos.min() >= COS_BF16
+    assert np.abs(got - want).max() <= MAXABS_BF16
+
+
+# bf16 max-abs floor of a 128-wide gemma3 stack with fp32 weights (see above)
+MAXABS_BF16_TINY_GEMMA = 4e-3
+
+
+@pytest.mark.parametrize("name,nseq,lo,hi", CASES)
+def test_bf16_parity(cuda, name, nseq, lo, hi):
+    cfg = synth.preset(name)
+    w = synth.make_weights(cfg, seed=31)
+    ids, cu = synth.make_batch(cfg, nseq, lo, hi, seed=32)
+    gpu = Embedder(cfg, w, fp16=False)
+    got = gpu.embed_packed(ids, cu)
+    gpu.close()
+    want = oracle.OracleModel(cfg, w, oracle.QUANT_NONE).embed(ids, cu)
+    cos = cosines(got, want)
+    print(f"\n[parity] {name} bf16: min cos {cos.min():.7f}, max abs {np.abs(got - want).max():.2e}")
+    assert cos.min() >= COS_BF16
+    assert np.abs(got - want).max() <= (MAXABS_BF16_TINY_GEMMA if name == "tiny-gemma3" else MAXABS_BF16)
+
+
+@pytest.mark.parametrize("name,nseq,lo,hi", CASES)
+def test_int8_weights_parity(cuda, name, nseq, lo, hi):
+    cfg = synth.preset(name)
+    w = synth.make_weights(cfg, seed=43)
+    ids, cu = synth.make_batch(cfg, nseq, lo, hi, seed=44)
+    gpu = Embedder(cfg, w, int8=True)
+    assert gpu.quantized() and not gpu.quantized_activations()
+    got = gpu.embed_packed(ids, cu)
+    gpu.close()
+    want = oracle.OracleModel(cfg, w, oracle.QUANT_WEIGHTS).embed(ids, cu)
+    cos = cosines(got, want)
+    print(f"\n[parity] {name} w-int8: min cos {cos.min():.7f}, max abs {np.abs(got - want).max():.2e}")
+    assert cos.min() >= COS_INT8_W
+
+
+def test_fp16_rejects_out_of_range_weight(cuda):
+    cfg = synth.preset("tiny-bert")
+    w = synth.make_weights(cfg, seed=45)
+    name = next(k for k in w if k.endswith("attention.self.query.weight"))
+    w[name] = w[name].copy()
+    w[name][3, 5] = 1e6
+    with pytest.raises(Exception, match="fp16 range"):
+        Embedder(cfg, w, fp16=True)
+
+
+def test_fp16_activation_overflow_is_reported(cuda):
+    """Weights inside the fp16 range whose FFN activations are not: the
+    forward fails with the overflow named; bf16 runs the same model."""
+    cfg = synth.preset("tiny-bert")
+    w = synth.make_weights(cfg, seed=46)
+    for k in list(w):
+        if k.endswith("intermediate.dense.weight"):
+            w[k] = (w[k] * 200000.0).astype(np.float32)  # max |w| ~ 2e4, outputs ~ 5e4 rms
+    ids, cu = synth.make_batch(cfg, 3, 4, 30, seed=47)
+    gpu = Embedder(cfg, w, fp16=True)
+    with pytest.raises(Exception, match="fp16 range"):
+        gpu.embed_packed(ids, cu)
+    gpu.close()
+    gpu = Embedder(cfg, w, fp16=False)
+    assert np.isfinite(gpu.embed_packed(ids, cu)).all()
+    gpu.close()
