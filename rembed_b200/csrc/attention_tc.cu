@@ -1,0 +1,406 @@
+// attention_tc.cu - varlen flash attention on the 5th-generation tensor
+// cores (tcgen05) for head dims 64 and 128.
+//
+// CTA = 128 query rows of one (sequence, query head); key/value blocks of
+// BKV rows.  Roles (192 threads):
+//   warp 0     TMA producer: the Q tile once, then K blocks into a 2-deep
+//              ring and V blocks into one buffer, straight from the fused
+//              token-major qkv buffer (128-byte swizzle);
+//   warp 1     TMEM allocator and MMA issuer (one thread):
+//                S  = Q K^T   (M 128, N BKV, K D; both operands K-major)
+//                O += P V     (M 128, N D, K BKV; P K-major from shared
+//                              memory, V MN-major as loaded);
+//   warps 2-5  softmax, thread = query row = TMEM lane: read the S row
+//              (64 keys),
+//              mask (sequence end, window, causal), scale (+ relative
+//              bias), online max / sum in the exp2 domain, rescale the O
+//              row in TMEM when the running max moves, write P (16-bit,
+//              swizzled K-major) for the next MMA; at the end O / l to the
+//              output rows of the sequence.
+// Rows of the packed buffer past the sequence's end are loaded like any
+// other (they belong to the next sequence or are zero-filled past T) and are
+// masked as keys and never stored as queries.  Every wait is bounded; on a
+// timeout the roles stop, in-flight copies and MMAs are drained and TMEM is
+// freed before the CTA exits with kStatusWaitTimeout raised.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "act16.cuh"
+#include "kernels.cuh"
+#include "sm100.cuh"
+
+namespace rg {
+
+template <int D>
+struct AttnTc {
+    static constexpr int BKV = 64;      // keys per block
+    static constexpr int QB = D / 64;   // 64-column (128-byte) blocks of a row
+    static constexpr int Q_BYTES = 128 * D * 2;
+    static constexpr int KV_BYTES = BKV * D * 2;
+    static constexpr int P_BYTES = 128 * BKV * 2;
+    static constexpr int SMEM = Q_BYTES + 3 * KV_BYTES + P_BYTES + 1024 + 256;
+    // S at column 0 (BKV wide), O at column O_COL (D wide)
+    static constexpr uint32_t O_COL = 64;
+    static constexpr uint32_t TMEM_COLS = D == 64 ? 128 : 256;
+    static constexpr int THREADS = 192;
+    static constexpr int MIN_BLOCKS = D == 64 ? 3 : 2;  // CTAs per SM (shared memory, TMEM, registers)
+};
+
+__device__ __forceinline__ float ex2f(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+template <int D, bool F16, bool PLAIN>
+__global__ void __launch_bounds__(192, AttnTc<D>::MIN_BLOCKS)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, AttnParams p, int* status) {
+    using S = AttnTc<D>;
+    constexpr int BKV = S::BKV, QB = S::QB;
+    const int s = blockIdx.z, h = blockIdx.y;
+    const int s0 = __ldg(p.cu + s), L = __ldg(p.cu + s + 1) - s0;
+    const int q0 = blockIdx.x * 128;
+    if (q0 >= L) return;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sK = sQ + S::Q_BYTES;  // [2][KV_BYTES]
+    uint8_t* sV = sK + 2 * S::KV_BYTES;
+    uint8_t* sP = sV + S::KV_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + S::P_BYTES);
+    uint64_t* qbar = bars + 0;
+    uint64_t* kfull = bars + 1;   // [2]
+    uint64_t* kempty = bars + 3;  // [2]
+    uint64_t* vfull = bars + 5;
+    uint64_t* vempty = bars + 6;
+    uint64_t* sfull = bars + 7;
+    uint64_t* sfree = bars + 8;
+    uint64_t* pfull = bars + 9;
+    uint64_t* ofull = bars + 10;
+    uint64_t* drain = bars + 11;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hk = h / p.group;
+    // key blocks any row of this tile may see: j - i in [rel_lo, rel_hi]
+    const int jmin = max(0, q0 + p.rel_lo);
+    const int jmax = min(L - 1, q0 + 127 + p.rel_hi);
+    const int kb0 = jmin / BKV, nb = jmax / BKV - kb0 + 1;
+
+    if (threadIdx.x == 0) {
+        mbar_init(qbar, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&kfull[i], 1);
+            mbar_init(&kempty[i], 1);
+        }
+        mbar_init(vfull, 1);
+        mbar_init(vempty, 1);
+        mbar_init(sfull, 1);
+        mbar_init(sfree, 4);  // one arrival per softmax warp
+        mbar_init(pfull, 4);
+        mbar_init(ofull, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, S::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tS = tmem, tO = tmem + S::O_COL;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            uint32_t armed = 0, parity = 0;  // barriers with a load in flight, their phase parity
+            auto arm = [&](int bit, uint32_t ph) {
+                armed |= 1u << bit;
+                parity = (parity & ~(1u << bit)) | (ph << bit);
+            };
+            mbar_arrive_expect_tx(qbar, S::Q_BYTES);
+            for (int b = 0; b < QB; ++b)
+                tma_load_2d(sQ + b * 16384, &tmQ, qbar, h * D + b * 64, s0 + q0);
+            arm(0, 0);
+            bool ok = true;
+            for (int i = 0; i < nb && ok; ++i) {
+                const int row = s0 + (kb0 + i) * BKV;
+                const int st = i & 1;
+                if (i >= 2 && !mbar_wait(&kempty[st], ((i >> 1) - 1) & 1, status, abort_flag)) break;
+                mbar_arrive_expect_tx(&kfull[st], S::KV_BYTES);
+                for (int b = 0; b < QB; ++b)
+                    tma_load_2d(sK + st * S::KV_BYTES + b * BKV * 128, &tmK, &kfull[st], hk * D + b * 64, row);
+                arm(1 + st, (i >> 1) & 1);
+                if (i >= 1 && !mbar_wait(vempty, (i - 1) & 1, status, abort_flag)) break;
+                mbar_arrive_expect_tx(vfull, S::KV_BYTES);
+                for (int b = 0; b < QB; ++b)
+                    tma_load_2d(sV + b * BKV * 128, &tmV, vfull, hk * D + b * 64, row);
+                arm(3, i & 1);
+            }
+            // every load issued has landed before the CTA may exit
+            if (armed & 1) mbar_drain(qbar, parity & 1);
+            for (int b = 0; b < 2; ++b)
+                if (armed & (2u << b)) mbar_drain(&kfull[b], (parity >> (1 + b)) & 1);
+            if (armed & 8) mbar_drain(vfull, (parity >> 3) & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            constexpr uint32_t fmt = F16 ? 0u : 1u;
+            constexpr uint32_t idS = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BKV >> 3) << 17) |
+                                     ((uint32_t)(128 >> 4) << 24);
+            constexpr uint32_t idO = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 16) |
+                                     ((uint32_t)(D >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+            bool issued = false;
+            if (mbar_wait(qbar, 0, status, abort_flag)) {
+                for (int i = 0; i < nb; ++i) {
+                    const int st = i & 1;
+                    if (!mbar_wait(&kfull[st], (i >> 1) & 1, status, abort_flag)) break;
+                    if (i > 0 && !mbar_wait(sfree, (i - 1) & 1, status, abort_flag)) break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int ks = 0; ks < D / 16; ++ks) {
+                        const uint64_t a = sdesc_k128(smem_u32(sQ + (ks >> 2) * 16384 + (ks & 3) * 32));
+                        const uint64_t b =
+                            sdesc_k128(smem_u32(sK + st * S::KV_BYTES + (ks >> 2) * BKV * 128 + (ks & 3) * 32));
+                        umma_bf16(tS, a, b, idS, ks > 0);
+                    }
+                    issued = true;
+                    umma_commit(sfull);
+                    umma_commit(&kempty[st]);
+                    if (!mbar_wait(pfull, i & 1, status, abort_flag) || !mbar_wait(vfull, i & 1, status, abort_flag))
+                        break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < BKV / 16; ++kk) {
+                        const uint64_t a = sdesc_k128(smem_u32(sP + (kk >> 2) * 16384 + (kk & 3) * 32));
+                        const uint64_t b = sdesc_mn128(smem_u32(sV + kk * 2048), BKV * 128);
+                        umma_bf16(tO, a, b, idO, (i | kk) != 0);
+                    }
+                    umma_commit(ofull);
+                    umma_commit(vempty);
+                }
+            }
+            if (issued) {
+                umma_commit(drain);
+                mbar_drain(drain, 0);
+            }
+        }
+    } else {
+        // ---------------- softmax (warps 2-5), thread = query row ----------------
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;  // row within the tile = TMEM lane
+        const int qi = q0 + r;              // query index within the sequence
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int i = 0; i < nb; ++i) {
+            const int kbase = (kb0 + i) * BKV;
+            if (!mbar_wait(sfull, i & 1, status, abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t sr[BKV];
+#pragma unroll
+            for (int c = 0; c < BKV / 32; ++c)
+                tmem_ld32(tS + lane_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+            tmem_ld_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(sfree);
+            // scores in the exp2 domain, masked keys at -inf
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < BKV; ++c) {
+                const int kj = kbase + c;
+                float x = __uint_as_float(sr[c]);
+                bool valid = kj < L;
+                if constexpr (PLAIN) {
+                    x *= p.scale_log2;
+                } else {
+                    const int rel = kj - qi;
+                    valid = valid && rel >= p.rel_lo && rel <= p.rel_hi;
+                    if (p.bias) {
+                        // scores * scale + bias[h][rel] (bert.go:876-889)
+                        const int bi = min(max(rel + p.bias_off, 0), 2 * p.bias_off);
+                        x = (x * p.scale + __ldg(p.bias + static_cast<int64_t>(h) * (2 * p.bias_off + 1) + bi)) *
+                            1.4426950408889634f;
+                    } else {
+                        x *= p.scale_log2;
+                    }
+                }
+                x = valid ? x : -INFINITY;
+                sr[c] = __float_as_uint(x);
+                mx = fmaxf(mx, x);
+            }
+            const float m_new = fmaxf(m, mx);
+            const float m_use = m_new == -INFINITY ? 0.f : m_new;  // a row with no key yet keeps p = 0
+            const float alpha = ex2f(m - m_use);                  // m = -inf: 0 (O and l are still 0)
+            // P V of the previous block is done: O is final for it and the P
+            // buffer is free
+            if (i > 0) {
+                if (!mbar_wait(ofull, (i - 1) & 1, status, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+            }
+            l *= alpha;
+            // P row: 16 bytes (8 keys) at a time into the swizzled K-major tile
+#pragma unroll
+            for (int q = 0; q < BKV / 8; ++q) {
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float a = ex2f(__uint_as_float(sr[8 * q + 2 * e]) - m_use);
+                    const float b = ex2f(__uint_as_float(sr[8 * q + 2 * e + 1]) - m_use);
+                    l += a + b;
+                    w[e] = pack2<F16>(a, b);
+                }
+                *reinterpret_cast<uint4*>(sP + r * 128 + ((q ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            // rescale the O row when the running max moved (warp-uniform: the
+            // TMEM accesses are warp-wide)
+            if (i > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+                for (int c = 0; c < D / 32; ++c) {
+                    uint32_t o[32];
+                    tmem_ld32(tO + lane_addr + c * 32, o);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                    tmem_st32(tO + lane_addr + c * 32, o);
+                }
+                tmem_st_wait();
+            }
+            m = m_new;
+            fence_proxy_async_smem();  // P (generic writes) -> the MMA (async proxy)
+            tc_fence_before();         // O rescale (tcgen05.st) -> the MMA
+            __syncwarp();
+            if (lane == 0) mbar_arrive(pfull);
+        }
+        if (ok && mbar_wait(ofull, (nb - 1) & 1, status, abort_flag)) {
+            tc_fence_after();
+            const float inv = l > 0.f ? 1.0f / l : 0.f;
+            uint16_t* out = p.out + static_cast<int64_t>(s0 + qi) * p.ldo + h * D;
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+                uint32_t o[32];
+                tmem_ld32(tO + lane_addr + c * 32, o);
+                tmem_ld_wait();
+                if (qi < L) {
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) {
+                        uint4 u;
+                        u.x = pack2<F16>(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+                        u.y = pack2<F16>(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+                        u.z = pack2<F16>(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+                        u.w = pack2<F16>(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+                        *reinterpret_cast<uint4*>(out + c * 32 + v * 8) = u;
+                    }
+                }
+            }
+        }
+    }
+
+    // teardown: every MMA has completed (drained by the issuer) and every
+    // TMEM access of the softmax warps is done before TMEM is freed
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, S::TMEM_COLS);
+    }
+}
+
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn_attn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+    return fn;
+}
+
+// [rows x cols] 16-bit matrix with row stride ld elements; boxes of 64
+// columns (128 bytes, 128-byte swizzle) x box_rows.
+static bool make_rows_tmap(CUtensorMap* map, const void* base, bool f16, uint64_t rows, uint64_t cols, uint64_t ld,
+                           uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn_attn();
+    if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * 2) % 16 != 0) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+              const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int D, bool F16, bool PLAIN>
+static cudaError_t launch_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                             const AttnParams& p, int nseq, int max_len, int heads, int* status, cudaStream_t st) {
+    constexpr int smem = AttnTc<D>::SMEM;
+    auto kern = attention_tc_kernel<D, F16, PLAIN>;
+    static unsigned configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 32 || !(__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & (1u << dev))) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        if (dev < 32) __atomic_fetch_or(&configured, 1u << dev, __ATOMIC_RELEASE);
+    }
+    const dim3 grid((max_len + 127) / 128, heads, nseq);
+    kern<<<grid, AttnTc<D>::THREADS, smem, st>>>(tq, tk, tv, p, status);
+    return cudaGetLastError();
+}
+
+bool attention_tc_supported(int head_dim) { return head_dim == 64 || head_dim == 128; }
+
+cudaError_t launch_attention_tc(const AttnParams& p, int T, int nseq, int max_len, int heads, int kv_heads,
+                                int head_dim, int* status, cudaStream_t st) {
+    if (nseq <= 0 || T <= 0) return cudaSuccess;
+    const int D = head_dim;
+    if (!attention_tc_supported(D) || !status) return cudaErrorInvalidValue;
+    const int bkv = 64;
+    CUtensorMap tq, tk, tv;
+    if (!make_rows_tmap(&tq, p.q, p.f16, T, static_cast<uint64_t>(heads) * D, p.ldq, 128) ||
+        !make_rows_tmap(&tk, p.k, p.f16, T, static_cast<uint64_t>(kv_heads) * D, p.ldk, bkv) ||
+        !make_rows_tmap(&tv, p.v, p.f16, T, static_cast<uint64_t>(kv_heads) * D, p.ldv, bkv))
+        return cudaErrorInvalidValue;
+    const bool plain = !p.bias && p.rel_lo <= -max_len && p.rel_hi >= max_len;
+#define RG_TC_CASE(DD, FF, PP)                                                              \
+    if (D == DD && p.f16 == FF && plain == PP)                                              \
+        return launch_tc<DD, FF, PP>(tq, tk, tv, p, nseq, max_len, heads, status, st);
+    RG_TC_CASE(64, false, true)
+    RG_TC_CASE(64, false, false)
+    RG_TC_CASE(64, true, true)
+    RG_TC_CASE(64, true, false)
+    RG_TC_CASE(128, false, true)
+    RG_TC_CASE(128, false, false)
+    RG_TC_CASE(128, true, true)
+    RG_TC_CASE(128, true, false)
+#undef RG_TC_CASE
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace rg

@@ -58,6 +58,60 @@ __device__ __forceinline__ float gelu_as(float x) {
     return fmaf(hx, copysignf(erf_abs, x), hx);
 }
 
+// ---- packed fp32 pairs (sm_100 f32x2 ALU ops: two lanes of work per issue)
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2split(uint64_t r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// The same A&S 7.1.26 GELU on a pair, with the polynomial on f32x2 and the
+// result in the cancellation-free form: with pe = p(t) exp(-a^2),
+// 0.5 x (1 + erf) = x - 0.5 x pe for x >= 0 and 0.5 x pe for x < 0.
+__device__ __forceinline__ void gelu_as2(float& x0, float& x1) {
+    const uint64_t a = f2(fabsf(x0) * 0.70710678118654752f, fabsf(x1) * 0.70710678118654752f);
+    float d0, d1;
+    f2split(fma2(a, f2(0.3275911f, 0.3275911f), f2(1.0f, 1.0f)), d0, d1);
+    const uint64_t t = f2(rcp_approx(d0), rcp_approx(d1));
+    uint64_t p = fma2(t, f2(1.061405429f, 1.061405429f), f2(-1.453152027f, -1.453152027f));
+    p = fma2(p, t, f2(1.421413741f, 1.421413741f));
+    p = fma2(p, t, f2(-0.284496736f, -0.284496736f));
+    p = fma2(p, t, f2(0.254829592f, 0.254829592f));
+    p = mul2(p, t);
+    float z0, z1;
+    f2split(mul2(mul2(a, a), f2(-1.4426950408889634f, -1.4426950408889634f)), z0, z1);
+    const uint64_t xs = f2(x0, x1);
+    const uint64_t q = mul2(mul2(xs, f2(0.5f, 0.5f)), mul2(p, f2(ex2_approx(z0), ex2_approx(z1))));
+    float q0, q1, r0, r1;
+    f2split(q, q0, q1);
+    f2split(fma2(q, f2(-1.0f, -1.0f), xs), r0, r1);
+    x0 = x0 >= 0.f ? r0 : q0;
+    x1 = x1 >= 0.f ? r1 : q1;
+}
+
 // SiLU x * sigmoid(x) (tensor.go:477-481 computes it through a float64 exp).
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 // tanh-approximation GELU (tensor.go:490-497; HF gelu_pytorch_tanh).
@@ -424,13 +478,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             w[4 * i + 3] *= qb.w;
                         }
                     }
+                    if constexpr (EPI == kEpiGluGeluErf) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        float a = v[i];
-                        if constexpr (EPI == kEpiGluSilu) a = silu_f(a);
-                        else if constexpr (EPI == kEpiGluGeluErf) a = gelu_as(a);
-                        else a = gelu_tanh_f(a);
-                        v[i] = a * w[i];
+                        for (int i = 0; i < 32; i += 2) {
+                            gelu_as2(v[i], v[i + 1]);
+                            f2split(mul2(f2(v[i], v[i + 1]), f2(w[i], w[i + 1])), v[i], v[i + 1]);
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            float a = v[i];
+                            if constexpr (EPI == kEpiGluSilu) a = silu_f(a);
+                            else a = gelu_tanh_f(a);
+                            v[i] = a * w[i];
+                        }
                     }
                 }
                 // (acc * row scale) * column scale + bias: the reference's
@@ -451,15 +512,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const float4 q = __ldg(bp + i);
-                        v[4 * i] += q.x;
-                        v[4 * i + 1] += q.y;
-                        v[4 * i + 2] += q.z;
-                        v[4 * i + 3] += q.w;
+                        f2split(add2(f2(v[4 * i], v[4 * i + 1]), f2(q.x, q.y)), v[4 * i], v[4 * i + 1]);
+                        f2split(add2(f2(v[4 * i + 2], v[4 * i + 3]), f2(q.z, q.w)), v[4 * i + 2], v[4 * i + 3]);
                     }
                 }
                 if constexpr (EPI == kEpiBiasGelu) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = gelu_as(v[i]);
+                    for (int i = 0; i < 32; i += 2) gelu_as2(v[i], v[i + 1]);
                 }
                 if constexpr (EPI == kEpiBiasRes) {
                     if (!mbar_wait(&rbar[b], (rphase >> b) & 1, args.status, abort_flag)) {
@@ -471,10 +530,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const float4 x = *reinterpret_cast<const float4*>(box + swz(lane, i, 128));
-                        v[4 * i] = x.x + v[4 * i];
-                        v[4 * i + 1] = x.y + v[4 * i + 1];
-                        v[4 * i + 2] = x.z + v[4 * i + 2];
-                        v[4 * i + 3] = x.w + v[4 * i + 3];
+                        f2split(add2(f2(x.x, x.y), f2(v[4 * i], v[4 * i + 1])), v[4 * i], v[4 * i + 1]);
+                        f2split(add2(f2(x.z, x.w), f2(v[4 * i + 2], v[4 * i + 3])), v[4 * i + 2], v[4 * i + 3]);
                     }
                 }
                 if constexpr (F32OUT) {
@@ -485,10 +542,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 } else {
                     if constexpr (F16) {
                         // fp16 outputs fail loudly instead of turning into inf
-                        bool bad = false;
+                        // (fp32 accumulators cannot overflow to NaN here)
+                        float amax = 0.f;
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) bad |= !(fabsf(v[i]) <= 65504.0f);
-                        if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(args.status, kStatusF16Overflow);
+                        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+                        if (__any_sync(0xffffffffu, amax > 65504.0f) && lane == 0)
+                            atomicOr(args.status, kStatusF16Overflow);
                     }
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {

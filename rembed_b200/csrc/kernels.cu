@@ -729,6 +729,13 @@ static cudaError_t launch_attention_d(const AttnParams& p, int nseq, int max_len
 }
 
 cudaError_t launch_attention(const AttnParams& p, int nseq, int max_len, int heads, int head_dim, cudaStream_t st) {
+    if (attention_tc_supported(head_dim) && p.status)
+        return launch_attention_tc(p, p.T, nseq, max_len, heads, p.kv_heads, head_dim, p.status, st);
+    return launch_attention_mma(p, nseq, max_len, heads, head_dim, st);
+}
+
+cudaError_t launch_attention_mma(const AttnParams& p, int nseq, int max_len, int heads, int head_dim,
+                                 cudaStream_t st) {
     if (nseq <= 0) return cudaSuccess;
     switch (head_dim) {
     case 32: return launch_attention_d<32>(p, nseq, max_len, heads, st);

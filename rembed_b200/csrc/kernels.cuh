@@ -97,8 +97,18 @@ struct AttnParams {
     int bias_off;
     uint16_t* out;
     int ldo;
+    int T;         // rows of the packed buffers (tensor-map extent)
+    int kv_heads;  // key/value heads (heads / group)
+    int* status;   // device status word (bounded waits)
 };
+// Head dims 64 and 128 run the tcgen05 kernel (attention_tc.cu); 32 and 256
+// the mma.sync kernel.
 cudaError_t launch_attention(const AttnParams& p, int nseq, int max_len, int heads, int head_dim, cudaStream_t st);
+bool attention_tc_supported(int head_dim);
+cudaError_t launch_attention_tc(const AttnParams& p, int T, int nseq, int max_len, int heads, int kv_heads,
+                                int head_dim, int* status, cudaStream_t st);
+// The mma.sync kernel for any supported head dim (32, 64, 128, 256).
+cudaError_t launch_attention_mma(const AttnParams& p, int nseq, int max_len, int heads, int head_dim, cudaStream_t st);
 
 // Pooling + L2 + Matryoshka truncation (bert.go:657-703, rembed.go:441-448):
 // out[nseq x dim].

@@ -953,6 +953,9 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
             ap.bias_off = r.rel_bias_off;
             ap.out = r.ctx;
             ap.ldo = m.qd;
+            ap.T = T;
+            ap.kv_heads = m.nkv;
+            ap.status = r.d_status;
             check(rg::launch_attention(ap, nseq, max_len, m.nq, dh, st), "attention launch");
             ++launches;
         }
