@@ -171,7 +171,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     constexpr bool S8 = KIND == static_cast<int>(GemmKind::kS8);
     constexpr bool W8 = KIND == static_cast<int>(GemmKind::kW8);
     constexpr bool F16 = KIND == static_cast<int>(GemmKind::kF16) || W8;  // fp16 operands and output
-    constexpr bool CSCALE = S8 || W8;                                      // per-column dequant scales
+    constexpr bool CSCALE = true;  // per-column dequant scales, whenever args.col_scale is set
     using S = GemmShape<BN, W8>;
     constexpr int STAGES = S::STAGES;
     constexpr int A_BYTES = S::A_BYTES, B_BYTES = S::B_BYTES, B8_BYTES = S::B8_BYTES;

@@ -8,6 +8,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "kernels.cuh"
 #include "act16.cuh"
 #include "sm100.cuh"
@@ -428,6 +430,40 @@ cudaError_t launch_dense_f32(const float* x, const float* w, float* out, int M, 
     if (M <= 0) return cudaSuccess;
     const dim3 grid((N + 31) / 32, (M + 31) / 32);
     dense_f32_kernel<<<grid, 256, 0, st>>>(x, w, out, M, N, K);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// int8 -> fp16 widening, 16 weights per thread: (q + 128) placed in the low
+// mantissa byte of 1024.0 is exactly 1024 + q + 128; subtracting 1152 leaves q.
+__global__ void __launch_bounds__(256) widen_s8_f16_kernel(const uint4* __restrict__ w, size_t n16,
+                                                          uint4* __restrict__ out) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n16;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const uint4 u = __ldg(w + i);
+        const uint32_t in[4] = {u.x, u.y, u.z, u.w};
+        uint32_t o[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t b = in[k] ^ 0x80808080u;
+            uint32_t lo, hi;
+            asm("prmt.b32 %0, %1, %2, %3;" : "=r"(lo) : "r"(b), "r"(0x64646464u), "r"(0x4140u));
+            asm("prmt.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(b), "r"(0x64646464u), "r"(0x4342u));
+            asm("sub.f16x2 %0, %1, %2;" : "=r"(o[2 * k]) : "r"(lo), "r"(0x64806480u));
+            asm("sub.f16x2 %0, %1, %2;" : "=r"(o[2 * k + 1]) : "r"(hi), "r"(0x64806480u));
+        }
+        out[2 * i] = make_uint4(o[0], o[1], o[2], o[3]);
+        out[2 * i + 1] = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+}
+
+cudaError_t launch_widen_s8_f16(const int8_t* w, size_t n, uint16_t* out, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    if (n % 16 != 0 || (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+        return cudaErrorInvalidValue;
+    const size_t n16 = n / 16;
+    const int grid = static_cast<int>(std::min<size_t>((n16 + 255) / 256, 148 * 8));
+    widen_s8_f16_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const uint4*>(w), n16, reinterpret_cast<uint4*>(out));
     return cudaGetLastError();
 }
 

@@ -73,6 +73,11 @@ cudaError_t launch_qk_norm_rope(const QkRopeParams& p, int head_dim, cudaStream_
 // out[M x N] = x[M x K] . W[N x K]^T in fp32 (the Gemma Dense head).
 cudaError_t launch_dense_f32(const float* x, const float* w, float* out, int M, int N, int K, cudaStream_t st);
 
+// int8 -> fp16, exact (weight-only int8 at large batch: one layer's weight
+// widened just before its GEMM; the per-channel scale stays in the GEMM
+// epilogue).  n must be a multiple of 16, both pointers 16-byte aligned.
+cudaError_t launch_widen_s8_f16(const int8_t* w, size_t n, uint16_t* out, cudaStream_t st);
+
 // Per-row symmetric int8 quantisation of a bf16 [T x K] matrix
 // (QuantizeRowU8 with the +128 offset removed: q in [-128, 127]).
 cudaError_t launch_quantize_rows(const __nv_bfloat16* x, int T, int K, int8_t* q, float* scale, cudaStream_t st);

@@ -68,8 +68,17 @@ struct DevDense {
     void* w = nullptr;
     float* scale = nullptr;
     float* bias = nullptr;
-    CUtensorMap tmap[3];  // for tile widths 256, 192, 128 (only widths dividing N are valid)
+    CUtensorMap tmap[3];    // for tile widths 256, 192, 128 (only widths dividing N are valid)
+    CUtensorMap tmap16[3];  // weight-only int8: the same shape over the replica's fp16 widening scratch
 };
+
+// Weight-only int8 GEMMs with at least this many rows widen the layer's
+// int8 weight to fp16 first (about 3 bytes of traffic per weight, a few
+// microseconds) and run the fp16 kernel: at this size the GEMM is
+// tensor-bound and the in-mainloop converter warps would set its pace.
+// Smaller GEMMs are weight-bandwidth-bound and keep the int8 weights
+// end to end (GemmKind::kW8).
+constexpr int kW8WidenRows = 4096;
 
 int bn_index(int bn) { return bn == 256 ? 0 : (bn == 192 ? 1 : 2); }
 constexpr int kBlockWidths[3] = {256, 192, 128};
@@ -114,6 +123,8 @@ struct Replica {
     int32_t* d_cu = nullptr;
     float* d_out = nullptr;
     int* d_status = nullptr;
+    uint16_t* w16 = nullptr;  // weight-only int8: fp16 widening scratch (largest weight)
+    size_t w16_elems = 0;
     int64_t* h_ids = nullptr;
     int32_t* h_cu = nullptr;
     float* h_out = nullptr;
@@ -355,6 +366,14 @@ DevDense make_dense(Replica& r, int mode, const float* w, const float* bias, int
         d.scale = dev_upload(r, s.data(), N);
     }
     const int eb = (mode == RG_MODE_BF16 || mode == RG_MODE_F16) ? 2 : 1;
+    if (mode == RG_MODE_INT8_W && n > r.w16_elems) {
+        // the widening scratch grows to the largest weight (sized before any
+        // tensor map over it is made: make_dense runs for every weight first)
+        if (r.w16) cudaFree(r.w16);
+        r.w16 = nullptr;
+        check(cudaMalloc(&r.w16, n * 2), "cudaMalloc");
+        r.w16_elems = n;
+    }
     for (int i = 0; i < 3; ++i) {
         if (N % kBlockWidths[i] != 0) continue;
         const uint32_t box_rows = rg::gemm_w_box_rows(kBlockWidths[i]);
@@ -618,6 +637,19 @@ void finalize_decoder(rg_ctx* c, Replica& r) {
     }
 }
 
+// Weight-only int8: tensor maps of each weight's shape over the fp16
+// widening scratch (made once the scratch has its final size).
+void make_widen_maps(Replica& r) {
+    for (DevLayer& L : r.layers)
+        for (DevDense* d : {&L.qkv, &L.o, &L.ffn1, &L.ffn2})
+            for (int i = 0; i < 3; ++i) {
+                if (d->N % kBlockWidths[i] != 0) continue;
+                if (!rg::make_kmajor_tmap(&d->tmap16[i], r.w16, 2, d->N, d->K, d->K,
+                                          rg::gemm_w_box_rows(kBlockWidths[i])))
+                    fail("cuTensorMapEncodeTiled failed for a [%d x %d] widened weight", d->N, d->K);
+            }
+}
+
 void free_workspace(Replica& r) {
     for (void* p : r.ws) cudaFree(p);
     r.ws.clear();
@@ -786,9 +818,22 @@ void gemm(Replica& r, int mode, const CUtensorMap& tmA, const DevDense& w, int M
     const double ob = (epi == rg::kEpiBiasRes || epi == rg::kEpiBiasF32) ? 4.0 : (rg::epi_is_glu(epi) ? 1.0 : 2.0);
     const double bytes = eb * (double(M) * w.K + double(w.N) * w.K) + ob * double(M) * w.N +
                          (epi == rg::kEpiBiasRes ? 4.0 * double(M) * w.N : 0.0);
-    ProfScope ps(r, st, RG_KC_GEMM, 2.0 * M * w.N * w.K, bytes);
     const int bn = rg::gemm_block_n(M, w.N, r.num_sms, rg::epi_is_glu(epi));
     if (bn == 0) fail("no GEMM tile width divides N=%d", w.N);
+    if (kind == rg::GemmKind::kW8 && M >= kW8WidenRows) {
+        {
+            ProfScope pw(r, st, RG_KC_QUANT, 0.0, 3.0 * double(w.N) * w.K);
+            check(rg::launch_widen_s8_f16(static_cast<const int8_t*>(w.w), static_cast<size_t>(w.N) * w.K, r.w16, st),
+                  "widen launch");
+            ++launches;
+        }
+        ProfScope ps(r, st, RG_KC_GEMM, 2.0 * M * w.N * w.K, bytes);
+        check(rg::gemm_launch(rg::GemmKind::kF16, epi, bn, tmA, w.tmap16[bn_index(bn)], a, r.num_sms, st),
+              "gemm launch");
+        ++launches;
+        return;
+    }
+    ProfScope ps(r, st, RG_KC_GEMM, 2.0 * M * w.N * w.K, bytes);
     check(rg::gemm_launch(kind, epi, bn, tmA, w.tmap[bn_index(bn)], a, r.num_sms, st), "gemm launch");
     ++launches;
 }
@@ -1231,6 +1276,7 @@ int rg_finalize(rg_ctx* c, char** err) {
                 finalize_bert(c, *r);
             else
                 finalize_decoder(c, *r);
+            if (c->mode == RG_MODE_INT8_W) make_widen_maps(*r);
         }
         c->host.clear();
         c->finalized = true;
@@ -1395,6 +1441,7 @@ void rg_free(rg_ctx* c) {
         free_workspace(*r);
         for (cudaEvent_t e : r->ev_pool) cudaEventDestroy(e);
         for (void* p : r->allocs) cudaFree(p);
+        if (r->w16) cudaFree(r->w16);
         if (r->h_status) cudaFreeHost(r->h_status);
         if (r->stream) cudaStreamDestroy(r->stream);
         delete r;

@@ -114,3 +114,23 @@ def test_fp16_activation_overflow_is_reported(cuda):
     gpu = Embedder(cfg, w, fp16=False)
     assert np.isfinite(gpu.embed_packed(ids, cu)).all()
     gpu.close()
+
+
+def test_int8_weights_large_batch_widened_path(cuda):
+    """At >= 4096 tokens the weight-only int8 GEMMs widen each int8 weight to
+    fp16 just before the GEMM instead of converting inside the mainloop; the
+    arithmetic is the same (exact integer weights, fp16 activations, fp32
+    accumulation, per-channel scale in the epilogue), so a sequence embeds
+    bit-identically on either path, and the batch matches the oracle."""
+    cfg = synth.preset("bge-base")
+    w = synth.make_weights(cfg, seed=48)
+    ids, cu = synth.make_batch(cfg, 40, 128, 128, seed=49)  # 5120 tokens
+    gpu = Embedder(cfg, w, int8=True)
+    big = gpu.embed_packed(ids, cu)
+    small = gpu.embed_packed(ids[:cu[6]], cu[:7])  # 768 tokens: in-mainloop int8 path
+    gpu.close()
+    assert np.array_equal(big[:6], small)
+    want = oracle.OracleModel(cfg, w, oracle.QUANT_WEIGHTS).embed(ids[:cu[8]], cu[:9])
+    cos = cosines(big[:8], want)
+    print(f"\n[parity] bge-base w-int8 widened path: min cos {cos.min():.7f}")
+    assert cos.min() >= COS_INT8_W
