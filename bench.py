@@ -61,7 +61,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="bge-base-b256xL128")
-    ap.add_argument("--mode", choices=list(MODES), default="f16")
+    ap.add_argument("--mode", choices=list(MODES), default="bf16")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target length of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()

@@ -106,7 +106,7 @@ cudaError_t gemm_launch(GemmKind kind, int epi, int block_n, const CUtensorMap& 
     if (args.M <= 0) return cudaSuccess;
     const int kel = kind == GemmKind::kS8 ? 128 : 64;
     if (args.K % kel != 0 || args.K <= 0 || block_n <= 0 || args.N % block_n != 0) return cudaErrorInvalidValue;
-    const bool f32out = epi == kEpiBiasRes || epi == kEpiBiasF32;
+    const bool f32out = epi_has_residual(epi) || epi == kEpiBiasF32;
     const bool f16out = kind == GemmKind::kF16 || kind == GemmKind::kW8;
     const bool glu = epi_is_glu(epi);
     // GLU tiles pair 32-column chunks inside each epilogue warp's columns.
@@ -114,7 +114,8 @@ cudaError_t gemm_launch(GemmKind kind, int epi, int block_n, const CUtensorMap& 
     CUtensorMap tmOut, tmRes;
     if (!make_epilogue_tmap(&tmOut, args.out, f32out, f16out, args.M, glu ? args.N / 2 : args.N, args.ld_out))
         return cudaErrorInvalidValue;
-    if (epi == kEpiBiasRes) {
+    if (epi == kEpiBiasResLN && (!args.ln_stats || !args.ln_g || !args.ln_b)) return cudaErrorInvalidValue;
+    if (epi_has_residual(epi)) {
         if (!args.residual || !make_epilogue_tmap(&tmRes, args.residual, true, false, args.M, args.N, args.N))
             return cudaErrorInvalidValue;
     } else {

@@ -19,15 +19,23 @@ enum Epilogue : int {
     kEpiGluSilu = 4,      // silu(a) * b   (qwen3.go:530-539, nomic.go:232-242)
     kEpiGluGeluErf = 5,   // gelu(a) * b   (modernbert.go:292-301)
     kEpiGluGeluTanh = 6,  // gelu_tanh(a) * b (gemma3.go:365-374)
+    // + bias, + LayerNorm(fp32 residual) rebuilt on load from the row's
+    // (mean, rstd) and the norm's gain/bias: (r - mean) * rstd * g + b, the
+    // LayerNorm output of a post-norm stack that was never written out in
+    // fp32 (bert.go:905-918)                                   -> fp32 (out may alias the residual)
+    kEpiBiasResLN = 7,
 };
-inline bool epi_is_glu(int epi) { return epi >= kEpiGluSilu; }
+inline bool epi_is_glu(int epi) { return epi >= kEpiGluSilu && epi <= kEpiGluGeluTanh; }
+inline bool epi_has_residual(int epi) { return epi == kEpiBiasRes || epi == kEpiBiasResLN; }
 
 struct GemmArgs {
     int M, N, K;
     const float* bias;       // [N] or nullptr
     const float* col_scale;  // [N] or nullptr: int8 weight dequant scale
     const float* row_scale;  // [M] or nullptr: int8 activation dequant scale
-    const float* residual;   // [M x N] fp32, kEpiBiasRes only
+    const float* residual;   // [M x N] fp32, kEpiBiasRes / kEpiBiasResLN
+    const float2* ln_stats;  // [M] (mean, rstd), kEpiBiasResLN
+    const float *ln_g, *ln_b;  // [N], kEpiBiasResLN
     void* out;               // [M x ld_out], 16-bit (bf16 / fp16 by kind) or fp32
     int ld_out;
     int* status;             // device status word

@@ -224,7 +224,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
         tma_prefetch_desc(&tmOut);
-        if (EPI == kEpiBiasRes) tma_prefetch_desc(&tmRes);
+        if (EPI == kEpiBiasRes || EPI == kEpiBiasResLN) tma_prefetch_desc(&tmRes);
     }
     if (warp == 2) {
         tmem_alloc_pair(tmem_slot, S::TMEM_COLS);
@@ -379,7 +379,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // (thread = row), dequant / bias / GELU / + residual in registers,
         // the row written into a swizzled staging box, one TMA store per box.
         // The fp32 residual box arrives by TMA one chunk ahead.
-        constexpr bool F32OUT = EPI == kEpiBiasRes || EPI == kEpiBiasF32;
+        constexpr bool RES = EPI == kEpiBiasRes || EPI == kEpiBiasResLN;
+        constexpr bool F32OUT = RES || EPI == kEpiBiasF32;
         const int ew = warp - 4;
         const int quarter = warp & 3;
         const int half = ew >> 2;
@@ -391,7 +392,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         constexpr int CHUNKS = HALF / kChunk;
         // Issue the residual box of chunk c of tile t into buffer b (lane 0).
         auto load_residual = [&](int t, int c, int b) {
-            if constexpr (EPI == kEpiBiasRes) {
+            if constexpr (RES) {
                 if (t >= num_tiles) return;
                 const int row0 = (t / n_tiles) * 256 + static_cast<int>(rank) * 128 + quarter * 32;
                 const int col0 = (t % n_tiles) * BN + half * HALF + c * kChunk;
@@ -413,9 +414,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if constexpr (S8) {
                 if (args.row_scale && row0 + lane < args.M) rs = args.row_scale[row0 + lane];
             }
+            float2 lnst = make_float2(0.f, 1.f);  // this row's (mean, rstd) for kEpiBiasResLN
+            if constexpr (EPI == kEpiBiasResLN) {
+                if (row0 + lane < args.M) lnst = args.ln_stats[row0 + lane];
+            }
             const uint32_t taddr =
                 tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + half * HALF;
-            constexpr bool GLU = EPI >= kEpiGluSilu;
+            constexpr bool GLU = EPI >= kEpiGluSilu && EPI <= kEpiGluGeluTanh;
             constexpr int STEP = GLU ? 2 : 1;  // accumulator chunks per output box
 #pragma unroll 1
             for (int c = 0; c < CHUNKS; c += STEP, ++k) {
@@ -424,7 +429,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const int col0 = n_blk * BN + half * HALF + c * kChunk;  // accumulator column
                 const int ocol0 = GLU ? col0 / 2 : col0;                  // output column
                 if (lane == 0) {
-                    if constexpr (EPI == kEpiBiasRes) {
+                    if constexpr (RES) {
                         // The other buffer's store (previous chunk) has read
                         // its box: it can take the next chunk's residual.
                         bulk_wait_read<0>();
@@ -520,7 +525,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) gelu_as2(v[i], v[i + 1]);
                 }
-                if constexpr (EPI == kEpiBiasRes) {
+                if constexpr (RES) {
                     if (!mbar_wait(&rbar[b], (rphase >> b) & 1, args.status, abort_flag)) {
                         ok = false;
                         break;
@@ -529,7 +534,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     rpending &= ~(1u << b);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        const float4 x = *reinterpret_cast<const float4*>(box + swz(lane, i, 128));
+                        float4 x = *reinterpret_cast<const float4*>(box + swz(lane, i, 128));
+                        if constexpr (EPI == kEpiBiasResLN) {
+                            // the LayerNorm kernel's own arithmetic: (x - mean) * rstd * g + b
+                            const float4 g = __ldg(reinterpret_cast<const float4*>(args.ln_g + col0) + i);
+                            const float4 bb = __ldg(reinterpret_cast<const float4*>(args.ln_b + col0) + i);
+                            x.x = (x.x - lnst.x) * lnst.y * g.x + bb.x;
+                            x.y = (x.y - lnst.x) * lnst.y * g.y + bb.y;
+                            x.z = (x.z - lnst.x) * lnst.y * g.z + bb.z;
+                            x.w = (x.w - lnst.x) * lnst.y * g.w + bb.w;
+                        }
                         f2split(add2(f2(x.x, x.y), f2(v[4 * i], v[4 * i + 1])), v[4 * i], v[4 * i + 1]);
                         f2split(add2(f2(x.z, x.w), f2(v[4 * i + 2], v[4 * i + 3])), v[4 * i + 2], v[4 * i + 3]);
                     }
@@ -654,6 +668,7 @@ static cudaError_t dispatch_epi(int epi, const CUtensorMap& tmA, const CUtensorM
     case kEpiGluSilu: return launch_one<BN, KIND, kEpiGluSilu>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
     case kEpiGluGeluErf: return launch_one<BN, KIND, kEpiGluGeluErf>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
     case kEpiGluGeluTanh: return launch_one<BN, KIND, kEpiGluGeluTanh>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
+    case kEpiBiasResLN: return launch_one<BN, KIND, kEpiBiasResLN>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -39,7 +39,8 @@ __device__ __forceinline__ float warp_max(float v) {
 // Returns true (in every lane) if an fp16 output overflowed or was NaN.
 template <int NV, bool RMS, bool F16>
 __device__ __forceinline__ bool norm_finish(float (&v)[NV][4], const float* g, const float* b, float eps, int H,
-                                            float* out32, uint16_t* outb, int8_t* outq, float* outqs, int lane) {
+                                            float* out32, uint16_t* outb, int8_t* outq, float* outqs, int lane,
+                                            float2* stats = nullptr) {
     float mean = 0.f, inv = 1.f;
     if (!g) {
         // identity (ModernBERT's layer-0 attention norm): only the stores
@@ -65,6 +66,7 @@ __device__ __forceinline__ bool norm_finish(float (&v)[NV][4], const float* g, c
             }
         inv = 1.0f / sqrtf(warp_sum(q) / static_cast<float>(H) + eps);
     }
+    if (stats && lane == 0) *stats = make_float2(mean, inv);
     float amax = 0.f;
 #pragma unroll
     for (int c = 0; c < NV; ++c) {
@@ -212,8 +214,9 @@ __global__ void __launch_bounds__(256) norm_kernel(NormParams p) {
         v[c][2] = a.z;
         v[c][3] = a.w;
     }
-    const bool overflow = norm_finish<NV, RMS, F16>(v, p.g, p.b, p.eps, p.H, p.out32 ? p.out32 + off : nullptr, p.outb ? p.outb + off : nullptr,
-                         p.outq ? p.outq + off : nullptr, p.outqs ? p.outqs + t : nullptr, lane);
+    const bool overflow = norm_finish<NV, RMS, F16>(v, p.g, p.b, p.eps, p.H, p.out32 ? p.out32 + off : nullptr,
+                                                    p.outb ? p.outb + off : nullptr, p.outq ? p.outq + off : nullptr,
+                                                    p.outqs ? p.outqs + t : nullptr, lane, p.stats ? p.stats + t : nullptr);
     if (overflow && p.status && lane == 0) atomicOr(p.status, kStatusF16Overflow);
 }
 

@@ -45,7 +45,9 @@ struct NormParams {
     bool f16;
     int8_t* outq;
     float* outqs;
-    int* status;  // optional: kStatusF16Overflow if an fp16 output overflows
+    int* status;    // optional: kStatusF16Overflow if an fp16 output overflows
+    float2* stats;  // optional: the row's (mean, rstd) (LayerNorm), for a consumer that
+                    // rebuilds the fp32 output on load instead of reading out32
 };
 cudaError_t launch_norm(const NormParams& p, bool rms, cudaStream_t st);
 cudaError_t launch_ln(const float* y32, const float* g, const float* b, float eps, int T, int H, float* x32,

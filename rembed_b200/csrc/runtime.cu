@@ -117,6 +117,7 @@ struct Replica {
     act16 *xb = nullptr, *qkv = nullptr, *ctx = nullptr, *ffh = nullptr;
     int8_t *xq = nullptr, *ctxq = nullptr, *ffhq = nullptr;
     float *xs = nullptr, *ctxs = nullptr, *ffhs = nullptr;
+    float2* lnst = nullptr;  // post-norm: the last LayerNorm's per-row (mean, rstd)
     float *pool32 = nullptr, *head_hid = nullptr, *head_out = nullptr;  // Gemma Dense head
     int32_t* iota = nullptr;                                            // [0, 1, ..., cap_seq]
     int64_t* d_ids = nullptr;
@@ -689,6 +690,7 @@ void ensure_workspace(rg_ctx* c, Replica& r, int T, int nseq, size_t nout) {
         r.x32 = ws_alloc<float>(r, t * H);
         r.y32 = ws_alloc<float>(r, t * H);
         r.xb = ws_alloc<act16>(r, t * H);
+        r.lnst = ws_alloc<float2>(r, t);
         r.qkv = ws_alloc<act16>(r, t * m.nqkv);
         r.ctx = ws_alloc<act16>(r, t * m.qd);
         r.ffh = ws_alloc<act16>(r, t * I);
@@ -796,8 +798,12 @@ void prof_collect(Replica& r) {
 }
 
 void gemm(Replica& r, int mode, const CUtensorMap& tmA, const DevDense& w, int M, int epi, const float* row_scale,
-          const float* residual, void* out, cudaStream_t st, int& launches) {
+          const float* residual, void* out, cudaStream_t st, int& launches, const float2* ln_stats = nullptr,
+          const float* ln_g = nullptr, const float* ln_b = nullptr) {
     rg::GemmArgs a{};
+    a.ln_stats = ln_stats;
+    a.ln_g = ln_g;
+    a.ln_b = ln_b;
     a.M = M;
     a.N = w.N;
     a.K = w.K;
@@ -815,9 +821,9 @@ void gemm(Replica& r, int mode, const CUtensorMap& tmA, const DevDense& w, int M
     // Algorithmic bytes: A and W read once, output written once (+ fp32
     // residual read); FLOPs 2*M*N*K.
     const double eb = kind == rg::GemmKind::kS8 ? 1.0 : 2.0;
-    const double ob = (epi == rg::kEpiBiasRes || epi == rg::kEpiBiasF32) ? 4.0 : (rg::epi_is_glu(epi) ? 1.0 : 2.0);
+    const double ob = (rg::epi_has_residual(epi) || epi == rg::kEpiBiasF32) ? 4.0 : (rg::epi_is_glu(epi) ? 1.0 : 2.0);
     const double bytes = eb * (double(M) * w.K + double(w.N) * w.K) + ob * double(M) * w.N +
-                         (epi == rg::kEpiBiasRes ? 4.0 * double(M) * w.N : 0.0);
+                         (rg::epi_has_residual(epi) ? 4.0 * double(M) * w.N : 0.0);
     const int bn = rg::gemm_block_n(M, w.N, r.num_sms, rg::epi_is_glu(epi));
     if (bn == 0) fail("no GEMM tile width divides N=%d", w.N);
     if (kind == rg::GemmKind::kW8 && M >= kW8WidenRows) {
@@ -885,7 +891,6 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
     const bool pre = is_prenorm(arch);
     int launches = 0;
     const double Td = T, Hd = H;
-    const double row_bytes = Td * Hd * (4.0 + 4.0 + 2.0 + (s8 ? 1.0 : 0.0));
 
     // ---- embeddings
     {
@@ -932,12 +937,40 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         check(rg::launch_norm(p, rms, st), "norm launch");  // g nullptr: identity
         ++launches;
     };
-    auto post_norm = [&](const float* g, const float* b) {  // y32 -> LN -> x32 (+ A operand)
-        ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, row_bytes);
-        check(rg::launch_ln(r.y32, g, b, eps, T, H, r.x32, r.xb, f16, s8 ? r.xq : nullptr, s8 ? r.xs : nullptr, st,
-                            r.d_status),
-              "ln launch");
+    // Post-norm stacks keep one fp32 buffer x32: a residual GEMM adds its
+    // sublayer output in place, and the LayerNorm after it writes only the
+    // next GEMM's A operand plus the row's (mean, rstd); the next residual
+    // GEMM rebuilds LN(x32) on load (kEpiBiasResLN).  res_g / res_b are the
+    // gain and bias of that pending LayerNorm (nullptr: x32 is the residual
+    // as is, i.e. the embedding output).  The stack's last LayerNorm writes
+    // x32 for pooling.
+    const float *res_g = nullptr, *res_b = nullptr;
+    auto residual_gemm = [&](const CUtensorMap& tmA, const DevDense& w, const float* row_scale) {
+        if (res_g)
+            gemm(r, mode, tmA, w, T, rg::kEpiBiasResLN, row_scale, r.x32, r.x32, st, launches, r.lnst, res_g, res_b);
+        else
+            gemm(r, mode, tmA, w, T, rg::kEpiBiasRes, row_scale, r.x32, r.x32, st, launches);
+    };
+    auto post_norm = [&](const float* g, const float* b, bool last) {
+        ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * Hd * (4.0 + 2.0 + (s8 ? 1.0 : 0.0) + (last ? 4.0 : 0.0)));
+        rg::NormParams p{};
+        p.in = r.x32;
+        p.g = g;
+        p.b = b;
+        p.eps = eps;
+        p.T = T;
+        p.H = H;
+        p.out32 = last ? r.x32 : nullptr;
+        p.outb = r.xb;
+        p.f16 = f16;
+        p.outq = s8 ? r.xq : nullptr;
+        p.outqs = s8 ? r.xs : nullptr;
+        p.status = r.d_status;
+        p.stats = last ? nullptr : r.lnst;
+        check(rg::launch_norm(p, false, st), "ln launch");
         ++launches;
+        res_g = last ? nullptr : g;
+        res_b = last ? nullptr : b;
     };
     auto quantize = [&](const act16* x, int K, int8_t* q, float* sc) {  // bf16 rows (full-int8 mode)
         ProfScope ps(r, st, RG_KC_QUANT, 0.0, Td * K * 3.0);
@@ -1006,8 +1039,8 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         }
         if (s8) quantize(r.ctx, m.qd, r.ctxq, r.ctxs);
         if (!pre) {
-            gemm(r, mode, r.tm_ctx, L.o, T, rg::kEpiBiasRes, s8 ? r.ctxs : nullptr, r.x32, r.y32, st, launches);
-            post_norm(L.ln1_g, L.ln1_b);
+            residual_gemm(r.tm_ctx, L.o, s8 ? r.ctxs : nullptr);
+            post_norm(L.ln1_g, L.ln1_b, false);
         } else if (arch == RG_ARCH_GEMMA3) {
             gemm(r, mode, r.tm_ctx, L.o, T, rg::kEpiBiasF32, s8 ? r.ctxs : nullptr, nullptr, r.y32, st, launches);
             ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * Hd * 12.0);
@@ -1022,8 +1055,8 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
              r.ffh, st, launches);
         if (s8) quantize(r.ffh, I, r.ffhq, r.ffhs);
         if (!pre) {
-            gemm(r, mode, r.tm_ffh, L.ffn2, T, rg::kEpiBiasRes, s8 ? r.ffhs : nullptr, r.x32, r.y32, st, launches);
-            post_norm(L.ln2_g, L.ln2_b);
+            residual_gemm(r.tm_ffh, L.ffn2, s8 ? r.ffhs : nullptr);
+            post_norm(L.ln2_g, L.ln2_b, li == d.num_hidden_layers - 1);
         } else if (arch == RG_ARCH_GEMMA3) {
             gemm(r, mode, r.tm_ffh, L.ffn2, T, rg::kEpiBiasF32, s8 ? r.ffhs : nullptr, nullptr, r.y32, st, launches);
             ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * Hd * 12.0);
