@@ -2,7 +2,7 @@
 """Benchmark: embeddings/sec of the rembed encoder forward pass on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload bge-base-b256xL128] [--mode f16|bf16|int8_w|int8_full]
+                    [--workload bge-base-b256xL128] [--mode bf16|f16|int8_w|int8_full|fp32]
 
 N > 1 runs under torchrun, one process per GPU.  Each rank embeds its own
 batch of the workload (data parallel, no collective on the data path:
@@ -51,6 +51,7 @@ MODES = {
     "bf16": ({"fp16": False}, "QUANT_NONE", "bf16"),
     "int8_w": ({"int8": True}, "QUANT_WEIGHTS", "s8 weights x f16"),
     "int8_full": ({"int8_activations": True}, "QUANT_FULL", "s8"),
+    "fp32": ({"strict_fp32": True}, "QUANT_NONE", "f32 (3xTF32 projections)"),
 }
 
 
@@ -97,7 +98,7 @@ def gemm_flops_per_token(cfg) -> float:
     return 2.0 * cfg.num_hidden_layers * (H * 3 * H + H * H + 2 * H * I)
 
 
-ORACLE_PATH = {"f16": "fp32", "bf16": "fp32", "int8_w": "weight-int8", "int8_full": "full int8"}
+ORACLE_PATH = {"f16": "fp32", "bf16": "fp32", "int8_w": "weight-int8", "int8_full": "full int8", "fp32": "fp32"}
 
 
 # ---------------------------------------------------------------------------

@@ -45,8 +45,11 @@ enum { RG_POOL_MEAN = 0, RG_POOL_CLS = 1, RG_POOL_LASTTOKEN = 2 };
  * (WithInt8, rembed.go:67-69): int8 weights in HBM, widened to fp16 inside
  * the GEMM mainloop, fp16 activations.  RG_MODE_INT8_FULL: int8 weights and
  * per-row int8 activations, the PackB8VNNI scheme (WithInt8Activations,
- * rembed.go:79-81). */
-enum { RG_MODE_BF16 = 0, RG_MODE_F16 = 1, RG_MODE_INT8_W = 2, RG_MODE_INT8_FULL = 3 };
+ * rembed.go:79-81).  RG_MODE_FP32: strict fp32 (the reference's own
+ * arithmetic width): fp32 activations end to end, projections as 3xTF32
+ * tensor-core GEMMs (tf32 hi/lo operand splits, fp32 accumulate), fp32
+ * attention. */
+enum { RG_MODE_BF16 = 0, RG_MODE_F16 = 1, RG_MODE_INT8_W = 2, RG_MODE_INT8_FULL = 3, RG_MODE_FP32 = 4 };
 /* Host dtypes accepted by rg_upload_weight (safetensors.go:188-209). */
 enum { RG_DTYPE_F32 = 0, RG_DTYPE_F16 = 1, RG_DTYPE_BF16 = 2 };
 /* rg_forward output kinds: pooled (Embed) or per-token hidden states

@@ -9,8 +9,7 @@
 namespace rg {
 
 template <int KIND>
-cudaError_t dispatch_kind(int block_n, int epi, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                          const CUtensorMap& tmOut, const CUtensorMap& tmRes, const GemmArgs& args, int num_sms,
+cudaError_t dispatch_kind(int block_n, int epi, const GemmMaps& m, const GemmArgs& args, int num_sms,
                           cudaStream_t stream);
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -39,7 +38,9 @@ bool make_kmajor_tmap(CUtensorMap* map, const void* base, int elem_bytes, uint64
     cuuint64_t strides[1] = {row_stride_elems * elem_bytes};
     cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / elem_bytes), box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUtensorMapDataType dt = elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    CUtensorMapDataType dt = elem_bytes == 4   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                             : elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                               : CU_TENSOR_MAP_DATA_TYPE_UINT8;
     CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
@@ -101,33 +102,55 @@ int gemm_block_n(int M, int N, int num_sms, bool glu) {
     return best;
 }
 
-cudaError_t gemm_launch(GemmKind kind, int epi, int block_n, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                        const GemmArgs& args, int num_sms, cudaStream_t stream) {
+static cudaError_t launch_impl(GemmKind kind, int epi, int block_n, GemmMaps& m, const GemmArgs& args, int num_sms,
+                               cudaStream_t stream) {
     if (args.M <= 0) return cudaSuccess;
-    const int kel = kind == GemmKind::kS8 ? 128 : 64;
+    const int kel = kind == GemmKind::kS8 ? 128 : (kind == GemmKind::kTF32x3 ? 32 : 64);
     if (args.K % kel != 0 || args.K <= 0 || block_n <= 0 || args.N % block_n != 0) return cudaErrorInvalidValue;
-    const bool f32out = epi_has_residual(epi) || epi == kEpiBiasF32;
+    const bool f32out = epi_has_residual(epi) || epi == kEpiBiasF32 || kind == GemmKind::kTF32x3;
     const bool f16out = kind == GemmKind::kF16 || kind == GemmKind::kW8;
     const bool glu = epi_is_glu(epi);
     // GLU tiles pair 32-column chunks inside each epilogue warp's columns.
     if (glu && (block_n == 192 || args.N % 64 != 0)) return cudaErrorInvalidValue;
-    CUtensorMap tmOut, tmRes;
-    if (!make_epilogue_tmap(&tmOut, args.out, f32out, f16out, args.M, glu ? args.N / 2 : args.N, args.ld_out))
+    if (!make_epilogue_tmap(&m.out, args.out, f32out, f16out, args.M, glu ? args.N / 2 : args.N, args.ld_out))
         return cudaErrorInvalidValue;
     if (epi == kEpiBiasResLN && (!args.ln_stats || !args.ln_g || !args.ln_b)) return cudaErrorInvalidValue;
     if (epi_has_residual(epi)) {
-        if (!args.residual || !make_epilogue_tmap(&tmRes, args.residual, true, false, args.M, args.N, args.N))
+        if (!args.residual || !make_epilogue_tmap(&m.res, args.residual, true, false, args.M, args.N, args.N))
             return cudaErrorInvalidValue;
     } else {
-        tmRes = tmOut;  // unused
+        m.res = m.out;  // unused
     }
     switch (kind) {
-    case GemmKind::kBF16: return dispatch_kind<0>(block_n, epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case GemmKind::kS8: return dispatch_kind<1>(block_n, epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case GemmKind::kF16: return dispatch_kind<2>(block_n, epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case GemmKind::kW8: return dispatch_kind<3>(block_n, epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream);
+    case GemmKind::kBF16: return dispatch_kind<0>(block_n, epi, m, args, num_sms, stream);
+    case GemmKind::kS8: return dispatch_kind<1>(block_n, epi, m, args, num_sms, stream);
+    case GemmKind::kF16: return dispatch_kind<2>(block_n, epi, m, args, num_sms, stream);
+    case GemmKind::kW8: return dispatch_kind<3>(block_n, epi, m, args, num_sms, stream);
+    case GemmKind::kTF32x3: return dispatch_kind<4>(block_n, epi, m, args, num_sms, stream);
     default: return cudaErrorInvalidValue;
     }
+}
+
+cudaError_t gemm_launch(GemmKind kind, int epi, int block_n, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                        const GemmArgs& args, int num_sms, cudaStream_t stream) {
+    if (kind == GemmKind::kTF32x3) return cudaErrorInvalidValue;  // needs the remainder maps
+    GemmMaps m;
+    m.a = tmA;
+    m.b = tmB;
+    m.a2 = tmA;  // unused
+    m.b2 = tmB;
+    return launch_impl(kind, epi, block_n, m, args, num_sms, stream);
+}
+
+cudaError_t gemm_launch_tf32x3(int epi, int block_n, const CUtensorMap& tmA, const CUtensorMap& tmA2,
+                               const CUtensorMap& tmB, const CUtensorMap& tmB2, const GemmArgs& args, int num_sms,
+                               cudaStream_t stream) {
+    GemmMaps m;
+    m.a = tmA;
+    m.b = tmB;
+    m.a2 = tmA2;
+    m.b2 = tmB2;
+    return launch_impl(GemmKind::kTF32x3, epi, block_n, m, args, num_sms, stream);
 }
 
 }  // namespace rg

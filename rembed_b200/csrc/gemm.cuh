@@ -47,11 +47,20 @@ struct GemmArgs {
 //   kF16:  fp16 A and W, fp16 output.
 //   kW8:   fp16 A, int8 W (column scales) widened to fp16 in shared memory
 //          inside the mainloop, fp16 output.
-enum class GemmKind : int { kBF16 = 0, kS8 = 1, kF16 = 2, kW8 = 3 };
+//   kTF32x3: fp32 A and W as tf32-exact hi parts plus fp32 remainders,
+//          kind::tf32 over K three times (A_hi W_hi + A_hi W_lo + A_lo W_hi),
+//          fp32 output for every epilogue (the strict-fp32 mode).
+enum class GemmKind : int { kBF16 = 0, kS8 = 1, kF16 = 2, kW8 = 3, kTF32x3 = 4 };
+
+// Tensor maps one launch reads: A, W, the output and residual boxes, and for
+// kTF32x3 the remainder parts of A (a2) and W (b2).
+struct GemmMaps {
+    CUtensorMap a, b, out, res, a2, b2;
+};
 
 // Encode a 2-D K-major tensor map over a row-major [rows x cols] matrix
 // (cols contiguous) with a (128-byte x box_rows) box and 128-byte swizzle.
-// elem_bytes: 2 (bf16) or 1 (int8).  Returns false on failure.
+// elem_bytes: 4 (fp32), 2 (bf16 / fp16) or 1 (int8).  Returns false on failure.
 bool make_kmajor_tmap(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols,
                       uint64_t row_stride_elems, uint32_t box_rows);
 // Tensor map over an int8 weight [rows x cols] for GemmKind::kW8: boxes of
@@ -73,5 +82,10 @@ inline int gemm_w_box_rows(int block_n) { return block_n / 2; }
 // 64 (128 for kS8) and N % block_n == 0.
 cudaError_t gemm_launch(GemmKind kind, int epi, int block_n, const CUtensorMap& tmA, const CUtensorMap& tmB,
                         const GemmArgs& args, int num_sms, cudaStream_t stream);
+// kTF32x3: tmA / tmB over the hi parts, tmA2 / tmB2 over the remainders
+// (fp32 maps, box 32 elements x rows, 128-byte swizzle; K % 32 == 0).
+cudaError_t gemm_launch_tf32x3(int epi, int block_n, const CUtensorMap& tmA, const CUtensorMap& tmA2,
+                               const CUtensorMap& tmB, const CUtensorMap& tmB2, const GemmArgs& args, int num_sms,
+                               cudaStream_t stream);
 
 }  // namespace rg

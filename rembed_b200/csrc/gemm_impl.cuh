@@ -167,15 +167,19 @@ __device__ __forceinline__ uint32_t swz(int r, int c, int row_bytes) {
 template <int BN, int KIND, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes, GemmArgs args) {
+                const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes,
+                const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, GemmArgs args) {
     constexpr bool S8 = KIND == static_cast<int>(GemmKind::kS8);
     constexpr bool W8 = KIND == static_cast<int>(GemmKind::kW8);
     constexpr bool F16 = KIND == static_cast<int>(GemmKind::kF16) || W8;  // fp16 operands and output
+    // 3xTF32: fp32 operands split hi + lo, K walked three times
+    // (A_hi W_hi, A_hi W_lo, A_lo W_hi), fp32 outputs
+    constexpr bool X3 = KIND == static_cast<int>(GemmKind::kTF32x3);
     constexpr bool CSCALE = true;  // per-column dequant scales, whenever args.col_scale is set
     using S = GemmShape<BN, W8>;
     constexpr int STAGES = S::STAGES;
     constexpr int A_BYTES = S::A_BYTES, B_BYTES = S::B_BYTES, B8_BYTES = S::B8_BYTES;
-    constexpr int K_ELEMS = S8 ? 128 : 64;  // elements per 128-byte k-block of A
+    constexpr int K_ELEMS = S8 ? 128 : (X3 ? 32 : 64);  // elements per 128-byte k-block of A
     constexpr int HALF = BN / 2;            // W rows per CTA; accumulator columns per epilogue warp
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -200,7 +204,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int m_tiles = (args.M + 255) / 256;
     const int n_tiles = args.N / BN;
     const int num_tiles = m_tiles * n_tiles;
-    const int kblocks = args.K / K_ELEMS;
+    const int kb_real = args.K / K_ELEMS;
+    const int kblocks = X3 ? 3 * kb_real : kb_real;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -223,6 +228,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        if (X3) {
+            tma_prefetch_desc(&tmA2);
+            tma_prefetch_desc(&tmB2);
+        }
         tma_prefetch_desc(&tmOut);
         if (EPI == kEpiBiasRes || EPI == kEpiBiasResLN) tma_prefetch_desc(&tmRes);
     }
@@ -254,14 +263,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 // Both CTAs' loads complete on the even CTA's barrier, which
                 // expects the bytes of both.
                 if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (A_BYTES + (W8 ? 0 : B_BYTES)));
-                tma_load_2d_pair(sA + stage * A_BYTES, &tmA, full_lead + 8 * stage, kb * K_ELEMS,
+                // 3xTF32: segment 0 = (A_hi, W_hi), 1 = (A_hi, W_lo), 2 = (A_lo, W_hi)
+                const int seg = X3 ? kb / kb_real : 0;
+                const int kx = (X3 ? kb - seg * kb_real : kb) * K_ELEMS;
+                tma_load_2d_pair(sA + stage * A_BYTES, seg == 2 ? &tmA2 : &tmA, full_lead + 8 * stage, kx,
                                  m_blk * 256 + rank * 128);
                 if constexpr (W8) {
                     // the int8 k-block lands on this CTA's own barrier for its converters
                     mbar_arrive_expect_tx(&wfull[stage], B8_BYTES);
-                    tma_load_2d(sB8 + stage * B8_BYTES, &tmB, &wfull[stage], kb * K_ELEMS, n_blk * BN + rank * HALF);
+                    tma_load_2d(sB8 + stage * B8_BYTES, &tmB, &wfull[stage], kx, n_blk * BN + rank * HALF);
                 } else {
-                    tma_load_2d_pair(sB + stage * B_BYTES, &tmB, full_lead + 8 * stage, kb * K_ELEMS,
+                    tma_load_2d_pair(sB + stage * B_BYTES, seg == 1 ? &tmB2 : &tmB, full_lead + 8 * stage, kx,
                                      n_blk * BN + rank * HALF);
                 }
                 issued_mask |= 1u << stage;
@@ -324,7 +336,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1 && lane == 0 && rank == 0) {
         // ---------------- pair MMA issuer (even CTA) ----------------
-        constexpr uint32_t idesc = S8 ? idesc_s8(256, BN) : (F16 ? idesc_f16(256, BN) : idesc_bf16(256, BN));
+        constexpr uint32_t idesc =
+            S8 ? idesc_s8(256, BN) : (F16 ? idesc_f16(256, BN) : (X3 ? idesc_tf32(256, BN) : idesc_bf16(256, BN)));
         int stage = 0;
         uint32_t phase = 0;
         int acc = 0;
@@ -349,6 +362,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     // 32 bytes of K per instruction: +2 in 16-byte units.
                     if constexpr (S8)
                         umma_s8_pair(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+                    else if constexpr (X3)
+                        umma_tf32_pair(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
                     else
                         umma_bf16_pair(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
                 }
@@ -380,7 +395,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // the row written into a swizzled staging box, one TMA store per box.
         // The fp32 residual box arrives by TMA one chunk ahead.
         constexpr bool RES = EPI == kEpiBiasRes || EPI == kEpiBiasResLN;
-        constexpr bool F32OUT = RES || EPI == kEpiBiasF32;
+        constexpr bool F32OUT = RES || EPI == kEpiBiasF32 || X3;
         const int ew = warp - 4;
         const int quarter = warp & 3;
         const int half = ew >> 2;
@@ -614,8 +629,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // kind is compiled in its own translation unit (gemm_kind_*.cu).
 
 template <int BN, int KIND, int EPI>
-static cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmOut,
-                              const CUtensorMap& tmRes, const GemmArgs& args, int num_sms, cudaStream_t stream) {
+static cudaError_t launch_one(const GemmMaps& m, const GemmArgs& args, int num_sms, cudaStream_t stream) {
     constexpr int smem = GemmShape<BN, KIND == static_cast<int>(GemmKind::kW8)>::SMEM;
     static_assert(smem <= 232448, "shared memory budget");
     auto kern = gemm_kernel<BN, KIND, EPI>;
@@ -653,34 +667,32 @@ static cudaError_t launch_one(const CUtensorMap& tmA, const CUtensorMap& tmB, co
     }
     const int tiles = ((args.M + 255) / 256) * (args.N / BN);
     const int grid = 2 * (tiles < pairs ? tiles : pairs);
-    kern<<<grid, kThreads, smem, stream>>>(tmA, tmB, tmOut, tmRes, args);
+    kern<<<grid, kThreads, smem, stream>>>(m.a, m.b, m.out, m.res, m.a2, m.b2, args);
     return cudaGetLastError();
 }
 
 template <int BN, int KIND>
-static cudaError_t dispatch_epi(int epi, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmOut,
-                                const CUtensorMap& tmRes, const GemmArgs& args, int num_sms, cudaStream_t stream) {
+static cudaError_t dispatch_epi(int epi, const GemmMaps& m, const GemmArgs& args, int num_sms, cudaStream_t stream) {
     switch (epi) {
-    case kEpiBias: return launch_one<BN, KIND, kEpiBias>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case kEpiBiasGelu: return launch_one<BN, KIND, kEpiBiasGelu>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case kEpiBiasRes: return launch_one<BN, KIND, kEpiBiasRes>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case kEpiBiasF32: return launch_one<BN, KIND, kEpiBiasF32>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case kEpiGluSilu: return launch_one<BN, KIND, kEpiGluSilu>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case kEpiGluGeluErf: return launch_one<BN, KIND, kEpiGluGeluErf>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case kEpiGluGeluTanh: return launch_one<BN, KIND, kEpiGluGeluTanh>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case kEpiBiasResLN: return launch_one<BN, KIND, kEpiBiasResLN>(tmA, tmB, tmOut, tmRes, args, num_sms, stream);
+    case kEpiBias: return launch_one<BN, KIND, kEpiBias>(m, args, num_sms, stream);
+    case kEpiBiasGelu: return launch_one<BN, KIND, kEpiBiasGelu>(m, args, num_sms, stream);
+    case kEpiBiasRes: return launch_one<BN, KIND, kEpiBiasRes>(m, args, num_sms, stream);
+    case kEpiBiasF32: return launch_one<BN, KIND, kEpiBiasF32>(m, args, num_sms, stream);
+    case kEpiGluSilu: return launch_one<BN, KIND, kEpiGluSilu>(m, args, num_sms, stream);
+    case kEpiGluGeluErf: return launch_one<BN, KIND, kEpiGluGeluErf>(m, args, num_sms, stream);
+    case kEpiGluGeluTanh: return launch_one<BN, KIND, kEpiGluGeluTanh>(m, args, num_sms, stream);
+    case kEpiBiasResLN: return launch_one<BN, KIND, kEpiBiasResLN>(m, args, num_sms, stream);
     default: return cudaErrorInvalidValue;
     }
 }
 
 template <int KIND>
-cudaError_t dispatch_kind(int block_n, int epi, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                          const CUtensorMap& tmOut, const CUtensorMap& tmRes, const GemmArgs& args, int num_sms,
+cudaError_t dispatch_kind(int block_n, int epi, const GemmMaps& m, const GemmArgs& args, int num_sms,
                           cudaStream_t stream) {
     switch (block_n) {
-    case 256: return dispatch_epi<256, KIND>(epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case 192: return dispatch_epi<192, KIND>(epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream);
-    case 128: return dispatch_epi<128, KIND>(epi, tmA, tmB, tmOut, tmRes, args, num_sms, stream);
+    case 256: return dispatch_epi<256, KIND>(epi, m, args, num_sms, stream);
+    case 192: return dispatch_epi<192, KIND>(epi, m, args, num_sms, stream);
+    case 128: return dispatch_epi<128, KIND>(epi, m, args, num_sms, stream);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -2,6 +2,5 @@
 #include "gemm_impl.cuh"
 
 namespace rg {
-template cudaError_t dispatch_kind<3>(int, int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
-                                      const CUtensorMap&, const GemmArgs&, int, cudaStream_t);
+template cudaError_t dispatch_kind<3>(int, int, const GemmMaps&, const GemmArgs&, int, cudaStream_t);
 }  // namespace rg

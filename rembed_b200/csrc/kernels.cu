@@ -40,7 +40,8 @@ __device__ __forceinline__ float warp_max(float v) {
 template <int NV, bool RMS, bool F16>
 __device__ __forceinline__ bool norm_finish(float (&v)[NV][4], const float* g, const float* b, float eps, int H,
                                             float* out32, uint16_t* outb, int8_t* outq, float* outqs, int lane,
-                                            float2* stats = nullptr) {
+                                            float2* stats = nullptr, float* outhi = nullptr,
+                                            float* outlo = nullptr) {
     float mean = 0.f, inv = 1.f;
     if (!g) {
         // identity (ModernBERT's layer-0 attention norm): only the stores
@@ -89,6 +90,15 @@ __device__ __forceinline__ bool norm_finish(float (&v)[NV][4], const float* g, c
         if (outb)
             reinterpret_cast<uint2*>(outb + j)[0] =
                 make_uint2(pack2<F16>(v[c][0], v[c][1]), pack2<F16>(v[c][2], v[c][3]));
+        if (outhi) {
+            float4 h, l;
+            tf32_split(v[c][0], h.x, l.x);
+            tf32_split(v[c][1], h.y, l.y);
+            tf32_split(v[c][2], h.z, l.z);
+            tf32_split(v[c][3], h.w, l.w);
+            reinterpret_cast<float4*>(outhi + j)[0] = h;
+            reinterpret_cast<float4*>(outlo + j)[0] = l;
+        }
         amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[c][0]), fabsf(v[c][1])), fmaxf(fabsf(v[c][2]), fabsf(v[c][3]))));
     }
     if (outq) {
@@ -193,7 +203,9 @@ __global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
     if (p.g)
         overflow = norm_finish<NV, false, F16>(v, p.g, p.b, p.eps, H, x32, xb,
                                                p.xq ? p.xq + static_cast<int64_t>(t) * H : nullptr,
-                                               p.xq_scale ? p.xq_scale + t : nullptr, lane);
+                                               p.xq_scale ? p.xq_scale + t : nullptr, lane, nullptr,
+                                               p.xhi ? p.xhi + static_cast<int64_t>(t) * H : nullptr,
+                                               p.xlo ? p.xlo + static_cast<int64_t>(t) * H : nullptr);
     else
         overflow = store_row<NV, F16>(v, x32, xb, lane);
     if (overflow && lane == 0) atomicOr(p.status, kStatusF16Overflow);
@@ -216,7 +228,8 @@ __global__ void __launch_bounds__(256) norm_kernel(NormParams p) {
     }
     const bool overflow = norm_finish<NV, RMS, F16>(v, p.g, p.b, p.eps, p.H, p.out32 ? p.out32 + off : nullptr,
                                                     p.outb ? p.outb + off : nullptr, p.outq ? p.outq + off : nullptr,
-                                                    p.outqs ? p.outqs + t : nullptr, lane, p.stats ? p.stats + t : nullptr);
+                                                    p.outqs ? p.outqs + t : nullptr, lane, p.stats ? p.stats + t : nullptr,
+                                                    p.outhi ? p.outhi + off : nullptr, p.outlo ? p.outlo + off : nullptr);
     if (overflow && p.status && lane == 0) atomicOr(p.status, kStatusF16Overflow);
 }
 
@@ -329,7 +342,7 @@ cudaError_t launch_add_rmsnorm(float* x32, const float* o32, const float* g, flo
 // the q or k gain (qwen3.go:485-508, gemma3.go:303-330), then the rotation
 // at the token's position in its sequence (modernbert.go:125-143: products
 // rounded before the add/sub).
-template <int DH, bool F16>
+template <int DH, bool F16, bool F32>
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkRopeParams p) {
     constexpr int E = DH / 32, HALF = DH / 2;
     const int lane = threadIdx.x & 31;
@@ -338,10 +351,12 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkRopeParams p) {
     if (item >= p.T * heads) return;
     const int t = item / heads, h = item % heads;
     const bool is_q = h < p.nq;
-    uint16_t* row = p.qkv + static_cast<int64_t>(t) * p.ld + (is_q ? h * DH : p.nq * DH + (h - p.nq) * DH);
+    const int64_t roff = static_cast<int64_t>(t) * p.ld + (is_q ? h * DH : p.nq * DH + (h - p.nq) * DH);
+    uint16_t* row = F32 ? nullptr : p.qkv + roff;
+    float* row32 = F32 ? p.qkv32 + roff : nullptr;
     float v[E];
 #pragma unroll
-    for (int k = 0; k < E; ++k) v[k] = to_f32<F16>(row[lane + 32 * k]);
+    for (int k = 0; k < E; ++k) v[k] = F32 ? row32[lane + 32 * k] : to_f32<F16>(row[lane + 32 * k]);
     const float* g = is_q ? p.q_norm : p.k_norm;
     if (g) {
         float q = 0.f;
@@ -368,7 +383,10 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkRopeParams p) {
     float amax = 0.f;
 #pragma unroll
     for (int k = 0; k < E; ++k) {
-        row[lane + 32 * k] = from_f32<F16>(v[k]);
+        if constexpr (F32)
+            row32[lane + 32 * k] = v[k];
+        else
+            row[lane + 32 * k] = from_f32<F16>(v[k]);
         amax = fmaxf(amax, fabsf(v[k]));
     }
     if constexpr (F16)
@@ -381,18 +399,14 @@ cudaError_t launch_qk_norm_rope(const QkRopeParams& p, int head_dim, cudaStream_
     const long items = static_cast<long>(p.T) * (p.nq + p.nkv);
     const int grid = static_cast<int>((items + 7) / 8);
     switch (head_dim) {
-    case 64:
-        if (p.f16) qk_norm_rope_kernel<64, true><<<grid, 256, 0, st>>>(p);
-        else qk_norm_rope_kernel<64, false><<<grid, 256, 0, st>>>(p);
-        break;
-    case 128:
-        if (p.f16) qk_norm_rope_kernel<128, true><<<grid, 256, 0, st>>>(p);
-        else qk_norm_rope_kernel<128, false><<<grid, 256, 0, st>>>(p);
-        break;
-    case 256:
-        if (p.f16) qk_norm_rope_kernel<256, true><<<grid, 256, 0, st>>>(p);
-        else qk_norm_rope_kernel<256, false><<<grid, 256, 0, st>>>(p);
-        break;
+#define RG_QKR(DH)                                                                   \
+    if (p.qkv32) qk_norm_rope_kernel<DH, false, true><<<grid, 256, 0, st>>>(p);    \
+    else if (p.f16) qk_norm_rope_kernel<DH, true, false><<<grid, 256, 0, st>>>(p); \
+    else qk_norm_rope_kernel<DH, false, false><<<grid, 256, 0, st>>>(p);
+    case 64: RG_QKR(64) break;
+    case 128: RG_QKR(128) break;
+    case 256: RG_QKR(256) break;
+#undef RG_QKR
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
@@ -781,6 +795,156 @@ cudaError_t launch_attention_mma(const AttnParams& p, int nseq, int max_len, int
     case 64: return launch_attention_d<64>(p, nseq, max_len, heads, st);
     case 128: return launch_attention_d<128>(p, nseq, max_len, heads, st);
     case 256: return launch_attention_d<256>(p, nseq, max_len, heads, st);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 3xTF32 operand split: hi = tf32(x) (nearest, ties to even), lo = x - hi.
+__global__ void __launch_bounds__(256) split_tf32_kernel(const float4* __restrict__ x, size_t n4, float4* hi,
+                                                        float4* lo) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const float4 v = x[i];
+        float4 h, l;
+        tf32_split(v.x, h.x, l.x);
+        tf32_split(v.y, h.y, l.y);
+        tf32_split(v.z, h.z, l.z);
+        tf32_split(v.w, h.w, l.w);
+        hi[i] = h;
+        lo[i] = l;
+    }
+}
+
+cudaError_t launch_split_tf32(const float* x, size_t n, float* hi, float* lo, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    if (n % 4 != 0) return cudaErrorInvalidValue;
+    const size_t n4 = n / 4;
+    const int grid = static_cast<int>(std::min<size_t>((n4 + 255) / 256, 148 * 16));
+    split_tf32_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const float4*>(x), n4, reinterpret_cast<float4*>(hi),
+                                            reinterpret_cast<float4*>(lo));
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Strict fp32 attention.  CTA = 8 query rows of one (sequence, head), one
+// warp per row.  Key/value blocks of 32 rows are staged in shared memory by
+// the whole CTA (coalesced; K rows padded by one float so that lane j reading
+// key j's row is bank-conflict-free).  Lane j computes q . k_j for its key,
+// the warp keeps the running max / sum, and lane d accumulates output dims
+// d, d + 32, ... over the block's probabilities (broadcast by shuffle).
+template <int D>
+__global__ void __launch_bounds__(256) attention_f32_kernel(AttnF32Params p) {
+    constexpr int E = D / 32, KP = D + 1;
+    extern __shared__ float fsm[];
+    float* qs = fsm;              // [8][D]
+    float* ks = qs + 8 * D;       // [32][D + 1]
+    float* vs = ks + 32 * KP;     // [32][D]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int s = blockIdx.z, h = blockIdx.y;
+    const int s0 = __ldg(p.cu + s), L = __ldg(p.cu + s + 1) - s0;
+    const int q0 = blockIdx.x * 8;
+    if (q0 >= L) return;  // the whole CTA
+    const int qi = q0 + warp;
+    const bool active = qi < L;
+    const int hk = h / p.group;
+    for (int t = threadIdx.x; t < 8 * D; t += 256) {
+        const int w = t / D, d = t % D;
+        qs[t] = q0 + w < L ? p.q[static_cast<int64_t>(s0 + q0 + w) * p.ldq + h * D + d] : 0.f;
+    }
+    const float* K = p.k + static_cast<int64_t>(s0) * p.ldk + hk * D;
+    const float* V = p.v + static_cast<int64_t>(s0) * p.ldv + hk * D;
+    // keys this row may see, and the union over the CTA's rows
+    const int jlo = max(0, qi + p.rel_lo), jhi = min(L - 1, qi + p.rel_hi);
+    const int clo = max(0, q0 + p.rel_lo), chi = min(L - 1, min(q0 + 7, L - 1) + p.rel_hi);
+    float m = -INFINITY, l = 0.f;
+    float o[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) o[e] = 0.f;
+    const float* qrow = qs + warp * D;
+    for (int j0 = clo; j0 <= chi; j0 += 32) {
+        __syncthreads();  // previous block consumed (and, first time, qs written)
+        const int nb = min(32, chi - j0 + 1);
+        for (int t = threadIdx.x; t < 32 * D; t += 256) {
+            const int r = t / D, d = t % D;
+            const bool in = r < nb;
+            ks[r * KP + d] = in ? __ldg(K + static_cast<int64_t>(j0 + r) * p.ldk + d) : 0.f;
+            vs[r * D + d] = in ? __ldg(V + static_cast<int64_t>(j0 + r) * p.ldv + d) : 0.f;
+        }
+        __syncthreads();
+        if (!active) continue;
+        const int j = j0 + lane;
+        const bool valid = lane < nb && j >= jlo && j <= jhi;
+        float sc = -INFINITY;
+        if (valid) {
+            const float* kr = ks + lane * KP;
+            float acc = 0.f;
+#pragma unroll 16
+            for (int d = 0; d < D; ++d) acc = fmaf(qrow[d], kr[d], acc);
+            sc = acc * p.scale;
+            if (p.bias) {
+                const int bi = min(max(j - qi + p.bias_off, 0), 2 * p.bias_off);
+                sc += __ldg(p.bias + static_cast<int64_t>(h) * (2 * p.bias_off + 1) + bi);
+            }
+        }
+        float bm = sc;
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o2));
+        if (bm == -INFINITY) continue;  // no key of this row in the block
+        const float mn = fmaxf(m, bm);
+        const float alpha = m == -INFINITY ? 0.f : expf(m - mn);
+        const float pj = valid ? expf(sc - mn) : 0.f;
+        float ps = pj;
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o2);
+        l = l * alpha + ps;
+#pragma unroll
+        for (int e = 0; e < E; ++e) o[e] *= alpha;
+        for (int kk = 0; kk < nb; ++kk) {
+            const float pk = __shfl_sync(0xffffffffu, pj, kk);
+#pragma unroll
+            for (int e = 0; e < E; ++e) o[e] = fmaf(pk, vs[kk * D + lane + 32 * e], o[e]);
+        }
+        m = mn;
+    }
+    if (!active) return;
+    const float inv = l > 0.f ? 1.0f / l : 0.f;
+    float* oh = p.out_hi + static_cast<int64_t>(s0 + qi) * p.ldo + h * D;
+    float* ol = p.out_lo + static_cast<int64_t>(s0 + qi) * p.ldo + h * D;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        float hi, lo;
+        tf32_split(o[e] * inv, hi, lo);
+        oh[lane + 32 * e] = hi;
+        ol[lane + 32 * e] = lo;
+    }
+}
+
+template <int D>
+static cudaError_t launch_attention_f32_d(const AttnF32Params& p, int nseq, int max_len, int heads,
+                                          cudaStream_t st) {
+    constexpr int smem = (8 * D + 32 * (D + 1) + 32 * D) * 4;
+    static unsigned configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (smem > 48 * 1024 && (dev >= 32 || !(__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & (1u << dev)))) {
+        cudaError_t e = cudaFuncSetAttribute(attention_f32_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        if (dev < 32) __atomic_fetch_or(&configured, 1u << dev, __ATOMIC_RELEASE);
+    }
+    const dim3 grid((max_len + 7) / 8, heads, nseq);
+    attention_f32_kernel<D><<<grid, 256, smem, st>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attention_f32(const AttnF32Params& p, int nseq, int max_len, int heads, int head_dim,
+                                 cudaStream_t st) {
+    if (nseq <= 0) return cudaSuccess;
+    switch (head_dim) {
+    case 32: return launch_attention_f32_d<32>(p, nseq, max_len, heads, st);
+    case 64: return launch_attention_f32_d<64>(p, nseq, max_len, heads, st);
+    case 128: return launch_attention_f32_d<128>(p, nseq, max_len, heads, st);
+    case 256: return launch_attention_f32_d<256>(p, nseq, max_len, heads, st);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -4,6 +4,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
 
 namespace rg {
 
@@ -28,8 +29,29 @@ struct EmbedParams {
     int8_t* xq;
     float* xq_scale;
     int* status;
+    float *xhi, *xlo;  // strict fp32: the normalised row as tf32-exact hi + fp32 remainder
 };
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t st);
+
+// hi = x rounded to the nearest tf32 value (10 mantissa bits, ties to
+// even), lo = x - hi (exact): the two operand parts of a 3xTF32 GEMM.
+__host__ __device__ inline void tf32_split(float x, float& hi, float& lo) {
+#ifdef __CUDA_ARCH__
+    uint32_t u = __float_as_uint(x);
+#else
+    uint32_t u;
+    memcpy(&u, &x, 4);
+#endif
+    u = (u + 0xfffu + ((u >> 13) & 1u)) & 0xffffe000u;
+#ifdef __CUDA_ARCH__
+    hi = __uint_as_float(u);
+#else
+    memcpy(&hi, &u, 4);
+#endif
+    lo = x - hi;
+}
+// x [n] -> hi [n], lo [n] (hi may alias x); n % 4 == 0, 16-byte aligned.
+cudaError_t launch_split_tf32(const float* x, size_t n, float* hi, float* lo, cudaStream_t st);
 
 // Row normalisation of in [T x H]: LayerNorm (g, b; b nullptr = zero) or
 // RMSNorm (g); g nullptr = identity.  Outputs (each optional): out32 (may
@@ -48,6 +70,7 @@ struct NormParams {
     int* status;    // optional: kStatusF16Overflow if an fp16 output overflows
     float2* stats;  // optional: the row's (mean, rstd) (LayerNorm), for a consumer that
                     // rebuilds the fp32 output on load instead of reading out32
+    float *outhi, *outlo;  // optional (strict fp32): the output as tf32 hi + fp32 remainder
 };
 cudaError_t launch_norm(const NormParams& p, bool rms, cudaStream_t st);
 cudaError_t launch_ln(const float* y32, const float* g, const float* b, float eps, int T, int H, float* x32,
@@ -62,6 +85,7 @@ cudaError_t launch_add_rmsnorm(float* x32, const float* o32, const float* g, flo
 struct QkRopeParams {
     uint16_t* qkv;  // 16-bit: fp16 if f16, else bf16
     bool f16;
+    float* qkv32;   // strict fp32: the fp32 qkv buffer instead (qkv unused)
     int ld, T, nq, nkv;
     const float *q_norm, *k_norm;
     float eps;
@@ -114,6 +138,24 @@ cudaError_t launch_attention(const AttnParams& p, int nseq, int max_len, int hea
 bool attention_tc_supported(int head_dim);
 cudaError_t launch_attention_tc(const AttnParams& p, int T, int nseq, int max_len, int heads, int kv_heads,
                                 int head_dim, int* status, cudaStream_t st);
+// Strict fp32 attention (one warp per query row, fp32 FMA throughout):
+// q/k/v are fp32 rows of the fp32 qkv buffer (strides ldq/ldk/ldv); the
+// output is written as tf32 hi (out_hi) + fp32 remainder (out_lo), the A
+// operand of the 3xTF32 projection that follows.
+struct AttnF32Params {
+    const float *q, *k, *v;
+    int ldq, ldk, ldv;
+    const int32_t* cu;
+    int group;
+    float scale;
+    int rel_lo, rel_hi;
+    const float* bias;
+    int bias_off;
+    float *out_hi, *out_lo;
+    int ldo;
+};
+cudaError_t launch_attention_f32(const AttnF32Params& p, int nseq, int max_len, int heads, int head_dim,
+                                 cudaStream_t st);
 // The mma.sync kernel for any supported head dim (32, 64, 128, 256).
 cudaError_t launch_attention_mma(const AttnParams& p, int nseq, int max_len, int heads, int head_dim, cudaStream_t st);
 

@@ -70,6 +70,14 @@ struct DevDense {
     float* bias = nullptr;
     CUtensorMap tmap[3];    // for tile widths 256, 192, 128 (only widths dividing N are valid)
     CUtensorMap tmap16[3];  // weight-only int8: the same shape over the replica's fp16 widening scratch
+    void* w_lo = nullptr;   // strict fp32: the fp32 remainder of the tf32-rounded weight in w
+    CUtensorMap tmap_lo[3];
+};
+
+// A GEMM's A operand: the tensor map of the buffer the MMA reads and, in the
+// strict fp32 mode, of the fp32 remainder buffer (3xTF32).
+struct OpMaps {
+    CUtensorMap m, lo;
 };
 
 // Weight-only int8 GEMMs with at least this many rows widen the layer's
@@ -131,7 +139,10 @@ struct Replica {
     float* h_out = nullptr;
     int* h_status = nullptr;
     size_t h_cap_ids = 0, h_cap_cu = 0, h_cap_out = 0;
-    CUtensorMap tm_x, tm_ctx, tm_ffh;
+    OpMaps tm_x, tm_ctx, tm_ffh;
+    // strict fp32: GEMM operands as tf32 hi + fp32 remainder; qkv in fp32
+    float *xh = nullptr, *xl = nullptr, *ctxh = nullptr, *ctxl = nullptr, *ffhh = nullptr, *ffhl = nullptr;
+    float* qkv32 = nullptr;
     int tm_T = -1;
     int last_launches = 0;
     const int32_t* h_cu_view = nullptr;  // host copy of the current batch's offsets
@@ -349,6 +360,14 @@ DevDense make_dense(Replica& r, int mode, const float* w, const float* bias, int
         std::vector<uint16_t> h(n);
         for (size_t i = 0; i < n; ++i) h[i] = to_bf16_bits(w[i]);
         d.w = dev_upload(r, h.data(), n);
+    } else if (mode == RG_MODE_FP32) {
+        std::vector<float> hi(n), lo(n);
+        for (size_t i = 0; i < n; ++i) {
+            if (!finite32(w[i])) fail("weight [%zu, %zu] is not finite", i / K, i % K);
+            rg::tf32_split(w[i], hi[i], lo[i]);
+        }
+        d.w = dev_upload(r, hi.data(), n);
+        d.w_lo = dev_upload(r, lo.data(), n);
     } else if (mode == RG_MODE_F16) {
         std::vector<uint16_t> h(n);
         for (size_t i = 0; i < n; ++i)
@@ -366,7 +385,7 @@ DevDense make_dense(Replica& r, int mode, const float* w, const float* bias, int
         d.w = dev_upload(r, q.data(), n);
         d.scale = dev_upload(r, s.data(), N);
     }
-    const int eb = (mode == RG_MODE_BF16 || mode == RG_MODE_F16) ? 2 : 1;
+    const int eb = mode == RG_MODE_FP32 ? 4 : ((mode == RG_MODE_BF16 || mode == RG_MODE_F16) ? 2 : 1);
     if (mode == RG_MODE_INT8_W && n > r.w16_elems) {
         // the widening scratch grows to the largest weight (sized before any
         // tensor map over it is made: make_dense runs for every weight first)
@@ -381,6 +400,8 @@ DevDense make_dense(Replica& r, int mode, const float* w, const float* bias, int
         const bool ok = mode == RG_MODE_INT8_W ? rg::make_w8_tmap(&d.tmap[i], d.w, N, K, box_rows)
                                                : rg::make_kmajor_tmap(&d.tmap[i], d.w, eb, N, K, K, box_rows);
         if (!ok) fail("cuTensorMapEncodeTiled failed for a [%d x %d] weight", N, K);
+        if (mode == RG_MODE_FP32 && !rg::make_kmajor_tmap(&d.tmap_lo[i], d.w_lo, 4, N, K, K, box_rows))
+            fail("cuTensorMapEncodeTiled failed for a [%d x %d] weight remainder", N, K);
     }
     if (bias) d.bias = dev_upload(r, bias, N);
     return d;
@@ -689,11 +710,21 @@ void ensure_workspace(rg_ctx* c, Replica& r, int T, int nseq, size_t nout) {
         const size_t t = static_cast<size_t>((capT + 255) / 256 * 256);
         r.x32 = ws_alloc<float>(r, t * H);
         r.y32 = ws_alloc<float>(r, t * H);
-        r.xb = ws_alloc<act16>(r, t * H);
         r.lnst = ws_alloc<float2>(r, t);
-        r.qkv = ws_alloc<act16>(r, t * m.nqkv);
-        r.ctx = ws_alloc<act16>(r, t * m.qd);
-        r.ffh = ws_alloc<act16>(r, t * I);
+        if (c->mode == RG_MODE_FP32) {
+            r.xh = ws_alloc<float>(r, t * H);
+            r.xl = ws_alloc<float>(r, t * H);
+            r.qkv32 = ws_alloc<float>(r, t * m.nqkv);
+            r.ctxh = ws_alloc<float>(r, t * m.qd);
+            r.ctxl = ws_alloc<float>(r, t * m.qd);
+            r.ffhh = ws_alloc<float>(r, t * I);
+            r.ffhl = ws_alloc<float>(r, t * I);
+        } else {
+            r.xb = ws_alloc<act16>(r, t * H);
+            r.qkv = ws_alloc<act16>(r, t * m.nqkv);
+            r.ctx = ws_alloc<act16>(r, t * m.qd);
+            r.ffh = ws_alloc<act16>(r, t * I);
+        }
         if (r.dense1) {
             r.pool32 = ws_alloc<float>(r, static_cast<size_t>(capS) * H);
             r.head_hid = ws_alloc<float>(r, static_cast<size_t>(capS) * d.dense_hidden);
@@ -722,14 +753,19 @@ void ensure_workspace(rg_ctx* c, Replica& r, int T, int nseq, size_t nout) {
     }
     if (r.tm_T != T) {
         const bool s8 = c->mode == RG_MODE_INT8_FULL;
-        const int eb = s8 ? 1 : 2;
-        const void* xa = s8 ? static_cast<const void*>(r.xq) : r.xb;
-        const void* ca = s8 ? static_cast<const void*>(r.ctxq) : r.ctx;
-        const void* fa = s8 ? static_cast<const void*>(r.ffhq) : r.ffh;
-        if (!rg::make_kmajor_tmap(&r.tm_x, xa, eb, T, H, H, 128) ||
-            !rg::make_kmajor_tmap(&r.tm_ctx, ca, eb, T, m.qd, m.qd, 128) ||
-            !rg::make_kmajor_tmap(&r.tm_ffh, fa, eb, T, I, I, 128))
+        const bool f32 = c->mode == RG_MODE_FP32;
+        const int eb = s8 ? 1 : (f32 ? 4 : 2);
+        const void* xa = s8 ? static_cast<const void*>(r.xq) : (f32 ? static_cast<const void*>(r.xh) : r.xb);
+        const void* ca = s8 ? static_cast<const void*>(r.ctxq) : (f32 ? static_cast<const void*>(r.ctxh) : r.ctx);
+        const void* fa = s8 ? static_cast<const void*>(r.ffhq) : (f32 ? static_cast<const void*>(r.ffhh) : r.ffh);
+        if (!rg::make_kmajor_tmap(&r.tm_x.m, xa, eb, T, H, H, 128) ||
+            !rg::make_kmajor_tmap(&r.tm_ctx.m, ca, eb, T, m.qd, m.qd, 128) ||
+            !rg::make_kmajor_tmap(&r.tm_ffh.m, fa, eb, T, I, I, 128))
             fail("cuTensorMapEncodeTiled failed for the activation buffers");
+        if (f32 && (!rg::make_kmajor_tmap(&r.tm_x.lo, r.xl, 4, T, H, H, 128) ||
+                    !rg::make_kmajor_tmap(&r.tm_ctx.lo, r.ctxl, 4, T, m.qd, m.qd, 128) ||
+                    !rg::make_kmajor_tmap(&r.tm_ffh.lo, r.ffhl, 4, T, I, I, 128)))
+            fail("cuTensorMapEncodeTiled failed for the activation remainder buffers");
         r.tm_T = T;
     }
 }
@@ -797,7 +833,7 @@ void prof_collect(Replica& r) {
     r.ev_used = 0;
 }
 
-void gemm(Replica& r, int mode, const CUtensorMap& tmA, const DevDense& w, int M, int epi, const float* row_scale,
+void gemm(Replica& r, int mode, const OpMaps& tmA, const DevDense& w, int M, int epi, const float* row_scale,
           const float* residual, void* out, cudaStream_t st, int& launches, const float2* ln_stats = nullptr,
           const float* ln_g = nullptr, const float* ln_b = nullptr) {
     rg::GemmArgs a{};
@@ -820,8 +856,10 @@ void gemm(Replica& r, int mode, const CUtensorMap& tmA, const DevDense& w, int M
                                                         : rg::GemmKind::kBF16;
     // Algorithmic bytes: A and W read once, output written once (+ fp32
     // residual read); FLOPs 2*M*N*K.
-    const double eb = kind == rg::GemmKind::kS8 ? 1.0 : 2.0;
-    const double ob = (rg::epi_has_residual(epi) || epi == rg::kEpiBiasF32) ? 4.0 : (rg::epi_is_glu(epi) ? 1.0 : 2.0);
+    const bool x3 = mode == RG_MODE_FP32;  // hi + lo fp32 operands, fp32 outputs
+    const double eb = kind == rg::GemmKind::kS8 ? 1.0 : (x3 ? 8.0 : 2.0);
+    const double ob = (rg::epi_has_residual(epi) || epi == rg::kEpiBiasF32 || x3) ? 4.0
+                      : (rg::epi_is_glu(epi) ? 1.0 : 2.0);
     const double bytes = eb * (double(M) * w.K + double(w.N) * w.K) + ob * double(M) * w.N +
                          (rg::epi_has_residual(epi) ? 4.0 * double(M) * w.N : 0.0);
     const int bn = rg::gemm_block_n(M, w.N, r.num_sms, rg::epi_is_glu(epi));
@@ -834,13 +872,19 @@ void gemm(Replica& r, int mode, const CUtensorMap& tmA, const DevDense& w, int M
             ++launches;
         }
         ProfScope ps(r, st, RG_KC_GEMM, 2.0 * M * w.N * w.K, bytes);
-        check(rg::gemm_launch(rg::GemmKind::kF16, epi, bn, tmA, w.tmap16[bn_index(bn)], a, r.num_sms, st),
+        check(rg::gemm_launch(rg::GemmKind::kF16, epi, bn, tmA.m, w.tmap16[bn_index(bn)], a, r.num_sms, st),
               "gemm launch");
         ++launches;
         return;
     }
     ProfScope ps(r, st, RG_KC_GEMM, 2.0 * M * w.N * w.K, bytes);
-    check(rg::gemm_launch(kind, epi, bn, tmA, w.tmap[bn_index(bn)], a, r.num_sms, st), "gemm launch");
+    if (mode == RG_MODE_FP32) {
+        const int i = bn_index(bn);
+        check(rg::gemm_launch_tf32x3(epi, bn, tmA.m, tmA.lo, w.tmap[i], w.tmap_lo[i], a, r.num_sms, st),
+              "gemm launch");
+    } else {
+        check(rg::gemm_launch(kind, epi, bn, tmA.m, w.tmap[bn_index(bn)], a, r.num_sms, st), "gemm launch");
+    }
     ++launches;
 }
 
@@ -888,6 +932,7 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
     const int mode = c->mode;
     const bool s8 = mode == RG_MODE_INT8_FULL;
     const bool f16 = mode == RG_MODE_F16 || mode == RG_MODE_INT8_W;  // fp16 activations, else bf16
+    const bool f32 = mode == RG_MODE_FP32;  // strict: fp32 activations, hi/lo GEMM operands
     const bool pre = is_prenorm(arch);
     int launches = 0;
     const double Td = T, Hd = H;
@@ -911,8 +956,10 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         e.b = arch == RG_ARCH_MODERNBERT ? r.zero_beta : r.emb_b;
         e.eps = eps;
         e.x32 = r.x32;
-        e.xb = pre ? nullptr : r.xb;  // pre-norm stacks normalise before the first GEMM
+        e.xb = (pre || f32) ? nullptr : r.xb;  // pre-norm stacks normalise before the first GEMM
         e.f16 = f16;
+        e.xhi = (!pre && f32) ? r.xh : nullptr;
+        e.xlo = (!pre && f32) ? r.xl : nullptr;
         e.xq = (!pre && s8) ? r.xq : nullptr;
         e.xq_scale = (!pre && s8) ? r.xs : nullptr;
         e.status = r.d_status;
@@ -929,7 +976,9 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         p.eps = eps;
         p.T = T;
         p.H = H;
-        p.outb = r.xb;
+        p.outb = f32 ? nullptr : r.xb;
+        p.outhi = f32 ? r.xh : nullptr;
+        p.outlo = f32 ? r.xl : nullptr;
         p.f16 = f16;
         p.status = r.d_status;
         p.outq = s8 ? r.xq : nullptr;
@@ -945,7 +994,7 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
     // as is, i.e. the embedding output).  The stack's last LayerNorm writes
     // x32 for pooling.
     const float *res_g = nullptr, *res_b = nullptr;
-    auto residual_gemm = [&](const CUtensorMap& tmA, const DevDense& w, const float* row_scale) {
+    auto residual_gemm = [&](const OpMaps& tmA, const DevDense& w, const float* row_scale) {
         if (res_g)
             gemm(r, mode, tmA, w, T, rg::kEpiBiasResLN, row_scale, r.x32, r.x32, st, launches, r.lnst, res_g, res_b);
         else
@@ -961,7 +1010,9 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         p.T = T;
         p.H = H;
         p.out32 = last ? r.x32 : nullptr;
-        p.outb = r.xb;
+        p.outb = f32 ? nullptr : r.xb;
+        p.outhi = f32 ? r.xh : nullptr;
+        p.outlo = f32 ? r.xl : nullptr;
         p.f16 = f16;
         p.outq = s8 ? r.xq : nullptr;
         p.outqs = s8 ? r.xs : nullptr;
@@ -988,11 +1039,13 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         const DevLayer& L = r.layers[li];
         // ---- attention sublayer
         if (pre) norm_into_a(L.attn_norm, arch == RG_ARCH_MODERNBERT ? r.zero_beta : nullptr, arch != RG_ARCH_MODERNBERT);
-        gemm(r, mode, r.tm_x, L.qkv, T, rg::kEpiBias, s8 ? r.xs : nullptr, nullptr, r.qkv, st, launches);
+        gemm(r, mode, r.tm_x, L.qkv, T, rg::kEpiBias, s8 ? r.xs : nullptr, nullptr,
+             f32 ? static_cast<void*>(r.qkv32) : r.qkv, st, launches);
         if (has_rope(arch)) {
             ProfScope ps(r, st, RG_KC_NORM, 0.0, Td * (m.qd + m.kvd) * 4.0);
             rg::QkRopeParams q{};
             q.qkv = r.qkv;
+            q.qkv32 = f32 ? r.qkv32 : nullptr;
             q.f16 = f16;
             q.status = r.d_status;
             q.ld = m.nqkv;
@@ -1015,26 +1068,45 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
             const double pairs = attn_pairs(r.h_cu_view, nseq, lo, hi);
             ProfScope ps(r, st, RG_KC_ATTENTION, 4.0 * dh * pairs * m.nq,
                          2.0 * Td * (2.0 * m.qd + 2.0 * m.kvd));
-            rg::AttnParams ap{};
-            ap.q = r.qkv;
-            ap.k = r.qkv + m.qd;
-            ap.v = r.qkv + m.qd + m.kvd;
-            ap.ldq = ap.ldk = ap.ldv = m.nqkv;
-            ap.f16 = f16;
-            ap.cu = d_cu;
-            ap.group = m.nq / m.nkv;
-            ap.scale = scale;
-            ap.scale_log2 = scale * 1.4426950408889634f;
-            ap.rel_lo = lo;
-            ap.rel_hi = hi;
-            ap.bias = r.rel_bias;
-            ap.bias_off = r.rel_bias_off;
-            ap.out = r.ctx;
-            ap.ldo = m.qd;
-            ap.T = T;
-            ap.kv_heads = m.nkv;
-            ap.status = r.d_status;
-            check(rg::launch_attention(ap, nseq, max_len, m.nq, dh, st), "attention launch");
+            if (f32) {
+                rg::AttnF32Params fp{};
+                fp.q = r.qkv32;
+                fp.k = r.qkv32 + m.qd;
+                fp.v = r.qkv32 + m.qd + m.kvd;
+                fp.ldq = fp.ldk = fp.ldv = m.nqkv;
+                fp.cu = d_cu;
+                fp.group = m.nq / m.nkv;
+                fp.scale = scale;
+                fp.rel_lo = lo;
+                fp.rel_hi = hi;
+                fp.bias = r.rel_bias;
+                fp.bias_off = r.rel_bias_off;
+                fp.out_hi = r.ctxh;
+                fp.out_lo = r.ctxl;
+                fp.ldo = m.qd;
+                check(rg::launch_attention_f32(fp, nseq, max_len, m.nq, dh, st), "attention launch");
+            } else {
+                rg::AttnParams ap{};
+                ap.q = r.qkv;
+                ap.k = r.qkv + m.qd;
+                ap.v = r.qkv + m.qd + m.kvd;
+                ap.ldq = ap.ldk = ap.ldv = m.nqkv;
+                ap.f16 = f16;
+                ap.cu = d_cu;
+                ap.group = m.nq / m.nkv;
+                ap.scale = scale;
+                ap.scale_log2 = scale * 1.4426950408889634f;
+                ap.rel_lo = lo;
+                ap.rel_hi = hi;
+                ap.bias = r.rel_bias;
+                ap.bias_off = r.rel_bias_off;
+                ap.out = r.ctx;
+                ap.ldo = m.qd;
+                ap.T = T;
+                ap.kv_heads = m.nkv;
+                ap.status = r.d_status;
+                check(rg::launch_attention(ap, nseq, max_len, m.nq, dh, st), "attention launch");
+            }
             ++launches;
         }
         if (s8) quantize(r.ctx, m.qd, r.ctxq, r.ctxs);
@@ -1052,7 +1124,12 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         // ---- FFN sublayer
         if (pre) norm_into_a(L.ffn_norm, arch == RG_ARCH_MODERNBERT ? r.zero_beta : nullptr, arch != RG_ARCH_MODERNBERT);
         gemm(r, mode, r.tm_x, L.ffn1, T, is_glu(arch) ? glu_epi : rg::kEpiBiasGelu, s8 ? r.xs : nullptr, nullptr,
-             r.ffh, st, launches);
+             f32 ? static_cast<void*>(r.ffhh) : r.ffh, st, launches);
+        if (f32) {  // the fp32 FFN hidden state -> tf32 hi (in place) + remainder
+            ProfScope ps(r, st, RG_KC_QUANT, 0.0, Td * I * 12.0);
+            check(rg::launch_split_tf32(r.ffhh, static_cast<size_t>(T) * I, r.ffhh, r.ffhl, st), "split launch");
+            ++launches;
+        }
         if (s8) quantize(r.ffh, I, r.ffhq, r.ffhs);
         if (!pre) {
             residual_gemm(r.tm_ffh, L.ffn2, s8 ? r.ffhs : nullptr);
@@ -1221,7 +1298,8 @@ int rg_init(const rg_model_desc* desc, const int* devices, int ndev, int mode, r
             fail("rg_init: mpnet needs relative_attention_num_buckets >= 2");
         if (max_seq_len(d) <= 0) fail("rg_init: no usable positions (max_position_embeddings %d, offset %d)",
                                       d.max_position_embeddings, pos_offset(d));
-        if (mode != RG_MODE_BF16 && mode != RG_MODE_F16 && mode != RG_MODE_INT8_W && mode != RG_MODE_INT8_FULL)
+        if (mode != RG_MODE_BF16 && mode != RG_MODE_F16 && mode != RG_MODE_INT8_W && mode != RG_MODE_INT8_FULL &&
+            mode != RG_MODE_FP32)
             fail("rg_init: mode %d is not available in this build", mode);
         if (mode == RG_MODE_INT8_FULL && (d.hidden_size % 128 != 0 || d.intermediate_size % 128 != 0 ||
                                           dims(d).qd % 128 != 0))

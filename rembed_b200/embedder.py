@@ -33,7 +33,7 @@ from .config import Config
 
 __all__ = ["Embedder", "RembedError", "TokenEmbeddings", "load", "library"]
 
-RG_MODE_BF16, RG_MODE_F16, RG_MODE_INT8_W, RG_MODE_INT8_FULL = 0, 1, 2, 3
+RG_MODE_BF16, RG_MODE_F16, RG_MODE_INT8_W, RG_MODE_INT8_FULL, RG_MODE_FP32 = 0, 1, 2, 3, 4
 RG_DTYPE_F32, RG_DTYPE_F16, RG_DTYPE_BF16 = 0, 1, 2
 RG_OUT_POOLED, RG_OUT_TOKENS = 0, 1
 
@@ -178,7 +178,7 @@ class Embedder:
     """
 
     def __init__(self, config: Config, weights: dict, *, int8: bool = False, int8_activations: bool = False,
-                 dim: int = 0, devices: Sequence[int] = (0,), fp16: bool = True):
+                 dim: int = 0, devices: Sequence[int] = (0,), fp16: bool = True, strict_fp32: bool = False):
         self._lib = library()
         self._ctx = None
         self.config = config.validate(config.name or "config")
@@ -186,8 +186,9 @@ class Embedder:
         # unquantised path runs fp16 tensor-core operands by default (closest
         # to the reference's fp32; an fp16 overflow is reported, never
         # silently turned into inf); fp16=False selects bf16 operands.
+        # strict_fp32 keeps fp32 activations end to end (3xTF32 projections).
         mode = (RG_MODE_INT8_FULL if int8_activations else RG_MODE_INT8_W if int8
-                else RG_MODE_F16 if fp16 else RG_MODE_BF16)
+                else RG_MODE_FP32 if strict_fp32 else RG_MODE_F16 if fp16 else RG_MODE_BF16)
         H = config.hidden_size
         if dim and not (1 <= dim <= H):
             raise RembedError(f"rembed: WithDim({dim}) out of range [1, {H}]")
@@ -325,7 +326,7 @@ class Embedder:
 
 
 def load(ref: str | os.PathLike, *, int8: bool = False, int8_activations: bool = False, dim: int = 0,
-         devices: Sequence[int] = (0,), fp16: bool = True) -> Embedder:
+         devices: Sequence[int] = (0,), fp16: bool = True, strict_fp32: bool = False) -> Embedder:
     """rembed.Load over a converted model directory (manifest.json +
     model.safetensors).  Hub download and HF-config derivation stay with the
     reference host."""
@@ -335,4 +336,4 @@ def load(ref: str | os.PathLike, *, int8: bool = False, int8_activations: bool =
     cfg = Config.load(p / "manifest.json")
     weights = read_safetensors(p / "model.safetensors")
     return Embedder(cfg, weights, int8=int8, int8_activations=int8_activations, dim=dim, devices=devices,
-                    fp16=fp16)
+                    fp16=fp16, strict_fp32=strict_fp32)

@@ -134,3 +134,23 @@ def test_int8_weights_large_batch_widened_path(cuda):
     cos = cosines(big[:8], want)
     print(f"\n[parity] bge-base w-int8 widened path: min cos {cos.min():.7f}")
     assert cos.min() >= COS_INT8_W
+
+
+# strict fp32 (RG_MODE_FP32): the north-star bar, max-abs <= 1e-4 per embedding
+MAXABS_STRICT = 1e-4
+
+
+@pytest.mark.parametrize("name,nseq,lo,hi", CASES + [("modernbert-base", 3, 100, 300), ("nomic-embed-v1.5", 3, 16, 256),
+                                                     ("mpnet-base", 3, 16, 300), ("tiny-roberta", 5, 1, 200)])
+def test_strict_fp32_parity(cuda, name, nseq, lo, hi):
+    cfg = synth.preset(name)
+    w = synth.make_weights(cfg, seed=51)
+    ids, cu = synth.make_batch(cfg, nseq, lo, hi, seed=52)
+    gpu = Embedder(cfg, w, strict_fp32=True)
+    assert not gpu.quantized()
+    got = gpu.embed_packed(ids, cu)
+    gpu.close()
+    want = oracle.OracleModel(cfg, w, oracle.QUANT_NONE).embed(ids, cu)
+    err = np.abs(got - want).max()
+    print(f"\n[parity] {name} strict fp32: min cos {cosines(got, want).min():.9f}, max abs {err:.2e}")
+    assert err <= MAXABS_STRICT
