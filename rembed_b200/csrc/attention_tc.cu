@@ -4,7 +4,8 @@
 // CTA = 128 query rows of one (sequence, query head); key/value blocks of
 // BKV rows.  Roles (192 threads):
 //   warp 0     TMA producer: the Q tile once, then K blocks into a 2-deep
-//              ring and V blocks into one buffer, straight from the fused
+//              ring and V blocks into a 2-deep (head dim 64) or single
+//              buffer, straight from the fused
 //              token-major qkv buffer (128-byte swizzle);
 //   warp 1     TMEM allocator and MMA issuer (one thread):
 //                S  = Q K^T   (M 128, N BKV, K D; both operands K-major)
@@ -38,7 +39,8 @@ struct AttnTc {
     static constexpr int Q_BYTES = 128 * D * 2;
     static constexpr int KV_BYTES = BKV * D * 2;
     static constexpr int P_BYTES = 128 * BKV * 2;
-    static constexpr int SMEM = Q_BYTES + 3 * KV_BYTES + P_BYTES + 1024 + 256;
+    static constexpr int VST = D == 64 ? 2 : 1;  // V stages (two CTAs of D = 128 fill the SM with one)
+    static constexpr int SMEM = Q_BYTES + (2 + VST) * KV_BYTES + P_BYTES + 1024 + 256;
     // S at column 0 (BKV wide), O at column O_COL (D wide)
     static constexpr uint32_t O_COL = 64;
     static constexpr uint32_t TMEM_COLS = D == 64 ? 128 : 256;
@@ -67,20 +69,20 @@ __global__ void __launch_bounds__(192, AttnTc<D>::MIN_BLOCKS)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem;
     uint8_t* sK = sQ + S::Q_BYTES;  // [2][KV_BYTES]
-    uint8_t* sV = sK + 2 * S::KV_BYTES;
-    uint8_t* sP = sV + S::KV_BYTES;
+    uint8_t* sV = sK + 2 * S::KV_BYTES;  // [VST][KV_BYTES]
+    uint8_t* sP = sV + S::VST * S::KV_BYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sP + S::P_BYTES);
     uint64_t* qbar = bars + 0;
     uint64_t* kfull = bars + 1;   // [2]
     uint64_t* kempty = bars + 3;  // [2]
-    uint64_t* vfull = bars + 5;
-    uint64_t* vempty = bars + 6;
-    uint64_t* sfull = bars + 7;
-    uint64_t* sfree = bars + 8;
-    uint64_t* pfull = bars + 9;
-    uint64_t* ofull = bars + 10;
-    uint64_t* drain = bars + 11;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+    uint64_t* vfull = bars + 5;   // [2]
+    uint64_t* vempty = bars + 7;  // [2]
+    uint64_t* sfull = bars + 9;
+    uint64_t* sfree = bars + 10;
+    uint64_t* pfull = bars + 11;
+    uint64_t* ofull = bars + 12;
+    uint64_t* drain = bars + 13;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -95,9 +97,9 @@ __global__ void __launch_bounds__(192, AttnTc<D>::MIN_BLOCKS)
         for (int i = 0; i < 2; ++i) {
             mbar_init(&kfull[i], 1);
             mbar_init(&kempty[i], 1);
+            mbar_init(&vfull[i], 1);
+            mbar_init(&vempty[i], 1);
         }
-        mbar_init(vfull, 1);
-        mbar_init(vempty, 1);
         mbar_init(sfull, 1);
         mbar_init(sfree, 4);  // one arrival per softmax warp
         mbar_init(pfull, 4);
@@ -140,17 +142,19 @@ __global__ void __launch_bounds__(192, AttnTc<D>::MIN_BLOCKS)
                 for (int b = 0; b < QB; ++b)
                     tma_load_2d(sK + st * S::KV_BYTES + b * BKV * 128, &tmK, &kfull[st], hk * D + b * 64, row);
                 arm(1 + st, (i >> 1) & 1);
-                if (i >= 1 && !mbar_wait(vempty, (i - 1) & 1, status, abort_flag)) break;
-                mbar_arrive_expect_tx(vfull, S::KV_BYTES);
+                const int vs = i % S::VST, vu = i / S::VST;  // V stage and its use count
+                if (vu >= 1 && !mbar_wait(&vempty[vs], (vu - 1) & 1, status, abort_flag)) break;
+                mbar_arrive_expect_tx(&vfull[vs], S::KV_BYTES);
                 for (int b = 0; b < QB; ++b)
-                    tma_load_2d(sV + b * BKV * 128, &tmV, vfull, hk * D + b * 64, row);
-                arm(3, i & 1);
+                    tma_load_2d(sV + vs * S::KV_BYTES + b * BKV * 128, &tmV, &vfull[vs], hk * D + b * 64, row);
+                arm(3 + vs, vu & 1);
             }
             // every load issued has landed before the CTA may exit
             if (armed & 1) mbar_drain(qbar, parity & 1);
-            for (int b = 0; b < 2; ++b)
+            for (int b = 0; b < 2; ++b) {
                 if (armed & (2u << b)) mbar_drain(&kfull[b], (parity >> (1 + b)) & 1);
-            if (armed & 8) mbar_drain(vfull, (parity >> 3) & 1);
+                if (armed & (8u << b)) mbar_drain(&vfull[b], (parity >> (3 + b)) & 1);
+            }
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -177,17 +181,19 @@ __global__ void __launch_bounds__(192, AttnTc<D>::MIN_BLOCKS)
                     issued = true;
                     umma_commit(sfull);
                     umma_commit(&kempty[st]);
-                    if (!mbar_wait(pfull, i & 1, status, abort_flag) || !mbar_wait(vfull, i & 1, status, abort_flag))
+                    const int vs = i % S::VST, vu = i / S::VST;
+                    if (!mbar_wait(pfull, i & 1, status, abort_flag) ||
+                        !mbar_wait(&vfull[vs], vu & 1, status, abort_flag))
                         break;
                     tc_fence_after();
 #pragma unroll
                     for (int kk = 0; kk < BKV / 16; ++kk) {
                         const uint64_t a = sdesc_k128(smem_u32(sP + (kk >> 2) * 16384 + (kk & 3) * 32));
-                        const uint64_t b = sdesc_mn128(smem_u32(sV + kk * 2048), BKV * 128);
+                        const uint64_t b = sdesc_mn128(smem_u32(sV + vs * S::KV_BYTES + kk * 2048), BKV * 128);
                         umma_bf16(tO, a, b, idO, (i | kk) != 0);
                     }
                     umma_commit(ofull);
-                    umma_commit(vempty);
+                    umma_commit(&vempty[vs]);
                 }
             }
             if (issued) {
@@ -218,34 +224,48 @@ __global__ void __launch_bounds__(192, AttnTc<D>::MIN_BLOCKS)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(sfree);
-            // scores in the exp2 domain, masked keys at -inf
-            float mx = -INFINITY;
+            // Scores in the exp2 domain, masked keys at -inf.  PLAIN blocks
+            // that lie inside the sequence need no mask, and the scale folds
+            // into the exponent's FMA: with c = scale * log2(e) > 0,
+            // max(c s) = c max(s) and exp2(c s - c m) = exp2(fma(s, c, -c m)).
+            float m_new;
+            float cs = 1.0f;  // factor applied inside the exponent
+            if (PLAIN && kbase + BKV <= L) {
+                float mx = __uint_as_float(sr[0]);
 #pragma unroll
-            for (int c = 0; c < BKV; ++c) {
-                const int kj = kbase + c;
-                float x = __uint_as_float(sr[c]);
-                bool valid = kj < L;
-                if constexpr (PLAIN) {
-                    x *= p.scale_log2;
-                } else {
-                    const int rel = kj - qi;
-                    valid = valid && rel >= p.rel_lo && rel <= p.rel_hi;
-                    if (p.bias) {
-                        // scores * scale + bias[h][rel] (bert.go:876-889)
-                        const int bi = min(max(rel + p.bias_off, 0), 2 * p.bias_off);
-                        x = (x * p.scale + __ldg(p.bias + static_cast<int64_t>(h) * (2 * p.bias_off + 1) + bi)) *
-                            1.4426950408889634f;
-                    } else {
+                for (int c = 1; c < BKV; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+                m_new = fmaxf(m, mx * p.scale_log2);
+                cs = p.scale_log2;
+            } else {
+                float mx = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < BKV; ++c) {
+                    const int kj = kbase + c;
+                    float x = __uint_as_float(sr[c]);
+                    bool valid = kj < L;
+                    if constexpr (PLAIN) {
                         x *= p.scale_log2;
+                    } else {
+                        const int rel = kj - qi;
+                        valid = valid && rel >= p.rel_lo && rel <= p.rel_hi;
+                        if (p.bias) {
+                            // scores * scale + bias[h][rel] (bert.go:876-889)
+                            const int bi = min(max(rel + p.bias_off, 0), 2 * p.bias_off);
+                            x = (x * p.scale + __ldg(p.bias + static_cast<int64_t>(h) * (2 * p.bias_off + 1) + bi)) *
+                                1.4426950408889634f;
+                        } else {
+                            x *= p.scale_log2;
+                        }
                     }
+                    x = valid ? x : -INFINITY;
+                    sr[c] = __float_as_uint(x);
+                    mx = fmaxf(mx, x);
                 }
-                x = valid ? x : -INFINITY;
-                sr[c] = __float_as_uint(x);
-                mx = fmaxf(mx, x);
+                m_new = fmaxf(m, mx);
             }
-            const float m_new = fmaxf(m, mx);
             const float m_use = m_new == -INFINITY ? 0.f : m_new;  // a row with no key yet keeps p = 0
-            const float alpha = ex2f(m - m_use);                  // m = -inf: 0 (O and l are still 0)
+            const float xoff = -m_use;
+            const float alpha = ex2f(m - m_use);  // m = -inf: 0 (O and l are still 0)
             // P V of the previous block is done: O is final for it and the P
             // buffer is free
             if (i > 0) {
@@ -262,8 +282,8 @@ __global__ void __launch_bounds__(192, AttnTc<D>::MIN_BLOCKS)
                 uint32_t w[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const float a = ex2f(__uint_as_float(sr[8 * q + 2 * e]) - m_use);
-                    const float b = ex2f(__uint_as_float(sr[8 * q + 2 * e + 1]) - m_use);
+                    const float a = ex2f(fmaf(__uint_as_float(sr[8 * q + 2 * e]), cs, xoff));
+                    const float b = ex2f(fmaf(__uint_as_float(sr[8 * q + 2 * e + 1]), cs, xoff));
                     l += a + b;
                     w[e] = pack2<F16>(a, b);
                 }
