@@ -43,6 +43,11 @@ WORKLOADS = {
     "bge-base-b256xL128": dict(preset="bge-base", nseq=256, lo=128, hi=128),
     "bge-base-b256xU16-512": dict(preset="bge-base", nseq=256, lo=16, hi=512),
     "minilm-l6-b32xU8-128": dict(preset="minilm-l6", nseq=32, lo=8, hi=128),
+    # the other architectures' configurations (per GPU; EmbeddingGemma's
+    # 512-sequence batch is sharded over 8 GPUs: 64 per GPU)
+    "qwen3-0.6b-b128xU32-1024": dict(preset="qwen3-0.6b", nseq=128, lo=32, hi=1024),
+    "modernbert-base-b64xU512-8192": dict(preset="modernbert-base", nseq=64, lo=512, hi=8192),
+    "embeddinggemma-300m-b64xU16-2048": dict(preset="embeddinggemma-300m", nseq=64, lo=16, hi=2048),
 }
 METRIC = "embeddings/sec at bge-base b256×L128 (fp & int8), 1–8 GPU; tensor-pipe util %"
 # mode -> (Embedder keyword arguments, oracle quantisation name, dtype the path computes in)
@@ -91,11 +96,6 @@ def make_inputs(wl, seed, n=None):
     cfg = synth.preset(wl["preset"])
     ids, cu = synth.make_batch(cfg, n or wl["nseq"], wl["lo"], wl["hi"], seed=seed)
     return cfg, ids, cu
-
-
-def gemm_flops_per_token(cfg) -> float:
-    H, I = cfg.hidden_size, cfg.intermediate_size
-    return 2.0 * cfg.num_hidden_layers * (H * 3 * H + H * H + 2 * H * I)
 
 
 ORACLE_PATH = {"f16": "fp32", "bf16": "fp32", "int8_w": "weight-int8", "int8_full": "full int8", "fp32": "fp32"}
@@ -389,7 +389,7 @@ def ours(args, rank, world, local_rank):
                 "d2h_bytes_per_step": int(host_out.nbytes + 4)},
         "clocks": clocks,
         "gpu_launches": int(launches_per_step * args.steps),
-        "gemm_tflops_effective": round(gemm_flops_per_token(cfg) * T * world * args.steps / (ms / 1000) / 1e12, 1),
+        "gemm_tflops_effective": round(g["flops"] / max(args.steps, 1) / (ms / args.steps / 1000) / 1e12, 1),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_sample(wl, args.mode, args.cpu_seconds, host_threads())

@@ -54,7 +54,10 @@ __device__ __forceinline__ float ex2f(float x) {
     return y;
 }
 
-template <int D, bool F16, bool PLAIN>
+// PLAIN: no window, no bias (only the sequence end masks keys); BIAS: the
+// MPNet relative-position bias (and any window); neither: a window / causal
+// mask without bias.
+template <int D, bool F16, bool PLAIN, bool BIAS>
 __global__ void __launch_bounds__(192, AttnTc<D>::MIN_BLOCKS)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, AttnParams p, int* status) {
@@ -224,50 +227,81 @@ __global__ void __launch_bounds__(192, AttnTc<D>::MIN_BLOCKS)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(sfree);
-            // Scores in the exp2 domain, masked keys at -inf.  PLAIN blocks
-            // that lie inside the sequence need no mask, and the scale folds
-            // into the exponent's FMA: with c = scale * log2(e) > 0,
-            // max(c s) = c max(s) and exp2(c s - c m) = exp2(fma(s, c, -c m)).
-            float m_new;
+            // Scores in the exp2 domain.  A block needs the per-key mask only
+            // if it reaches past the sequence end or some (row, key) pair of
+            // the tile falls outside the window [rel_lo, rel_hi]; otherwise
+            // the scale folds into the exponent's FMA: with c = scale *
+            // log2(e) > 0, max(c s) = c max(s) and exp2(c s - m) =
+            // exp2(fma(s, c, -m)).  Uniform across the CTA.
+            const bool fast = !BIAS && kbase + BKV <= L && kbase - (q0 + 127) >= p.rel_lo &&
+                              kbase + BKV - 1 - q0 <= p.rel_hi;
+            float mx;
             float cs = 1.0f;  // factor applied inside the exponent
-            if (PLAIN && kbase + BKV <= L) {
-                float mx = __uint_as_float(sr[0]);
+            if (fast) {
+                // 8 independent partial maxima (instruction-level parallelism)
+                float pm[8];
 #pragma unroll
-                for (int c = 1; c < BKV; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
-                m_new = fmaxf(m, mx * p.scale_log2);
+                for (int e = 0; e < 8; ++e) pm[e] = __uint_as_float(sr[e]);
+#pragma unroll
+                for (int c = 8; c < BKV; ++c) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(sr[c]));
+                mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                           fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) *
+                     p.scale_log2;
                 cs = p.scale_log2;
-            } else {
-                float mx = -INFINITY;
+            } else if constexpr (BIAS) {
+                // the bias term: one table load per key; sr stays in
+                // registers (the loop is unrolled) but the loads are issued
+                // a few at a time
+                mx = -INFINITY;
+                const float* brow = p.bias + static_cast<int64_t>(h) * (2 * p.bias_off + 1);
 #pragma unroll
                 for (int c = 0; c < BKV; ++c) {
                     const int kj = kbase + c;
-                    float x = __uint_as_float(sr[c]);
-                    bool valid = kj < L;
-                    if constexpr (PLAIN) {
-                        x *= p.scale_log2;
-                    } else {
-                        const int rel = kj - qi;
-                        valid = valid && rel >= p.rel_lo && rel <= p.rel_hi;
-                        if (p.bias) {
-                            // scores * scale + bias[h][rel] (bert.go:876-889)
-                            const int bi = min(max(rel + p.bias_off, 0), 2 * p.bias_off);
-                            x = (x * p.scale + __ldg(p.bias + static_cast<int64_t>(h) * (2 * p.bias_off + 1) + bi)) *
-                                1.4426950408889634f;
-                        } else {
-                            x *= p.scale_log2;
-                        }
-                    }
+                    const int rel = kj - qi;
+                    const int bi = min(max(rel + p.bias_off, 0), 2 * p.bias_off);
+                    // scores * scale + bias[h][rel] (bert.go:876-889)
+                    float x = (__uint_as_float(sr[c]) * p.scale + __ldg(brow + bi)) * 1.4426950408889634f;
+                    const bool valid = kj < L && rel >= p.rel_lo && rel <= p.rel_hi;
                     x = valid ? x : -INFINITY;
                     sr[c] = __float_as_uint(x);
                     mx = fmaxf(mx, x);
                 }
-                m_new = fmaxf(m, mx);
+            } else {
+                mx = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < BKV; ++c) {
+                    const int kj = kbase + c;
+                    const int rel = kj - qi;
+                    float x = __uint_as_float(sr[c]);
+                    const bool valid = kj < L && rel >= p.rel_lo && rel <= p.rel_hi;
+                    x *= p.scale_log2;
+                    x = valid ? x : -INFINITY;
+                    sr[c] = __float_as_uint(x);
+                    mx = fmaxf(mx, x);
+                }
             }
-            const float m_use = m_new == -INFINITY ? 0.f : m_new;  // a row with no key yet keeps p = 0
+            // Lazy rescaling: the exponent keeps the max it used (m) until
+            // the block max exceeds it by more than 2^8, so P <= 256 and O
+            // needs rescaling (and the wait for the previous P V before it)
+            // only then.  The final division by l cancels the stale max.
+            const bool grow = mx > m + 8.0f;  // always true while m = -inf and the row has a key
+            const float m_use0 = grow ? mx : m;
+            const float m_use = m_use0 == -INFINITY ? 0.f : m_use0;  // a row with no key yet keeps p = 0
             const float xoff = -m_use;
             const float alpha = ex2f(m - m_use);  // m = -inf: 0 (O and l are still 0)
-            // P V of the previous block is done: O is final for it and the P
-            // buffer is free
+            // exponentials into packed 16-bit pairs (before waiting on the
+            // previous P V, so they overlap it); the row sum in 4 partials
+            uint32_t pk[BKV / 2];
+            float ls[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int c = 0; c < BKV / 2; ++c) {
+                const float a = ex2f(fmaf(__uint_as_float(sr[2 * c]), cs, xoff));
+                const float b = ex2f(fmaf(__uint_as_float(sr[2 * c + 1]), cs, xoff));
+                ls[c & 3] += a + b;
+                pk[c] = pack2<F16>(a, b);
+            }
+            // The previous P V is done: the P buffer is free and O holds
+            // every earlier block.
             if (i > 0) {
                 if (!mbar_wait(ofull, (i - 1) & 1, status, abort_flag)) {
                     ok = false;
@@ -275,22 +309,13 @@ __global__ void __launch_bounds__(192, AttnTc<D>::MIN_BLOCKS)
                 }
                 tc_fence_after();
             }
-            l *= alpha;
-            // P row: 16 bytes (8 keys) at a time into the swizzled K-major tile
+            l = l * alpha + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
 #pragma unroll
-            for (int q = 0; q < BKV / 8; ++q) {
-                uint32_t w[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float a = ex2f(fmaf(__uint_as_float(sr[8 * q + 2 * e]), cs, xoff));
-                    const float b = ex2f(fmaf(__uint_as_float(sr[8 * q + 2 * e + 1]), cs, xoff));
-                    l += a + b;
-                    w[e] = pack2<F16>(a, b);
-                }
-                *reinterpret_cast<uint4*>(sP + r * 128 + ((q ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-            }
-            // rescale the O row when the running max moved (warp-uniform: the
-            // TMEM accesses are warp-wide)
+            for (int q = 0; q < BKV / 8; ++q)
+                *reinterpret_cast<uint4*>(sP + r * 128 + ((q ^ (r & 7)) << 4)) =
+                    make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+            // rescale the O row when its max moved (warp-uniform: the TMEM
+            // accesses are warp-wide; rows that did not move scale by 1)
             if (i > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll
                 for (int c = 0; c < D / 32; ++c) {
@@ -303,7 +328,7 @@ __global__ void __launch_bounds__(192, AttnTc<D>::MIN_BLOCKS)
                 }
                 tmem_st_wait();
             }
-            m = m_new;
+            m = m_use0;
             fence_proxy_async_smem();  // P (generic writes) -> the MMA (async proxy)
             tc_fence_before();         // O rescale (tcgen05.st) -> the MMA
             __syncwarp();
@@ -376,11 +401,11 @@ static bool make_rows_tmap(CUtensorMap* map, const void* base, bool f16, uint64_
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int D, bool F16, bool PLAIN>
+template <int D, bool F16, bool PLAIN, bool BIAS>
 static cudaError_t launch_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                              const AttnParams& p, int nseq, int max_len, int heads, int* status, cudaStream_t st) {
     constexpr int smem = AttnTc<D>::SMEM;
-    auto kern = attention_tc_kernel<D, F16, PLAIN>;
+    auto kern = attention_tc_kernel<D, F16, PLAIN, BIAS>;
     static unsigned configured = 0;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -408,17 +433,16 @@ cudaError_t launch_attention_tc(const AttnParams& p, int T, int nseq, int max_le
         !make_rows_tmap(&tv, p.v, p.f16, T, static_cast<uint64_t>(kv_heads) * D, p.ldv, bkv))
         return cudaErrorInvalidValue;
     const bool plain = !p.bias && p.rel_lo <= -max_len && p.rel_hi >= max_len;
-#define RG_TC_CASE(DD, FF, PP)                                                              \
-    if (D == DD && p.f16 == FF && plain == PP)                                              \
-        return launch_tc<DD, FF, PP>(tq, tk, tv, p, nseq, max_len, heads, status, st);
-    RG_TC_CASE(64, false, true)
-    RG_TC_CASE(64, false, false)
-    RG_TC_CASE(64, true, true)
-    RG_TC_CASE(64, true, false)
-    RG_TC_CASE(128, false, true)
-    RG_TC_CASE(128, false, false)
-    RG_TC_CASE(128, true, true)
-    RG_TC_CASE(128, true, false)
+#define RG_TC_CASE(DD, FF)                                                                         \
+    if (D == DD && p.f16 == FF) {                                                                  \
+        if (p.bias) return launch_tc<DD, FF, false, true>(tq, tk, tv, p, nseq, max_len, heads, status, st); \
+        if (plain) return launch_tc<DD, FF, true, false>(tq, tk, tv, p, nseq, max_len, heads, status, st);  \
+        return launch_tc<DD, FF, false, false>(tq, tk, tv, p, nseq, max_len, heads, status, st);            \
+    }
+    RG_TC_CASE(64, false)
+    RG_TC_CASE(64, true)
+    RG_TC_CASE(128, false)
+    RG_TC_CASE(128, true)
 #undef RG_TC_CASE
     return cudaErrorInvalidValue;
 }
