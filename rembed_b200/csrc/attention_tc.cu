@@ -1,5 +1,5 @@
 // attention_tc.cu - varlen flash attention on the 5th-generation tensor
-// cores (tcgen05) for head dims 64 and 128.
+// cores (tcgen05) for head dims 32, 64, 128 and 256.
 //
 // CTA = 128 query rows of one (sequence, query head); key/value blocks of
 // BKV rows.  Roles (192 threads):
@@ -34,18 +34,21 @@ namespace rg {
 
 template <int D>
 struct AttnTc {
-    static constexpr int BKV = 64;      // keys per block
-    static constexpr int QB = D / 64;   // 64-column (128-byte) blocks of a row
-    static constexpr int Q_BYTES = 128 * D * 2;
-    static constexpr int KV_BYTES = BKV * D * 2;
+    static constexpr int BKV = 64;  // keys per block
+    // 64-column (128-byte, one swizzle atom wide) blocks loaded per row; a
+    // head of 32 loads one such block and the MMAs use its first 32 columns
+    static constexpr int QB = D < 64 ? 1 : D / 64;
+    static constexpr int Q_BYTES = 128 * QB * 128;
+    static constexpr int KV_BYTES = BKV * QB * 128;
     static constexpr int P_BYTES = 128 * BKV * 2;
-    static constexpr int VST = D == 64 ? 2 : 1;  // V stages (two CTAs of D = 128 fill the SM with one)
+    static constexpr int VST = D <= 64 ? 2 : 1;  // V stages (larger heads fill the SM with one)
     static constexpr int SMEM = Q_BYTES + (2 + VST) * KV_BYTES + P_BYTES + 1024 + 256;
     // S at column 0 (BKV wide), O at column O_COL (D wide)
     static constexpr uint32_t O_COL = 64;
-    static constexpr uint32_t TMEM_COLS = D == 64 ? 128 : 256;
+    static constexpr uint32_t TMEM_COLS = D <= 64 ? 128 : (D == 128 ? 256 : 512);
     static constexpr int THREADS = 192;
-    static constexpr int MIN_BLOCKS = D == 64 ? 3 : 2;  // CTAs per SM (shared memory, TMEM, registers)
+    // CTAs per SM (shared memory, TMEM, registers)
+    static constexpr int MIN_BLOCKS = D <= 64 ? 3 : (D == 128 ? 2 : 1);
 };
 
 __device__ __forceinline__ float ex2f(float x) {
@@ -168,22 +171,30 @@ __global__ void __launch_bounds__(192, AttnTc<D>::MIN_BLOCKS)
             constexpr uint32_t idO = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 16) |
                                      ((uint32_t)(D >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
             bool issued = false;
-            if (mbar_wait(qbar, 0, status, abort_flag)) {
-                for (int i = 0; i < nb; ++i) {
-                    const int st = i & 1;
-                    if (!mbar_wait(&kfull[st], (i >> 1) & 1, status, abort_flag)) break;
-                    if (i > 0 && !mbar_wait(sfree, (i - 1) & 1, status, abort_flag)) break;
-                    tc_fence_after();
+            // S = Q K^T of block i into the (single) S buffer, once the
+            // softmax warps have read the previous one
+            auto issue_s = [&](int i) -> bool {
+                const int st = i & 1;
+                if (!mbar_wait(&kfull[st], (i >> 1) & 1, status, abort_flag)) return false;
+                if (i > 0 && !mbar_wait(sfree, (i - 1) & 1, status, abort_flag)) return false;
+                tc_fence_after();
 #pragma unroll
-                    for (int ks = 0; ks < D / 16; ++ks) {
-                        const uint64_t a = sdesc_k128(smem_u32(sQ + (ks >> 2) * 16384 + (ks & 3) * 32));
-                        const uint64_t b =
-                            sdesc_k128(smem_u32(sK + st * S::KV_BYTES + (ks >> 2) * BKV * 128 + (ks & 3) * 32));
-                        umma_bf16(tS, a, b, idS, ks > 0);
-                    }
-                    issued = true;
-                    umma_commit(sfull);
-                    umma_commit(&kempty[st]);
+                for (int ks = 0; ks < D / 16; ++ks) {
+                    const uint64_t a = sdesc_k128(smem_u32(sQ + (ks >> 2) * 16384 + (ks & 3) * 32));
+                    const uint64_t b =
+                        sdesc_k128(smem_u32(sK + st * S::KV_BYTES + (ks >> 2) * BKV * 128 + (ks & 3) * 32));
+                    umma_bf16(tS, a, b, idS, ks > 0);
+                }
+                issued = true;
+                umma_commit(sfull);
+                umma_commit(&kempty[st]);
+                return true;
+            };
+            if (mbar_wait(qbar, 0, status, abort_flag) && issue_s(0)) {
+                for (int i = 0; i < nb; ++i) {
+                    // the next block's S goes first: it runs while the softmax
+                    // warps work on this block
+                    if (i + 1 < nb && !issue_s(i + 1)) break;
                     const int vs = i % S::VST, vu = i / S::VST;
                     if (!mbar_wait(pfull, i & 1, status, abort_flag) ||
                         !mbar_wait(&vfull[vs], vu & 1, status, abort_flag))
@@ -419,7 +430,9 @@ static cudaError_t launch_tc(const CUtensorMap& tq, const CUtensorMap& tk, const
     return cudaGetLastError();
 }
 
-bool attention_tc_supported(int head_dim) { return head_dim == 64 || head_dim == 128; }
+bool attention_tc_supported(int head_dim) {
+    return head_dim == 32 || head_dim == 64 || head_dim == 128 || head_dim == 256;
+}
 
 cudaError_t launch_attention_tc(const AttnParams& p, int T, int nseq, int max_len, int heads, int kv_heads,
                                 int head_dim, int* status, cudaStream_t st) {
@@ -439,10 +452,14 @@ cudaError_t launch_attention_tc(const AttnParams& p, int T, int nseq, int max_le
         if (plain) return launch_tc<DD, FF, true, false>(tq, tk, tv, p, nseq, max_len, heads, status, st);  \
         return launch_tc<DD, FF, false, false>(tq, tk, tv, p, nseq, max_len, heads, status, st);            \
     }
+    RG_TC_CASE(32, false)
+    RG_TC_CASE(32, true)
     RG_TC_CASE(64, false)
     RG_TC_CASE(64, true)
     RG_TC_CASE(128, false)
     RG_TC_CASE(128, true)
+    RG_TC_CASE(256, false)
+    RG_TC_CASE(256, true)
 #undef RG_TC_CASE
     return cudaErrorInvalidValue;
 }

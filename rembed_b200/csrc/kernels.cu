@@ -337,57 +337,116 @@ cudaError_t launch_add_rmsnorm(float* x32, const float* o32, const float* g, flo
 
 // ---------------------------------------------------------------------------
 // QK-norm + RoPE in place on the q and k heads of the fused qkv buffer: one
-// warp per (token, head).  Lane holds elements d = lane + 32k; with dh >= 64
-// the rotate-half partner d + dh/2 is in the same lane.  RMSNorm over dh with
-// the q or k gain (qwen3.go:485-508, gemma3.go:303-330), then the rotation
-// at the token's position in its sequence (modernbert.go:125-143: products
-// rounded before the add/sub).
+// warp per token, over all its q and k heads.  A unit is 8 consecutive dims
+// d in [8j, 8j + 8) of a head and their rotate-half partners d + dh/2: two
+// 16-byte vectors (32 bytes for fp32).  A head has U = dh/16 units, held by
+// U consecutive lanes (U divides 32), so the head's RMS (qwen3.go:485-508,
+// gemma3.go:303-330) reduces with U-lane shuffles; then the rotation at the
+// token's position in its sequence (modernbert.go:125-143: products rounded
+// before the add/sub).
+template <bool F16, bool F32>
+__device__ __forceinline__ void load8(const void* base, int64_t off, float (&v)[8]) {
+    if constexpr (F32) {
+        const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(base) + off);
+        const float4 a = q[0], b = q[1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+        const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + off);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 f = unpack2<F16>(w[e]);
+            v[2 * e] = f.x;
+            v[2 * e + 1] = f.y;
+        }
+    }
+}
+template <bool F16, bool F32>
+__device__ __forceinline__ float store8(void* base, int64_t off, const float (&v)[8]) {
+    if constexpr (F32) {
+        float4* q = reinterpret_cast<float4*>(static_cast<float*>(base) + off);
+        q[0] = make_float4(v[0], v[1], v[2], v[3]);
+        q[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+        *reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + off) =
+            make_uint4(pack2<F16>(v[0], v[1]), pack2<F16>(v[2], v[3]), pack2<F16>(v[4], v[5]),
+                       pack2<F16>(v[6], v[7]));
+    }
+    float a = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) a = fmaxf(a, fabsf(v[e]));
+    return a;
+}
+
 template <int DH, bool F16, bool F32>
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkRopeParams p) {
-    constexpr int E = DH / 32, HALF = DH / 2;
+    constexpr int HALF = DH / 2, U = DH / 16;
     const int lane = threadIdx.x & 31;
-    const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int heads = p.nq + p.nkv;
-    if (item >= p.T * heads) return;
-    const int t = item / heads, h = item % heads;
-    const bool is_q = h < p.nq;
-    const int64_t roff = static_cast<int64_t>(t) * p.ld + (is_q ? h * DH : p.nq * DH + (h - p.nq) * DH);
-    uint16_t* row = F32 ? nullptr : p.qkv + roff;
-    float* row32 = F32 ? p.qkv32 + roff : nullptr;
-    float v[E];
-#pragma unroll
-    for (int k = 0; k < E; ++k) v[k] = F32 ? row32[lane + 32 * k] : to_f32<F16>(row[lane + 32 * k]);
-    const float* g = is_q ? p.q_norm : p.k_norm;
-    if (g) {
-        float q = 0.f;
-#pragma unroll
-        for (int k = 0; k < E; ++k) q += v[k] * v[k];
-        const float inv = 1.0f / sqrtf(warp_sum(q) / static_cast<float>(DH) + p.eps);
-#pragma unroll
-        for (int k = 0; k < E; ++k) v[k] = v[k] * inv * __ldg(g + lane + 32 * k);
-    }
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= p.T) return;
+    void* base = F32 ? static_cast<void*>(p.qkv32) : static_cast<void*>(p.qkv);
+    const int64_t row = static_cast<int64_t>(t) * p.ld;
+    const float* cs = nullptr;
+    const float* sn = nullptr;
     if (p.cos) {
         const int s = seq_of_token(p.cu, p.nseq, t);
         const int pos = t - __ldg(p.cu + s);
-        const float* cs = p.cos + static_cast<int64_t>(pos) * HALF;
-        const float* sn = p.sin + static_cast<int64_t>(pos) * HALF;
-#pragma unroll
-        for (int k = 0; k < E / 2; ++k) {
-            const int d = lane + 32 * k;
-            const float x1 = v[k], x2 = v[k + E / 2];
-            const float cc = __ldg(cs + d), ss = __ldg(sn + d);
-            v[k] = __fsub_rn(__fmul_rn(x1, cc), __fmul_rn(x2, ss));
-            v[k + E / 2] = __fadd_rn(__fmul_rn(x2, cc), __fmul_rn(x1, ss));
-        }
+        cs = p.cos + static_cast<int64_t>(pos) * HALF;
+        sn = p.sin + static_cast<int64_t>(pos) * HALF;
     }
+    const int heads = p.nq + p.nkv;
     float amax = 0.f;
+    for (int u0 = 0; u0 < heads * U; u0 += 32) {
+        const int u = u0 + lane;
+        const bool on = u < heads * U;  // lanes past the last head still join the shuffles
+        const int h = on ? u / U : 0, j = u % U;
+        const bool is_q = h < p.nq;
+        const int64_t off = row + (is_q ? h * DH : p.nq * DH + (h - p.nq) * DH) + 8 * j;
+        float x1[8], x2[8];
+        if (on) {
+            load8<F16, F32>(base, off, x1);
+            load8<F16, F32>(base, off + HALF, x2);
+        } else {
 #pragma unroll
-    for (int k = 0; k < E; ++k) {
-        if constexpr (F32)
-            row32[lane + 32 * k] = v[k];
-        else
-            row[lane + 32 * k] = from_f32<F16>(v[k]);
-        amax = fmaxf(amax, fabsf(v[k]));
+            for (int e = 0; e < 8; ++e) x1[e] = x2[e] = 0.f;
+        }
+        const float* g = is_q ? p.q_norm : p.k_norm;
+        if (p.q_norm || p.k_norm) {
+            float q = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) q += x1[e] * x1[e] + x2[e] * x2[e];
+#pragma unroll
+            for (int o = U / 2; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+            if (on && g) {
+                const float inv = 1.0f / sqrtf(q / static_cast<float>(DH) + p.eps);
+                const float4* g1 = reinterpret_cast<const float4*>(g + 8 * j);
+                const float4* g2 = reinterpret_cast<const float4*>(g + HALF + 8 * j);
+                const float4 a0 = __ldg(g1), a1 = __ldg(g1 + 1), b0 = __ldg(g2), b1 = __ldg(g2 + 1);
+                const float ga[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const float gb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    x1[e] = x1[e] * inv * ga[e];
+                    x2[e] = x2[e] * inv * gb[e];
+                }
+            }
+        }
+        if (!on) continue;
+        if (cs) {
+            const float4* c4 = reinterpret_cast<const float4*>(cs + 8 * j);
+            const float4* s4 = reinterpret_cast<const float4*>(sn + 8 * j);
+            const float4 c0 = __ldg(c4), c1 = __ldg(c4 + 1), s0 = __ldg(s4), s1 = __ldg(s4 + 1);
+            const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+            const float ss[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float a = x1[e], b = x2[e];
+                x1[e] = __fsub_rn(__fmul_rn(a, cc[e]), __fmul_rn(b, ss[e]));
+                x2[e] = __fadd_rn(__fmul_rn(b, cc[e]), __fmul_rn(a, ss[e]));
+            }
+        }
+        amax = fmaxf(amax, store8<F16, F32>(base, off, x1));
+        amax = fmaxf(amax, store8<F16, F32>(base, off + HALF, x2));
     }
     if constexpr (F16)
         if (__any_sync(0xffffffffu, !(amax <= 65504.0f)) && lane == 0 && p.status)
@@ -396,13 +455,13 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkRopeParams p) {
 
 cudaError_t launch_qk_norm_rope(const QkRopeParams& p, int head_dim, cudaStream_t st) {
     if (p.T <= 0) return cudaSuccess;
-    const long items = static_cast<long>(p.T) * (p.nq + p.nkv);
-    const int grid = static_cast<int>((items + 7) / 8);
+    const int grid = (p.T + 7) / 8;
     switch (head_dim) {
 #define RG_QKR(DH)                                                                   \
     if (p.qkv32) qk_norm_rope_kernel<DH, false, true><<<grid, 256, 0, st>>>(p);    \
     else if (p.f16) qk_norm_rope_kernel<DH, true, false><<<grid, 256, 0, st>>>(p); \
     else qk_norm_rope_kernel<DH, false, false><<<grid, 256, 0, st>>>(p);
+    case 32: RG_QKR(32) break;
     case 64: RG_QKR(64) break;
     case 128: RG_QKR(128) break;
     case 256: RG_QKR(256) break;

@@ -1278,7 +1278,6 @@ int rg_init(const rg_model_desc* desc, const int* devices, int ndev, int mode, r
         const int dh = dm.dh;
         if (dh != 32 && dh != 64 && dh != 128 && dh != 256)
             fail("rg_init: head dim %d unsupported (32, 64, 128 or 256)", dh);
-        if (has_rope(d.arch) && dh == 32) fail("rg_init: RoPE needs head dim >= 64");
         if (dm.nkv <= 0 || dm.nq % dm.nkv != 0)
             fail("rg_init: num_attention_heads %d not divisible by num_key_value_heads %d", dm.nq, dm.nkv);
         if (d.arch == RG_ARCH_MODERNBERT && (d.global_attn_every_n_layers < 1 || d.local_attention < 2))
