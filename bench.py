@@ -256,21 +256,16 @@ def ours(args, rank, world, local_rank):
     from rembed_b200 import synth
     from rembed_b200.embedder import Embedder
 
+    from rembed_b200 import ranks
+
     torch.cuda.set_device(local_rank)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local_rank))
+    dist = ranks.init(ranks.RankInfo(rank, world, local_rank), "nccl", device=torch.device("cuda", local_rank))
     wl = WORKLOADS[args.workload]
     cfg = synth.preset(wl["preset"])
     weights = synth.make_weights(cfg, seed=0)
     emb = Embedder(cfg, weights, devices=[local_rank], **MODES[args.mode][0])
     del weights
-    _, ids, cu = make_inputs(wl, seed=1000 + rank)
+    _, ids, cu = make_inputs(wl, seed=ranks.batch_seed(rank))
     nseq, T = len(cu) - 1, int(cu[-1])
     d_ids = torch.from_numpy(ids).cuda()
     d_cu = torch.from_numpy(cu).cuda()
@@ -285,16 +280,11 @@ def ours(args, rank, world, local_rank):
         emb.forward_device(d_ids.data_ptr(), d_cu.data_ptr(), cu, d_out.data_ptr(), stream=stream.cuda_stream)
 
     def barrier():
-        if dist is not None:
-            dist.barrier()
+        ranks.barrier(dist)
         torch.cuda.synchronize()
 
     def max_over_ranks(x: float) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return ranks.max_over_ranks(dist, x, device="cuda")
 
     for _ in range(max(args.warmup, 1)):
         step()
@@ -394,18 +384,17 @@ def ours(args, rank, world, local_rank):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_sample(wl, args.mode, args.cpu_seconds, host_threads())
     emb.close()
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    ranks.finish(dist)
     if rank == 0:
         print(json.dumps(line), flush=True)
 
 
 def main():
     args = parse()
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    from rembed_b200.ranks import rank_info
+
+    info = rank_info()
+    rank, world, local_rank = info.rank, info.world, info.local_rank
     if args.impl == "reference":
         reference_arm(args, rank, world)
         return

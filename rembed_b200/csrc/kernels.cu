@@ -590,272 +590,11 @@ cudaError_t launch_quantize_rows(const __nv_bfloat16* x, int T, int K, int8_t* q
 }
 
 // ---------------------------------------------------------------------------
-// Attention.  CTA = (64 query rows, head, sequence), 4 warps x 16 rows;
-// key/value tiles of 64 rows; S = Q K^T and O += P V on bf16 mma.sync with
-// fp32 accumulators; online softmax in the exp2 domain.  Rows of the
-// shared tiles are padded by 16 bytes so ldmatrix is conflict-free.
-template <bool F16>
-__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    if constexpr (F16)
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-            "{%0,%1,%2,%3};"
-            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-    else
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-            "{%0,%1,%2,%3};"
-            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit_wait() {
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-}
-template <int D, int ROWS>
-__device__ __forceinline__ void load_tile(uint16_t* s, const uint16_t* g, int r0, int L, int ld) {
-    constexpr int LDS = D + 8;
-    constexpr int CPR = D / 8;  // 16-byte chunks per row
-    for (int i = threadIdx.x; i < ROWS * CPR; i += 128) {
-        const int r = i / CPR, c = i % CPR;
-        const int gr = r0 + r;
-        const bool ok = gr >= 0 && gr < L;
-        const uint16_t* src = g + static_cast<int64_t>(ok ? gr : 0) * ld + c * 8;
-        cp_async16(s + r * LDS + c * 8, src, ok);
-    }
-}
-
-// CTA = (64 query rows, query head, sequence); 4 warps x 16 rows; key
-// blocks of BKV rows.  Q (D <= 128: in registers; D = 256: re-read from
-// shared memory per k-step), S = Q K^T and O += P V on bf16 mma.sync with
-// fp32 accumulators, online softmax in the exp2 domain.
-template <int D, bool PLAIN, bool F16>
-__global__ void __launch_bounds__(128) attention_kernel(AttnParams p) {
-    constexpr int BKV = D == 256 ? 32 : 64;
-    constexpr int LDS = D + 8;
-    constexpr int KS = D / 16;     // k-steps over the head dim
-    constexpr int DT = D / 8;      // n-tiles of the output
-    constexpr int NT = BKV / 8;    // n-tiles of S
-    constexpr bool QREG = D <= 128;
-    extern __shared__ __align__(16) uint8_t attn_smem[];
-    uint16_t* sQ = reinterpret_cast<uint16_t*>(attn_smem);
-    uint16_t* sK = sQ + 64 * LDS;
-    uint16_t* sV = sK + BKV * LDS;
-
-    const int s = blockIdx.z, h = blockIdx.y;
-    const int s0 = __ldg(p.cu + s), L = __ldg(p.cu + s + 1) - s0;
-    const int q0 = blockIdx.x * 64;
-    if (q0 >= L) return;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int hk = h / p.group;
-    const uint16_t* Qg = p.q + static_cast<int64_t>(s0) * p.ldq + h * D;
-    const uint16_t* Kg = p.k + static_cast<int64_t>(s0) * p.ldk + hk * D;
-    const uint16_t* Vg = p.v + static_cast<int64_t>(s0) * p.ldv + hk * D;
-
-    load_tile<D, 64>(sQ, Qg, q0, L, p.ldq);
-    cp_async_commit_wait();
-    __syncthreads();
-
-    uint32_t qf[QREG ? KS : 1][4];
-    if constexpr (QREG) {
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-            const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-            const int c = ks * 16 + (lane >> 4) * 8;
-            ldsm_x4(qf[ks], sQ + r * LDS + c);
-        }
-    }
-
-    float o[DT][4];
-#pragma unroll
-    for (int i = 0; i < DT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-    float m0 = -1e30f, m1 = -1e30f, l0 = 0.f, l1 = 0.f;
-    const int qi0 = q0 + warp * 16 + (lane >> 2);  // this thread's first query row (second: +8)
-
-    // Key range any row of this block may see: j - i in [lo, hi].
-    const int jmin = max(0, q0 + p.rel_lo);
-    const int jmax = min(L - 1, q0 + 63 + p.rel_hi);
-    const int kb0 = jmin / BKV, kb1 = jmax / BKV;
-    for (int kb = kb0; kb <= kb1; ++kb) {
-        __syncthreads();  // previous tile fully consumed
-        load_tile<D, BKV>(sK, Kg, kb * BKV, L, p.ldk);
-        load_tile<D, BKV>(sV, Vg, kb * BKV, L, p.ldv);
-        cp_async_commit_wait();
-        __syncthreads();
-
-        float sc[NT][4];
-#pragma unroll
-        for (int i = 0; i < NT; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-            uint32_t a[4];
-            if constexpr (QREG) {
-                a[0] = qf[ks][0];
-                a[1] = qf[ks][1];
-                a[2] = qf[ks][2];
-                a[3] = qf[ks][3];
-            } else {
-                const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-                const int c = ks * 16 + (lane >> 4) * 8;
-                ldsm_x4(a, sQ + r * LDS + c);
-            }
-#pragma unroll
-            for (int j = 0; j < NT / 2; ++j) {
-                uint32_t b[4];
-                const int r = 16 * j + (lane & 7) + (lane >> 4) * 8;
-                const int c = ks * 16 + ((lane >> 3) & 1) * 8;
-                ldsm_x4(b, sK + r * LDS + c);
-                mma_16816<F16>(sc[2 * j], a, b[0], b[1]);
-                mma_16816<F16>(sc[2 * j + 1], a, b[2], b[3]);
-            }
-        }
-        // scale (+ relative bias), mask, into the exp2 domain
-        float tm0 = -1e30f, tm1 = -1e30f;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int qi = qi0 + (e >> 1) * 8;
-                const int j = kb * BKV + nt * 8 + (lane & 3) * 2 + (e & 1);
-                const int rel = j - qi;
-                // PLAIN: no window and no bias, only the sequence end masks keys
-                const bool ok = PLAIN ? j < L : (j < L && rel >= p.rel_lo && rel <= p.rel_hi);
-                float x = sc[nt][e];
-                if (!PLAIN && p.bias) {
-                    // bias[h][rel + bias_off]: scores * scale + bias (bert.go:876-889)
-                    const int bi = min(max(rel + p.bias_off, 0), 2 * p.bias_off);
-                    x = (x * p.scale + __ldg(p.bias + static_cast<int64_t>(h) * (2 * p.bias_off + 1) + bi)) *
-                        1.4426950408889634f;
-                } else {
-                    x = x * p.scale_log2;
-                }
-                sc[nt][e] = ok ? x : -1e30f;
-                if (e < 2)
-                    tm0 = fmaxf(tm0, sc[nt][e]);
-                else
-                    tm1 = fmaxf(tm1, sc[nt][e]);
-            }
-        }
-        tm0 = fmaxf(tm0, __shfl_xor_sync(0xffffffffu, tm0, 1));
-        tm0 = fmaxf(tm0, __shfl_xor_sync(0xffffffffu, tm0, 2));
-        tm1 = fmaxf(tm1, __shfl_xor_sync(0xffffffffu, tm1, 1));
-        tm1 = fmaxf(tm1, __shfl_xor_sync(0xffffffffu, tm1, 2));
-        const float nm0 = fmaxf(m0, tm0), nm1 = fmaxf(m1, tm1);
-        const float c0 = exp2f(m0 - nm0), c1 = exp2f(m1 - nm1);
-        m0 = nm0;
-        m1 = nm1;
-        l0 *= c0;
-        l1 *= c1;
-#pragma unroll
-        for (int i = 0; i < DT; ++i) {
-            o[i][0] *= c0;
-            o[i][1] *= c0;
-            o[i][2] *= c1;
-            o[i][3] *= c1;
-        }
-        uint32_t pf[NT / 2][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            // a fully masked row keeps m = -1e30: its probabilities are 0
-            const float p0 = sc[nt][0] > -1e29f ? exp2f(sc[nt][0] - m0) : 0.f;
-            const float p1 = sc[nt][1] > -1e29f ? exp2f(sc[nt][1] - m0) : 0.f;
-            const float p2 = sc[nt][2] > -1e29f ? exp2f(sc[nt][2] - m1) : 0.f;
-            const float p3 = sc[nt][3] > -1e29f ? exp2f(sc[nt][3] - m1) : 0.f;
-            l0 += p0 + p1;
-            l1 += p2 + p3;
-            pf[nt >> 1][(nt & 1) * 2 + 0] = pack2<F16>(p0, p1);
-            pf[nt >> 1][(nt & 1) * 2 + 1] = pack2<F16>(p2, p3);
-        }
-        // O += P V over the key sub-blocks of 16
-#pragma unroll
-        for (int j = 0; j < NT / 2; ++j) {
-            const uint32_t a[4] = {pf[j][0], pf[j][1], pf[j][2], pf[j][3]};
-#pragma unroll
-            for (int i = 0; i < DT / 2; ++i) {
-                uint32_t b[4];
-                const int r = 16 * j + (lane & 7) + ((lane >> 3) & 1) * 8;
-                const int c = 16 * i + (lane >> 4) * 8;
-                ldsm_x4_t(b, sV + r * LDS + c);
-                mma_16816<F16>(o[2 * i], a, b[0], b[1]);
-                mma_16816<F16>(o[2 * i + 1], a, b[2], b[3]);
-            }
-        }
-    }
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-    const float i0 = l0 > 0.f ? 1.0f / l0 : 0.f, i1 = l1 > 0.f ? 1.0f / l1 : 0.f;
-    uint16_t* out = p.out + static_cast<int64_t>(s0) * p.ldo + h * D + (lane & 3) * 2;
-#pragma unroll
-    for (int i = 0; i < DT; ++i) {
-        if (qi0 < L)
-            *reinterpret_cast<uint32_t*>(out + static_cast<int64_t>(qi0) * p.ldo + i * 8) =
-                pack2<F16>(o[i][0] * i0, o[i][1] * i0);
-        if (qi0 + 8 < L)
-            *reinterpret_cast<uint32_t*>(out + static_cast<int64_t>(qi0 + 8) * p.ldo + i * 8) =
-                pack2<F16>(o[i][2] * i1, o[i][3] * i1);
-    }
-}
-
-template <int D, bool PLAIN, bool F16>
-static cudaError_t launch_attention_dp(const AttnParams& p, int nseq, int max_len, int heads, cudaStream_t st) {
-    constexpr int BKV = D == 256 ? 32 : 64;
-    constexpr int smem = (64 + 2 * BKV) * (D + 8) * 2;
-    static unsigned configured = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (smem > 48 * 1024 && (dev >= 32 || !(__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & (1u << dev)))) {
-        cudaError_t e =
-            cudaFuncSetAttribute(attention_kernel<D, PLAIN, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        if (dev < 32) __atomic_fetch_or(&configured, 1u << dev, __ATOMIC_RELEASE);
-    }
-    const dim3 grid((max_len + 63) / 64, heads, nseq);
-    attention_kernel<D, PLAIN, F16><<<grid, 128, smem, st>>>(p);
-    return cudaGetLastError();
-}
-
-template <int D>
-static cudaError_t launch_attention_d(const AttnParams& p, int nseq, int max_len, int heads, cudaStream_t st) {
-    const bool plain = !p.bias && p.rel_lo <= -max_len && p.rel_hi >= max_len;
-    if (p.f16)
-        return plain ? launch_attention_dp<D, true, true>(p, nseq, max_len, heads, st)
-                     : launch_attention_dp<D, false, true>(p, nseq, max_len, heads, st);
-    return plain ? launch_attention_dp<D, true, false>(p, nseq, max_len, heads, st)
-                 : launch_attention_dp<D, false, false>(p, nseq, max_len, heads, st);
-}
-
+// Attention: every supported head dim (32, 64, 128, 256) runs the tcgen05
+// kernel (attention_tc.cu).
 cudaError_t launch_attention(const AttnParams& p, int nseq, int max_len, int heads, int head_dim, cudaStream_t st) {
-    if (attention_tc_supported(head_dim) && p.status)
-        return launch_attention_tc(p, p.T, nseq, max_len, heads, p.kv_heads, head_dim, p.status, st);
-    return launch_attention_mma(p, nseq, max_len, heads, head_dim, st);
-}
-
-cudaError_t launch_attention_mma(const AttnParams& p, int nseq, int max_len, int heads, int head_dim,
-                                 cudaStream_t st) {
-    if (nseq <= 0) return cudaSuccess;
-    switch (head_dim) {
-    case 32: return launch_attention_d<32>(p, nseq, max_len, heads, st);
-    case 64: return launch_attention_d<64>(p, nseq, max_len, heads, st);
-    case 128: return launch_attention_d<128>(p, nseq, max_len, heads, st);
-    case 256: return launch_attention_d<256>(p, nseq, max_len, heads, st);
-    default: return cudaErrorInvalidValue;
-    }
+    if (!attention_tc_supported(head_dim) || !p.status) return cudaErrorInvalidValue;
+    return launch_attention_tc(p, p.T, nseq, max_len, heads, p.kv_heads, head_dim, p.status, st);
 }
 
 // ---------------------------------------------------------------------------

@@ -132,8 +132,7 @@ struct AttnParams {
     int kv_heads;  // key/value heads (heads / group)
     int* status;   // device status word (bounded waits)
 };
-// Head dims 64 and 128 run the tcgen05 kernel (attention_tc.cu); 32 and 256
-// the mma.sync kernel.
+// Head dims 32, 64, 128 and 256 (the tcgen05 kernel, attention_tc.cu).
 cudaError_t launch_attention(const AttnParams& p, int nseq, int max_len, int heads, int head_dim, cudaStream_t st);
 bool attention_tc_supported(int head_dim);
 cudaError_t launch_attention_tc(const AttnParams& p, int T, int nseq, int max_len, int heads, int kv_heads,
@@ -156,8 +155,7 @@ struct AttnF32Params {
 };
 cudaError_t launch_attention_f32(const AttnF32Params& p, int nseq, int max_len, int heads, int head_dim,
                                  cudaStream_t st);
-// The mma.sync kernel for any supported head dim (32, 64, 128, 256).
-cudaError_t launch_attention_mma(const AttnParams& p, int nseq, int max_len, int heads, int head_dim, cudaStream_t st);
+
 
 // Pooling + L2 + Matryoshka truncation (bert.go:657-703, rembed.go:441-448):
 // out[nseq x dim].
