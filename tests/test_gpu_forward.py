@@ -193,3 +193,23 @@ def test_full_int8_parity_bge(cuda):
     print(f"\n[parity] bge full int8: min cos {cos.min():.6f}, max abs {np.abs(got - want).max():.2e}")
     assert cos.min() >= COS_INT8_FULL
     m.gpu.close()
+
+
+def test_multi_device_context_matches_single_device(cuda):
+    """rg_forward over a context holding two devices splits the batch into
+    contiguous cost-balanced shards, one host thread per device, each
+    landing in its slice of the output; the result equals one device's."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two visible GPUs")
+    cfg = synth.preset("minilm-l6")
+    w = synth.make_weights(cfg, seed=61)
+    ids, cu = synth.make_batch(cfg, 21, 4, 128, seed=62)
+    one = Embedder(cfg, w, devices=(0,))
+    two = Embedder(cfg, w, devices=(0, 1))
+    a = one.embed_packed(ids, cu)
+    b = two.embed_packed(ids, cu)
+    one.close()
+    two.close()
+    assert np.array_equal(a, b)
