@@ -545,20 +545,26 @@ cudaError_t launch_widen_s8_f16(const int8_t* w, size_t n, uint16_t* out, cudaSt
 
 // ---------------------------------------------------------------------------
 // int8 row quantisation of a bf16 matrix (full-int8 mode inputs that are not
-// produced by a LayerNorm: the attention context and the GELU output).
+// produced by a LayerNorm: the attention context and the FFN hidden state).
+// One warp per row, single pass: the row (up to 16 vectors of 8 per lane,
+// K <= 4096) stays in registers between the max and the quantisation.
+template <int NV>
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const __nv_bfloat16* __restrict__ x, int T, int K,
                                                            int8_t* q, float* scale) {
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= T) return;
-    const __nv_bfloat16* row = x + static_cast<int64_t>(t) * K;
+    const uint4* row = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * K);
+    const int nvec = K / 8;  // 8-element vectors in the row
+    uint4 u[NV];
     float amax = 0.f;
-    for (int j = lane * 8; j < K; j += 256) {
-        const uint4 u = __ldg(reinterpret_cast<const uint4*>(row + j));
-        const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+        u[c] = lane + 32 * c < nvec ? __ldg(row + lane + 32 * c) : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t w[4] = {u[c].x, u[c].y, u[c].z, u[c].w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(p[e]);
+            const float2 f = unpack2<false>(w[e]);
             amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
         }
     }
@@ -566,26 +572,34 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const __nv_bfloat16*
     float s = amax / 127.0f;
     if (s == 0.0f) s = 1.0f;
     const float rinv = 1.0f / s;
-    int8_t* qr = q + static_cast<int64_t>(t) * K;
-    for (int j = lane * 8; j < K; j += 256) {
-        const uint4 u = __ldg(reinterpret_cast<const uint4*>(row + j));
-        const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
+    uint2* qr = reinterpret_cast<uint2*>(q + static_cast<int64_t>(t) * K);
+#pragma unroll
+    for (int c = 0; c < NV; ++c) {
+        const uint32_t w[4] = {u[c].x, u[c].y, u[c].z, u[c].w};
         int8_t o[8];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(p[e]);
+            const float2 f = unpack2<false>(w[e]);
             o[2 * e] = (int8_t)max(-128, min(127, __float2int_rn(f.x * rinv)));
             o[2 * e + 1] = (int8_t)max(-128, min(127, __float2int_rn(f.y * rinv)));
         }
-        *reinterpret_cast<uint2*>(qr + j) = *reinterpret_cast<uint2*>(o);
+        if (lane + 32 * c < nvec) qr[lane + 32 * c] = *reinterpret_cast<uint2*>(o);
     }
     if (lane == 0) scale[t] = s;
 }
 
 cudaError_t launch_quantize_rows(const __nv_bfloat16* x, int T, int K, int8_t* q, float* scale, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
-    if (K % 8 != 0) return cudaErrorInvalidValue;
-    quantize_rows_kernel<<<(T + 7) / 8, 256, 0, st>>>(x, T, K, q, scale);
+    if (K % 8 != 0 || K > 16 * 256) return cudaErrorInvalidValue;
+    const int grid = (T + 7) / 8;
+    switch ((K + 255) / 256) {
+#define RG_QR(NV) \
+    case NV: quantize_rows_kernel<NV><<<grid, 256, 0, st>>>(x, T, K, q, scale); break;
+        RG_QR(1) RG_QR(2) RG_QR(3) RG_QR(4) RG_QR(5) RG_QR(6) RG_QR(7) RG_QR(8)
+        RG_QR(9) RG_QR(10) RG_QR(11) RG_QR(12) RG_QR(13) RG_QR(14) RG_QR(15) RG_QR(16)
+#undef RG_QR
+    default: return cudaErrorInvalidValue;
+    }
     return cudaGetLastError();
 }
 

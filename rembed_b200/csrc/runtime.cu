@@ -1303,6 +1303,9 @@ int rg_init(const rg_model_desc* desc, const int* devices, int ndev, int mode, r
         if (mode == RG_MODE_INT8_FULL && (d.hidden_size % 128 != 0 || d.intermediate_size % 128 != 0 ||
                                           dims(d).qd % 128 != 0))
             fail("rg_init: full-int8 needs K multiples of 128");
+        if (mode == RG_MODE_INT8_FULL && (d.intermediate_size > 4096 || dims(d).qd > 4096))
+            fail("rg_init: full-int8 row quantisation supports widths up to 4096 (got %d, %d)", dims(d).qd,
+                 d.intermediate_size);
         int ndevs = 0;
         check(cudaGetDeviceCount(&ndevs), "cudaGetDeviceCount");
         std::vector<int> devs;
