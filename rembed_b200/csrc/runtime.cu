@@ -148,6 +148,22 @@ struct Replica {
     const int32_t* h_cu_view = nullptr;  // host copy of the current batch's offsets
     // kernel timing (rg_profile)
     bool prof = false;
+    // CUDA graphs of whole forwards, one per batch shape and buffer set (see
+    // GraphKey); ws_gen changes whenever a workspace or staging buffer is
+    // reallocated, which retires every graph that captured the old ones.
+    uint64_t ws_gen = 1;
+    struct GraphKey {
+        int T, nseq, max_len, out_kind, out_dim;
+        const void *ids, *cu, *out;  // device inputs / output (nullptr: host path)
+        uint64_t gen;
+        bool operator==(const GraphKey& o) const {
+            return T == o.T && nseq == o.nseq && max_len == o.max_len && out_kind == o.out_kind &&
+                   out_dim == o.out_dim && ids == o.ids && cu == o.cu && out == o.out && gen == o.gen;
+        }
+    };
+    std::vector<std::pair<GraphKey, cudaGraphExec_t>> graphs;
+    std::vector<GraphKey> seen_once;  // shapes run once eagerly; captured on their second call
+    int graph_launches = 0;           // kernel launches inside the cached graphs (last capture)
     std::vector<cudaEvent_t> ev_pool;
     size_t ev_used = 0;
     struct Rec {
@@ -747,6 +763,7 @@ void ensure_workspace(rg_ctx* c, Replica& r, int T, int nseq, size_t nout) {
         r.d_out = ws_alloc<float>(r, capO);
         r.d_status = ws_alloc<int>(r, 1);
         r.cap_T = static_cast<int>(t);
+        ++r.ws_gen;
         r.cap_seq = capS;
         r.cap_out = static_cast<int>(capO);
         r.tm_T = -1;
@@ -771,6 +788,7 @@ void ensure_workspace(rg_ctx* c, Replica& r, int T, int nseq, size_t nout) {
 }
 
 void ensure_host_staging(Replica& r, size_t nids, size_t ncu, size_t nout) {
+    if (nids > r.h_cap_ids || ncu > r.h_cap_cu || nout > r.h_cap_out || !r.h_status) ++r.ws_gen;
     if (nids > r.h_cap_ids) {
         if (r.h_ids) cudaFreeHost(r.h_ids);
         check(cudaMallocHost(&r.h_ids, nids * sizeof(int64_t)), "cudaMallocHost");
@@ -1207,6 +1225,63 @@ void validate_batch(const rg_model_desc& d, const int64_t* ids, const int32_t* c
 }
 
 // Run sequences [s_lo, s_hi) of a host batch on replica r.
+void drop_graphs(Replica& r) {
+    for (auto& g : r.graphs) cudaGraphExecDestroy(g.second);
+    r.graphs.clear();
+    r.seen_once.clear();
+}
+
+// Run `enqueue` (the stream work of one forward) on st: eagerly the first
+// time a key is seen, captured into a graph the second time, replayed from
+// then on.  Profiling runs stay eager (their events time every launch).
+template <typename F>
+void run_graphed(Replica& r, cudaStream_t st, const Replica::GraphKey& key, F&& enqueue) {
+    if (r.prof) {
+        enqueue();
+        return;
+    }
+    for (auto& g : r.graphs)
+        if (g.first == key) {
+            check(cudaGraphLaunch(g.second, st), "cudaGraphLaunch");
+            r.last_launches = r.graph_launches;
+            return;
+        }
+    // graphs of retired buffers go before a new one is made
+    bool stale = false;
+    for (auto& g : r.graphs) stale |= g.first.gen != key.gen;
+    if (stale) drop_graphs(r);
+    bool seen = false;
+    for (auto& k : r.seen_once) seen |= k == key;
+    if (!seen) {
+        if (r.seen_once.size() >= 16) r.seen_once.erase(r.seen_once.begin());
+        r.seen_once.push_back(key);
+        enqueue();
+        return;
+    }
+    if (r.graphs.size() >= 16) {
+        cudaGraphExecDestroy(r.graphs.front().second);
+        r.graphs.erase(r.graphs.begin());
+    }
+    check(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+    try {
+        enqueue();
+    } catch (...) {
+        cudaGraph_t g = nullptr;
+        cudaStreamEndCapture(st, &g);  // leave the stream usable
+        if (g) cudaGraphDestroy(g);
+        throw;
+    }
+    cudaGraph_t g = nullptr;
+    check(cudaStreamEndCapture(st, &g), "cudaStreamEndCapture");
+    cudaGraphExec_t ge = nullptr;
+    const cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    check(e, "cudaGraphInstantiate");
+    r.graphs.push_back({key, ge});
+    r.graph_launches = r.last_launches;
+    check(cudaGraphLaunch(ge, st), "cudaGraphLaunch");
+}
+
 void run_host_shard(rg_ctx* c, Replica& r, const int64_t* ids, const int32_t* cu, int s_lo, int s_hi, int out_kind,
                     int out_dim, float* host_out) {
     std::lock_guard<std::mutex> lk(r.mu);
@@ -1223,13 +1298,18 @@ void run_host_shard(rg_ctx* c, Replica& r, const int64_t* ids, const int32_t* cu
     for (int i = 0; i < nseq; ++i) max_len = std::max(max_len, r.h_cu[i + 1] - r.h_cu[i]);
     memcpy(r.h_ids, ids + t0, sizeof(int64_t) * T);
     cudaStream_t st = r.stream;
-    check(cudaMemsetAsync(r.d_status, 0, sizeof(int), st), "cudaMemsetAsync");
     r.h_cu_view = r.h_cu;
-    check(cudaMemcpyAsync(r.d_ids, r.h_ids, sizeof(int64_t) * T, cudaMemcpyHostToDevice, st), "H2D ids");
-    check(cudaMemcpyAsync(r.d_cu, r.h_cu, sizeof(int32_t) * (nseq + 1), cudaMemcpyHostToDevice, st), "H2D cu");
-    forward_on_device(c, r, r.d_ids, r.d_cu, nseq, T, max_len, out_kind, out_dim, r.d_out, st);
-    check(cudaMemcpyAsync(r.h_out, r.d_out, sizeof(float) * nout, cudaMemcpyDeviceToHost, st), "D2H out");
-    check(cudaMemcpyAsync(r.h_status, r.d_status, sizeof(int), cudaMemcpyDeviceToHost, st), "D2H status");
+    // pinned staging -> device, the forward, device -> pinned staging: one
+    // graph per shape once the shape repeats
+    const Replica::GraphKey key{T, nseq, max_len, out_kind, out_dim, nullptr, nullptr, nullptr, r.ws_gen};
+    run_graphed(r, st, key, [&] {
+        check(cudaMemsetAsync(r.d_status, 0, sizeof(int), st), "cudaMemsetAsync");
+        check(cudaMemcpyAsync(r.d_ids, r.h_ids, sizeof(int64_t) * T, cudaMemcpyHostToDevice, st), "H2D ids");
+        check(cudaMemcpyAsync(r.d_cu, r.h_cu, sizeof(int32_t) * (nseq + 1), cudaMemcpyHostToDevice, st), "H2D cu");
+        forward_on_device(c, r, r.d_ids, r.d_cu, nseq, T, max_len, out_kind, out_dim, r.d_out, st);
+        check(cudaMemcpyAsync(r.h_out, r.d_out, sizeof(float) * nout, cudaMemcpyDeviceToHost, st), "D2H out");
+        check(cudaMemcpyAsync(r.h_status, r.d_status, sizeof(int), cudaMemcpyDeviceToHost, st), "D2H status");
+    });
     check(cudaStreamSynchronize(st), "forward");
     if (*r.h_status != 0) fail("rembed: %s", status_message(*r.h_status).c_str());
     float* dst = host_out + (out_kind == RG_OUT_POOLED ? static_cast<size_t>(s_lo) * out_dim
@@ -1471,7 +1551,8 @@ int rg_forward_device(rg_ctx* c, int dev_index, const int64_t* d_ids, const int3
         ensure_workspace(c, r, T, nseq, nout);
         cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : r.stream;
         r.h_cu_view = h_cu;
-        forward_on_device(c, r, d_ids, d_cu, nseq, T, max_len, out_kind, out_dim, d_out, st);
+        const Replica::GraphKey key{T, nseq, max_len, out_kind, out_dim, d_ids, d_cu, d_out, r.ws_gen};
+        run_graphed(r, st, key, [&] { forward_on_device(c, r, d_ids, d_cu, nseq, T, max_len, out_kind, out_dim, d_out, st); });
         r.h_cu_view = nullptr;
         return 0;
     } catch (const Error& e) {
@@ -1551,6 +1632,7 @@ void rg_free(rg_ctx* c) {
     for (Replica* r : c->reps) {
         cudaSetDevice(r->device);
         if (r->stream) cudaStreamSynchronize(r->stream);
+        drop_graphs(*r);
         free_workspace(*r);
         for (cudaEvent_t e : r->ev_pool) cudaEventDestroy(e);
         for (void* p : r->allocs) cudaFree(p);
