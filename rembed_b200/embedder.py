@@ -3,10 +3,13 @@
 Names and meaning follow the reference (rembed.go and its Python binding
 python/rembed/__init__.py):
 
-* ``load(ref, int8=..., int8_activations=..., dim=...)`` = ``rembed.Load``
-  with ``WithInt8`` / ``WithInt8Activations`` / ``WithDim``
-  (rembed.go:60-121, 139-270), over a converted model directory
-  (manifest.json + model.safetensors);
+* ``load(ref, int8=..., int8_activations=..., dim=..., disk_weights=...)``
+  = ``rembed.Load`` with ``WithInt8`` / ``WithInt8Activations`` /
+  ``WithDim`` / ``WithDiskWeights`` (rembed.go:60-121, 139-270), over a
+  converted model directory (manifest.json + model.safetensors or a sharded
+  set, or the weights.rembedpack file; see weights.py); ``fp16=False``
+  selects bf16 tensor-core operands and ``strict_fp32=True`` the strict
+  fp32 path;
 * ``Embedder.embed`` = ``Embed`` (rembed.go:287-332): one L2-normalised
   vector per sequence, truncated to ``dim`` and re-normalised;
 * ``Embedder.embed_tokens`` = ``EmbedTokens`` (rembed.go:370-411);
@@ -326,14 +329,17 @@ class Embedder:
 
 
 def load(ref: str | os.PathLike, *, int8: bool = False, int8_activations: bool = False, dim: int = 0,
-         devices: Sequence[int] = (0,), fp16: bool = True, strict_fp32: bool = False) -> Embedder:
-    """rembed.Load over a converted model directory (manifest.json +
-    model.safetensors).  Hub download and HF-config derivation stay with the
-    reference host."""
-    from .synth import read_safetensors
+         devices: Sequence[int] = (0,), fp16: bool = True, strict_fp32: bool = False,
+         disk_weights: bool = False) -> Embedder:
+    """rembed.Load over a converted model directory: manifest.json plus
+    model.safetensors or a sharded set (model.safetensors.index.json).
+    disk_weights = WithDiskWeights: the weights are mapped from
+    <dir>/weights.rembedpack, built from the checkpoint on first use.  Hub
+    download and HF-config derivation stay with the reference host."""
+    from . import weights as W
 
     p = Path(ref)
     cfg = Config.load(p / "manifest.json")
-    weights = read_safetensors(p / "model.safetensors")
-    return Embedder(cfg, weights, int8=int8, int8_activations=int8_activations, dim=dim, devices=devices,
+    tensors = W.disk_weights(p) if disk_weights else W.read_checkpoint(p)
+    return Embedder(cfg, tensors, int8=int8, int8_activations=int8_activations, dim=dim, devices=devices,
                     fp16=fp16, strict_fp32=strict_fp32)

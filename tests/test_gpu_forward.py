@@ -213,3 +213,31 @@ def test_multi_device_context_matches_single_device(cuda):
     one.close()
     two.close()
     assert np.array_equal(a, b)
+
+
+def test_load_sharded_and_disk_weights(cuda, tmp_path):
+    """load() over a sharded checkpoint and over the weights.rembedpack it
+    builds (WithDiskWeights) gives the same embeddings as the in-memory
+    weights."""
+    import json
+
+    from rembed_b200.embedder import load
+
+    cfg = synth.preset("tiny-bert")
+    w = synth.make_weights(cfg, seed=71)
+    names = sorted(w)
+    shards = {"model-00001-of-00002.safetensors": names[::2], "model-00002-of-00002.safetensors": names[1::2]}
+    for f, ns in shards.items():
+        synth.write_safetensors(tmp_path / f, {n: w[n] for n in ns})
+    (tmp_path / "model.safetensors.index.json").write_text(
+        json.dumps({"weight_map": {n: f for f, ns in shards.items() for n in ns}}))
+    (tmp_path / "manifest.json").write_text(cfg.to_json())
+    ids, cu = synth.make_batch(cfg, 5, 3, 60, seed=72)
+    ref = Embedder(cfg, w)
+    want = ref.embed_packed(ids, cu)
+    ref.close()
+    for disk in (False, True):
+        e = load(tmp_path, disk_weights=disk)
+        assert np.array_equal(e.embed_packed(ids, cu), want)
+        e.close()
+    assert (tmp_path / "weights.rembedpack").exists()
