@@ -313,20 +313,28 @@ def ours(args, rank, world, local_rank):
     value = world * nseq * args.steps / (ms / 1000.0)
 
     # ---- e2e: host buffers through the public API ----
-    host_out = np.empty((nseq, emb.dim), dtype=np.float32)
-    for _ in range(2):
-        emb.embed_packed(ids, cu, out=host_out)
+    # Every step stages its ids from host memory into pinned memory, copies
+    # them to the device, runs the forward and copies the embeddings back to
+    # a host array; steps are pipelined as a serving loop would run them
+    # (rg_submit of step k+1 before rg_collect of step k).
+    host_outs = [np.empty((nseq, emb.dim), dtype=np.float32) for _ in range(2)]
+
+    def e2e_steps(n):
+        pending = None
+        for k in range(n):
+            nxt = emb.submit(ids, cu, out=host_outs[k % 2])
+            if pending is not None:
+                pending.result()
+            pending = nxt
+        pending.result()
+
+    e2e_steps(3)
     barrier()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
-    f0.record(stream)
-    for _ in range(args.steps):
-        emb.embed_packed(ids, cu, out=host_out)
-    f1.record(stream)
-    torch.cuda.synchronize()
+    e2e_steps(args.steps)
     wall = time.perf_counter() - t0
     barrier()
-    e2e_ms = max_over_ranks(max(f0.elapsed_time(f1), 1000.0 * wall))
+    e2e_ms = max_over_ranks(1000.0 * wall)
     e2e_value = world * nseq * args.steps / (e2e_ms / 1000.0)
 
     # ---- roofline: per-kernel-class device time, second pass ----
@@ -376,7 +384,8 @@ def ours(args, rank, world, local_rank):
         "roofline": roofline,
         "e2e": {"value": round(e2e_value, 2), "unit": "embeddings/s",
                 "h2d_bytes_per_step": int(ids.nbytes + cu.nbytes),
-                "d2h_bytes_per_step": int(host_out.nbytes + 4)},
+                "d2h_bytes_per_step": int(host_outs[0].nbytes + 4),
+                "how": "rg_submit/rg_collect from host arrays, wall clock, two batches in flight"},
         "clocks": clocks,
         "gpu_launches": int(launches_per_step * args.steps),
         "gemm_tflops_effective": round(g["flops"] / max(args.steps, 1) / (ms / args.steps / 1000) / 1e12, 1),

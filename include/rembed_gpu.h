@@ -107,6 +107,19 @@ int rg_finalize(rg_ctx *ctx, char **err);
 int rg_forward(rg_ctx *ctx, const int64_t *ids, const int32_t *cu_seqlens, int nseq, int out_kind,
                int out_dim, float *host_out, char **err);
 
+/* The same forward, asynchronous: validates and stages the batch (ids and
+ * cu_seqlens are copied before returning), enqueues it and returns a ticket
+ * at once, so the caller can tokenise / pack the next batch while this one
+ * runs.  host_out must stay valid until rg_collect(ticket), which waits for
+ * the batch and writes host_out.  Two submissions may be outstanding per
+ * context (two pinned staging slots per device); a third fails until the
+ * oldest is collected.  Replaces nothing in the reference, whose Embed is
+ * synchronous; it is the CPU-tokeniser / GPU overlap the reference host
+ * needs to keep a GPU busy. */
+int rg_submit(rg_ctx *ctx, const int64_t *ids, const int32_t *cu_seqlens, int nseq, int out_kind,
+              int out_dim, float *host_out, int64_t *ticket, char **err);
+int rg_collect(rg_ctx *ctx, int64_t ticket, char **err);
+
 /* Forward a packed batch already resident on device `dev_index` (an index
  * into the rg_init device list): d_ids, d_cu_seqlens and d_out are device
  * pointers on that device; `stream` is a cudaStream_t (NULL = the context's

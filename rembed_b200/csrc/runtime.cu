@@ -134,11 +134,21 @@ struct Replica {
     int* d_status = nullptr;
     uint16_t* w16 = nullptr;  // weight-only int8: fp16 widening scratch (largest weight)
     size_t w16_elems = 0;
-    int64_t* h_ids = nullptr;
-    int32_t* h_cu = nullptr;
-    float* h_out = nullptr;
-    int* h_status = nullptr;
-    size_t h_cap_ids = 0, h_cap_cu = 0, h_cap_out = 0;
+    // Pinned host staging, two slots so that one batch can be staged while
+    // the previous one runs (rg_submit / rg_collect); the device buffers are
+    // shared, the slots' work being ordered on the replica's stream.
+    struct Staging {
+        int64_t* ids = nullptr;
+        int32_t* cu = nullptr;
+        float* out = nullptr;
+        int* status = nullptr;
+        size_t cap_ids = 0, cap_cu = 0, cap_out = 0;
+        cudaEvent_t done = nullptr;  // recorded after the slot's D2H copies
+        bool busy = false;           // submitted, not yet collected
+        float* user_out = nullptr;   // where rg_collect copies the slot's result
+        size_t nout = 0;
+    };
+    Staging stage[2];
     OpMaps tm_x, tm_ctx, tm_ffh;
     // strict fp32: GEMM operands as tf32 hi + fp32 remainder; qkv in fp32
     float *xh = nullptr, *xl = nullptr, *ctxh = nullptr, *ctxl = nullptr, *ffhh = nullptr, *ffhl = nullptr;
@@ -187,6 +197,11 @@ struct rg_ctx {
     std::vector<Replica*> reps;
     bool finalized = false;
     std::mutex mu;
+    // host-batch submissions: ticket t uses staging slot t % 2 of every
+    // replica; pending[slot] is the ticket in flight there (-1: none)
+    std::mutex tmu;
+    int64_t next_ticket = 0;
+    int64_t pending[2] = {-1, -1};
 };
 
 namespace {
@@ -691,13 +706,6 @@ void make_widen_maps(Replica& r) {
 void free_workspace(Replica& r) {
     for (void* p : r.ws) cudaFree(p);
     r.ws.clear();
-    if (r.h_ids) cudaFreeHost(r.h_ids);
-    if (r.h_cu) cudaFreeHost(r.h_cu);
-    if (r.h_out) cudaFreeHost(r.h_out);
-    r.h_ids = nullptr;
-    r.h_cu = nullptr;
-    r.h_out = nullptr;
-    r.h_cap_ids = r.h_cap_cu = r.h_cap_out = 0;
     r.cap_T = r.cap_seq = r.cap_out = 0;
     r.tm_T = -1;
 }
@@ -787,24 +795,40 @@ void ensure_workspace(rg_ctx* c, Replica& r, int T, int nseq, size_t nout) {
     }
 }
 
-void ensure_host_staging(Replica& r, size_t nids, size_t ncu, size_t nout) {
-    if (nids > r.h_cap_ids || ncu > r.h_cap_cu || nout > r.h_cap_out || !r.h_status) ++r.ws_gen;
-    if (nids > r.h_cap_ids) {
-        if (r.h_ids) cudaFreeHost(r.h_ids);
-        check(cudaMallocHost(&r.h_ids, nids * sizeof(int64_t)), "cudaMallocHost");
-        r.h_cap_ids = nids;
+// Grow one staging slot (which is not in flight) to hold a batch.
+void ensure_host_staging(Replica& r, Replica::Staging& s, size_t nids, size_t ncu, size_t nout) {
+    if (nids > s.cap_ids || ncu > s.cap_cu || nout > s.cap_out || !s.status) ++r.ws_gen;
+    if (nids > s.cap_ids) {
+        if (s.ids) cudaFreeHost(s.ids);
+        s.ids = nullptr;
+        check(cudaMallocHost(&s.ids, nids * sizeof(int64_t)), "cudaMallocHost");
+        s.cap_ids = nids;
     }
-    if (ncu > r.h_cap_cu) {
-        if (r.h_cu) cudaFreeHost(r.h_cu);
-        check(cudaMallocHost(&r.h_cu, ncu * sizeof(int32_t)), "cudaMallocHost");
-        r.h_cap_cu = ncu;
+    if (ncu > s.cap_cu) {
+        if (s.cu) cudaFreeHost(s.cu);
+        s.cu = nullptr;
+        check(cudaMallocHost(&s.cu, ncu * sizeof(int32_t)), "cudaMallocHost");
+        s.cap_cu = ncu;
     }
-    if (nout > r.h_cap_out) {
-        if (r.h_out) cudaFreeHost(r.h_out);
-        check(cudaMallocHost(&r.h_out, nout * sizeof(float)), "cudaMallocHost");
-        r.h_cap_out = nout;
+    if (nout > s.cap_out) {
+        if (s.out) cudaFreeHost(s.out);
+        s.out = nullptr;
+        check(cudaMallocHost(&s.out, nout * sizeof(float)), "cudaMallocHost");
+        s.cap_out = nout;
     }
-    if (!r.h_status) check(cudaMallocHost(&r.h_status, sizeof(int)), "cudaMallocHost");
+    if (!s.status) check(cudaMallocHost(&s.status, sizeof(int)), "cudaMallocHost");
+    if (!s.done) check(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming), "cudaEventCreate");
+}
+
+void free_staging(Replica& r) {
+    for (auto& s : r.stage) {
+        if (s.ids) cudaFreeHost(s.ids);
+        if (s.cu) cudaFreeHost(s.cu);
+        if (s.out) cudaFreeHost(s.out);
+        if (s.status) cudaFreeHost(s.status);
+        if (s.done) cudaEventDestroy(s.done);
+        s = Replica::Staging{};
+    }
 }
 
 size_t prof_event(Replica& r, cudaStream_t st) {
@@ -1282,39 +1306,63 @@ void run_graphed(Replica& r, cudaStream_t st, const Replica::GraphKey& key, F&& 
     check(cudaGraphLaunch(ge, st), "cudaGraphLaunch");
 }
 
-void run_host_shard(rg_ctx* c, Replica& r, const int64_t* ids, const int32_t* cu, int s_lo, int s_hi, int out_kind,
-                    int out_dim, float* host_out) {
+// Stage sequences [s_lo, s_hi) of a host batch in staging slot `slot` of
+// replica r and enqueue pinned H2D -> forward -> D2H on its stream (a graph
+// per repeated shape); the result is copied to host_out at collect time.
+void submit_shard(rg_ctx* c, Replica& r, int slot, const int64_t* ids, const int32_t* cu, int s_lo, int s_hi,
+                  int out_kind, int out_dim, float* host_out) {
     std::lock_guard<std::mutex> lk(r.mu);
     check(cudaSetDevice(r.device), "cudaSetDevice");
     const int nseq = s_hi - s_lo;
     if (nseq <= 0) return;
+    Replica::Staging& sg = r.stage[slot];
+    if (sg.busy) fail("rembed: staging slot %d is still in flight (collect the oldest submission first)", slot);
     const int t0 = cu[s_lo], T = cu[s_hi] - t0;
     const int H = c->d.hidden_size;
     const size_t nout = out_kind == RG_OUT_POOLED ? static_cast<size_t>(nseq) * out_dim : static_cast<size_t>(T) * H;
     ensure_workspace(c, r, T, nseq, nout);
-    ensure_host_staging(r, T, nseq + 1, nout);
+    ensure_host_staging(r, sg, T, nseq + 1, nout);
     int max_len = 0;
-    for (int i = 0; i <= nseq; ++i) r.h_cu[i] = cu[s_lo + i] - t0;
-    for (int i = 0; i < nseq; ++i) max_len = std::max(max_len, r.h_cu[i + 1] - r.h_cu[i]);
-    memcpy(r.h_ids, ids + t0, sizeof(int64_t) * T);
+    for (int i = 0; i <= nseq; ++i) sg.cu[i] = cu[s_lo + i] - t0;
+    for (int i = 0; i < nseq; ++i) max_len = std::max(max_len, sg.cu[i + 1] - sg.cu[i]);
+    memcpy(sg.ids, ids + t0, sizeof(int64_t) * T);
     cudaStream_t st = r.stream;
-    r.h_cu_view = r.h_cu;
+    r.h_cu_view = sg.cu;
     // pinned staging -> device, the forward, device -> pinned staging: one
-    // graph per shape once the shape repeats
-    const Replica::GraphKey key{T, nseq, max_len, out_kind, out_dim, nullptr, nullptr, nullptr, r.ws_gen};
+    // graph per shape and slot once the shape repeats
+    const Replica::GraphKey key{T, nseq, max_len, out_kind, out_dim, sg.ids, sg.cu, sg.out, r.ws_gen};
     run_graphed(r, st, key, [&] {
         check(cudaMemsetAsync(r.d_status, 0, sizeof(int), st), "cudaMemsetAsync");
-        check(cudaMemcpyAsync(r.d_ids, r.h_ids, sizeof(int64_t) * T, cudaMemcpyHostToDevice, st), "H2D ids");
-        check(cudaMemcpyAsync(r.d_cu, r.h_cu, sizeof(int32_t) * (nseq + 1), cudaMemcpyHostToDevice, st), "H2D cu");
+        check(cudaMemcpyAsync(r.d_ids, sg.ids, sizeof(int64_t) * T, cudaMemcpyHostToDevice, st), "H2D ids");
+        check(cudaMemcpyAsync(r.d_cu, sg.cu, sizeof(int32_t) * (nseq + 1), cudaMemcpyHostToDevice, st), "H2D cu");
         forward_on_device(c, r, r.d_ids, r.d_cu, nseq, T, max_len, out_kind, out_dim, r.d_out, st);
-        check(cudaMemcpyAsync(r.h_out, r.d_out, sizeof(float) * nout, cudaMemcpyDeviceToHost, st), "D2H out");
-        check(cudaMemcpyAsync(r.h_status, r.d_status, sizeof(int), cudaMemcpyDeviceToHost, st), "D2H status");
+        check(cudaMemcpyAsync(sg.out, r.d_out, sizeof(float) * nout, cudaMemcpyDeviceToHost, st), "D2H out");
+        check(cudaMemcpyAsync(sg.status, r.d_status, sizeof(int), cudaMemcpyDeviceToHost, st), "D2H status");
     });
-    check(cudaStreamSynchronize(st), "forward");
-    if (*r.h_status != 0) fail("rembed: %s", status_message(*r.h_status).c_str());
-    float* dst = host_out + (out_kind == RG_OUT_POOLED ? static_cast<size_t>(s_lo) * out_dim
-                                                      : static_cast<size_t>(t0) * H);
-    memcpy(dst, r.h_out, sizeof(float) * nout);
+    r.h_cu_view = nullptr;
+    check(cudaEventRecord(sg.done, st), "cudaEventRecord");
+    sg.busy = true;
+    sg.user_out = host_out + (out_kind == RG_OUT_POOLED ? static_cast<size_t>(s_lo) * out_dim
+                                                        : static_cast<size_t>(t0) * H);
+    sg.nout = nout;
+}
+
+// Wait for replica r's slot and copy its result out (no-op if idle).
+void collect_shard(Replica& r, int slot) {
+    std::lock_guard<std::mutex> lk(r.mu);
+    Replica::Staging& sg = r.stage[slot];
+    if (!sg.busy) return;
+    check(cudaSetDevice(r.device), "cudaSetDevice");
+    sg.busy = false;
+    check(cudaEventSynchronize(sg.done), "forward");
+    if (*sg.status != 0) fail("rembed: %s", status_message(*sg.status).c_str());
+    memcpy(sg.user_out, sg.out, sizeof(float) * sg.nout);
+}
+
+void run_host_shard(rg_ctx* c, Replica& r, int slot, const int64_t* ids, const int32_t* cu, int s_lo, int s_hi,
+                    int out_kind, int out_dim, float* host_out) {
+    submit_shard(c, r, slot, ids, cu, s_lo, s_hi, out_kind, out_dim, host_out);
+    collect_shard(r, slot);
 }
 
 // Contiguous shards with near-equal estimated cost (linear + quadratic
@@ -1335,6 +1383,54 @@ std::vector<int> shard_bounds(const rg_model_desc& d, const int32_t* cu, int nse
         b[k] = s;
     }
     return b;
+}
+
+// Submit a validated host batch: split over the replicas (contiguous,
+// cost-balanced shards) and staged in slot ticket % 2 of each.
+int64_t submit_batch(rg_ctx* c, const int64_t* ids, const int32_t* cu, int nseq, int out_kind, int out_dim,
+                     float* host_out) {
+    std::lock_guard<std::mutex> tl(c->tmu);
+    const int64_t t = c->next_ticket;
+    const int slot = static_cast<int>(t & 1);
+    if (c->pending[slot] >= 0)
+        fail("rembed: two submissions are outstanding; collect ticket %lld first",
+             static_cast<long long>(c->pending[slot]));
+    const int nrep = static_cast<int>(c->reps.size());
+    const std::vector<int> b = nrep == 1 ? std::vector<int>{0, nseq} : shard_bounds(c->d, cu, nseq, nrep);
+    int k = 0;
+    try {
+        for (; k < nrep; ++k) submit_shard(c, *c->reps[k], slot, ids, cu, b[k], b[k + 1], out_kind, out_dim, host_out);
+    } catch (...) {
+        for (int j = 0; j < k; ++j) {  // the shards already in flight finish before the slot is reused
+            try {
+                collect_shard(*c->reps[j], slot);
+            } catch (...) {
+            }
+        }
+        throw;
+    }
+    c->pending[slot] = t;
+    c->next_ticket = t + 1;
+    return t;
+}
+
+// Wait for a submitted batch and copy its results to the caller's buffer.
+void collect_batch(rg_ctx* c, int64_t t) {
+    const int slot = static_cast<int>(t & 1);
+    {
+        std::lock_guard<std::mutex> tl(c->tmu);
+        if (t < 0 || c->pending[slot] != t) fail("rembed: ticket %lld is not outstanding", static_cast<long long>(t));
+        c->pending[slot] = -1;
+    }
+    std::string first;
+    for (Replica* r : c->reps) {
+        try {
+            collect_shard(*r, slot);
+        } catch (const Error& e) {
+            if (first.empty()) first = e.msg;
+        }
+    }
+    if (!first.empty()) fail("%s", first.c_str());
 }
 
 }  // namespace
@@ -1497,25 +1593,44 @@ int rg_forward(rg_ctx* c, const int64_t* ids, const int32_t* cu, int nseq, int o
             fail("rembed: bad out_kind %d", out_kind);
         }
         validate_batch(c->d, ids, cu, nseq);
-        const int nrep = static_cast<int>(c->reps.size());
-        if (nrep == 1) {
-            run_host_shard(c, *c->reps[0], ids, cu, 0, nseq, out_kind, out_dim, host_out);
-            return 0;
+        const int64_t t = submit_batch(c, ids, cu, nseq, out_kind, out_dim, host_out);
+        collect_batch(c, t);
+        return 0;
+    } catch (const Error& e) {
+        set_err(err, e.msg);
+        return -1;
+    }
+}
+
+int rg_submit(rg_ctx* c, const int64_t* ids, const int32_t* cu, int nseq, int out_kind, int out_dim, float* host_out,
+              int64_t* ticket, char** err) {
+    try {
+        if (!c) fail("rembed: invalid context");
+        if (!c->finalized) fail("rembed: weights not finalized");
+        if (!ticket) fail("rembed: null ticket");
+        if (nseq <= 0) fail("rembed: empty batch");
+        if (!ids || !cu || !host_out) fail("rembed: null buffer");
+        const int H = c->d.hidden_size;
+        if (out_kind == RG_OUT_POOLED) {
+            if (out_dim < 1 || out_dim > H) fail("rembed: WithDim(%d) out of range [1, %d]", out_dim, H);
+        } else if (out_kind == RG_OUT_TOKENS) {
+            if (out_dim != H) fail("rembed: token output needs out_dim == hidden (%d)", H);
+        } else {
+            fail("rembed: bad out_kind %d", out_kind);
         }
-        std::vector<int> b = shard_bounds(c->d, cu, nseq, nrep);
-        std::vector<std::string> errs(nrep);
-        std::vector<std::thread> th;
-        for (int k = 0; k < nrep; ++k)
-            th.emplace_back([&, k] {
-                try {
-                    run_host_shard(c, *c->reps[k], ids, cu, b[k], b[k + 1], out_kind, out_dim, host_out);
-                } catch (const Error& e) {
-                    errs[k] = e.msg;
-                }
-            });
-        for (auto& t : th) t.join();
-        for (auto& e : errs)
-            if (!e.empty()) fail("%s", e.c_str());
+        validate_batch(c->d, ids, cu, nseq);
+        *ticket = submit_batch(c, ids, cu, nseq, out_kind, out_dim, host_out);
+        return 0;
+    } catch (const Error& e) {
+        set_err(err, e.msg);
+        return -1;
+    }
+}
+
+int rg_collect(rg_ctx* c, int64_t ticket, char** err) {
+    try {
+        if (!c) fail("rembed: invalid context");
+        collect_batch(c, ticket);
         return 0;
     } catch (const Error& e) {
         set_err(err, e.msg);
@@ -1637,7 +1752,7 @@ void rg_free(rg_ctx* c) {
         for (cudaEvent_t e : r->ev_pool) cudaEventDestroy(e);
         for (void* p : r->allocs) cudaFree(p);
         if (r->w16) cudaFree(r->w16);
-        if (r->h_status) cudaFreeHost(r->h_status);
+        free_staging(*r);
         if (r->stream) cudaStreamDestroy(r->stream);
         delete r;
     }

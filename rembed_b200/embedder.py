@@ -34,7 +34,7 @@ import numpy as np
 
 from .config import Config
 
-__all__ = ["Embedder", "RembedError", "TokenEmbeddings", "load", "library"]
+__all__ = ["Embedder", "Pending", "RembedError", "TokenEmbeddings", "load", "library"]
 
 RG_MODE_BF16, RG_MODE_F16, RG_MODE_INT8_W, RG_MODE_INT8_FULL, RG_MODE_FP32 = 0, 1, 2, 3, 4
 RG_DTYPE_F32, RG_DTYPE_F16, RG_DTYPE_BF16 = 0, 1, 2
@@ -93,6 +93,10 @@ SIGNATURES = {
     "rg_finalize": (ctypes.c_int, [_VP, _ERR]),
     "rg_forward": (ctypes.c_int, [_VP, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int32), ctypes.c_int,
                                   ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_float), _ERR]),
+    "rg_submit": (ctypes.c_int, [_VP, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int32), ctypes.c_int,
+                                 ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_float),
+                                 ctypes.POINTER(ctypes.c_int64), _ERR]),
+    "rg_collect": (ctypes.c_int, [_VP, ctypes.c_int64, _ERR]),
     "rg_forward_device": (ctypes.c_int, [_VP, ctypes.c_int, _VP, _VP, ctypes.POINTER(ctypes.c_int32), ctypes.c_int,
                                          ctypes.c_int, ctypes.c_int, _VP, _VP, _ERR]),
     "rg_sync": (ctypes.c_int, [_VP, ctypes.c_int, _ERR]),
@@ -162,6 +166,20 @@ class TokenEmbeddings:
 
     ids: np.ndarray
     vectors: np.ndarray  # [len(ids) x hidden]
+
+
+class Pending:
+    """A submitted batch (Embedder.submit); ``result()`` waits for it once."""
+
+    def __init__(self, emb: "Embedder", ticket: int, out: np.ndarray):
+        self._emb, self._ticket, self._out = emb, ticket, out
+        self._done = False
+
+    def result(self) -> np.ndarray:
+        if not self._done:
+            self._done = True
+            _call(self._emb._lib.rg_collect, self._emb._ctx, self._ticket)
+        return self._out
 
 
 def pack(seqs: Iterable[Sequence[int]]) -> tuple[np.ndarray, np.ndarray]:
@@ -257,6 +275,35 @@ class Embedder:
                   cu.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), n, RG_OUT_POOLED, self._dim,
                   out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
         return out
+
+    def submit(self, ids: np.ndarray, cu_seqlens: np.ndarray, out: np.ndarray | None = None) -> "Pending":
+        """Start embedding a packed batch and return at once (rg_submit): the
+        next batch can be prepared while this one runs.  ``result()`` on the
+        returned handle waits for it.  Two batches may be in flight."""
+        self._check_open()
+        ids = np.ascontiguousarray(ids, dtype=np.int64)
+        cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
+        n = len(cu) - 1
+        if out is None:
+            out = np.empty((n, self._dim), dtype=np.float32)
+        ticket = ctypes.c_int64(-1)
+        _call(self._lib.rg_submit, self._ctx, ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
+              cu.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), n, RG_OUT_POOLED, self._dim,
+              out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), ctypes.byref(ticket))
+        return Pending(self, ticket.value, out)
+
+    def embed_stream(self, batches: Iterable[tuple[np.ndarray, np.ndarray]]):
+        """Embed packed (ids, cu_seqlens) batches in order, yielding each
+        result while the next batch is already on the GPU (one submission
+        ahead of the consumer)."""
+        pending = None
+        for ids, cu in batches:
+            nxt = self.submit(ids, cu)
+            if pending is not None:
+                yield pending.result()
+            pending = nxt
+        if pending is not None:
+            yield pending.result()
 
     def embed_tokens(self, seqs: Iterable[Sequence[int]]) -> list[TokenEmbeddings]:
         """Per-token final hidden states, unpooled and unnormalised."""

@@ -241,3 +241,28 @@ def test_load_sharded_and_disk_weights(cuda, tmp_path):
         assert np.array_equal(e.embed_packed(ids, cu), want)
         e.close()
     assert (tmp_path / "weights.rembedpack").exists()
+
+
+def test_submit_collect_pipeline(minilm):
+    """rg_submit / rg_collect: two batches in flight, results identical to
+    the synchronous call; a third submission is refused until one is
+    collected; a collected ticket cannot be collected again."""
+    b1 = synth.make_batch(minilm.cfg, 9, 4, 128, seed=81)
+    b2 = synth.make_batch(minilm.cfg, 5, 4, 128, seed=82)
+    b3 = synth.make_batch(minilm.cfg, 7, 4, 128, seed=83)
+    want = [minilm.gpu.embed_packed(*b) for b in (b1, b2, b3)]
+    p1 = minilm.gpu.submit(*b1)
+    p2 = minilm.gpu.submit(*b2)
+    with pytest.raises(RembedError, match="outstanding"):
+        minilm.gpu.submit(*b3)
+    assert np.array_equal(p1.result(), want[0])
+    p3 = minilm.gpu.submit(*b3)
+    assert np.array_equal(p2.result(), want[1])
+    assert np.array_equal(p3.result(), want[2])
+    got = list(minilm.gpu.embed_stream([b1, b2, b3, b1]))
+    assert all(np.array_equal(g, w) for g, w in zip(got, want + [want[0]]))
+    import ctypes
+
+    err = ctypes.c_char_p()
+    assert minilm.gpu._lib.rg_collect(minilm.gpu._ctx, 0, ctypes.byref(err)) != 0
+    minilm.gpu._lib.rg_free_string(ctypes.cast(err, ctypes.c_void_p))
