@@ -18,6 +18,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <condition_variable>
 #include <mutex>
 #include <string>
 #include <thread>
@@ -200,6 +201,7 @@ struct rg_ctx {
     // host-batch submissions: ticket t uses staging slot t % 2 of every
     // replica; pending[slot] is the ticket in flight there (-1: none)
     std::mutex tmu;
+    std::condition_variable tcv;  // a slot was collected
     int64_t next_ticket = 0;
     int64_t pending[2] = {-1, -1};
 };
@@ -1387,14 +1389,20 @@ std::vector<int> shard_bounds(const rg_model_desc& d, const int32_t* cu, int nse
 
 // Submit a validated host batch: split over the replicas (contiguous,
 // cost-balanced shards) and staged in slot ticket % 2 of each.
+// wait_for_slot: the synchronous rg_forward waits for another thread to
+// collect the slot it needs; rg_submit (whose caller may hold both
+// outstanding tickets itself) reports the limit instead.
 int64_t submit_batch(rg_ctx* c, const int64_t* ids, const int32_t* cu, int nseq, int out_kind, int out_dim,
-                     float* host_out) {
-    std::lock_guard<std::mutex> tl(c->tmu);
+                     float* host_out, bool wait_for_slot) {
+    std::unique_lock<std::mutex> tl(c->tmu);
+    while (c->pending[c->next_ticket & 1] >= 0) {
+        if (!wait_for_slot)
+            fail("rembed: two submissions are outstanding; collect ticket %lld first",
+                 static_cast<long long>(c->pending[c->next_ticket & 1]));
+        c->tcv.wait(tl);
+    }
     const int64_t t = c->next_ticket;
     const int slot = static_cast<int>(t & 1);
-    if (c->pending[slot] >= 0)
-        fail("rembed: two submissions are outstanding; collect ticket %lld first",
-             static_cast<long long>(c->pending[slot]));
     const int nrep = static_cast<int>(c->reps.size());
     const std::vector<int> b = nrep == 1 ? std::vector<int>{0, nseq} : shard_bounds(c->d, cu, nseq, nrep);
     int k = 0;
@@ -1422,6 +1430,7 @@ void collect_batch(rg_ctx* c, int64_t t) {
         if (t < 0 || c->pending[slot] != t) fail("rembed: ticket %lld is not outstanding", static_cast<long long>(t));
         c->pending[slot] = -1;
     }
+    c->tcv.notify_all();
     std::string first;
     for (Replica* r : c->reps) {
         try {
@@ -1593,7 +1602,7 @@ int rg_forward(rg_ctx* c, const int64_t* ids, const int32_t* cu, int nseq, int o
             fail("rembed: bad out_kind %d", out_kind);
         }
         validate_batch(c->d, ids, cu, nseq);
-        const int64_t t = submit_batch(c, ids, cu, nseq, out_kind, out_dim, host_out);
+        const int64_t t = submit_batch(c, ids, cu, nseq, out_kind, out_dim, host_out, true);
         collect_batch(c, t);
         return 0;
     } catch (const Error& e) {
@@ -1619,7 +1628,7 @@ int rg_submit(rg_ctx* c, const int64_t* ids, const int32_t* cu, int nseq, int ou
             fail("rembed: bad out_kind %d", out_kind);
         }
         validate_batch(c->d, ids, cu, nseq);
-        *ticket = submit_batch(c, ids, cu, nseq, out_kind, out_dim, host_out);
+        *ticket = submit_batch(c, ids, cu, nseq, out_kind, out_dim, host_out, false);
         return 0;
     } catch (const Error& e) {
         set_err(err, e.msg);

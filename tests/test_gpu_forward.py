@@ -266,3 +266,29 @@ def test_submit_collect_pipeline(minilm):
     err = ctypes.c_char_p()
     assert minilm.gpu._lib.rg_collect(minilm.gpu._ctx, 0, ctypes.byref(err)) != 0
     minilm.gpu._lib.rg_free_string(ctypes.cast(err, ctypes.c_void_p))
+
+
+def test_concurrent_forward_calls(minilm):
+    """The Embedder is safe for concurrent use (rembed.go:37-41): four
+    threads calling the synchronous forward on one context all succeed and
+    get the single-threaded results."""
+    import threading
+
+    batches = [synth.make_batch(minilm.cfg, 6, 4, 100, seed=90 + k) for k in range(4)]
+    want = [minilm.gpu.embed_packed(*b) for b in batches]
+    got, errs = [None] * 4, []
+
+    def run(k):
+        try:
+            for _ in range(3):
+                got[k] = minilm.gpu.embed_packed(*batches[k])
+        except Exception as e:  # pragma: no cover - reported below
+            errs.append(e)
+
+    th = [threading.Thread(target=run, args=(k,)) for k in range(4)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    assert not errs
+    assert all(np.array_equal(g, w) for g, w in zip(got, want))
