@@ -115,6 +115,18 @@ static cudaError_t launch_impl(GemmKind kind, int epi, int block_n, GemmMaps& m,
     if (!make_epilogue_tmap(&m.out, args.out, f32out, f16out, args.M, glu ? args.N / 2 : args.N, args.ld_out))
         return cudaErrorInvalidValue;
     if (epi == kEpiBiasResLN && (!args.ln_stats || !args.ln_g || !args.ln_b)) return cudaErrorInvalidValue;
+    // Folded LayerNorm and the chunk statistics / 16-bit copy of residual
+    // outputs: 16-bit kinds only.
+    const bool k16 = kind == GemmKind::kBF16 || kind == GemmKind::kF16;
+    if (args.fold_stats && (!k16 || !args.fold_c1 || !args.bias || (epi != kEpiBias && epi != kEpiBiasGelu)))
+        return cudaErrorInvalidValue;
+    if ((args.parts_out || args.out16) && (!k16 || !epi_has_residual(epi))) return cudaErrorInvalidValue;
+    if (args.out16) {
+        if (!make_epilogue_tmap(&m.out16, args.out16, false, kind == GemmKind::kF16, args.M, args.N, args.ld16))
+            return cudaErrorInvalidValue;
+    } else {
+        m.out16 = m.out;  // unused
+    }
     if (epi_has_residual(epi)) {
         if (!args.residual || !make_epilogue_tmap(&m.res, args.residual, true, false, args.M, args.N, args.N))
             return cudaErrorInvalidValue;

@@ -39,6 +39,18 @@ struct GemmArgs {
     void* out;               // [M x ld_out], 16-bit (bf16 / fp16 by kind) or fp32
     int ld_out;
     int* status;             // device status word
+    // LayerNorm folded into this GEMM (kEpiBias / kEpiBiasGelu): A holds the
+    // unnormalised rows y and W the weight times the norm's gain; with the
+    // row's (mean, rstd) from fold_stats the epilogue computes
+    // rstd * acc + (bias[n] - rstd * mean * fold_c1[n]) (bias = W.beta + b).
+    const float2* fold_stats;  // [M] (mean, rstd)
+    const float* fold_c1;      // [N] column sums of the folded 16-bit weight
+    // residual epilogues: also write the output as 16 bits (out16, row
+    // stride ld16) and the (mean, M2) of each 32-column chunk of each row
+    // (parts_out: [N / 32 x M], chunk-major)
+    uint16_t* out16;
+    int ld16;
+    float2* parts_out;
 };
 
 // Operand element kind of the GEMM.
@@ -55,7 +67,7 @@ enum class GemmKind : int { kBF16 = 0, kS8 = 1, kF16 = 2, kW8 = 3, kTF32x3 = 4 }
 // Tensor maps one launch reads: A, W, the output and residual boxes, and for
 // kTF32x3 the remainder parts of A (a2) and W (b2).
 struct GemmMaps {
-    CUtensorMap a, b, out, res, a2, b2;
+    CUtensorMap a, b, out, res, a2, b2, out16;
 };
 
 // Encode a 2-D K-major tensor map over a row-major [rows x cols] matrix

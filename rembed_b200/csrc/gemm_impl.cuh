@@ -124,20 +124,29 @@ constexpr int kEpiWarps = 8;        // two epilogue warps per SM sub-partition
 constexpr int kThreads = 128 + 32 * kEpiWarps;
 constexpr int kChunk = 32;          // accumulator columns per TMEM load / TMA store box
 constexpr int kStageBytes = 4096;   // one 32 x 32 fp32 (or 32 x 32 bf16, half used) staging box
+constexpr int kY16Bytes = 2048;     // one 32 x 32 16-bit staging box
 
 // Per-CTA shapes of the pair kernel: the tile is 256 x BN, each CTA of the
 // pair holds 128 rows of A and BN/2 rows of W per 128-byte k-block.  With
 // int8 weights widened in shared memory (W8), each stage also holds the
 // int8 k-block as loaded (64 bytes x BN/2 rows).
-template <int BN, bool W8>
+// Residual epilogues of the 16-bit kinds (Y16) also stage the output's
+// 16-bit copy: one 32 x 32 box per epilogue warp.
+template <int BN, int KIND, int EPI>
 struct GemmShape {
+    static constexpr bool W8 = KIND == static_cast<int>(GemmKind::kW8);
+    static constexpr bool Y16 = (EPI == kEpiBiasRes || EPI == kEpiBiasResLN) &&
+                                (KIND == static_cast<int>(GemmKind::kBF16) || KIND == static_cast<int>(GemmKind::kF16));
     static constexpr int A_BYTES = 128 * 128;
     static constexpr int B_BYTES = (BN / 2) * 128;
     static constexpr int B8_BYTES = W8 ? (BN / 2) * 64 : 0;
-    static constexpr int STAGES = W8 ? (BN == 128 ? 5 : 4) : (BN == 128 ? 6 : 5);
+    static constexpr int Y16_BYTES = Y16 ? kEpiWarps * kY16Bytes : 0;
+    static constexpr int STAGES = W8 ? (BN == 128 ? 5 : 4) : (BN == 128 ? 6 : (Y16 && BN == 256 ? 4 : 5));
     static constexpr uint32_t TMEM_COLS = BN == 128 ? 256 : 512;  // 2 accumulators, power of two
-    // mainloop ring + two staging boxes per epilogue warp + barriers
-    static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES + B8_BYTES) + kEpiWarps * 2 * kStageBytes + 1024 + 512;
+    // mainloop ring + two staging boxes per epilogue warp (+ the 16-bit
+    // copy's box) + barriers
+    static constexpr int SMEM =
+        STAGES * (A_BYTES + B_BYTES + B8_BYTES) + kEpiWarps * 2 * kStageBytes + Y16_BYTES + 1024 + 512;
 };
 
 // Four int8 weights (bytes of x) to four exact fp16 values (lo: elements 0,
@@ -168,7 +177,8 @@ template <int BN, int KIND, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmRes,
-                const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, GemmArgs args) {
+                const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
+                const __grid_constant__ CUtensorMap tmOut16, GemmArgs args) {
     constexpr bool S8 = KIND == static_cast<int>(GemmKind::kS8);
     constexpr bool W8 = KIND == static_cast<int>(GemmKind::kW8);
     constexpr bool F16 = KIND == static_cast<int>(GemmKind::kF16) || W8;  // fp16 operands and output
@@ -176,7 +186,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // (A_hi W_hi, A_hi W_lo, A_lo W_hi), fp32 outputs
     constexpr bool X3 = KIND == static_cast<int>(GemmKind::kTF32x3);
     constexpr bool CSCALE = true;  // per-column dequant scales, whenever args.col_scale is set
-    using S = GemmShape<BN, W8>;
+    using S = GemmShape<BN, KIND, EPI>;
     constexpr int STAGES = S::STAGES;
     constexpr int A_BYTES = S::A_BYTES, B_BYTES = S::B_BYTES, B8_BYTES = S::B8_BYTES;
     constexpr int K_ELEMS = S8 ? 128 : (X3 ? 32 : 64);  // elements per 128-byte k-block of A
@@ -187,7 +197,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint8_t* sB = smem + STAGES * A_BYTES;          // W k-blocks as the MMA reads them
     uint8_t* sB8 = sB + STAGES * B_BYTES;           // W8: int8 k-blocks as loaded
     uint8_t* stage_base = sB8 + STAGES * B8_BYTES;  // 1024-byte aligned
-    uint64_t* full = reinterpret_cast<uint64_t*>(stage_base + kEpiWarps * 2 * kStageBytes);
+    uint8_t* y16_base = stage_base + kEpiWarps * 2 * kStageBytes;  // Y16: [kEpiWarps] 16-bit boxes
+    uint64_t* full = reinterpret_cast<uint64_t*>(y16_base + S::Y16_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
@@ -234,6 +245,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         tma_prefetch_desc(&tmOut);
         if (EPI == kEpiBiasRes || EPI == kEpiBiasResLN) tma_prefetch_desc(&tmRes);
+        if (S::Y16 && args.out16) tma_prefetch_desc(&tmOut16);
     }
     if (warp == 2) {
         tmem_alloc_pair(tmem_slot, S::TMEM_COLS);
@@ -422,17 +434,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
             const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
-            if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
-            tc_fence_after();
             const int row0 = m_blk * 256 + static_cast<int>(rank) * 128 + quarter * 32;
+            const int row = row0 + lane;
+            // Per-row operands of the epilogue, fetched while the tile's MMAs run.
             float rs = 1.0f;
             if constexpr (S8) {
-                if (args.row_scale && row0 + lane < args.M) rs = args.row_scale[row0 + lane];
+                if (args.row_scale && row < args.M) rs = args.row_scale[row];
             }
             float2 lnst = make_float2(0.f, 1.f);  // this row's (mean, rstd) for kEpiBiasResLN
             if constexpr (EPI == kEpiBiasResLN) {
-                if (row0 + lane < args.M) lnst = args.ln_stats[row0 + lane];
+                if (row < args.M) lnst = args.ln_stats[row];
             }
+            // folded LayerNorm of the A rows: rstd and -rstd * mean
+            float fr = 1.f, fnm = 0.f;
+            if constexpr (EPI == kEpiBias || EPI == kEpiBiasGelu) {
+                if (args.fold_stats && row < args.M) {
+                    const float2 st = args.fold_stats[row];
+                    fr = st.y;
+                    fnm = -st.x * st.y;
+                }
+            }
+            if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
+            tc_fence_after();
             const uint32_t taddr =
                 tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + half * HALF;
             constexpr bool GLU = EPI >= kEpiGluSilu && EPI <= kEpiGluGeluTanh;
@@ -527,7 +550,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         v[4 * i + 3] *= q.w;
                     }
                 }
-                if (!GLU && args.bias) {
+                bool folded = false;
+                if constexpr (EPI == kEpiBias || EPI == kEpiBiasGelu) {
+                    if (args.fold_stats) {  // rstd * acc + (bias - rstd * mean * c1)
+                        folded = true;
+                        const float4* c1 = reinterpret_cast<const float4*>(args.fold_c1 + col0);
+                        const float4* bp = reinterpret_cast<const float4*>(args.bias + col0);
+                        const uint64_t r2 = f2(fr, fr), nm2 = f2(fnm, fnm);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float4 q = __ldg(c1 + i), bb = __ldg(bp + i);
+                            const uint64_t u0 = fma2(nm2, f2(q.x, q.y), f2(bb.x, bb.y));
+                            const uint64_t u1 = fma2(nm2, f2(q.z, q.w), f2(bb.z, bb.w));
+                            f2split(fma2(r2, f2(v[4 * i], v[4 * i + 1]), u0), v[4 * i], v[4 * i + 1]);
+                            f2split(fma2(r2, f2(v[4 * i + 2], v[4 * i + 3]), u1), v[4 * i + 2], v[4 * i + 3]);
+                        }
+                    }
+                }
+                if (!GLU && !folded && args.bias) {
                     const float4* bp = reinterpret_cast<const float4*>(args.bias + col0);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
@@ -562,6 +602,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         f2split(add2(f2(x.x, x.y), f2(v[4 * i], v[4 * i + 1])), v[4 * i], v[4 * i + 1]);
                         f2split(add2(f2(x.z, x.w), f2(v[4 * i + 2], v[4 * i + 3])), v[4 * i + 2], v[4 * i + 3]);
                     }
+                    if (args.parts_out && row < args.M) {  // this chunk's (mean, M2)
+                        float cs = 0.f;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) cs += v[i];
+                        const float cm = cs * (1.0f / 32.0f);
+                        float c2 = 0.f;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) c2 = fmaf(v[i] - cm, v[i] - cm, c2);
+                        args.parts_out[static_cast<int64_t>(col0 / kChunk) * args.M + row] = make_float2(cm, c2);
+                    }
+                    if constexpr (S::Y16) {
+                        // the 16-bit copy, staged for its own TMA store (the
+                        // box is free: every earlier store has read its box)
+                        if (args.out16) {
+                            uint8_t* y16 = y16_base + ew * kY16Bytes;
+#pragma unroll
+                            for (int i = 0; i < 4; ++i)
+                                *reinterpret_cast<uint4*>(y16 + swz(lane, i, 64)) = make_uint4(
+                                    pack2<F16>(v[8 * i], v[8 * i + 1]), pack2<F16>(v[8 * i + 2], v[8 * i + 3]),
+                                    pack2<F16>(v[8 * i + 4], v[8 * i + 5]), pack2<F16>(v[8 * i + 6], v[8 * i + 7]));
+                        }
+                    }
                 }
                 if constexpr (F32OUT) {
 #pragma unroll
@@ -590,6 +652,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) {
                     tma_store_2d(&tmOut, box, ocol0, row0);
+                    if constexpr (S::Y16) {
+                        if (args.out16) tma_store_2d(&tmOut16, y16_base + ew * kY16Bytes, col0, row0);
+                    }
                     bulk_commit();
                 }
             }
@@ -630,7 +695,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
 template <int BN, int KIND, int EPI>
 static cudaError_t launch_one(const GemmMaps& m, const GemmArgs& args, int num_sms, cudaStream_t stream) {
-    constexpr int smem = GemmShape<BN, KIND == static_cast<int>(GemmKind::kW8)>::SMEM;
+    constexpr int smem = GemmShape<BN, KIND, EPI>::SMEM;
     static_assert(smem <= 232448, "shared memory budget");
     auto kern = gemm_kernel<BN, KIND, EPI>;
     // The shared-memory opt-in is a per-device function attribute.
@@ -667,7 +732,7 @@ static cudaError_t launch_one(const GemmMaps& m, const GemmArgs& args, int num_s
     }
     const int tiles = ((args.M + 255) / 256) * (args.N / BN);
     const int grid = 2 * (tiles < pairs ? tiles : pairs);
-    kern<<<grid, kThreads, smem, stream>>>(m.a, m.b, m.out, m.res, m.a2, m.b2, args);
+    kern<<<grid, kThreads, smem, stream>>>(m.a, m.b, m.out, m.res, m.a2, m.b2, m.out16, args);
     return cudaGetLastError();
 }
 

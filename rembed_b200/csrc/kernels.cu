@@ -612,6 +612,47 @@ cudaError_t launch_attention(const AttnParams& p, int nseq, int max_len, int hea
 }
 
 // ---------------------------------------------------------------------------
+// Row statistics of a folded LayerNorm: the chunks merged in a fixed order
+// (Chan et al.'s update for equal-size parts): mean = sum of the chunk means
+// / n, M2 = sum of (M2_i + 32 (mean_i - mean)^2), var = M2 / (32 n).  One
+// thread per row; for each chunk the warp's 32 rows are 256 contiguous bytes.
+__global__ void __launch_bounds__(256) merge_row_stats_kernel(const float2* __restrict__ parts, int nparts, int T,
+                                                              float eps, float2* __restrict__ stats) {
+    const int row = blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= T) return;
+    constexpr int kMax = 32;  // chunks held in registers at once
+    float2 q[kMax];
+    float s = 0.f;
+    for (int c0 = 0; c0 < nparts; c0 += kMax) {
+#pragma unroll
+        for (int i = 0; i < kMax; ++i)
+            if (c0 + i < nparts) s += parts[static_cast<size_t>(c0 + i) * T + row].x;
+    }
+    const float mean = s / static_cast<float>(nparts);
+    float m2 = 0.f;
+    for (int c0 = 0; c0 < nparts; c0 += kMax) {
+#pragma unroll
+        for (int i = 0; i < kMax; ++i)
+            if (c0 + i < nparts) q[i] = parts[static_cast<size_t>(c0 + i) * T + row];
+#pragma unroll
+        for (int i = 0; i < kMax; ++i) {
+            if (c0 + i < nparts) {
+                const float d = q[i].x - mean;
+                m2 += fmaf(32.0f * d, d, q[i].y);
+            }
+        }
+    }
+    stats[row] = make_float2(mean, 1.0f / sqrtf(m2 / static_cast<float>(32 * nparts) + eps));
+}
+
+cudaError_t launch_merge_row_stats(const float2* parts, int nparts, int T, float eps, float2* stats, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    if (nparts <= 0 || !parts || !stats) return cudaErrorInvalidValue;
+    merge_row_stats_kernel<<<(T + 255) / 256, 256, 0, st>>>(parts, nparts, T, eps, stats);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
 // 3xTF32 operand split: hi = tf32(x) (nearest, ties to even), lo = x - hi.
 __global__ void __launch_bounds__(256) split_tf32_kernel(const float4* __restrict__ x, size_t n4, float4* hi,
                                                         float4* lo) {

@@ -53,6 +53,11 @@ __host__ __device__ inline void tf32_split(float x, float& hi, float& lo) {
 // x [n] -> hi [n], lo [n] (hi may alias x); n % 4 == 0, 16-byte aligned.
 cudaError_t launch_split_tf32(const float* x, size_t n, float* hi, float* lo, cudaStream_t st);
 
+// Per-row LayerNorm statistics from the (mean, M2) of each row's nparts
+// 32-column chunks (parts[i * T + row], as residual GEMM epilogues write
+// them): stats[row] = (mean, 1 / sqrt(var + eps)).
+cudaError_t launch_merge_row_stats(const float2* parts, int nparts, int T, float eps, float2* stats, cudaStream_t st);
+
 // Row normalisation of in [T x H]: LayerNorm (g, b; b nullptr = zero) or
 // RMSNorm (g); g nullptr = identity.  Outputs (each optional): out32 (may
 // alias in), outb (16-bit: fp16 if f16, else bf16), outq + outqs (int8 row

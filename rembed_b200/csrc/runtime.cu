@@ -73,6 +73,7 @@ struct DevDense {
     CUtensorMap tmap16[3];  // weight-only int8: the same shape over the replica's fp16 widening scratch
     void* w_lo = nullptr;   // strict fp32: the fp32 remainder of the tf32-rounded weight in w
     CUtensorMap tmap_lo[3];
+    float* fold_c1 = nullptr;  // folded LayerNorm: column sums of the 16-bit w (w = W * gain)
 };
 
 // A GEMM's A operand: the tensor map of the buffer the MMA reads and, in the
@@ -127,6 +128,13 @@ struct Replica {
     int8_t *xq = nullptr, *ctxq = nullptr, *ffhq = nullptr;
     float *xs = nullptr, *ctxs = nullptr, *ffhs = nullptr;
     float2* lnst = nullptr;  // post-norm: the last LayerNorm's per-row (mean, rstd)
+    // Post-norm stacks in the 16-bit modes fold each inner LayerNorm into
+    // the GEMMs around it: the residual GEMM writes its output's 32-column
+    // chunk statistics (parts) and a 16-bit copy in xb, a small kernel
+    // merges the chunks into lnst, and the next GEMM reads the copy with the
+    // norm's gain folded into its weight.
+    bool fold = false;
+    float2* parts = nullptr;  // [H / 32 x T]
     float *pool32 = nullptr, *head_hid = nullptr, *head_out = nullptr;  // Gemma Dense head
     int32_t* iota = nullptr;                                            // [0, 1, ..., cap_seq]
     int64_t* d_ids = nullptr;
@@ -310,6 +318,19 @@ bool to_f16_bits(float f, uint16_t* out) {
 
 bool finite32(float v) { return std::isfinite(v); }
 
+float bf16_bits_to_float(uint16_t h) {
+    const uint32_t u = static_cast<uint32_t>(h) << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+float f16_bits_to_float(uint16_t h) {  // exact: every fp16 value is a float
+    const int e = (h >> 10) & 0x1f, m = h & 0x3ff;
+    const float v = e == 0 ? std::ldexp(static_cast<float>(m), -24) : std::ldexp(static_cast<float>(m | 0x400), e - 25);
+    return (h & 0x8000) ? -v : v;
+}
+
 // PackB8 (pack8.go:25-76): float32 scale maxAbs/127, float64 division,
 // round half to even, clamp +-127.
 void quant_packb8(const float* w, int N, int K, int8_t* q, float* scales) {
@@ -440,6 +461,46 @@ DevDense make_dense(Replica& r, int mode, const float* w, const float* bias, int
     return d;
 }
 
+// The weight W [N x K] of a GEMM whose input is LN(y) = (y - mean) * rstd *
+// g + b, folded so the GEMM reads y itself: w = round16(W * g) by column,
+// bias' = W.b + bias, and c1[n] = sum_k w[n][k] so the epilogue computes
+// rstd * (y.w - mean * c1) + bias'.  In the fp16 mode it returns false
+// (nothing uploaded) when some W * g falls outside the fp16 range.
+bool fold_ok(int mode, const float* W, const float* g, int N, int K) {
+    if (mode != RG_MODE_F16) return true;
+    uint16_t h;
+    for (int n = 0; n < N; ++n)
+        for (int k = 0; k < K; ++k)
+            if (!to_f16_bits(W[static_cast<size_t>(n) * K + k] * g[k], &h)) return false;
+    return true;
+}
+
+DevDense make_dense_folded(Replica& r, int mode, const float* W, const float* bias, int N, int K, const float* g,
+                           const float* b) {
+    std::vector<float> wf(static_cast<size_t>(N) * K), bf(N), c1(N);
+    for (int n = 0; n < N; ++n) {
+        const float* row = W + static_cast<size_t>(n) * K;
+        double wb = bias ? bias[n] : 0.0, cs = 0.0;
+        for (int k = 0; k < K; ++k) {
+            const float v = row[k] * g[k];
+            wf[static_cast<size_t>(n) * K + k] = v;
+            wb += static_cast<double>(row[k]) * b[k];
+            uint16_t h;
+            if (mode == RG_MODE_F16) {
+                if (!to_f16_bits(v, &h)) fail("folded weight [%d, %d] outside the fp16 range", n, k);
+                cs += f16_bits_to_float(h);
+            } else {
+                cs += bf16_bits_to_float(to_bf16_bits(v));
+            }
+        }
+        bf[n] = static_cast<float>(wb);
+        c1[n] = static_cast<float>(cs);
+    }
+    DevDense d = make_dense(r, mode, wf.data(), bf.data(), N, K);
+    d.fold_c1 = dev_upload(r, c1.data(), N);
+    return d;
+}
+
 void finalize_bert(rg_ctx* c, Replica& r) {
     const rg_model_desc& d = c->d;
     const int H = d.hidden_size, I = d.intermediate_size, V = d.vocab_size, P = d.max_position_embeddings;
@@ -477,77 +538,100 @@ void finalize_bert(rg_ctx* c, Replica& r) {
         r.type0 = dev_upload(r, tt->data.data(), H);
     }
     r.layers.resize(d.num_hidden_layers);
+    struct HostLayer {
+        const float *qW, *qB, *kW, *kB, *vW, *vB, *oW, *oB, *f1W, *f1B, *f2W, *f2B, *g1, *b1, *g2, *b2;
+    };
+    std::vector<HostLayer> hl(d.num_hidden_layers);
     for (int li = 0; li < d.num_hidden_layers; ++li) {
-        DevLayer& L = r.layers[li];
         const std::string p = (distil ? "transformer.layer." : "encoder.layer.") + std::to_string(li) + ".";
         auto T = [&](const std::string& n, std::initializer_list<int64_t> s) -> const float* {
             return get_tensor(c, p + n, s).data.data();
         };
-        const float *qW, *qB, *kW, *kB, *vW, *vB, *oW, *oB, *f1W, *f1B, *f2W, *f2B;
+        HostLayer& w = hl[li];
         if (distil) {
-            qW = T("attention.q_lin.weight", {H, H});
-            qB = T("attention.q_lin.bias", {H});
-            kW = T("attention.k_lin.weight", {H, H});
-            kB = T("attention.k_lin.bias", {H});
-            vW = T("attention.v_lin.weight", {H, H});
-            vB = T("attention.v_lin.bias", {H});
-            oW = T("attention.out_lin.weight", {H, H});
-            oB = T("attention.out_lin.bias", {H});
-            L.ln1_g = dev_upload(r, T("sa_layer_norm.weight", {H}), H);
-            L.ln1_b = dev_upload(r, T("sa_layer_norm.bias", {H}), H);
-            f1W = T("ffn.lin1.weight", {I, H});
-            f1B = T("ffn.lin1.bias", {I});
-            f2W = T("ffn.lin2.weight", {H, I});
-            f2B = T("ffn.lin2.bias", {H});
-            L.ln2_g = dev_upload(r, T("output_layer_norm.weight", {H}), H);
-            L.ln2_b = dev_upload(r, T("output_layer_norm.bias", {H}), H);
+            w.qW = T("attention.q_lin.weight", {H, H});
+            w.qB = T("attention.q_lin.bias", {H});
+            w.kW = T("attention.k_lin.weight", {H, H});
+            w.kB = T("attention.k_lin.bias", {H});
+            w.vW = T("attention.v_lin.weight", {H, H});
+            w.vB = T("attention.v_lin.bias", {H});
+            w.oW = T("attention.out_lin.weight", {H, H});
+            w.oB = T("attention.out_lin.bias", {H});
+            w.g1 = T("sa_layer_norm.weight", {H});
+            w.b1 = T("sa_layer_norm.bias", {H});
+            w.f1W = T("ffn.lin1.weight", {I, H});
+            w.f1B = T("ffn.lin1.bias", {I});
+            w.f2W = T("ffn.lin2.weight", {H, I});
+            w.f2B = T("ffn.lin2.bias", {H});
+            w.g2 = T("output_layer_norm.weight", {H});
+            w.b2 = T("output_layer_norm.bias", {H});
         } else if (mpnet) {
-            qW = T("attention.attn.q.weight", {H, H});
-            qB = T("attention.attn.q.bias", {H});
-            kW = T("attention.attn.k.weight", {H, H});
-            kB = T("attention.attn.k.bias", {H});
-            vW = T("attention.attn.v.weight", {H, H});
-            vB = T("attention.attn.v.bias", {H});
-            oW = T("attention.attn.o.weight", {H, H});
-            oB = T("attention.attn.o.bias", {H});
-            L.ln1_g = dev_upload(r, T("attention.LayerNorm.weight", {H}), H);
-            L.ln1_b = dev_upload(r, T("attention.LayerNorm.bias", {H}), H);
-            f1W = T("intermediate.dense.weight", {I, H});
-            f1B = T("intermediate.dense.bias", {I});
-            f2W = T("output.dense.weight", {H, I});
-            f2B = T("output.dense.bias", {H});
-            L.ln2_g = dev_upload(r, T("output.LayerNorm.weight", {H}), H);
-            L.ln2_b = dev_upload(r, T("output.LayerNorm.bias", {H}), H);
+            w.qW = T("attention.attn.q.weight", {H, H});
+            w.qB = T("attention.attn.q.bias", {H});
+            w.kW = T("attention.attn.k.weight", {H, H});
+            w.kB = T("attention.attn.k.bias", {H});
+            w.vW = T("attention.attn.v.weight", {H, H});
+            w.vB = T("attention.attn.v.bias", {H});
+            w.oW = T("attention.attn.o.weight", {H, H});
+            w.oB = T("attention.attn.o.bias", {H});
+            w.g1 = T("attention.LayerNorm.weight", {H});
+            w.b1 = T("attention.LayerNorm.bias", {H});
+            w.f1W = T("intermediate.dense.weight", {I, H});
+            w.f1B = T("intermediate.dense.bias", {I});
+            w.f2W = T("output.dense.weight", {H, I});
+            w.f2B = T("output.dense.bias", {H});
+            w.g2 = T("output.LayerNorm.weight", {H});
+            w.b2 = T("output.LayerNorm.bias", {H});
         } else {
-            qW = T("attention.self.query.weight", {H, H});
-            qB = T("attention.self.query.bias", {H});
-            kW = T("attention.self.key.weight", {H, H});
-            kB = T("attention.self.key.bias", {H});
-            vW = T("attention.self.value.weight", {H, H});
-            vB = T("attention.self.value.bias", {H});
-            oW = T("attention.output.dense.weight", {H, H});
-            oB = T("attention.output.dense.bias", {H});
-            L.ln1_g = dev_upload(r, T("attention.output.LayerNorm.weight", {H}), H);
-            L.ln1_b = dev_upload(r, T("attention.output.LayerNorm.bias", {H}), H);
-            f1W = T("intermediate.dense.weight", {I, H});
-            f1B = T("intermediate.dense.bias", {I});
-            f2W = T("output.dense.weight", {H, I});
-            f2B = T("output.dense.bias", {H});
-            L.ln2_g = dev_upload(r, T("output.LayerNorm.weight", {H}), H);
-            L.ln2_b = dev_upload(r, T("output.LayerNorm.bias", {H}), H);
+            w.qW = T("attention.self.query.weight", {H, H});
+            w.qB = T("attention.self.query.bias", {H});
+            w.kW = T("attention.self.key.weight", {H, H});
+            w.kB = T("attention.self.key.bias", {H});
+            w.vW = T("attention.self.value.weight", {H, H});
+            w.vB = T("attention.self.value.bias", {H});
+            w.oW = T("attention.output.dense.weight", {H, H});
+            w.oB = T("attention.output.dense.bias", {H});
+            w.g1 = T("attention.output.LayerNorm.weight", {H});
+            w.b1 = T("attention.output.LayerNorm.bias", {H});
+            w.f1W = T("intermediate.dense.weight", {I, H});
+            w.f1B = T("intermediate.dense.bias", {I});
+            w.f2W = T("output.dense.weight", {H, I});
+            w.f2B = T("output.dense.bias", {H});
+            w.g2 = T("output.LayerNorm.weight", {H});
+            w.b2 = T("output.LayerNorm.bias", {H});
         }
+    }
+    // LayerNorm folding (16-bit modes; every folded weight in range)
+    r.fold = (c->mode == RG_MODE_BF16 || c->mode == RG_MODE_F16) && H % 32 == 0;
+    for (int li = 0; li < d.num_hidden_layers && r.fold; ++li) {
+        const HostLayer& w = hl[li];
+        r.fold = fold_ok(c->mode, w.f1W, w.g1, I, H);
+        if (li > 0)
+            for (const float* W : {w.qW, w.kW, w.vW}) r.fold = r.fold && fold_ok(c->mode, W, hl[li - 1].g2, H, H);
+    }
+    for (int li = 0; li < d.num_hidden_layers; ++li) {
+        const HostLayer& w = hl[li];
+        DevLayer& L = r.layers[li];
+        L.ln1_g = dev_upload(r, w.g1, H);
+        L.ln1_b = dev_upload(r, w.b1, H);
+        L.ln2_g = dev_upload(r, w.g2, H);
+        L.ln2_b = dev_upload(r, w.b2, H);
         // Q||K||V fused as [3H x H] rows (bert.go:479-485).
         std::vector<float> qkvW(static_cast<size_t>(3) * H * H), qkvB(3 * H);
-        memcpy(qkvW.data(), qW, sizeof(float) * H * H);
-        memcpy(qkvW.data() + (size_t)H * H, kW, sizeof(float) * H * H);
-        memcpy(qkvW.data() + (size_t)2 * H * H, vW, sizeof(float) * H * H);
-        memcpy(qkvB.data(), qB, sizeof(float) * H);
-        memcpy(qkvB.data() + H, kB, sizeof(float) * H);
-        memcpy(qkvB.data() + 2 * H, vB, sizeof(float) * H);
-        L.qkv = make_dense(r, c->mode, qkvW.data(), qkvB.data(), 3 * H, H);
-        L.o = make_dense(r, c->mode, oW, oB, H, H);
-        L.ffn1 = make_dense(r, c->mode, f1W, f1B, I, H);
-        L.ffn2 = make_dense(r, c->mode, f2W, f2B, H, I);
+        memcpy(qkvW.data(), w.qW, sizeof(float) * H * H);
+        memcpy(qkvW.data() + (size_t)H * H, w.kW, sizeof(float) * H * H);
+        memcpy(qkvW.data() + (size_t)2 * H * H, w.vW, sizeof(float) * H * H);
+        memcpy(qkvB.data(), w.qB, sizeof(float) * H);
+        memcpy(qkvB.data() + H, w.kB, sizeof(float) * H);
+        memcpy(qkvB.data() + 2 * H, w.vB, sizeof(float) * H);
+        // layer 0's QKV reads the embedding LayerNorm's output as is
+        L.qkv = r.fold && li > 0
+                    ? make_dense_folded(r, c->mode, qkvW.data(), qkvB.data(), 3 * H, H, hl[li - 1].g2, hl[li - 1].b2)
+                    : make_dense(r, c->mode, qkvW.data(), qkvB.data(), 3 * H, H);
+        L.o = make_dense(r, c->mode, w.oW, w.oB, H, H);
+        L.ffn1 = r.fold ? make_dense_folded(r, c->mode, w.f1W, w.f1B, I, H, w.g1, w.b1)
+                        : make_dense(r, c->mode, w.f1W, w.f1B, I, H);
+        L.ffn2 = make_dense(r, c->mode, w.f2W, w.f2B, H, I);
     }
 }
 
@@ -737,6 +821,7 @@ void ensure_workspace(rg_ctx* c, Replica& r, int T, int nseq, size_t nout) {
         r.x32 = ws_alloc<float>(r, t * H);
         r.y32 = ws_alloc<float>(r, t * H);
         r.lnst = ws_alloc<float2>(r, t);
+        if (r.fold) r.parts = ws_alloc<float2>(r, t * (H / 32));
         if (c->mode == RG_MODE_FP32) {
             r.xh = ws_alloc<float>(r, t * H);
             r.xl = ws_alloc<float>(r, t * H);
@@ -877,13 +962,37 @@ void prof_collect(Replica& r) {
     r.ev_used = 0;
 }
 
+// Folded-LayerNorm plumbing of one GEMM (post-norm stacks, 16-bit modes):
+// fold_stats = the (mean, rstd) of the A rows whose LayerNorm is folded into
+// the weight; out16 / parts_out = a residual output's 16-bit copy and chunk
+// statistics.
+struct LnFold {
+    const float2* fold_stats = nullptr;
+    act16* out16 = nullptr;
+    float2* parts_out = nullptr;
+};
+
 void gemm(Replica& r, int mode, const OpMaps& tmA, const DevDense& w, int M, int epi, const float* row_scale,
           const float* residual, void* out, cudaStream_t st, int& launches, const float2* ln_stats = nullptr,
-          const float* ln_g = nullptr, const float* ln_b = nullptr) {
+          const float* ln_g = nullptr, const float* ln_b = nullptr, const LnFold* lf = nullptr) {
     rg::GemmArgs a{};
     a.ln_stats = ln_stats;
     a.ln_g = ln_g;
     a.ln_b = ln_b;
+    double fold_bytes = 0.0;
+    if (lf) {
+        if (lf->fold_stats) {
+            if (!w.fold_c1) fail("folded GEMM without folded weights");
+            a.fold_stats = lf->fold_stats;
+            a.fold_c1 = w.fold_c1;
+            fold_bytes += 8.0 * M;
+        }
+        a.out16 = reinterpret_cast<uint16_t*>(lf->out16);
+        a.ld16 = w.N;
+        a.parts_out = lf->parts_out;
+        if (lf->out16) fold_bytes += 2.0 * M * w.N;
+        if (lf->parts_out) fold_bytes += 8.0 * M * (w.N / 32);
+    }
     a.M = M;
     a.N = w.N;
     a.K = w.K;
@@ -905,7 +1014,7 @@ void gemm(Replica& r, int mode, const OpMaps& tmA, const DevDense& w, int M, int
     const double ob = (rg::epi_has_residual(epi) || epi == rg::kEpiBiasF32 || x3) ? 4.0
                       : (rg::epi_is_glu(epi) ? 1.0 : 2.0);
     const double bytes = eb * (double(M) * w.K + double(w.N) * w.K) + ob * double(M) * w.N +
-                         (rg::epi_has_residual(epi) ? 4.0 * double(M) * w.N : 0.0);
+                         (rg::epi_has_residual(epi) ? 4.0 * double(M) * w.N : 0.0) + fold_bytes;
     const int bn = rg::gemm_block_n(M, w.N, r.num_sms, rg::epi_is_glu(epi));
     if (bn == 0) fail("no GEMM tile width divides N=%d", w.N);
     if (kind == rg::GemmKind::kW8 && M >= kW8WidenRows) {
@@ -1037,12 +1146,47 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
     // gain and bias of that pending LayerNorm (nullptr: x32 is the residual
     // as is, i.e. the embedding output).  The stack's last LayerNorm writes
     // x32 for pooling.
+    //
+    // With r.fold the inner LayerNorms run no normalisation kernel: the
+    // residual GEMM also writes its output's 16-bit copy (xb) and 32-column
+    // chunk statistics (r.parts), merge_row_stats turns those into lnst, the
+    // consumer GEMM (QKV, FFN1) folds the norm into its weight and epilogue,
+    // and the next residual GEMM rebuilds LN(x32) from lnst as before.
     const float *res_g = nullptr, *res_b = nullptr;
-    auto residual_gemm = [&](const OpMaps& tmA, const DevDense& w, const float* row_scale) {
+    bool folded = false;  // xb holds the unnormalised rows of the pending LayerNorm
+    auto residual_gemm = [&](const OpMaps& tmA, const DevDense& w, const float* row_scale, bool fold_out) {
+        LnFold lf;
+        lf.out16 = fold_out ? r.xb : nullptr;
+        lf.parts_out = fold_out ? r.parts : nullptr;
+        const LnFold* lfp = fold_out ? &lf : nullptr;
         if (res_g)
-            gemm(r, mode, tmA, w, T, rg::kEpiBiasResLN, row_scale, r.x32, r.x32, st, launches, r.lnst, res_g, res_b);
+            gemm(r, mode, tmA, w, T, rg::kEpiBiasResLN, row_scale, r.x32, r.x32, st, launches, r.lnst, res_g, res_b,
+                 lfp);
         else
-            gemm(r, mode, tmA, w, T, rg::kEpiBiasRes, row_scale, r.x32, r.x32, st, launches);
+            gemm(r, mode, tmA, w, T, rg::kEpiBiasRes, row_scale, r.x32, r.x32, st, launches, nullptr, nullptr,
+                 nullptr, lfp);
+    };
+    // The folded form of post_norm (not the stack's last): the chunk
+    // statistics merged into lnst; the norm (g, b) becomes the pending one.
+    auto fold_norm = [&](const float* g, const float* b) {
+        {
+            ProfScope ps(r, st, RG_KC_NORM, 4.0 * Td * (H / 32), Td * (8.0 * (H / 32) + 8.0));
+            check(rg::launch_merge_row_stats(r.parts, H / 32, T, eps, r.lnst, st), "merge_row_stats launch");
+            ++launches;
+        }
+        res_g = g;
+        res_b = b;
+        folded = true;
+    };
+    // A GEMM reading xb: LN(y) folded into it when the last norm was folded.
+    auto input_gemm = [&](const DevDense& w, const OpMaps& tmA, int epi, void* out) {
+        if (folded) {
+            LnFold lf;
+            lf.fold_stats = r.lnst;
+            gemm(r, mode, tmA, w, T, epi, nullptr, nullptr, out, st, launches, nullptr, nullptr, nullptr, &lf);
+        } else {
+            gemm(r, mode, tmA, w, T, epi, s8 ? r.xs : nullptr, nullptr, out, st, launches);
+        }
     };
     auto post_norm = [&](const float* g, const float* b, bool last) {
         ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * Hd * (4.0 + 2.0 + (s8 ? 1.0 : 0.0) + (last ? 4.0 : 0.0)));
@@ -1066,6 +1210,7 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         ++launches;
         res_g = last ? nullptr : g;
         res_b = last ? nullptr : b;
+        folded = false;
     };
     auto quantize = [&](const act16* x, int K, int8_t* q, float* sc) {  // bf16 rows (full-int8 mode)
         ProfScope ps(r, st, RG_KC_QUANT, 0.0, Td * K * 3.0);
@@ -1083,8 +1228,7 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         const DevLayer& L = r.layers[li];
         // ---- attention sublayer
         if (pre) norm_into_a(L.attn_norm, arch == RG_ARCH_MODERNBERT ? r.zero_beta : nullptr, arch != RG_ARCH_MODERNBERT);
-        gemm(r, mode, r.tm_x, L.qkv, T, rg::kEpiBias, s8 ? r.xs : nullptr, nullptr,
-             f32 ? static_cast<void*>(r.qkv32) : r.qkv, st, launches);
+        input_gemm(L.qkv, r.tm_x, rg::kEpiBias, f32 ? static_cast<void*>(r.qkv32) : r.qkv);
         if (has_rope(arch)) {
             ProfScope ps(r, st, RG_KC_NORM, 0.0, Td * (m.qd + m.kvd) * 4.0);
             rg::QkRopeParams q{};
@@ -1154,8 +1298,11 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
             ++launches;
         }
         if (s8) quantize(r.ctx, m.qd, r.ctxq, r.ctxs);
-        if (!pre) {
-            residual_gemm(r.tm_ctx, L.o, s8 ? r.ctxs : nullptr);
+        if (!pre && r.fold) {
+            residual_gemm(r.tm_ctx, L.o, nullptr, true);
+            fold_norm(L.ln1_g, L.ln1_b);
+        } else if (!pre) {
+            residual_gemm(r.tm_ctx, L.o, s8 ? r.ctxs : nullptr, false);
             post_norm(L.ln1_g, L.ln1_b, false);
         } else if (arch == RG_ARCH_GEMMA3) {
             gemm(r, mode, r.tm_ctx, L.o, T, rg::kEpiBiasF32, s8 ? r.ctxs : nullptr, nullptr, r.y32, st, launches);
@@ -1167,17 +1314,21 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         }
         // ---- FFN sublayer
         if (pre) norm_into_a(L.ffn_norm, arch == RG_ARCH_MODERNBERT ? r.zero_beta : nullptr, arch != RG_ARCH_MODERNBERT);
-        gemm(r, mode, r.tm_x, L.ffn1, T, is_glu(arch) ? glu_epi : rg::kEpiBiasGelu, s8 ? r.xs : nullptr, nullptr,
-             f32 ? static_cast<void*>(r.ffhh) : r.ffh, st, launches);
+        input_gemm(L.ffn1, r.tm_x, is_glu(arch) ? glu_epi : rg::kEpiBiasGelu,
+                   f32 ? static_cast<void*>(r.ffhh) : r.ffh);
         if (f32) {  // the fp32 FFN hidden state -> tf32 hi (in place) + remainder
             ProfScope ps(r, st, RG_KC_QUANT, 0.0, Td * I * 12.0);
             check(rg::launch_split_tf32(r.ffhh, static_cast<size_t>(T) * I, r.ffhh, r.ffhl, st), "split launch");
             ++launches;
         }
         if (s8) quantize(r.ffh, I, r.ffhq, r.ffhs);
-        if (!pre) {
-            residual_gemm(r.tm_ffh, L.ffn2, s8 ? r.ffhs : nullptr);
-            post_norm(L.ln2_g, L.ln2_b, li == d.num_hidden_layers - 1);
+        const bool last = li == d.num_hidden_layers - 1;
+        if (!pre && r.fold && !last) {
+            residual_gemm(r.tm_ffh, L.ffn2, nullptr, true);
+            fold_norm(L.ln2_g, L.ln2_b);
+        } else if (!pre) {
+            residual_gemm(r.tm_ffh, L.ffn2, s8 ? r.ffhs : nullptr, false);
+            post_norm(L.ln2_g, L.ln2_b, last);
         } else if (arch == RG_ARCH_GEMMA3) {
             gemm(r, mode, r.tm_ffh, L.ffn2, T, rg::kEpiBiasF32, s8 ? r.ffhs : nullptr, nullptr, r.y32, st, launches);
             ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * Hd * 12.0);
