@@ -28,6 +28,7 @@
 
 #include "act16.cuh"
 #include "kernels.cuh"
+#include "pdl.cuh"
 #include "sm100.cuh"
 
 namespace rg {
@@ -66,6 +67,8 @@ __global__ void __launch_bounds__(192, AttnTc<D>::MIN_BLOCKS)
                         const __grid_constant__ CUtensorMap tmV, AttnParams p, int* status) {
     using S = AttnTc<D>;
     constexpr int BKV = S::BKV, QB = S::QB;
+    pdl_trigger();
+    pdl_wait();  // the previous kernel's outputs are complete from here on
     const int s = blockIdx.z, h = blockIdx.y;
     const int s0 = __ldg(p.cu + s), L = __ldg(p.cu + s + 1) - s0;
     const int q0 = blockIdx.x * 128;
@@ -426,7 +429,7 @@ static cudaError_t launch_tc(const CUtensorMap& tq, const CUtensorMap& tk, const
         if (dev < 32) __atomic_fetch_or(&configured, 1u << dev, __ATOMIC_RELEASE);
     }
     const dim3 grid((max_len + 127) / 128, heads, nseq);
-    kern<<<grid, AttnTc<D>::THREADS, smem, st>>>(tq, tk, tv, p, status);
+    launch_pdl(kern, grid, dim3(AttnTc<D>::THREADS), smem, st, tq, tk, tv, p, status);
     return cudaGetLastError();
 }
 

@@ -31,6 +31,7 @@
 
 #include "act16.cuh"
 #include "gemm.cuh"
+#include "pdl.cuh"
 #include "sm100.cuh"
 
 namespace rg {
@@ -254,6 +255,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_fence_before();
     cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
     tc_fence_after();
+    pdl_trigger();
+    pdl_wait();  // the previous kernel's outputs (A, residual, statistics) are complete from here on
     const uint32_t tmem_base = *tmem_slot;
     // shared::cluster addresses of the even CTA's full / tempty barriers.
     const uint32_t full_lead = mapa_shared(smem_u32(full), 0);
@@ -732,7 +735,7 @@ static cudaError_t launch_one(const GemmMaps& m, const GemmArgs& args, int num_s
     }
     const int tiles = ((args.M + 255) / 256) * (args.N / BN);
     const int grid = 2 * (tiles < pairs ? tiles : pairs);
-    kern<<<grid, kThreads, smem, stream>>>(m.a, m.b, m.out, m.res, m.a2, m.b2, m.out16, args);
+    launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, m.a, m.b, m.out, m.res, m.a2, m.b2, m.out16, args);
     return cudaGetLastError();
 }
 

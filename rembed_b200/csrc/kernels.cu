@@ -11,6 +11,7 @@
 #include <algorithm>
 
 #include "kernels.cuh"
+#include "pdl.cuh"
 #include "act16.cuh"
 #include "sm100.cuh"
 
@@ -150,6 +151,8 @@ __device__ __forceinline__ int seq_of_token(const int32_t* __restrict__ cu, int 
 
 template <int NV, bool F16>
 __global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= p.T) return;
@@ -213,6 +216,8 @@ __global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
 
 template <int NV, bool RMS, bool F16>
 __global__ void __launch_bounds__(256) norm_kernel(NormParams p) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= p.T) return;
@@ -238,6 +243,8 @@ __global__ void __launch_bounds__(256) norm_kernel(NormParams p) {
 template <int NV>
 __global__ void __launch_bounds__(256) add_rmsnorm_kernel(float* __restrict__ x32, const float* __restrict__ o32,
                                                          const float* __restrict__ g, float eps, int T, int H) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= T) return;
@@ -286,9 +293,9 @@ cudaError_t launch_embed(const EmbedParams& p, cudaStream_t st) {
     if (p.H % 128 != 0) return cudaErrorInvalidValue;
     const int grid = (p.T + 7) / 8;
     if (p.f16) {
-        RG_NV_DISPATCH(p.H, (embed_kernel<NV, true><<<grid, 256, 0, st>>>(p)));
+        RG_NV_DISPATCH(p.H, (launch_pdl(embed_kernel<NV, true>, dim3(grid), dim3(256), 0, st, p)));
     } else {
-        RG_NV_DISPATCH(p.H, (embed_kernel<NV, false><<<grid, 256, 0, st>>>(p)));
+        RG_NV_DISPATCH(p.H, (launch_pdl(embed_kernel<NV, false>, dim3(grid), dim3(256), 0, st, p)));
     }
     return cudaGetLastError();
 }
@@ -298,13 +305,13 @@ cudaError_t launch_norm(const NormParams& p, bool rms, cudaStream_t st) {
     if (p.H % 128 != 0) return cudaErrorInvalidValue;
     const int grid = (p.T + 7) / 8;
     if (rms && p.f16) {
-        RG_NV_DISPATCH(p.H, (norm_kernel<NV, true, true><<<grid, 256, 0, st>>>(p)));
+        RG_NV_DISPATCH(p.H, (launch_pdl(norm_kernel<NV, true, true>, dim3(grid), dim3(256), 0, st, p)));
     } else if (rms) {
-        RG_NV_DISPATCH(p.H, (norm_kernel<NV, true, false><<<grid, 256, 0, st>>>(p)));
+        RG_NV_DISPATCH(p.H, (launch_pdl(norm_kernel<NV, true, false>, dim3(grid), dim3(256), 0, st, p)));
     } else if (p.f16) {
-        RG_NV_DISPATCH(p.H, (norm_kernel<NV, false, true><<<grid, 256, 0, st>>>(p)));
+        RG_NV_DISPATCH(p.H, (launch_pdl(norm_kernel<NV, false, true>, dim3(grid), dim3(256), 0, st, p)));
     } else {
-        RG_NV_DISPATCH(p.H, (norm_kernel<NV, false, false><<<grid, 256, 0, st>>>(p)));
+        RG_NV_DISPATCH(p.H, (launch_pdl(norm_kernel<NV, false, false>, dim3(grid), dim3(256), 0, st, p)));
     }
     return cudaGetLastError();
 }
@@ -331,7 +338,7 @@ cudaError_t launch_add_rmsnorm(float* x32, const float* o32, const float* g, flo
     if (T <= 0) return cudaSuccess;
     if (H % 128 != 0) return cudaErrorInvalidValue;
     const int grid = (T + 7) / 8;
-    RG_NV_DISPATCH(H, (add_rmsnorm_kernel<NV><<<grid, 256, 0, st>>>(x32, o32, g, eps, T, H)));
+    RG_NV_DISPATCH(H, (launch_pdl(add_rmsnorm_kernel<NV>, dim3(grid), dim3(256), 0, st, x32, o32, g, eps, T, H)));
     return cudaGetLastError();
 }
 
@@ -380,6 +387,8 @@ __device__ __forceinline__ float store8(void* base, int64_t off, const float (&v
 
 template <int DH, bool F16, bool F32>
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkRopeParams p) {
+    pdl_trigger();
+    pdl_wait();
     constexpr int HALF = DH / 2, U = DH / 16;
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -457,10 +466,10 @@ cudaError_t launch_qk_norm_rope(const QkRopeParams& p, int head_dim, cudaStream_
     if (p.T <= 0) return cudaSuccess;
     const int grid = (p.T + 7) / 8;
     switch (head_dim) {
-#define RG_QKR(DH)                                                                   \
-    if (p.qkv32) qk_norm_rope_kernel<DH, false, true><<<grid, 256, 0, st>>>(p);    \
-    else if (p.f16) qk_norm_rope_kernel<DH, true, false><<<grid, 256, 0, st>>>(p); \
-    else qk_norm_rope_kernel<DH, false, false><<<grid, 256, 0, st>>>(p);
+#define RG_QKR(DH)                                                                                  \
+    if (p.qkv32) launch_pdl(qk_norm_rope_kernel<DH, false, true>, dim3(grid), dim3(256), 0, st, p);    \
+    else if (p.f16) launch_pdl(qk_norm_rope_kernel<DH, true, false>, dim3(grid), dim3(256), 0, st, p); \
+    else launch_pdl(qk_norm_rope_kernel<DH, false, false>, dim3(grid), dim3(256), 0, st, p);
     case 32: RG_QKR(32) break;
     case 64: RG_QKR(64) break;
     case 128: RG_QKR(128) break;
@@ -476,6 +485,8 @@ cudaError_t launch_qk_norm_rope(const QkRopeParams& p, int head_dim, cudaStream_
 // out[M x N] = x[M x K] . W[N x K]^T, 32 x 32 output tiles, K in steps of 32.
 __global__ void __launch_bounds__(256) dense_f32_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                        float* __restrict__ out, int M, int N, int K) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float xs[32][33];
     __shared__ float ws[32][33];
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
@@ -505,7 +516,7 @@ __global__ void __launch_bounds__(256) dense_f32_kernel(const float* __restrict_
 cudaError_t launch_dense_f32(const float* x, const float* w, float* out, int M, int N, int K, cudaStream_t st) {
     if (M <= 0) return cudaSuccess;
     const dim3 grid((N + 31) / 32, (M + 31) / 32);
-    dense_f32_kernel<<<grid, 256, 0, st>>>(x, w, out, M, N, K);
+    launch_pdl(dense_f32_kernel, dim3(grid), dim3(256), 0, st, x, w, out, M, N, K);
     return cudaGetLastError();
 }
 
@@ -514,6 +525,8 @@ cudaError_t launch_dense_f32(const float* x, const float* w, float* out, int M, 
 // mantissa byte of 1024.0 is exactly 1024 + q + 128; subtracting 1152 leaves q.
 __global__ void __launch_bounds__(256) widen_s8_f16_kernel(const uint4* __restrict__ w, size_t n16,
                                                           uint4* __restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n16;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
         const uint4 u = __ldg(w + i);
@@ -539,7 +552,8 @@ cudaError_t launch_widen_s8_f16(const int8_t* w, size_t n, uint16_t* out, cudaSt
         return cudaErrorInvalidValue;
     const size_t n16 = n / 16;
     const int grid = static_cast<int>(std::min<size_t>((n16 + 255) / 256, 148 * 8));
-    widen_s8_f16_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const uint4*>(w), n16, reinterpret_cast<uint4*>(out));
+    launch_pdl(widen_s8_f16_kernel, dim3(grid), dim3(256), 0, st, reinterpret_cast<const uint4*>(w), n16,
+               reinterpret_cast<uint4*>(out));
     return cudaGetLastError();
 }
 
@@ -551,6 +565,8 @@ cudaError_t launch_widen_s8_f16(const int8_t* w, size_t n, uint16_t* out, cudaSt
 template <int NV>
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const __nv_bfloat16* __restrict__ x, int T, int K,
                                                            int8_t* q, float* scale) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= T) return;
@@ -594,7 +610,7 @@ cudaError_t launch_quantize_rows(const __nv_bfloat16* x, int T, int K, int8_t* q
     const int grid = (T + 7) / 8;
     switch ((K + 255) / 256) {
 #define RG_QR(NV) \
-    case NV: quantize_rows_kernel<NV><<<grid, 256, 0, st>>>(x, T, K, q, scale); break;
+    case NV: launch_pdl(quantize_rows_kernel<NV>, dim3(grid), dim3(256), 0, st, x, T, K, q, scale); break;
         RG_QR(1) RG_QR(2) RG_QR(3) RG_QR(4) RG_QR(5) RG_QR(6) RG_QR(7) RG_QR(8)
         RG_QR(9) RG_QR(10) RG_QR(11) RG_QR(12) RG_QR(13) RG_QR(14) RG_QR(15) RG_QR(16)
 #undef RG_QR
@@ -615,31 +631,40 @@ cudaError_t launch_attention(const AttnParams& p, int nseq, int max_len, int hea
 // Row statistics of a folded LayerNorm: the chunks merged in a fixed order
 // (Chan et al.'s update for equal-size parts): mean = sum of the chunk means
 // / n, M2 = sum of (M2_i + 32 (mean_i - mean)^2), var = M2 / (32 n).  One
-// thread per row; for each chunk the warp's 32 rows are 256 contiguous bytes.
-__global__ void __launch_bounds__(256) merge_row_stats_kernel(const float2* __restrict__ parts, int nparts, int T,
-                                                              float eps, float2* __restrict__ stats) {
+// thread per row; for each chunk a warp's 32 rows are 256 contiguous bytes.
+// Rows of up to kMergeRegs chunks are loaded once into registers (every
+// load in flight together); longer rows are read twice.
+constexpr int kMergeRegs = 32;
+
+__global__ void __launch_bounds__(64) merge_row_stats_kernel(const float2* __restrict__ parts, int nparts, int T,
+                                                             float eps, float2* __restrict__ stats) {
+    pdl_trigger();
+    pdl_wait();
     const int row = blockIdx.x * blockDim.x + threadIdx.x;
     if (row >= T) return;
-    constexpr int kMax = 32;  // chunks held in registers at once
-    float2 q[kMax];
-    float s = 0.f;
-    for (int c0 = 0; c0 < nparts; c0 += kMax) {
+    const float2* p = parts + row;
+    float mean, m2 = 0.f;
+    if (nparts <= kMergeRegs) {
+        float2 q[kMergeRegs];
 #pragma unroll
-        for (int i = 0; i < kMax; ++i)
-            if (c0 + i < nparts) s += parts[static_cast<size_t>(c0 + i) * T + row].x;
-    }
-    const float mean = s / static_cast<float>(nparts);
-    float m2 = 0.f;
-    for (int c0 = 0; c0 < nparts; c0 += kMax) {
+        for (int i = 0; i < kMergeRegs; ++i) q[i] = i < nparts ? p[static_cast<size_t>(i) * T] : make_float2(0.f, 0.f);
+        float s = 0.f;
 #pragma unroll
-        for (int i = 0; i < kMax; ++i)
-            if (c0 + i < nparts) q[i] = parts[static_cast<size_t>(c0 + i) * T + row];
+        for (int i = 0; i < kMergeRegs; ++i) s += q[i].x;
+        mean = s / static_cast<float>(nparts);
 #pragma unroll
-        for (int i = 0; i < kMax; ++i) {
-            if (c0 + i < nparts) {
-                const float d = q[i].x - mean;
-                m2 += fmaf(32.0f * d, d, q[i].y);
-            }
+        for (int i = 0; i < kMergeRegs; ++i) {
+            const float d = q[i].x - mean;
+            if (i < nparts) m2 += fmaf(32.0f * d, d, q[i].y);
+        }
+    } else {
+        float s = 0.f;
+        for (int i = 0; i < nparts; ++i) s += p[static_cast<size_t>(i) * T].x;
+        mean = s / static_cast<float>(nparts);
+        for (int i = 0; i < nparts; ++i) {
+            const float2 q = p[static_cast<size_t>(i) * T];
+            const float d = q.x - mean;
+            m2 += fmaf(32.0f * d, d, q.y);
         }
     }
     stats[row] = make_float2(mean, 1.0f / sqrtf(m2 / static_cast<float>(32 * nparts) + eps));
@@ -648,7 +673,7 @@ __global__ void __launch_bounds__(256) merge_row_stats_kernel(const float2* __re
 cudaError_t launch_merge_row_stats(const float2* parts, int nparts, int T, float eps, float2* stats, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if (nparts <= 0 || !parts || !stats) return cudaErrorInvalidValue;
-    merge_row_stats_kernel<<<(T + 255) / 256, 256, 0, st>>>(parts, nparts, T, eps, stats);
+    launch_pdl(merge_row_stats_kernel, dim3((T + 63) / 64), dim3(64), 0, st, parts, nparts, T, eps, stats);
     return cudaGetLastError();
 }
 
@@ -656,6 +681,8 @@ cudaError_t launch_merge_row_stats(const float2* parts, int nparts, int T, float
 // 3xTF32 operand split: hi = tf32(x) (nearest, ties to even), lo = x - hi.
 __global__ void __launch_bounds__(256) split_tf32_kernel(const float4* __restrict__ x, size_t n4, float4* hi,
                                                         float4* lo) {
+    pdl_trigger();
+    pdl_wait();
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
         const float4 v = x[i];
@@ -674,8 +701,8 @@ cudaError_t launch_split_tf32(const float* x, size_t n, float* hi, float* lo, cu
     if (n % 4 != 0) return cudaErrorInvalidValue;
     const size_t n4 = n / 4;
     const int grid = static_cast<int>(std::min<size_t>((n4 + 255) / 256, 148 * 16));
-    split_tf32_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const float4*>(x), n4, reinterpret_cast<float4*>(hi),
-                                            reinterpret_cast<float4*>(lo));
+    launch_pdl(split_tf32_kernel, dim3(grid), dim3(256), 0, st, reinterpret_cast<const float4*>(x), n4,
+               reinterpret_cast<float4*>(hi), reinterpret_cast<float4*>(lo));
     return cudaGetLastError();
 }
 
@@ -688,6 +715,8 @@ cudaError_t launch_split_tf32(const float* x, size_t n, float* hi, float* lo, cu
 // d, d + 32, ... over the block's probabilities (broadcast by shuffle).
 template <int D>
 __global__ void __launch_bounds__(256) attention_f32_kernel(AttnF32Params p) {
+    pdl_trigger();
+    pdl_wait();
     constexpr int E = D / 32, KP = D + 1;
     extern __shared__ float fsm[];
     float* qs = fsm;              // [8][D]
@@ -786,7 +815,7 @@ static cudaError_t launch_attention_f32_d(const AttnF32Params& p, int nseq, int 
         if (dev < 32) __atomic_fetch_or(&configured, 1u << dev, __ATOMIC_RELEASE);
     }
     const dim3 grid((max_len + 7) / 8, heads, nseq);
-    attention_f32_kernel<D><<<grid, 256, smem, st>>>(p);
+    launch_pdl(attention_f32_kernel<D>, dim3(grid), dim3(256), smem, st, p);
     return cudaGetLastError();
 }
 
@@ -806,6 +835,8 @@ cudaError_t launch_attention_f32(const AttnF32Params& p, int nseq, int max_len, 
 // Pooling + L2 + truncate: one CTA per sequence.
 __global__ void __launch_bounds__(256) pool_kernel(const float* __restrict__ x32, const int32_t* __restrict__ cu,
                                                   int H, int pooling, int normalize, int dim, float* __restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float pooled[];  // [H]
     __shared__ double red[8];
     const int s = blockIdx.x;
@@ -858,7 +889,7 @@ __global__ void __launch_bounds__(256) pool_kernel(const float* __restrict__ x32
 cudaError_t launch_pool(const float* x32, const int32_t* cu, int nseq, int H, int pooling, int normalize, int dim,
                         float* out, cudaStream_t st) {
     if (nseq <= 0) return cudaSuccess;
-    pool_kernel<<<nseq, 256, H * sizeof(float), st>>>(x32, cu, H, pooling, normalize, dim, out);
+    launch_pdl(pool_kernel, dim3(nseq), dim3(256), H * sizeof(float), st, x32, cu, H, pooling, normalize, dim, out);
     return cudaGetLastError();
 }
 
