@@ -89,28 +89,28 @@ __device__ __forceinline__ float rcp_approx(float x) {
     return y;
 }
 
-// The same A&S 7.1.26 GELU on a pair, with the polynomial on f32x2 and the
-// result in the cancellation-free form: with pe = p(t) exp(-a^2),
-// 0.5 x (1 + erf) = x - 0.5 x pe for x >= 0 and 0.5 x pe for x < 0.
+// The same A&S 7.1.26 GELU on a pair, in the reference's form
+// 0.5 x (1 + sign(x) (1 - t P(t) exp(-a^2))), a = |x| / sqrt(2),
+// t = 1 / (1 + 0.3275911 a): the polynomial and products on f32x2, the
+// coefficients negated so that one fma gives erf(a).
 __device__ __forceinline__ void gelu_as2(float& x0, float& x1) {
-    const uint64_t a = f2(fabsf(x0) * 0.70710678118654752f, fabsf(x1) * 0.70710678118654752f);
-    float d0, d1;
-    f2split(fma2(a, f2(0.3275911f, 0.3275911f), f2(1.0f, 1.0f)), d0, d1);
+    const float d0 = fmaf(fabsf(x0), 0.3275911f * 0.70710678118654752f, 1.0f);
+    const float d1 = fmaf(fabsf(x1), 0.3275911f * 0.70710678118654752f, 1.0f);
     const uint64_t t = f2(rcp_approx(d0), rcp_approx(d1));
-    uint64_t p = fma2(t, f2(1.061405429f, 1.061405429f), f2(-1.453152027f, -1.453152027f));
-    p = fma2(p, t, f2(1.421413741f, 1.421413741f));
-    p = fma2(p, t, f2(-0.284496736f, -0.284496736f));
-    p = fma2(p, t, f2(0.254829592f, 0.254829592f));
-    p = mul2(p, t);
-    float z0, z1;
-    f2split(mul2(mul2(a, a), f2(-1.4426950408889634f, -1.4426950408889634f)), z0, z1);
+    uint64_t p = fma2(t, f2(-1.061405429f, -1.061405429f), f2(1.453152027f, 1.453152027f));
+    p = fma2(p, t, f2(-1.421413741f, -1.421413741f));
+    p = fma2(p, t, f2(0.284496736f, 0.284496736f));
+    p = fma2(p, t, f2(-0.254829592f, -0.254829592f));
+    p = mul2(p, t);  // -t P(t)
     const uint64_t xs = f2(x0, x1);
-    const uint64_t q = mul2(mul2(xs, f2(0.5f, 0.5f)), mul2(p, f2(ex2_approx(z0), ex2_approx(z1))));
-    float q0, q1, r0, r1;
-    f2split(q, q0, q1);
-    f2split(fma2(q, f2(-1.0f, -1.0f), xs), r0, r1);
-    x0 = x0 >= 0.f ? r0 : q0;
-    x1 = x1 >= 0.f ? r1 : q1;
+    float z0, z1;  // -a^2 log2(e) = -x^2 log2(e) / 2
+    f2split(mul2(mul2(xs, xs), f2(-0.72134752044448170f, -0.72134752044448170f)), z0, z1);
+    float s0, s1;
+    f2split(fma2(p, f2(ex2_approx(z0), ex2_approx(z1)), f2(1.0f, 1.0f)), s0, s1);
+    s0 = copysignf(s0, x0);
+    s1 = copysignf(s1, x1);
+    const uint64_t h = mul2(xs, f2(0.5f, 0.5f));
+    f2split(fma2(h, f2(s0, s1), h), x0, x1);
 }
 
 // SiLU x * sigmoid(x) (tensor.go:477-481 computes it through a float64 exp).

@@ -207,12 +207,15 @@ struct rg_ctx {
     bool finalized = false;
     std::mutex mu;
     // host-batch submissions: ticket t uses staging slot t % 2 of every
-    // replica; pending[slot] is the ticket in flight there (-1: none)
+    // replica; pending[slot] is the ticket in flight there, kSlotFree, or
+    // kSlotCollecting while its results are being copied out
     std::mutex tmu;
-    std::condition_variable tcv;  // a slot was collected
+    std::condition_variable tcv;  // a slot became free
     int64_t next_ticket = 0;
     int64_t pending[2] = {-1, -1};
 };
+
+constexpr int64_t kSlotFree = -1, kSlotCollecting = -2;
 
 namespace {
 
@@ -1546,10 +1549,13 @@ std::vector<int> shard_bounds(const rg_model_desc& d, const int32_t* cu, int nse
 int64_t submit_batch(rg_ctx* c, const int64_t* ids, const int32_t* cu, int nseq, int out_kind, int out_dim,
                      float* host_out, bool wait_for_slot) {
     std::unique_lock<std::mutex> tl(c->tmu);
-    while (c->pending[c->next_ticket & 1] >= 0) {
-        if (!wait_for_slot)
-            fail("rembed: two submissions are outstanding; collect ticket %lld first",
-                 static_cast<long long>(c->pending[c->next_ticket & 1]));
+    while (c->pending[c->next_ticket & 1] != kSlotFree) {
+        if (!wait_for_slot) {
+            const int64_t p = c->pending[c->next_ticket & 1];
+            if (p >= 0)
+                fail("rembed: two submissions are outstanding; collect ticket %lld first", static_cast<long long>(p));
+            fail("rembed: staging slot %d is still being collected", static_cast<int>(c->next_ticket & 1));
+        }
         c->tcv.wait(tl);
     }
     const int64_t t = c->next_ticket;
@@ -1579,9 +1585,8 @@ void collect_batch(rg_ctx* c, int64_t t) {
     {
         std::lock_guard<std::mutex> tl(c->tmu);
         if (t < 0 || c->pending[slot] != t) fail("rembed: ticket %lld is not outstanding", static_cast<long long>(t));
-        c->pending[slot] = -1;
+        c->pending[slot] = kSlotCollecting;  // no second collect; no submission into the slot yet
     }
-    c->tcv.notify_all();
     std::string first;
     for (Replica* r : c->reps) {
         try {
@@ -1590,6 +1595,11 @@ void collect_batch(rg_ctx* c, int64_t t) {
             if (first.empty()) first = e.msg;
         }
     }
+    {
+        std::lock_guard<std::mutex> tl(c->tmu);
+        c->pending[slot] = kSlotFree;  // the slot's staging buffers are idle again
+    }
+    c->tcv.notify_all();
     if (!first.empty()) fail("%s", first.c_str());
 }
 
