@@ -30,6 +30,7 @@ import math
 import os
 import subprocess
 import sys
+import threading
 import time
 from pathlib import Path
 
@@ -172,6 +173,78 @@ def reference_arm(args, rank, world):
 
 
 # ---------------------------------------------------------------------------
+class NvmlClockSampler:
+    """SM clock, power and clock-event reasons read through NVML every 10 ms
+    by a background thread while the timed region runs (reads only)."""
+
+    def __init__(self, uuid: str | None):
+        import pynvml  # nvidia_ml_py
+        self.nv = pynvml
+        pynvml.nvmlInit()
+        if uuid:
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        else:
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(0)
+        self.rows = []
+        self.stop = threading.Event()
+
+    def _run(self):
+        nv, h = self.nv, self.h
+        while not self.stop.is_set():
+            try:
+                self.rows.append({"sm": float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                  "power": nv.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                                  "reasons": int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))})
+            except nv.NVMLError:
+                pass
+            self.stop.wait(0.01)
+
+    def __enter__(self):
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self.stop.set()
+        self.thread.join(timeout=5)
+
+    def summary(self):
+        nv = self.nv
+        try:
+            mx = float(nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM))
+        except nv.NVMLError:
+            mx = None
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": ["no samples"]}
+        bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+        # the other event reasons, reported apart (a clock lock shows as
+        # user_defined_clocks or applications_clocks_setting)
+        other = {"gpu_idle": nv.nvmlClocksEventReasonGpuIdle,
+                 "applications_clocks_setting": nv.nvmlClocksEventReasonApplicationsClocksSetting,
+                 "sync_boost": nv.nvmlClocksEventReasonSyncBoost,
+                 "hw_power_brake_slowdown": nv.nvmlClocksEventReasonHwPowerBrakeSlowdown,
+                 "display_clock_setting": nv.nvmlClocksEventReasonDisplayClockSetting,
+                 "user_defined_clocks": getattr(nv, "nvmlClocksEventReasonUserDefinedClocks", 0)}
+        reasons = sorted({k for r in self.rows for k, b in bits.items() if r["reasons"] & b})
+        others = sorted({k for r in self.rows for k, b in other.items() if b and r["reasons"] & b})
+        sm = [r["sm"] for r in self.rows]
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": reasons, "other_reasons": others,
+                "sm_mhz_range": [min(sm), max(sm)], "samples": len(self.rows),
+                "source": "NVML every 10 ms during the timed region",
+                "power_w_max": round(max(r["power"] for r in self.rows), 1)}
+
+
+def clock_sampler(uuid: str | None):
+    """NVML sampler, or nvidia-smi when NVML cannot be loaded."""
+    try:
+        return NvmlClockSampler(uuid)
+    except Exception:  # no pynvml / no NVML library: fall back to nvidia-smi
+        return ClockSampler(uuid)
+
+
 class ClockSampler:
     """nvidia-smi clock/throttle samples every 200 ms during the timed region."""
 
@@ -300,7 +373,7 @@ def ours(args, rank, world, local_rank):
         uuid = None
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
-    with ClockSampler(uuid) as clk:
+    with clock_sampler(uuid) as clk:
         e0.record(stream)
         for _ in range(args.steps):
             step()

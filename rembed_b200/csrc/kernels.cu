@@ -222,10 +222,16 @@ __global__ void __launch_bounds__(256) norm_kernel(NormParams p) {
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= p.T) return;
     const int64_t off = static_cast<int64_t>(t) * p.H;
+    int64_t ioff = off;
+    if (p.row_pick) {
+        int row = p.row_pick == 1 ? __ldg(p.row_cu + t) : __ldg(p.row_cu + t + 1) - 1;
+        row = min(max(row, 0), p.in_rows - 1);
+        ioff = static_cast<int64_t>(row) * p.H;
+    }
     float v[NV][4];
 #pragma unroll
     for (int c = 0; c < NV; ++c) {
-        const float4 a = __ldg(reinterpret_cast<const float4*>(p.in + off + (lane + 32 * c) * 4));
+        const float4 a = __ldg(reinterpret_cast<const float4*>(p.in + ioff + (lane + 32 * c) * 4));
         v[c][0] = a.x;
         v[c][1] = a.y;
         v[c][2] = a.z;

@@ -76,6 +76,11 @@ struct NormParams {
     float2* stats;  // optional: the row's (mean, rstd) (LayerNorm), for a consumer that
                     // rebuilds the fp32 output on load instead of reading out32
     float *outhi, *outlo;  // optional (strict fp32): the output as tf32 hi + fp32 remainder
+    // optional: output row t normalises input row row_cu[t] (row_pick 1, a
+    // sequence's first token) or row_cu[t + 1] - 1 (row_pick 2, its last),
+    // clamped to [0, in_rows); T is then the number of sequences
+    const int32_t* row_cu;
+    int row_pick, in_rows;
 };
 cudaError_t launch_norm(const NormParams& p, bool rms, cudaStream_t st);
 cudaError_t launch_ln(const float* y32, const float* g, const float* b, float eps, int T, int H, float* x32,

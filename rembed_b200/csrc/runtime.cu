@@ -136,6 +136,7 @@ struct Replica {
     bool fold = false;
     float2* parts = nullptr;  // [H / 32 x T]
     float *pool32 = nullptr, *head_hid = nullptr, *head_out = nullptr;  // Gemma Dense head
+    float* pick32 = nullptr;  // [sequences x H]: the final norm of each sequence's pooled row
     int32_t* iota = nullptr;                                            // [0, 1, ..., cap_seq]
     int64_t* d_ids = nullptr;
     int32_t* d_cu = nullptr;
@@ -839,14 +840,17 @@ void ensure_workspace(rg_ctx* c, Replica& r, int T, int nseq, size_t nout) {
             r.ctx = ws_alloc<act16>(r, t * m.qd);
             r.ffh = ws_alloc<act16>(r, t * I);
         }
+        r.pick32 = ws_alloc<float>(r, static_cast<size_t>(capS) * H);
+        r.iota = ws_alloc<int32_t>(r, capS + 1);
+        {
+            std::vector<int32_t> io(capS + 1);
+            for (int i = 0; i <= capS; ++i) io[i] = i;
+            check(cudaMemcpy(r.iota, io.data(), sizeof(int32_t) * (capS + 1), cudaMemcpyHostToDevice), "cudaMemcpy");
+        }
         if (r.dense1) {
             r.pool32 = ws_alloc<float>(r, static_cast<size_t>(capS) * H);
             r.head_hid = ws_alloc<float>(r, static_cast<size_t>(capS) * d.dense_hidden);
             r.head_out = ws_alloc<float>(r, static_cast<size_t>(capS) * H);
-            r.iota = ws_alloc<int32_t>(r, capS + 1);
-            std::vector<int32_t> io(capS + 1);
-            for (int i = 0; i <= capS; ++i) io[i] = i;
-            check(cudaMemcpy(r.iota, io.data(), sizeof(int32_t) * (capS + 1), cudaMemcpyHostToDevice), "H2D iota");
         }
         if (c->mode == RG_MODE_INT8_FULL) {
             r.xq = ws_alloc<int8_t>(r, t * H);
@@ -1215,6 +1219,26 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         res_b = last ? nullptr : b;
         folded = false;
     };
+    // Pooled output with CLS / last-token pooling: only each sequence's
+    // pooled row reaches the output, so the stack's final norm runs on
+    // those rows alone (the same per-row arithmetic) into pick32.
+    const bool pick = out_kind == RG_OUT_POOLED && (d.pooling == 1 || d.pooling == 2);
+    auto picked_norm = [&](const float* g, const float* b, bool rms) {
+        ProfScope ps(r, st, RG_KC_NORM, 8.0 * nseq * Hd, nseq * Hd * 8.0);
+        rg::NormParams p{};
+        p.in = r.x32;
+        p.g = g;
+        p.b = b;
+        p.eps = eps;
+        p.T = nseq;
+        p.H = H;
+        p.out32 = r.pick32;
+        p.row_cu = d_cu;
+        p.row_pick = d.pooling;
+        p.in_rows = T;
+        check(rg::launch_norm(p, rms, st), "final norm launch");
+        ++launches;
+    };
     auto quantize = [&](const act16* x, int K, int8_t* q, float* sc) {  // bf16 rows (full-int8 mode)
         ProfScope ps(r, st, RG_KC_QUANT, 0.0, Td * K * 3.0);
         check(rg::launch_quantize_rows(reinterpret_cast<const __nv_bfloat16*>(x), T, K, q, sc, st),
@@ -1329,6 +1353,9 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         if (!pre && r.fold && !last) {
             residual_gemm(r.tm_ffh, L.ffn2, nullptr, true);
             fold_norm(L.ln2_g, L.ln2_b);
+        } else if (!pre && last && pick) {
+            residual_gemm(r.tm_ffh, L.ffn2, s8 ? r.ffhs : nullptr, false);
+            picked_norm(L.ln2_g, L.ln2_b, false);
         } else if (!pre) {
             residual_gemm(r.tm_ffh, L.ffn2, s8 ? r.ffhs : nullptr, false);
             post_norm(L.ln2_g, L.ln2_b, last);
@@ -1341,7 +1368,9 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
             gemm(r, mode, r.tm_ffh, L.ffn2, T, rg::kEpiBiasRes, s8 ? r.ffhs : nullptr, r.x32, r.x32, st, launches);
         }
     }
-    if (r.final_norm) {  // qwen3.go:544, gemma3.go:380, modernbert.go:307
+    if (r.final_norm && pick) {
+        picked_norm(r.final_norm, arch == RG_ARCH_MODERNBERT ? r.zero_beta : nullptr, arch != RG_ARCH_MODERNBERT);
+    } else if (r.final_norm) {  // qwen3.go:544, gemma3.go:380, modernbert.go:307
         ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * Hd * 8.0);
         rg::NormParams p{};
         p.in = r.x32;
@@ -1357,16 +1386,21 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
     if (out_kind == RG_OUT_POOLED) {
         const double rows = d.pooling == 0 ? Td : double(nseq);
         ProfScope ps(r, st, RG_KC_POOL, rows * Hd, 4.0 * (rows * Hd + double(nseq) * out_dim));
+        // With the final norm applied to the pooled rows only (pick32), the
+        // pool reads those rows as one-row sequences.
+        const float* src = pick ? r.pick32 : r.x32;
+        const int32_t* src_cu = pick ? r.iota : d_cu;
+        const int pooling = pick ? 1 : d.pooling;
         if (r.dense1) {
             // pool, Dense head H -> D -> H (fp32), then L2 and truncate (gemma3.go:177-198)
             const int D = d.dense_hidden;
-            check(rg::launch_pool(r.x32, d_cu, nseq, H, d.pooling, 0, H, r.pool32, st), "pool launch");
+            check(rg::launch_pool(src, src_cu, nseq, H, pooling, 0, H, r.pool32, st), "pool launch");
             check(rg::launch_dense_f32(r.pool32, r.dense1, r.head_hid, nseq, D, H, st), "dense launch");
             check(rg::launch_dense_f32(r.head_hid, r.dense2, r.head_out, nseq, H, D, st), "dense launch");
             check(rg::launch_pool(r.head_out, r.iota, nseq, H, 1, d.normalize, out_dim, d_out, st), "l2 launch");
             launches += 4;
         } else {
-            check(rg::launch_pool(r.x32, d_cu, nseq, H, d.pooling, d.normalize, out_dim, d_out, st), "pool launch");
+            check(rg::launch_pool(src, src_cu, nseq, H, pooling, d.normalize, out_dim, d_out, st), "pool launch");
             ++launches;
         }
     } else {

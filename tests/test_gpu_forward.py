@@ -98,6 +98,24 @@ def test_tokens_parity(minilm):
     assert cosines(pooled, minilm.gpu.embed(seqs)).min() >= 0.99999
 
 
+@pytest.mark.parametrize("name,first", [("bge-base", True), ("tiny-qwen3", False)])
+def test_pooled_row_equals_token_output(cuda, name, first):
+    """CLS / last-token pooling normalises only the pooled rows at the end
+    of the stack: without the L2 step the pooled vector is bit-identical to
+    that row of the per-token output, which normalises every row."""
+    cfg = synth.preset(name)
+    cfg.normalize = False
+    w = synth.make_weights(cfg, seed=61)
+    ids, cu = synth.make_batch(cfg, 6, 5, 90, seed=62)
+    seqs = [ids[cu[i]:cu[i + 1]] for i in range(len(cu) - 1)]
+    e = Embedder(cfg, w)
+    pooled = e.embed_packed(ids, cu)
+    toks = e.embed_tokens(seqs)
+    e.close()
+    for i, t in enumerate(toks):
+        assert np.array_equal(pooled[i], t.vectors[0 if first else -1]), i
+
+
 def test_batch_equals_single_bit_identical(minilm):
     """Packed varlen batching changes nothing (rembed_test.go:1265-1315)."""
     ids, cu = synth.make_batch(minilm.cfg, 7, 1, 128, seed=13)
