@@ -118,7 +118,9 @@ static cudaError_t launch_impl(GemmKind kind, int epi, int block_n, GemmMaps& m,
     // Folded LayerNorm and the chunk statistics / 16-bit copy of residual
     // outputs: 16-bit kinds only.
     const bool k16 = kind == GemmKind::kBF16 || kind == GemmKind::kF16;
-    if (args.fold_stats && (!k16 || !args.fold_c1 || !args.bias || (epi != kEpiBias && epi != kEpiBiasGelu)))
+    // (a gated epilogue adds no bias: its folded norm must have none either)
+    if (args.fold_stats && (!k16 || !args.fold_c1 ||
+                            (epi_is_glu(epi) ? false : (!args.bias || (epi != kEpiBias && epi != kEpiBiasGelu)))))
         return cudaErrorInvalidValue;
     if ((args.parts_out || args.out16) && (!k16 || !epi_has_residual(epi))) return cudaErrorInvalidValue;
     if (args.out16) {

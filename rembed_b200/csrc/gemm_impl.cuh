@@ -450,7 +450,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             // folded LayerNorm of the A rows: rstd and -rstd * mean
             float fr = 1.f, fnm = 0.f;
-            if constexpr (EPI == kEpiBias || EPI == kEpiBiasGelu) {
+            if constexpr (EPI == kEpiBias || EPI == kEpiBiasGelu || (EPI >= kEpiGluSilu && EPI <= kEpiGluGeluTanh)) {
                 if (args.fold_stats && row < args.M) {
                     const float2 st = args.fold_stats[row];
                     fr = st.y;
@@ -507,6 +507,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             w[i] = static_cast<float>(static_cast<int32_t>(rb[i])) * rs;
                         else
                             w[i] = __uint_as_float(rb[i]);
+                    }
+                    if (args.fold_stats) {  // folded norm: rstd * acc - rstd * mean * c1 (bias-free)
+                        const float4* c1a = reinterpret_cast<const float4*>(args.fold_c1 + col0);
+                        const float4* c1b = reinterpret_cast<const float4*>(args.fold_c1 + col0 + kChunk);
+                        const uint64_t r2 = f2(fr, fr), nm2 = f2(fnm, fnm);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float4 qa = __ldg(c1a + i), qb = __ldg(c1b + i);
+                            f2split(fma2(r2, f2(v[4 * i], v[4 * i + 1]), mul2(nm2, f2(qa.x, qa.y))), v[4 * i],
+                                    v[4 * i + 1]);
+                            f2split(fma2(r2, f2(v[4 * i + 2], v[4 * i + 3]), mul2(nm2, f2(qa.z, qa.w))), v[4 * i + 2],
+                                    v[4 * i + 3]);
+                            f2split(fma2(r2, f2(w[4 * i], w[4 * i + 1]), mul2(nm2, f2(qb.x, qb.y))), w[4 * i],
+                                    w[4 * i + 1]);
+                            f2split(fma2(r2, f2(w[4 * i + 2], w[4 * i + 3]), mul2(nm2, f2(qb.z, qb.w))), w[4 * i + 2],
+                                    w[4 * i + 3]);
+                        }
                     }
                     if (CSCALE && args.col_scale) {
                         const float4* ca = reinterpret_cast<const float4*>(args.col_scale + col0);
@@ -617,8 +634,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     }
                     if constexpr (S::Y16) {
                         // the 16-bit copy, staged for its own TMA store (the
-                        // box is free: every earlier store has read its box)
+                        // box is free: every earlier store has read its box);
+                        // an fp16 copy fails loudly instead of turning into inf
                         if (args.out16) {
+                            if constexpr (F16) {
+                                float amax = 0.f;
+#pragma unroll
+                                for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+                                if (__any_sync(0xffffffffu, amax > 65504.0f) && lane == 0)
+                                    atomicOr(args.status, kStatusF16Overflow);
+                            }
                             uint8_t* y16 = y16_base + ew * kY16Bytes;
 #pragma unroll
                             for (int i = 0; i < 4; ++i)

@@ -643,13 +643,22 @@ cudaError_t launch_attention(const AttnParams& p, int nseq, int max_len, int hea
 constexpr int kMergeRegs = 32;
 
 __global__ void __launch_bounds__(64) merge_row_stats_kernel(const float2* __restrict__ parts, int nparts, int T,
-                                                             float eps, float2* __restrict__ stats) {
+                                                             float eps, float2* __restrict__ stats, bool rms) {
     pdl_trigger();
     pdl_wait();
     const int row = blockIdx.x * blockDim.x + threadIdx.x;
     if (row >= T) return;
     const float2* p = parts + row;
     float mean, m2 = 0.f;
+    if (rms) {  // sum of squares about zero, the chunks in order
+        float ss = 0.f;
+        for (int i = 0; i < nparts; ++i) {
+            const float2 q = p[static_cast<size_t>(i) * T];
+            ss += fmaf(32.0f * q.x, q.x, q.y);
+        }
+        stats[row] = make_float2(0.f, 1.0f / sqrtf(ss / static_cast<float>(32 * nparts) + eps));
+        return;
+    }
     if (nparts <= kMergeRegs) {
         float2 q[kMergeRegs];
 #pragma unroll
@@ -676,10 +685,11 @@ __global__ void __launch_bounds__(64) merge_row_stats_kernel(const float2* __res
     stats[row] = make_float2(mean, 1.0f / sqrtf(m2 / static_cast<float>(32 * nparts) + eps));
 }
 
-cudaError_t launch_merge_row_stats(const float2* parts, int nparts, int T, float eps, float2* stats, cudaStream_t st) {
+cudaError_t launch_merge_row_stats(const float2* parts, int nparts, int T, float eps, float2* stats, cudaStream_t st,
+                                   bool rms) {
     if (T <= 0) return cudaSuccess;
     if (nparts <= 0 || !parts || !stats) return cudaErrorInvalidValue;
-    launch_pdl(merge_row_stats_kernel, dim3((T + 63) / 64), dim3(64), 0, st, parts, nparts, T, eps, stats);
+    launch_pdl(merge_row_stats_kernel, dim3((T + 63) / 64), dim3(64), 0, st, parts, nparts, T, eps, stats, rms);
     return cudaGetLastError();
 }
 

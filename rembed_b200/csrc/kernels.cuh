@@ -56,7 +56,10 @@ cudaError_t launch_split_tf32(const float* x, size_t n, float* hi, float* lo, cu
 // Per-row LayerNorm statistics from the (mean, M2) of each row's nparts
 // 32-column chunks (parts[i * T + row], as residual GEMM epilogues write
 // them): stats[row] = (mean, 1 / sqrt(var + eps)).
-cudaError_t launch_merge_row_stats(const float2* parts, int nparts, int T, float eps, float2* stats, cudaStream_t st);
+// rms: RMSNorm statistics instead, stats[row] = (0, 1 / sqrt(mean(y^2) + eps))
+// with sum(y^2) = sum(M2_i + 32 mean_i^2).
+cudaError_t launch_merge_row_stats(const float2* parts, int nparts, int T, float eps, float2* stats, cudaStream_t st,
+                                   bool rms = false);
 
 // Row normalisation of in [T x H]: LayerNorm (g, b; b nullptr = zero) or
 // RMSNorm (g); g nullptr = identity.  Outputs (each optional): out32 (may

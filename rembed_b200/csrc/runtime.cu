@@ -134,6 +134,7 @@ struct Replica {
     // merges the chunks into lnst, and the next GEMM reads the copy with the
     // norm's gain folded into its weight.
     bool fold = false;
+    bool fold_rms = false;    // pre-norm stacks: the folded norms are RMSNorms (Qwen3)
     float2* parts = nullptr;  // [H / 32 x T]
     float *pool32 = nullptr, *head_hid = nullptr, *head_out = nullptr;  // Gemma Dense head
     float* pick32 = nullptr;  // [sequences x H]: the final norm of each sequence's pooled row
@@ -723,6 +724,18 @@ void finalize_decoder(rg_ctx* c, Replica& r) {
         rope_tables(r, npos, dh, d.rope_theta, &r.cos_g, &r.sin_g);
     }
     r.layers.resize(d.num_hidden_layers);
+    // Pre-norm stacks whose input norms fold into the GEMMs (bf16 mode): the
+    // residual GEMMs write a 16-bit copy of the stream and its chunk
+    // statistics; QKV (layers 1...) and the gated FFN use gain-folded
+    // weights.  Qwen3's RMSNorm (no mean) and ModernBERT's bias-free
+    // LayerNorm; the first layer's first norm still runs as a kernel.
+    r.fold = c->mode == RG_MODE_BF16 && (arch == RG_ARCH_QWEN3 || arch == RG_ARCH_MODERNBERT) && H % 32 == 0;
+    r.fold_rms = r.fold && arch == RG_ARCH_QWEN3;
+    const std::vector<float> zero_h(H, 0.f);
+    auto dense = [&](const float* W, int N, int K, const float* gain) {
+        return r.fold && gain ? make_dense_folded(r, c->mode, W, nullptr, N, K, gain, zero_h.data())
+                              : make_dense(r, c->mode, W, nullptr, N, K);
+    };
     for (int li = 0; li < d.num_hidden_layers; ++li) {
         DevLayer& L = r.layers[li];
         if (arch == RG_ARCH_QWEN3 || arch == RG_ARCH_GEMMA3) {
@@ -746,22 +759,25 @@ void finalize_decoder(rg_ctx* c, Replica& r) {
             std::vector<float> wqkv = concat_rows({{G(p + "self_attn.q_proj.weight", {m.qd, H}), qn},
                                                    {G(p + "self_attn.k_proj.weight", {m.kvd, H}), kn},
                                                    {G(p + "self_attn.v_proj.weight", {m.kvd, H}), kn}});
-            L.qkv = make_dense(r, c->mode, wqkv.data(), nullptr, m.nqkv, H);
+            // (Gemma never folds: r.fold is off for it)
+            L.qkv = dense(wqkv.data(), m.nqkv, H, li > 0 ? G(p + "input_layernorm.weight", {H}) : nullptr);
             L.o = make_dense(r, c->mode, G(p + "self_attn.o_proj.weight", {H, m.qd}), nullptr, H, m.qd);
             std::vector<float> wgu = interleave_glu(G(p + "mlp.gate_proj.weight", {I, H}),
                                                     G(p + "mlp.up_proj.weight", {I, H}), I, H);
-            L.ffn1 = make_dense(r, c->mode, wgu.data(), nullptr, 2 * I, H);
+            L.ffn1 = dense(wgu.data(), 2 * I, H,
+                           arch == RG_ARCH_QWEN3 ? G(p + "post_attention_layernorm.weight", {H}) : nullptr);
             L.ffn2 = make_dense(r, c->mode, G(p + "mlp.down_proj.weight", {H, I}), nullptr, H, I);
         } else if (arch == RG_ARCH_MODERNBERT) {
             const std::string p = "layers." + std::to_string(li) + ".";
             L.global = li % d.global_attn_every_n_layers == 0;  // modernbert.go:73
             if (li != 0) L.attn_norm = up(G(p + "attn_norm.weight", {H}), H);
             L.ffn_norm = up(G(p + "mlp_norm.weight", {H}), H);
-            L.qkv = make_dense(r, c->mode, G(p + "attn.Wqkv.weight", {3 * H, H}), nullptr, 3 * H, H);
+            L.qkv = dense(G(p + "attn.Wqkv.weight", {3 * H, H}), 3 * H, H,
+                          li != 0 ? G(p + "attn_norm.weight", {H}) : nullptr);
             L.o = make_dense(r, c->mode, G(p + "attn.Wo.weight", {H, H}), nullptr, H, H);
             const float* wi = G(p + "mlp.Wi.weight", {2 * I, H});  // value rows [0, I), gate rows [I, 2I)
             std::vector<float> wgu = interleave_glu(wi, wi + static_cast<size_t>(I) * H, I, H);
-            L.ffn1 = make_dense(r, c->mode, wgu.data(), nullptr, 2 * I, H);
+            L.ffn1 = dense(wgu.data(), 2 * I, H, G(p + "mlp_norm.weight", {H}));
             L.ffn2 = make_dense(r, c->mode, G(p + "mlp.Wo.weight", {H, I}), nullptr, H, I);
         } else {  // nomic
             const std::string p = "encoder.layers." + std::to_string(li) + ".";
@@ -1160,7 +1176,7 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
     // consumer GEMM (QKV, FFN1) folds the norm into its weight and epilogue,
     // and the next residual GEMM rebuilds LN(x32) from lnst as before.
     const float *res_g = nullptr, *res_b = nullptr;
-    bool folded = false;  // xb holds the unnormalised rows of the pending LayerNorm
+    bool folded = false;  // xb holds the unnormalised rows of the pending (folded) norm
     auto residual_gemm = [&](const OpMaps& tmA, const DevDense& w, const float* row_scale, bool fold_out) {
         LnFold lf;
         lf.out16 = fold_out ? r.xb : nullptr;
@@ -1183,6 +1199,19 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         }
         res_g = g;
         res_b = b;
+        folded = true;
+    };
+    // Pre-norm stacks: the residual GEMM adds in place on x32 and writes
+    // the stream's 16-bit copy and chunk statistics; the merge gives the
+    // next (folded) norm's per-row statistics.
+    auto pre_residual_fold = [&](const OpMaps& tmA, const DevDense& w) {
+        LnFold lf;
+        lf.out16 = r.xb;
+        lf.parts_out = r.parts;
+        gemm(r, mode, tmA, w, T, rg::kEpiBiasRes, nullptr, r.x32, r.x32, st, launches, nullptr, nullptr, nullptr, &lf);
+        ProfScope ps(r, st, RG_KC_NORM, 4.0 * Td * (H / 32), Td * (8.0 * (H / 32) + 8.0));
+        check(rg::launch_merge_row_stats(r.parts, H / 32, T, eps, r.lnst, st, r.fold_rms), "merge_row_stats launch");
+        ++launches;
         folded = true;
     };
     // A GEMM reading xb: LN(y) folded into it when the last norm was folded.
@@ -1254,7 +1283,12 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
     for (int li = 0; li < d.num_hidden_layers; ++li) {
         const DevLayer& L = r.layers[li];
         // ---- attention sublayer
-        if (pre) norm_into_a(L.attn_norm, arch == RG_ARCH_MODERNBERT ? r.zero_beta : nullptr, arch != RG_ARCH_MODERNBERT);
+        // (a folded pre-norm stack enters layers 1... with the norm's
+        // statistics already merged by the previous FFN's residual GEMM)
+        if (pre && !(r.fold && li > 0)) {
+            norm_into_a(L.attn_norm, arch == RG_ARCH_MODERNBERT ? r.zero_beta : nullptr, arch != RG_ARCH_MODERNBERT);
+            folded = false;
+        }
         input_gemm(L.qkv, r.tm_x, rg::kEpiBias, f32 ? static_cast<void*>(r.qkv32) : r.qkv);
         if (has_rope(arch)) {
             ProfScope ps(r, st, RG_KC_NORM, 0.0, Td * (m.qd + m.kvd) * 4.0);
@@ -1336,11 +1370,13 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
             ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * Hd * 12.0);
             check(rg::launch_add_rmsnorm(r.x32, r.y32, L.post_attn, eps, T, H, st), "add_rmsnorm launch");
             ++launches;
+        } else if (r.fold) {  // residual in place + the folded FFN norm's statistics
+            pre_residual_fold(r.tm_ctx, L.o);
         } else {  // residual added in place on x32
             gemm(r, mode, r.tm_ctx, L.o, T, rg::kEpiBiasRes, s8 ? r.ctxs : nullptr, r.x32, r.x32, st, launches);
         }
         // ---- FFN sublayer
-        if (pre) norm_into_a(L.ffn_norm, arch == RG_ARCH_MODERNBERT ? r.zero_beta : nullptr, arch != RG_ARCH_MODERNBERT);
+        if (pre && !r.fold) norm_into_a(L.ffn_norm, arch == RG_ARCH_MODERNBERT ? r.zero_beta : nullptr, arch != RG_ARCH_MODERNBERT);
         input_gemm(L.ffn1, r.tm_x, is_glu(arch) ? glu_epi : rg::kEpiBiasGelu,
                    f32 ? static_cast<void*>(r.ffhh) : r.ffh);
         if (f32) {  // the fp32 FFN hidden state -> tf32 hi (in place) + remainder
@@ -1365,7 +1401,11 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
             check(rg::launch_add_rmsnorm(r.x32, r.y32, L.post_ffn, eps, T, H, st), "add_rmsnorm launch");
             ++launches;
         } else {
-            gemm(r, mode, r.tm_ffh, L.ffn2, T, rg::kEpiBiasRes, s8 ? r.ffhs : nullptr, r.x32, r.x32, st, launches);
+            if (r.fold && !last)
+                pre_residual_fold(r.tm_ffh, L.ffn2);
+            else
+                gemm(r, mode, r.tm_ffh, L.ffn2, T, rg::kEpiBiasRes, s8 ? r.ffhs : nullptr, r.x32, r.x32, st,
+                     launches);
         }
     }
     if (r.final_norm && pick) {

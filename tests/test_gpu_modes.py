@@ -116,6 +116,26 @@ def test_fp16_activation_overflow_is_reported(cuda):
     gpu.close()
 
 
+def test_fp16_residual_copy_overflow_is_reported(cuda):
+    """With the post-norm LayerNorms folded, the residual GEMM also writes
+    the unnormalised rows as fp16 for the next GEMM: a residual outside the
+    fp16 range fails loudly there instead of turning into inf; in bf16 the
+    same model stays finite (its accuracy is not the point: a row mean this
+    far above the row's spread is not what a LayerNorm input looks like)."""
+    cfg = synth.preset("tiny-bert")
+    w = synth.make_weights(cfg, seed=50)
+    k = next(n for n in w if n.endswith("layer.0.output.dense.bias"))
+    w[k] = w[k] + np.float32(1e5)  # the residual after layer 0's FFN, finite in fp32
+    ids, cu = synth.make_batch(cfg, 3, 4, 30, seed=51)
+    gpu = Embedder(cfg, w, fp16=True)
+    with pytest.raises(Exception, match="fp16 range"):
+        gpu.embed_packed(ids, cu)
+    gpu.close()
+    gpu = Embedder(cfg, w, fp16=False)
+    assert np.isfinite(gpu.embed_packed(ids, cu)).all()
+    gpu.close()
+
+
 def test_int8_weights_large_batch_widened_path(cuda):
     """At >= 4096 tokens the weight-only int8 GEMMs widen each int8 weight to
     fp16 just before the GEMM instead of converting inside the mainloop; the
