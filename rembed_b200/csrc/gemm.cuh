@@ -39,10 +39,12 @@ struct GemmArgs {
     void* out;               // [M x ld_out], 16-bit (bf16 / fp16 by kind) or fp32
     int ld_out;
     int* status;             // device status word
-    // LayerNorm folded into this GEMM (kEpiBias / kEpiBiasGelu): A holds the
-    // unnormalised rows y and W the weight times the norm's gain; with the
-    // row's (mean, rstd) from fold_stats the epilogue computes
-    // rstd * acc + (bias[n] - rstd * mean * fold_c1[n]) (bias = W.beta + b).
+    // Norm folded into this GEMM (kEpiBias / kEpiBiasGelu, and the gated
+    // epilogues for bias-free norms): A holds the unnormalised rows y and W
+    // the weight times the norm's gain; with the row's (mean, rstd) from
+    // fold_stats (mean 0 for an RMSNorm) the epilogue computes
+    // rstd * acc + (bias[n] - rstd * mean * fold_c1[n]) (bias = W.beta + b;
+    // the gated epilogues apply it to both halves without a bias).
     const float2* fold_stats;  // [M] (mean, rstd)
     const float* fold_c1;      // [N] column sums of the folded 16-bit weight
     // residual epilogues: also write the output as 16 bits (out16, row
@@ -64,8 +66,9 @@ struct GemmArgs {
 //          fp32 output for every epilogue (the strict-fp32 mode).
 enum class GemmKind : int { kBF16 = 0, kS8 = 1, kF16 = 2, kW8 = 3, kTF32x3 = 4 };
 
-// Tensor maps one launch reads: A, W, the output and residual boxes, and for
-// kTF32x3 the remainder parts of A (a2) and W (b2).
+// Tensor maps one launch reads: A, W, the output and residual boxes, for
+// kTF32x3 the remainder parts of A (a2) and W (b2), and the residual
+// epilogues' 16-bit copy (out16).
 struct GemmMaps {
     CUtensorMap a, b, out, res, a2, b2, out16;
 };

@@ -128,11 +128,11 @@ struct Replica {
     int8_t *xq = nullptr, *ctxq = nullptr, *ffhq = nullptr;
     float *xs = nullptr, *ctxs = nullptr, *ffhs = nullptr;
     float2* lnst = nullptr;  // post-norm: the last LayerNorm's per-row (mean, rstd)
-    // Post-norm stacks in the 16-bit modes fold each inner LayerNorm into
-    // the GEMMs around it: the residual GEMM writes its output's 32-column
-    // chunk statistics (parts) and a 16-bit copy in xb, a small kernel
-    // merges the chunks into lnst, and the next GEMM reads the copy with the
-    // norm's gain folded into its weight.
+    // Folded norms (post-norm BERT family in the 16-bit modes; Qwen3 and
+    // ModernBERT input norms in bf16): the residual GEMM writes its
+    // output's 32-column chunk statistics (parts) and a 16-bit copy in xb, a
+    // small kernel merges the chunks into lnst, and the next GEMM reads the
+    // copy with the norm's gain folded into its weight.
     bool fold = false;
     bool fold_rms = false;    // pre-norm stacks: the folded norms are RMSNorms (Qwen3)
     float2* parts = nullptr;  // [H / 32 x T]
