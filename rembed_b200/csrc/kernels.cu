@@ -729,99 +729,165 @@ cudaError_t launch_split_tf32(const float* x, size_t n, float* hi, float* lo, cu
 // key j's row is bank-conflict-free).  Lane j computes q . k_j for its key,
 // the warp keeps the running max / sum, and lane d accumulates output dims
 // d, d + 32, ... over the block's probabilities (broadcast by shuffle).
+// Strict fp32 attention, register-tiled on the FMA pipes: a CTA takes 64
+// query rows of one (sequence, head) and walks 64-key blocks staged in
+// shared memory.  Thread t = (row group rg = t / 16, column group cg =
+// t % 16) holds the scores of rows 4 rg .. 4 rg + 3 against keys cg + 16 j
+// (j < 4) and the output of the same rows at dims cg + 16 c (c < D / 16);
+// the keys / dims strided by 16 keep the shared-memory reads of a warp on
+// distinct banks.  Online softmax in the natural exp domain (expf), like the
+// reference's fp32 path; a row's 64 scores of a block are reduced over its
+// 16 threads by shuffles.
+constexpr int kF32Rows = 64, kF32Keys = 64;
+
+template <int D>
+struct AttnF32Smem {
+    static constexpr int QP = D + 1, KP = D + 1, VP = D, PP = kF32Keys + 1;
+    static constexpr int FLOATS = kF32Rows * QP + kF32Keys * KP + kF32Keys * VP + kF32Rows * PP;
+};
+
 template <int D>
 __global__ void __launch_bounds__(256) attention_f32_kernel(AttnF32Params p) {
     pdl_trigger();
     pdl_wait();
-    constexpr int E = D / 32, KP = D + 1;
+    using SM = AttnF32Smem<D>;
+    constexpr int QP = SM::QP, KP = SM::KP, VP = SM::VP, PP = SM::PP;
+    constexpr int NC = D / 16;  // output dims per thread and row
     extern __shared__ float fsm[];
-    float* qs = fsm;              // [8][D]
-    float* ks = qs + 8 * D;       // [32][D + 1]
-    float* vs = ks + 32 * KP;     // [32][D]
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* qs = fsm;                        // [64][D + 1]
+    float* ks = qs + kF32Rows * QP;         // [64][D + 1]
+    float* vs = ks + kF32Keys * KP;         // [64][D]
+    float* ps = vs + kF32Keys * VP;         // [64][65]
+    const int t = threadIdx.x, rg = t >> 4, cg = t & 15;
     const int s = blockIdx.z, h = blockIdx.y;
     const int s0 = __ldg(p.cu + s), L = __ldg(p.cu + s + 1) - s0;
-    const int q0 = blockIdx.x * 8;
+    const int q0 = blockIdx.x * kF32Rows;
     if (q0 >= L) return;  // the whole CTA
-    const int qi = q0 + warp;
-    const bool active = qi < L;
     const int hk = h / p.group;
-    for (int t = threadIdx.x; t < 8 * D; t += 256) {
-        const int w = t / D, d = t % D;
-        qs[t] = q0 + w < L ? p.q[static_cast<int64_t>(s0 + q0 + w) * p.ldq + h * D + d] : 0.f;
+    const int nrow = min(kF32Rows, L - q0);
+    for (int i = t; i < kF32Rows * D; i += 256) {
+        const int r = i / D, d = i % D;
+        qs[r * QP + d] = r < nrow ? p.q[static_cast<int64_t>(s0 + q0 + r) * p.ldq + h * D + d] : 0.f;
     }
     const float* K = p.k + static_cast<int64_t>(s0) * p.ldk + hk * D;
     const float* V = p.v + static_cast<int64_t>(s0) * p.ldv + hk * D;
-    // keys this row may see, and the union over the CTA's rows
-    const int jlo = max(0, qi + p.rel_lo), jhi = min(L - 1, qi + p.rel_hi);
-    const int clo = max(0, q0 + p.rel_lo), chi = min(L - 1, min(q0 + 7, L - 1) + p.rel_hi);
-    float m = -INFINITY, l = 0.f;
-    float o[E];
+    // keys any row of the tile may see
+    const int clo = max(0, q0 + p.rel_lo), chi = min(L - 1, q0 + nrow - 1 + p.rel_hi);
+    float m[4], l[4], o[4][NC];
 #pragma unroll
-    for (int e = 0; e < E; ++e) o[e] = 0.f;
-    const float* qrow = qs + warp * D;
-    for (int j0 = clo; j0 <= chi; j0 += 32) {
-        __syncthreads();  // previous block consumed (and, first time, qs written)
-        const int nb = min(32, chi - j0 + 1);
-        for (int t = threadIdx.x; t < 32 * D; t += 256) {
-            const int r = t / D, d = t % D;
-            const bool in = r < nb;
+    for (int i = 0; i < 4; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) o[i][c] = 0.f;
+    }
+    const float* bias_row = p.bias ? p.bias + static_cast<int64_t>(h) * (2 * p.bias_off + 1) : nullptr;
+    for (int j0 = clo; j0 <= chi; j0 += kF32Keys) {
+        __syncthreads();  // the previous block's K / V / P consumed (and, first time, Q written)
+        const int nk = min(kF32Keys, chi - j0 + 1);
+        for (int i = t; i < kF32Keys * D; i += 256) {
+            const int r = i / D, d = i % D;
+            const bool in = r < nk;
             ks[r * KP + d] = in ? __ldg(K + static_cast<int64_t>(j0 + r) * p.ldk + d) : 0.f;
-            vs[r * D + d] = in ? __ldg(V + static_cast<int64_t>(j0 + r) * p.ldv + d) : 0.f;
+            vs[r * VP + d] = in ? __ldg(V + static_cast<int64_t>(j0 + r) * p.ldv + d) : 0.f;
         }
         __syncthreads();
-        if (!active) continue;
-        const int j = j0 + lane;
-        const bool valid = lane < nb && j >= jlo && j <= jhi;
-        float sc = -INFINITY;
-        if (valid) {
-            const float* kr = ks + lane * KP;
-            float acc = 0.f;
-#pragma unroll 16
-            for (int d = 0; d < D; ++d) acc = fmaf(qrow[d], kr[d], acc);
-            sc = acc * p.scale;
-            if (p.bias) {
-                const int bi = min(max(j - qi + p.bias_off, 0), 2 * p.bias_off);
-                sc += __ldg(p.bias + static_cast<int64_t>(h) * (2 * p.bias_off + 1) + bi);
+        // S = Q K^T for the thread's 4 rows x 4 keys
+        float sc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sc[i][j] = 0.f;
+#pragma unroll 4
+        for (int d = 0; d < D; ++d) {
+            float qv[4], kv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) qv[i] = qs[(4 * rg + i) * QP + d];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) kv[j] = ks[(cg + 16 * j) * KP + d];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) sc[i][j] = fmaf(qv[i], kv[j], sc[i][j]);
+        }
+        // scale (+ relative bias), mask, online softmax per row
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int qi = q0 + 4 * rg + i;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int kj = j0 + cg + 16 * j;
+                const int rel = kj - qi;
+                const bool valid = kj <= chi && rel >= p.rel_lo && rel <= p.rel_hi;
+                float x = sc[i][j] * p.scale;
+                if (bias_row) x += __ldg(bias_row + min(max(rel + p.bias_off, 0), 2 * p.bias_off));
+                x = valid ? x : -INFINITY;
+                sc[i][j] = x;
+                mx = fmaxf(mx, x);
             }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float mn = fmaxf(m[i], mx);
+            float alpha = 1.f, ls = 0.f;
+            if (mn != -INFINITY) {  // the row has a key so far
+                alpha = m[i] == -INFINITY ? 0.f : expf(m[i] - mn);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float e = sc[i][j] == -INFINITY ? 0.f : expf(sc[i][j] - mn);
+                    sc[i][j] = e;
+                    ls += e;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) sc[i][j] = 0.f;
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+            l[i] = l[i] * alpha + ls;
+            m[i] = mn;
+#pragma unroll
+            for (int c = 0; c < NC; ++c) o[i][c] *= alpha;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ps[(4 * rg + i) * PP + cg + 16 * j] = sc[i][j];
         }
-        float bm = sc;
+        __syncthreads();  // P complete
+        // O += P V for the thread's 4 rows x NC dims
+#pragma unroll 4
+        for (int k = 0; k < nk; ++k) {
+            float pv[4], vv[NC];
 #pragma unroll
-        for (int o2 = 16; o2 > 0; o2 >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o2));
-        if (bm == -INFINITY) continue;  // no key of this row in the block
-        const float mn = fmaxf(m, bm);
-        const float alpha = m == -INFINITY ? 0.f : expf(m - mn);
-        const float pj = valid ? expf(sc - mn) : 0.f;
-        float ps = pj;
+            for (int i = 0; i < 4; ++i) pv[i] = ps[(4 * rg + i) * PP + k];
 #pragma unroll
-        for (int o2 = 16; o2 > 0; o2 >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o2);
-        l = l * alpha + ps;
+            for (int c = 0; c < NC; ++c) vv[c] = vs[k * VP + cg + 16 * c];
 #pragma unroll
-        for (int e = 0; e < E; ++e) o[e] *= alpha;
-        for (int kk = 0; kk < nb; ++kk) {
-            const float pk = __shfl_sync(0xffffffffu, pj, kk);
+            for (int i = 0; i < 4; ++i)
 #pragma unroll
-            for (int e = 0; e < E; ++e) o[e] = fmaf(pk, vs[kk * D + lane + 32 * e], o[e]);
+                for (int c = 0; c < NC; ++c) o[i][c] = fmaf(pv[i], vv[c], o[i][c]);
         }
-        m = mn;
     }
-    if (!active) return;
-    const float inv = l > 0.f ? 1.0f / l : 0.f;
-    float* oh = p.out_hi + static_cast<int64_t>(s0 + qi) * p.ldo + h * D;
-    float* ol = p.out_lo + static_cast<int64_t>(s0 + qi) * p.ldo + h * D;
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-        float hi, lo;
-        tf32_split(o[e] * inv, hi, lo);
-        oh[lane + 32 * e] = hi;
-        ol[lane + 32 * e] = lo;
+    for (int i = 0; i < 4; ++i) {
+        const int r = 4 * rg + i;
+        if (r >= nrow) continue;
+        const float inv = l[i] > 0.f ? 1.0f / l[i] : 0.f;
+        float* oh = p.out_hi + static_cast<int64_t>(s0 + q0 + r) * p.ldo + h * D;
+        float* ol = p.out_lo + static_cast<int64_t>(s0 + q0 + r) * p.ldo + h * D;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            float hi, lo;
+            tf32_split(o[i][c] * inv, hi, lo);
+            oh[cg + 16 * c] = hi;
+            ol[cg + 16 * c] = lo;
+        }
     }
 }
 
 template <int D>
 static cudaError_t launch_attention_f32_d(const AttnF32Params& p, int nseq, int max_len, int heads,
                                           cudaStream_t st) {
-    constexpr int smem = (8 * D + 32 * (D + 1) + 32 * D) * 4;
+    constexpr int smem = AttnF32Smem<D>::FLOATS * 4;
+    static_assert(smem <= 232448, "shared memory budget");
     static unsigned configured = 0;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -830,7 +896,7 @@ static cudaError_t launch_attention_f32_d(const AttnF32Params& p, int nseq, int 
         if (e != cudaSuccess) return e;
         if (dev < 32) __atomic_fetch_or(&configured, 1u << dev, __ATOMIC_RELEASE);
     }
-    const dim3 grid((max_len + 7) / 8, heads, nseq);
+    const dim3 grid((max_len + kF32Rows - 1) / kF32Rows, heads, nseq);
     launch_pdl(attention_f32_kernel<D>, dim3(grid), dim3(256), smem, st, p);
     return cudaGetLastError();
 }
