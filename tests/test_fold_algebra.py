@@ -6,8 +6,9 @@ residual GEMM writes the unnormalised rows y and the (mean, M2) of each
 next GEMM uses the weight W' = W * gamma (gamma along K) with the epilogue
     rstd * (y . W'^T) + (b + beta . W^T - rstd * mean * c1),  c1 = sum_k W'.
 These tests check that identity against LN(y) . W^T + b, the chunk merge
-against a direct two-pass mean / variance, and the LayerNorm-on-load rebuild
-of the residual (the reference's LayerNorm, bert.go:905-918).
+against a direct two-pass mean / variance, the LayerNorm-on-load rebuild of
+the residual (the reference's LayerNorm, bert.go:905-918), and the RMSNorm
+form the pre-norm stacks fold (no mean; both halves of a gated FFN).
 """
 
 import numpy as np
@@ -77,3 +78,30 @@ def test_layernorm_on_load_rebuild():
     mean, rstd = merge(chunk_stats(r), 1e-12)
     got = (r - mean[:, None]) * rstd[:, None] * g + b
     assert np.allclose(got, layer_norm(r, g, b, 1e-12), rtol=1e-10, atol=1e-12)
+
+
+def merge_rms(parts, eps):
+    """The RMSNorm merge: sum(y^2) = sum(M2_i + 32 mean_i^2) in chunk order."""
+    n = parts.shape[0]
+    ss = (parts[:, :, 1] + 32.0 * parts[:, :, 0] ** 2).sum(axis=0)
+    return 1.0 / np.sqrt(ss / (32 * n) + eps)
+
+
+@pytest.mark.parametrize("T,H,I", [(6, 256, 512), (17, 1024, 3072)])
+def test_folded_rmsnorm_gated_ffn(T, H, I):
+    """Pre-norm (Qwen3): RMSNorm(y) . W^T = rstd * (y . (W * g)^T), applied
+    to both halves of the gated FFN before the activation."""
+    rng = np.random.default_rng(I)
+    eps = 1e-6
+    y = rng.normal(0.0, 3.0, size=(T, H))
+    y[:, 7] *= 50.0  # a massive-activation column
+    g = rng.normal(1.0, 0.2, size=H)
+    Wg = rng.normal(0.0, 0.02, size=(I, H))
+    Wu = rng.normal(0.0, 0.02, size=(I, H))
+    xn = y / np.sqrt((y ** 2).mean(axis=1, keepdims=True) + eps) * g
+    silu = lambda a: a / (1.0 + np.exp(-a))
+    want = silu(xn @ Wg.T) * (xn @ Wu.T)
+    rstd = merge_rms(chunk_stats(y), eps)
+    a = rstd[:, None] * (y @ (Wg * g).T)
+    b = rstd[:, None] * (y @ (Wu * g).T)
+    assert np.allclose(silu(a) * b, want, rtol=1e-10, atol=1e-12)
