@@ -57,7 +57,8 @@ def bge(cuda):
     return Model("bge-base")
 
 
-@pytest.mark.parametrize("which,nseq,lo,hi", [("tiny", 9, 1, 200), ("minilm", 16, 8, 128), ("bge", 8, 16, 512)])
+@pytest.mark.parametrize("which,nseq,lo,hi", [("tiny", 9, 1, 200), ("minilm", 16, 8, 128), ("bge", 8, 16, 512),
+                                              ("bge", 12, 1, 128)])
 def test_pooled_parity(request, which, nseq, lo, hi):
     m = request.getfixturevalue(which)
     ids, cu = synth.make_batch(m.cfg, nseq, lo, hi, seed=11, id_hi=min(m.cfg.vocab_size - 1, 30521))
