@@ -199,7 +199,13 @@ class Embedder:
     """
 
     def __init__(self, config: Config, weights: dict, *, int8: bool = False, int8_activations: bool = False,
-                 dim: int = 0, devices: Sequence[int] = (0,), fp16: bool = True, strict_fp32: bool = False):
+                 dim: int = 0, devices: Sequence[int] = (0,), fp16: bool = True, strict_fp32: bool = False,
+                 workers: int = 0):
+        # workers = WithWorkers (rembed.go:109-121): a cap on the CPU fan-out
+        # of one Embed call.  The GPU forward has no CPU fan-out (one stream
+        # per device, the whole batch in one pass), so the cap is accepted for
+        # drop-in use and has no effect.
+        del workers
         self._lib = library()
         self._ctx = None
         self.config = config.validate(config.name or "config")
@@ -377,11 +383,12 @@ class Embedder:
 
 def load(ref: str | os.PathLike, *, int8: bool = False, int8_activations: bool = False, dim: int = 0,
          devices: Sequence[int] = (0,), fp16: bool = True, strict_fp32: bool = False,
-         disk_weights: bool = False) -> Embedder:
+         disk_weights: bool = False, workers: int = 0) -> Embedder:
     """rembed.Load over a converted model directory: manifest.json plus
     model.safetensors or a sharded set (model.safetensors.index.json).
     disk_weights = WithDiskWeights: the weights are mapped from
-    <dir>/weights.rembedpack, built from the checkpoint on first use.  Hub
+    <dir>/weights.rembedpack, built from the checkpoint on first use;
+    workers = WithWorkers, accepted with no effect (no CPU fan-out here).  Hub
     download and HF-config derivation stay with the reference host."""
     from . import weights as W
 
@@ -389,4 +396,4 @@ def load(ref: str | os.PathLike, *, int8: bool = False, int8_activations: bool =
     cfg = Config.load(p / "manifest.json")
     tensors = W.disk_weights(p) if disk_weights else W.read_checkpoint(p)
     return Embedder(cfg, tensors, int8=int8, int8_activations=int8_activations, dim=dim, devices=devices,
-                    fp16=fp16, strict_fp32=strict_fp32)
+                    fp16=fp16, strict_fp32=strict_fp32, workers=workers)

@@ -51,3 +51,21 @@ def test_error_strings_round_trip_without_gpu():
         pass
     with pytest.raises(RembedError):
         Embedder(cfg, {})
+
+
+def test_python_mirror_takes_every_load_option():
+    """The reference's Load options (rembed.go:67-121: WithInt8,
+    WithInt8Activations, WithDiskWeights, WithDim, WithWorkers) are keyword
+    arguments of load(); the Embedder exposes dim, model, quantized,
+    quantized_activations, close and the context-manager protocol like the
+    reference's Python binding."""
+    import inspect
+
+    from rembed_b200.embedder import Embedder, load
+
+    params = inspect.signature(load).parameters
+    for opt in ("int8", "int8_activations", "disk_weights", "dim", "workers"):
+        assert opt in params, opt
+    for attr in ("dim", "model", "quantized", "quantized_activations", "close", "__enter__", "__exit__",
+                 "embed", "embed_tokens", "embed_packed", "submit"):
+        assert hasattr(Embedder, attr), attr
