@@ -3,6 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload bge-base-b256xL128] [--mode bf16|f16|int8_w|int8_full|fp32]
+                    [--modes auto|none|m1,m2,...]
 
 N > 1 runs under torchrun, one process per GPU.  Each rank embeds its own
 batch of the workload (data parallel, no collective on the data path:
@@ -11,15 +12,22 @@ batch of the workload (data parallel, no collective on the data path:
 One JSON line on rank 0:
   value     embeddings/s over all ranks, inputs resident in HBM
             (rg_forward_device), K steps bracketed by barrier + sync;
-  e2e       the same through the public host API (rg_forward: host ids in,
-            host embeddings out, copies inside the timed region);
+  e2e       the same through the public host API (rg_submit / rg_collect:
+            host ids in, host embeddings out, copies inside the timed region);
   roofline  the dominant kernel (the tcgen05 GEMMs, 4 per layer), timed
-            live with CUDA events around each launch in a second pass;
-  cpu_baseline  the CPU restatement of the reference forward (oracle/) on a
-            bounded sample of the same workload, all host cores;
-  clocks    nvidia-smi samples taken during the timed region.
-``--impl reference`` times only that CPU path, on rank 0, as the
-reference arm.
+            live with CUDA events around each launch in a second pass,
+            against the burst bf16 peak when the timed region ran at the
+            maximum SM clock (else the sustained one, burst beside it);
+  parity    the timed batch's embeddings (last timed step) against the CPU
+            oracle on its first sequences, with the mode's bar;
+  cpu_baseline  the CPU restatement of the reference forward (oracle/) timed
+            on those same sequences, all host cores;
+  modes     the other numeric modes of the headline metric (f16, weight-only
+            int8, full int8, strict fp32), each with its own value, e2e,
+            roofline, parity and CPU baseline;
+  clocks    NVML samples taken during the timed region.
+``--impl reference`` times only the CPU path, on rank 0, as the reference
+arm.
 """
 
 from __future__ import annotations
@@ -69,6 +77,10 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="bge-base-b256xL128")
     ap.add_argument("--mode", choices=list(MODES), default="bf16")
+    ap.add_argument("--modes", default="auto",
+                    help="further modes measured after --mode, each in a sub-object of the line: a comma list, "
+                         "'none', or 'auto' (every other mode on the headline workload, none elsewhere)")
+    ap.add_argument("--mode-steps", type=int, default=20, help="timed steps of each further mode (at most --steps)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target length of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -102,36 +114,74 @@ def make_inputs(wl, seed, n=None):
 ORACLE_PATH = {"f16": "fp32", "bf16": "fp32", "int8_w": "weight-int8", "int8_full": "full int8", "fp32": "fp32"}
 
 
+def head(ids, cu, n):
+    """The first n sequences of a packed batch."""
+    return ids[: cu[n]], cu[: n + 1]
+
+
+def cosines(a, b):
+    a = a.astype(np.float64)
+    b = b.astype(np.float64)
+    return (a * b).sum(1) / (np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1))
+
+
+PARITY_BARS = {"bf16": "cos >= 0.9999, max-abs <= 2e-3", "f16": "cos >= 0.9999, max-abs <= 2e-3",
+               "fp32": "max-abs <= 1e-4", "int8_w": "cos >= 0.999 (vs the oracle's weight-int8 path)",
+               "int8_full": "cos >= 0.998 (vs the oracle's full-int8 path)"}
+
+
+def parity_ok(mode, cos_min, max_abs):
+    if mode == "fp32":
+        return max_abs <= 1e-4
+    if mode == "int8_w":
+        return cos_min >= 0.999
+    if mode == "int8_full":
+        return cos_min >= 0.998
+    return cos_min >= 0.9999 and max_abs <= 2e-3
+
+
 # ---------------------------------------------------------------------------
-def cpu_sample(wl, mode: str, target_s: float, nthreads: int):
-    """Time the oracle (CPU restatement of the reference forward) on a bounded
-    sample of the workload: one serial forward per sequence across nthreads
-    threads, as the reference's Embed fans out (rembed.go:309-331)."""
+def oracle_on(wl, mode, ids, cu, nthreads):
+    """The oracle (CPU restatement of the reference forward, in the mode's
+    path) on a packed batch, one serial forward per sequence across nthreads
+    threads as the reference's Embed fans out (rembed.go:309-331): (outputs,
+    seconds)."""
     import oracle
     from rembed_b200 import synth
 
     cfg = synth.preset(wl["preset"])
     w = synth.make_weights(cfg, seed=0)
-    quant = getattr(oracle, MODES[mode][1])
-    m = oracle.OracleModel(cfg, w, quant)
-    # calibrate on one sequence per thread
-    _, ids, cu = make_inputs(wl, seed=1, n=nthreads)
+    m = oracle.OracleModel(cfg, w, getattr(oracle, MODES[mode][1]))
     t0 = time.perf_counter()
-    m.embed(ids, cu, nthreads=nthreads)
-    t1 = time.perf_counter() - t0
-    reps = max(1, min(64, int(target_s / max(t1, 1e-3))))
-    n = nthreads * reps
-    _, ids, cu = make_inputs(wl, seed=1, n=n)
-    t0 = time.perf_counter()
-    m.embed(ids, cu, nthreads=nthreads)
+    out = m.embed(ids, cu, nthreads=nthreads)
     dt = time.perf_counter() - t0
     m.close()
-    return {
+    return out, dt
+
+
+def cpu_and_parity(wl, mode, ids, cu, got, target_s, nthreads, timed=True):
+    """Time the oracle on the first n sequences of the timed batch (n sized for
+    about target_s seconds of CPU work, at least 2 per thread) and compare the
+    GPU's embeddings of the same sequences with its outputs."""
+    nseq = len(cu) - 1
+    n0 = min(nseq, nthreads)
+    _, t1 = oracle_on(wl, mode, *head(ids, cu, n0), nthreads)  # calibration
+    per_seq = t1 / n0 * nthreads  # seconds of one thread per sequence
+    n = int(max(min(nseq, 2 * nthreads), min(nseq, target_s / max(per_seq / nthreads, 1e-6))))
+    want, dt = oracle_on(wl, mode, *head(ids, cu, n), nthreads)
+    g = got[:n]
+    cos = cosines(g, want)
+    err = float(np.abs(g.astype(np.float64) - want).max())
+    par = {"n": n, "mode": mode, "min_cos": round(float(cos.min()), 7), "max_abs": float(f"{err:.3g}"),
+           "bar": PARITY_BARS[mode], "ok": bool(parity_ok(mode, float(cos.min()), err)),
+           "against": f"oracle ({ORACLE_PATH[mode]} path) on the first {n} sequences of the timed batch"}
+    cpu = {
         "value": round(n / dt, 3), "unit": "embeddings/s", "cores": nthreads, "kind": "port",
-        "sample": f"{n} sequences of the {wl['preset']} workload (L in [{wl['lo']},{wl['hi']}]), one serial "
-                  f"forward each across {nthreads} threads, {dt:.1f} s; C restatement of the reference "
+        "sample": f"the first {n} sequences of the timed {wl['preset']} batch (L in [{wl['lo']},{wl['hi']}]), one "
+                  f"serial forward each across {nthreads} threads, {dt:.1f} s; C restatement of the reference "
                   f"({ORACLE_PATH[mode]} path), not the Go binary; CPU: {cpu_model()}",
     }
+    return cpu, par
 
 
 def reference_arm(args, rank, world):
@@ -146,14 +196,24 @@ def reference_arm(args, rank, world):
     w = synth.make_weights(cfg, seed=0)
     quant = getattr(oracle, MODES[args.mode][1])
     m = oracle.OracleModel(cfg, w, quant)
-    _, ids, cu = make_inputs(wl, seed=1, n=nth)  # one sequence per thread per step
+    # every step embeds 4 sequences per thread (so that one slow thread does
+    # not set the pace); fewer only if that would take more than ~4 minutes
+    _, ids1, cu1 = make_inputs(wl, seed=1, n=nth)
+    t0 = time.perf_counter()
+    m.embed(ids1, cu1, nthreads=nth)
+    t_one = time.perf_counter() - t0
+    per_thread = 4
+    while per_thread > 1 and t_one * per_thread * (args.steps + args.warmup) > 240.0:
+        per_thread //= 2
+    _, ids, cu = make_inputs(wl, seed=1, n=nth * per_thread)
     for _ in range(args.warmup):
         m.embed(ids, cu, nthreads=nth)
     t0 = time.perf_counter()
     for _ in range(args.steps):
         m.embed(ids, cu, nthreads=nth)
     dt = time.perf_counter() - t0
-    value = nth * args.steps / dt
+    value = nth * per_thread * args.steps / dt
+    path = {"QUANT_NONE": "fp32", "QUANT_WEIGHTS": "weight-int8", "QUANT_FULL": "full-int8"}[MODES[args.mode][1]]
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "embeddings/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -161,11 +221,12 @@ def reference_arm(args, rank, world):
         "vs_baseline": None, "dtype": {"QUANT_NONE": "f32", "QUANT_WEIGHTS": "s8 weights x f32",
                                        "QUANT_FULL": "u8 x s8"}[MODES[args.mode][1]], "data": "synthetic",
         "config": {"workload": args.workload, "global_batch": wl["nseq"], "seq_len": f"{wl['lo']}-{wl['hi']}",
-                   "parallelism": "cpu threads", "mode": args.mode},
+                   "parallelism": "cpu threads", "mode": path,
+                   "compared_with": f"our --mode {args.mode} arm (the reference computes this path in fp32)"},
         "cpu_baseline": {"value": round(value, 3), "unit": "embeddings/s", "cores": nth, "kind": "port",
-                         "sample": f"each step embeds {nth} sequences of the workload, one serial forward per "
-                                   f"sequence per thread; C restatement of the reference forward (Go is not "
-                                   f"installed on this image); CPU: {cpu_model()}"},
+                         "sample": f"each step embeds {nth * per_thread} sequences of the workload ({per_thread} "
+                                   f"per thread), one serial forward per sequence; C restatement of the reference "
+                                   f"forward ({path} path; Go is not installed on this image); CPU: {cpu_model()}"},
         "e2e": {"value": round(value, 3), "unit": "embeddings/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     m.close()
@@ -323,22 +384,34 @@ def committed_traffic(workload: str, mode: str):
         return None
 
 
-def ours(args, rank, world, local_rank):
+def peak_for(mode, peaks, clocks):
+    """(peak TFLOP/s, which, the other fraction's peak or None) for a mode's
+    GEMMs.  The burst cuBLAS figure applies when the timed region ran at the
+    maximum SM clock (a short region, like a kernel timed alone); otherwise
+    the sustained one, with the burst fraction reported beside it."""
+    sm, mx = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
+    at_max = bool(sm and mx and sm >= 0.97 * mx)
+    burst, sust = peaks["bf16_tflops"], peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    # dense int8 runs at 2x the bf16 rate; 3xTF32 makes three passes at the
+    # tf32 rate (half of bf16) for each fp32 product
+    scale = {"int8_full": 2.0, "fp32": 1.0 / 6.0}.get(mode, 1.0)
+    if at_max:
+        return burst * scale, "burst", None
+    return sust * scale, "sustained", burst * scale
+
+
+class Measured:
+    pass
+
+
+def measure_mode(args, mode, wl, cfg, weights, ids, cu, world, local_rank, dist, primary):
+    """value, e2e and the GEMM roofline of one numeric mode on this rank."""
     import torch
 
-    from rembed_b200 import synth
+    from rembed_b200 import ranks
     from rembed_b200.embedder import Embedder
 
-    from rembed_b200 import ranks
-
-    torch.cuda.set_device(local_rank)
-    dist = ranks.init(ranks.RankInfo(rank, world, local_rank), "nccl", device=torch.device("cuda", local_rank))
-    wl = WORKLOADS[args.workload]
-    cfg = synth.preset(wl["preset"])
-    weights = synth.make_weights(cfg, seed=0)
-    emb = Embedder(cfg, weights, devices=[local_rank], **MODES[args.mode][0])
-    del weights
-    _, ids, cu = make_inputs(wl, seed=ranks.batch_seed(rank))
+    emb = Embedder(cfg, weights, devices=[local_rank], **MODES[mode][0])
     nseq, T = len(cu) - 1, int(cu[-1])
     d_ids = torch.from_numpy(ids).cuda()
     d_cu = torch.from_numpy(cu).cuda()
@@ -348,6 +421,7 @@ def ours(args, rank, world, local_rank):
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     assert stream.cuda_stream != 0
+    steps = args.steps if primary else max(3, min(args.steps, args.mode_steps))
 
     def step():
         emb.forward_device(d_ids.data_ptr(), d_cu.data_ptr(), cu, d_out.data_ptr(), stream=stream.cuda_stream)
@@ -356,13 +430,11 @@ def ours(args, rank, world, local_rank):
         ranks.barrier(dist)
         torch.cuda.synchronize()
 
-    def max_over_ranks(x: float) -> float:
-        return ranks.max_over_ranks(dist, x, device="cuda")
-
     for _ in range(max(args.warmup, 1)):
         step()
     emb.sync()
-    launches_per_step = emb.last_launches()
+    r = Measured()
+    r.launches_per_step = emb.last_launches()
 
     # ---- value: device-resident inputs ----
     uuid = None
@@ -375,15 +447,17 @@ def ours(args, rank, world, local_rank):
     barrier()
     with clock_sampler(uuid) as clk:
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             step()
         e1.record(stream)
         torch.cuda.synchronize()
     emb.sync()
     barrier()
-    ms = max_over_ranks(e0.elapsed_time(e1))
-    clocks = clk.summary()
-    value = world * nseq * args.steps / (ms / 1000.0)
+    r.ms = ranks.max_over_ranks(dist, e0.elapsed_time(e1), device="cuda")
+    r.clocks = clk.summary()
+    r.steps = steps
+    r.value = world * nseq * steps / (r.ms / 1000.0)
+    r.out = d_out.cpu().numpy()  # the last timed step's embeddings (parity sample)
 
     # ---- e2e: host buffers through the public API ----
     # Every step stages its ids from host memory into pinned memory, copies
@@ -404,68 +478,130 @@ def ours(args, rank, world, local_rank):
     e2e_steps(3)
     barrier()
     t0 = time.perf_counter()
-    e2e_steps(args.steps)
+    e2e_steps(steps)
     wall = time.perf_counter() - t0
     barrier()
-    e2e_ms = max_over_ranks(1000.0 * wall)
-    e2e_value = world * nseq * args.steps / (e2e_ms / 1000.0)
+    e2e_ms = ranks.max_over_ranks(dist, 1000.0 * wall, device="cuda")
+    r.e2e = {"value": round(world * nseq * steps / (e2e_ms / 1000.0), 2), "unit": "embeddings/s",
+             "h2d_bytes_per_step": int(ids.nbytes + cu.nbytes), "d2h_bytes_per_step": int(host_outs[0].nbytes + 4),
+             "how": "rg_submit/rg_collect from host arrays, wall clock, two batches in flight"}
 
     # ---- roofline: per-kernel-class device time, second pass ----
     emb.profile(True)
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
     stats = emb.profile_stats()
     emb.profile(False)
     peaks, peak_src = measured_peaks()
     g = stats["gemm"]
     total_ms = sum(v["ms"] for v in stats.values())
-    if args.mode == "int8_full":
-        peak = 2.0 * peaks["bf16_tflops_sustained"]
-        peak_note = f"2x {peak_src} sustained bf16 (dense int8 rate is 2x bf16 on B200)"
-    else:
-        peak = peaks["bf16_tflops_sustained"]
-        peak_note = (f"{peak_src} sustained bf16 (kernel timed inside a long forward; fp16 and bf16 share "
-                     f"the kind::f16 tensor rate)")
+    peak, which, other = peak_for(mode, peaks, r.clocks)
     gemm_avg_ms = g["ms"] / max(g["launches"], 1)
     achieved = (g["flops"] / max(g["launches"], 1)) / (gemm_avg_ms / 1000.0) / 1e12
-    traffic = committed_traffic(args.workload, args.mode)
-    roofline = {
+    unit_note = {"int8_full": "TOPS against 2x the bf16 peak (dense int8 rate)",
+                 "fp32": "fp32-equivalent TFLOP/s against the bf16 peak / 6 (3xTF32: three tf32 passes, tf32 at "
+                         "half the bf16 rate)"}.get(mode, "TFLOP/s against the bf16 peak (kind::f16 rate)")
+    r.roofline = {
         "kernel": "tcgen05 GEMM (gemm_kernel), all dense projections",
         "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
-        "frac": round(achieved / peak, 4), "traffic": traffic,
-        "peak_source": peak_note,
+        "frac": round(achieved / peak, 4), "traffic": committed_traffic(args.workload, mode),
+        "peak_source": f"{peak_src} {which} bf16 ({'median SM clock at max' if which == 'burst' else 'SM clock below max'}"
+                       f"); {unit_note}",
         "algorithmic_per_launch": {"flops": g["flops"] / max(g["launches"], 1),
                                    "bytes": g["bytes"] / max(g["launches"], 1)},
         "avg_launch_ms": round(gemm_avg_ms, 4),
+        "timing": "CUDA events around every launch on the library's stream in a second pass (per-launch events "
+                  "break the programmatic-launch overlap, so this pass is slower than the timed one)",
         "share_of_forward": round(g["ms"] / total_ms, 4) if total_ms else None,
-        "kernel_classes": {k: {"ms_per_step": round(v["ms"] / args.steps, 4),
-                               "launches_per_step": v["launches"] // max(args.steps, 1),
+        "kernel_classes": {k: {"ms_per_step": round(v["ms"] / steps, 4),
+                               "launches_per_step": v["launches"] // max(steps, 1),
                                "achieved_tflops": round(v["flops"] / (v["ms"] / 1000) / 1e12, 1) if v["ms"] else 0,
                                "achieved_gbs": round(v["bytes"] / (v["ms"] / 1000) / 1e9, 1) if v["ms"] else 0}
                            for k, v in stats.items() if v["launches"]},
     }
+    if other:
+        r.roofline["frac_of_burst"] = round(achieved / other, 4)
+    pipe = committed_tensor_pipe(args.workload, mode)
+    if pipe:
+        r.roofline["tensor_pipe_pct_ncu"] = pipe
+    r.gemm_tflops_effective = round(g["flops"] / max(steps, 1) / (r.ms / steps / 1000) / 1e12, 1)
+    emb.close()
+    torch.cuda.set_stream(torch.cuda.default_stream())
+    return r
 
+
+def committed_tensor_pipe(workload: str, mode: str):
+    """ncu tensor-pipe utilisation per GEMM of one layer from the committed
+    capture summary (profiles/traffic.json), or None."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text()).get(f"{workload}/{mode}/tensor_pipe_pct")
+    except (ValueError, OSError):
+        return None
+
+
+def ours(args, rank, world, local_rank):
+    import torch
+
+    from rembed_b200 import ranks, synth
+
+    torch.cuda.set_device(local_rank)
+    dist = ranks.init(ranks.RankInfo(rank, world, local_rank), "nccl", device=torch.device("cuda", local_rank))
+    wl = WORKLOADS[args.workload]
+    cfg = synth.preset(wl["preset"])
+    weights = synth.make_weights(cfg, seed=0)
+    _, ids, cu = make_inputs(wl, seed=ranks.batch_seed(rank))
+    nseq, T = len(cu) - 1, int(cu[-1])
+    modes = args.modes
+    if modes == "auto":
+        modes = ",".join(MODES) if args.workload == "bge-base-b256xL128" else "none"
+    extra = [m for m in (modes.split(",") if modes not in ("", "none") else []) if m != args.mode]
+    for m in extra:
+        if m not in MODES:
+            raise SystemExit(f"unknown mode {m}")
+    main_r = measure_mode(args, args.mode, wl, cfg, weights, ids, cu, world, local_rank, dist, primary=True)
+    others = {m: measure_mode(args, m, wl, cfg, weights, ids, cu, world, local_rank, dist, primary=False)
+              for m in extra}
+    del weights
     line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "embeddings/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": MODES[args.mode][2],
+        "metric": METRIC, "value": round(main_r.value, 2), "unit": "embeddings/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(main_r.ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": MODES[args.mode][2],
         "data": "synthetic (seeded random-init weights N(0,0.02) of the named architecture; seeded token ids)",
         "config": {"workload": args.workload, "global_batch": world * nseq, "per_gpu_batch": nseq,
                    "seq_len": f"{wl['lo']}-{wl['hi']}", "tokens_per_gpu_step": T, "parallelism": f"dp{world}",
                    "mode": args.mode,
                    "l2": "no flush: per-step working set (activations ~0.8 GB + weights) exceeds the 126 MB L2"},
-        "roofline": roofline,
-        "e2e": {"value": round(e2e_value, 2), "unit": "embeddings/s",
-                "h2d_bytes_per_step": int(ids.nbytes + cu.nbytes),
-                "d2h_bytes_per_step": int(host_outs[0].nbytes + 4),
-                "how": "rg_submit/rg_collect from host arrays, wall clock, two batches in flight"},
-        "clocks": clocks,
-        "gpu_launches": int(launches_per_step * args.steps),
-        "gemm_tflops_effective": round(g["flops"] / max(args.steps, 1) / (ms / args.steps / 1000) / 1e12, 1),
+        "roofline": main_r.roofline,
+        "e2e": main_r.e2e,
+        "clocks": main_r.clocks,
+        "gpu_launches": int(main_r.launches_per_step * args.steps),
+        "gemm_tflops_effective": main_r.gemm_tflops_effective,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_sample(wl, args.mode, args.cpu_seconds, host_threads())
-    emb.close()
+    if rank == 0 and not args.no_cpu_baseline:
+        nth = host_threads()
+        cpu, par = cpu_and_parity(wl, args.mode, ids, cu, main_r.out, args.cpu_seconds, nth)
+        line["parity"] = par
+        if world == 1:
+            line["cpu_baseline"] = cpu
+    if others:
+        line["modes"] = {}
+        for m, r in others.items():
+            sub = {"value": round(r.value, 2), "unit": "embeddings/s", "ms_per_step": round(r.ms / r.steps, 4),
+                   "steps": r.steps, "dtype": MODES[m][2], "e2e": r.e2e, "roofline": {
+                       k: r.roofline[k] for k in ("achieved", "peak", "unit", "frac", "frac_of_burst", "peak_source",
+                                                  "avg_launch_ms", "share_of_forward", "kernel_classes",
+                                                  "traffic", "tensor_pipe_pct_ncu") if k in r.roofline},
+                   "clocks": {k: r.clocks.get(k) for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+                   "gpu_launches": int(r.launches_per_step * r.steps)}
+            if rank == 0 and not args.no_cpu_baseline:
+                cpu, par = cpu_and_parity(wl, m, ids, cu, r.out, args.cpu_seconds / 4, host_threads())
+                sub["parity"] = par
+                if world == 1:
+                    sub["cpu_baseline"] = cpu
+            line["modes"][m] = sub
     ranks.finish(dist)
     if rank == 0:
         print(json.dumps(line), flush=True)

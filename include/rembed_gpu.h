@@ -159,6 +159,24 @@ int rg_profile_stats(rg_ctx *ctx, int dev_index, int kernel_class, double *ms, i
 void rg_free(rg_ctx *ctx);
 void rg_free_string(char *s);
 
+/* Failure injection for tests of the error paths (never needed in
+ * production; nothing is injected unless this is called).  Each injection
+ * fires once:
+ *   RG_INJECT_GEMM_WAIT (ctx may be NULL): the next rg_dense_bf16 launch
+ *     withholds one of its pipeline's barrier arrivals and bounds every wait
+ *     at `arg` cycles, so the wait runs out on the device; the kernel stops,
+ *     drains what is in flight, frees its tensor memory and records the
+ *     timeout, which the next rg_kernel_status reports;
+ *   RG_INJECT_HOST_ALLOC: the next submission on ctx fails as if its pinned
+ *     host staging could not be allocated;
+ *   RG_INJECT_REPLICA: the next submission on ctx fails in the worker of
+ *     replica `arg` (an index into rg_init's device list) after the replicas
+ *     before it have started; their work is collected and the call returns
+ *     the worker's error.
+ * Returns 0, or -1 for an unknown injection or a bad argument. */
+enum { RG_INJECT_GEMM_WAIT = 1, RG_INJECT_HOST_ALLOC = 2, RG_INJECT_REPLICA = 3 };
+int rg_test_inject(rg_ctx *ctx, int what, long long arg, char **err);
+
 /* ---- kernel-level entry points (parity tests, benchmarks) --------------
  * Device pointers on the current CUDA device; stream = cudaStream_t or NULL.
  *
@@ -169,6 +187,15 @@ void rg_free_string(char *s);
  * K must be a multiple of 64, N of 128 (checked). */
 int rg_dense_bf16(const void *x, const void *w, const float *bias, const float *residual, void *y,
                   int M, int N, int K, int epilogue, void *stream, char **err);
+
+/* Every kernel-level call below is asynchronous.  A failure a kernel
+ * detects on the device (a bounded pipeline wait that gave up, an fp16
+ * output overflow) sets a bit in a status word of the device instead of
+ * hanging or aborting; rg_kernel_status synchronises `stream`, reads and
+ * clears the status words of the current device (the kernel-level calls'
+ * and the no-allocation variant's) and returns -1 with a message if a
+ * failure was recorded since the last check. */
+int rg_kernel_status(void *stream, char **err);
 
 /* rg_dense_residual_layernorm_bf16: the post-attention / post-FFN sublayer
  * of the BERT family (applyDense + Add + LayerNorm, bert.go:905-907 and
@@ -184,21 +211,55 @@ int rg_dense_residual_layernorm_bf16(const void *x, const void *w, const float *
 
 /* rg_dense_residual_layernorm_bf16_noalloc: no counterpart in the reference.
  * The same sublayer as rg_dense_residual_layernorm_bf16, for callers that
- * must not allocate device memory (code running while a stream is captured
- * into a CUDA graph, or a host whose memory manager owns all device
- * allocations).  It calls no allocator: its scratch is a fixed static device
- * array of RG_NOALLOC_SCRATCH_FLOATS floats (16 MiB) that the library image
- * holds on every GPU where the library is loaded, until process exit.
+ * cannot let a library call cudaMalloc: a host whose memory manager owns
+ * every byte of device memory (an arena carved out of HBM up front, or an
+ * allocator that must account for each buffer), or a latency-bound caller
+ * that cannot afford the device synchronisation an allocation may bring.
+ * It calls no allocator: its scratch is a fixed static device array of
+ * RG_NOALLOC_SCRATCH_FLOATS floats (16 MiB) that the library image holds on
+ * every GPU where the library is loaded, until process exit.
  * Limit: M * N <= RG_NOALLOC_SCRATCH_FLOATS (larger calls fail with an
  * error naming the limit).  The first call on each device looks up the
- * array's device address; make that first call before any stream capture.
+ * array's device address (in the device's primary context, the one the CUDA
+ * runtime API uses); make that first call before any stream capture.
  * All calls share the array: calls that overlap on the GPU race; order them
- * on one stream. */
+ * on one stream.  An in-kernel failure is reported by rg_kernel_status. */
 #define RG_NOALLOC_SCRATCH_FLOATS ((size_t)4 * 1024 * 1024)
 int rg_dense_residual_layernorm_bf16_noalloc(const void *x, const void *w, const float *bias,
                                              const float *residual, const float *gamma, const float *beta,
                                              float eps, float *out32, void *outb, int M, int N, int K,
                                              void *stream, char **err);
+
+/* rg_attention: the attention core of encodeWorkers and of the per-arch
+ * encoders (bert.go:853-902, modernbert.go:239-281, gemma3.go:303-354) and
+ * flashAttnCausalHead (qwen3.go:307-390) over a packed batch, as one fused
+ * kernel.  q [T x ldq], k [T x ldk], v [T x ldv]: token-major rows, query
+ * head h at columns h*head_dim, key/value head h / (heads / kv_heads) (GQA).
+ * cu_seqlens [nseq+1] are device offsets; host_cu the same offsets in host
+ * memory (shapes only).  Query i attends to keys j of its own sequence with
+ * rel_lo <= j - i <= rel_hi (causal: rel_hi = 0; window w: +-w; unbounded:
+ * +-2^30), scores scaled by `scale`.  dtype RG_DTYPE_BF16 / RG_DTYPE_F16:
+ * the tcgen05 kernel, out 16-bit [T x ldo]; RG_DTYPE_F32: the strict fp32
+ * kernel, q/k/v/out fp32.  Head dims 32, 64, 128, 256. */
+int rg_attention(const void *q, const void *k, const void *v, int ldq, int ldk, int ldv, const int32_t *cu_seqlens,
+                 const int32_t *host_cu, int nseq, int heads, int kv_heads, int head_dim, float scale, int rel_lo,
+                 int rel_hi, int dtype, void *out, int ldo, void *stream, char **err);
+
+/* rg_quantize_rows_s8: the full-int8 mode's per-row activation quantiser,
+ * QuantizeRowU8 (pack_vnni.go:85-117) with the +128 offset removed:
+ * scale[r] = maxabs(x[r]) / 127 (1 for an all-zero row), q = clamp(
+ * RoundToEven(x * (1 / scale)), -128, 127).  x bf16 [M x K], K % 8 == 0,
+ * K <= 4096. */
+int rg_quantize_rows_s8(const void *x, int M, int K, int8_t *q, float *row_scale, void *stream, char **err);
+
+/* rg_dense_s8: the full-int8 projection, MatMulPackedVNNI + AddBias
+ * (pack_vnni.go:124-176, bert.go:297-300) on tcgen05 kind::i8:
+ * y[M x N] = f32(sum_k xq[m][k] * wq[n][k]) * row_scale[m] * col_scale[n]
+ * (+ bias[n]), the integer sum exact (it equals the reference's
+ * acc - 128 * colSum).  xq [M x K], wq [N x K] int8 (PackB8VNNI weights);
+ * K % 128 == 0, N % 128 == 0; y fp32. */
+int rg_dense_s8(const int8_t *xq, const float *row_scale, const int8_t *wq, const float *col_scale, const float *bias,
+                float *y, int M, int N, int K, void *stream, char **err);
 
 #ifdef __cplusplus
 }

@@ -77,6 +77,8 @@ def lib() -> ctypes.CDLL:
         L.or_model_finalize.argtypes = [ctypes.c_void_p, ctypes.c_char_p]
         L.or_model_free.restype = None
         L.or_model_free.argtypes = [ctypes.c_void_p]
+        L.or_flash_attn_causal_head.restype = ctypes.c_int
+        L.or_flash_attn_causal_head.argtypes = [f32p, f32p, f32p, f32p, ctypes.c_int, ctypes.c_int, ctypes.c_float]
         L.or_embed_batch.restype = ctypes.c_int
         L.or_embed_batch.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64),
                                      ctypes.POINTER(ctypes.c_int32), ctypes.c_int, ctypes.c_int,
@@ -221,6 +223,18 @@ def matmul_vnni(a, q, colsum, scales, m, k, n):
                          _p(np.ascontiguousarray(scales, dtype=np.float32)),
                          ctypes.c_int(m), ctypes.c_int(k), ctypes.c_int(n))
     return dst
+
+
+def flash_attn_causal_head(q, k, v, scale):
+    """flashAttnCausalHead (qwen3.go:307-390) on one head: q, k, v [seq x dh]."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    k = np.ascontiguousarray(k, dtype=np.float32)
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    seq, dh = q.shape
+    out = np.zeros((seq, dh), dtype=np.float32)
+    if lib().or_flash_attn_causal_head(_p(q), _p(k), _p(v), _p(out), seq, dh, float(scale)) != 0:
+        raise OracleError("flash attention scratch allocation failed")
+    return out
 
 
 # ---- model ----------------------------------------------------------------

@@ -58,6 +58,12 @@ float or_quantize_row_u8(uint8_t *dst, const float *a, int k, int kpad);
 void or_matmul_vnni(float *dst, const float *a, const int8_t *q, const int32_t *colsum,
                     const float *scales, int m, int k, int n);
 
+/* flashAttnCausalHead (qwen3.go:307-390): one head, q/k/v/out [seq x dh],
+ * 64-row blocks with online softmax and future key blocks skipped.
+ * Returns 0 or -1 (no scratch). */
+int or_flash_attn_causal_head(const float *qH, const float *kH, const float *vH, float *out, int seq, int dh,
+                              float scale);
+
 /* ---- model ---------------------------------------------------------- */
 enum { OR_ARCH_BERT = 0, OR_ARCH_DISTILBERT = 1, OR_ARCH_ROBERTA = 2, OR_ARCH_MPNET = 3,
        OR_ARCH_MODERNBERT = 4, OR_ARCH_QWEN3 = 5, OR_ARCH_GEMMA3 = 6, OR_ARCH_NOMIC = 7 };

@@ -623,6 +623,28 @@ static void flash_attn_causal_head(const float *qH, const float *kH, const float
     }
 }
 
+/* Exported form of flash_attn_causal_head with its own scratch, so the
+ * reference's TestFlashAttnCausalHead (qwen3_test.go:15-80) can pin it
+ * against a naive softmax.  Returns 0, or -1 if scratch cannot be had. */
+int or_flash_attn_causal_head(const float *qH, const float *kH, const float *vH, float *out, int seq, int dh,
+                              float scale) {
+    int bq = seq < FLASH_BLK ? seq : FLASH_BLK;
+    float *sblk = malloc(sizeof(float) * (size_t)bq * bq);
+    float *acc = malloc(sizeof(float) * (size_t)bq * dh);
+    float *mrow = malloc(sizeof(float) * (size_t)bq);
+    float *lrow = malloc(sizeof(float) * (size_t)bq);
+    int rc = -1;
+    if (sblk && acc && mrow && lrow) {
+        flash_attn_causal_head(qH, kH, vH, out, seq, dh, scale, sblk, acc, mrow, lrow);
+        rc = 0;
+    }
+    free(sblk);
+    free(acc);
+    free(mrow);
+    free(lrow);
+    return rc;
+}
+
 /* Full-score attention of one head with a bidirectional window (the
  * ModernBERT / Gemma / nomic pattern: MatMulSerial, scale, mask, Softmax,
  * MatMulSerial). window_kind: 0 none; 1 |i-j| <= w (modernbert.go:268-274);

@@ -24,7 +24,8 @@ BUILD = PKG / "_build"
 LIB = PKG / "librembed_gpu.so"
 INCLUDE = PKG.parent / "include"
 SOURCES = ["gemm.cu", "gemm_kind_bf16.cu", "gemm_kind_s8.cu", "gemm_kind_f16.cu", "gemm_kind_w8.cu",
-           "gemm_kind_tf32x3.cu", "kernels.cu", "attention_tc.cu", "runtime.cu", "noalloc.cu"]
+           "gemm_kind_tf32x3.cu", "kernels.cu", "attention_tc.cu", "runtime.cu", "noalloc.cu",
+           "kernel_abi.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "--expt-relaxed-constexpr", f"-I{INCLUDE}"]

@@ -53,6 +53,13 @@ struct GemmArgs {
     uint16_t* out16;
     int ld16;
     float2* parts_out;
+    // Failure injection for tests (zero in production): wait_limit > 0
+    // bounds every mbarrier wait of the launch at that many cycles instead of
+    // about a second, and inject_withhold makes the even CTA of every pair
+    // withhold its arrival on the first k-block of its first tile, so the
+    // MMA issuer's wait runs out and the launch ends with kStatusWaitTimeout.
+    long long wait_limit;
+    int inject_withhold;
 };
 
 // Operand element kind of the GEMM.

@@ -218,6 +218,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int num_tiles = m_tiles * n_tiles;
     const int kb_real = args.K / K_ELEMS;
     const int kblocks = X3 ? 3 * kb_real : kb_real;
+    const long long wlim = args.wait_limit > 0 ? args.wait_limit : kWaitLimitCycles;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -271,13 +272,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
             bool ok = true;
             for (int kb = 0; kb < kblocks; ++kb) {
-                if (!mbar_wait(&empty[stage], phase ^ 1, args.status, abort_flag)) {
+                if (!mbar_wait(&empty[stage], phase ^ 1, args.status, abort_flag, wlim)) {
                     ok = false;
                     break;
                 }
                 // Both CTAs' loads complete on the even CTA's barrier, which
                 // expects the bytes of both.
-                if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (A_BYTES + (W8 ? 0 : B_BYTES)));
+                const bool withhold = args.inject_withhold && tile == pair && kb == 0;
+                if (rank == 0 && !withhold) mbar_arrive_expect_tx(&full[stage], 2 * (A_BYTES + (W8 ? 0 : B_BYTES)));
                 // 3xTF32: segment 0 = (A_hi, W_hi), 1 = (A_hi, W_lo), 2 = (A_lo, W_hi)
                 const int seg = X3 ? kb / kb_real : 0;
                 const int kx = (X3 ? kb - seg * kb_real : kb) * K_ELEMS;
@@ -304,8 +306,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // each CTA sees its own int8 W loads land.
         for (int s = 0; s < STAGES; ++s) {
             if (!(issued_mask & (1u << s))) continue;
-            if (rank == 0) mbar_drain(&full[s], (issued_parity >> s) & 1);
-            if constexpr (W8) mbar_drain(&wfull[s], (issued_parity >> s) & 1);
+            if (rank == 0) mbar_drain(&full[s], (issued_parity >> s) & 1, wlim);
+            if constexpr (W8) mbar_drain(&wfull[s], (issued_parity >> s) & 1, wlim);
         }
     } else if (W8 && (warp == 2 || warp == 3)) {
         // ---------------- int8 -> fp16 converters (kW8, both CTAs) ----------------
@@ -320,7 +322,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
             for (int kb = 0; kb < kblocks; ++kb) {
-                if (!mbar_wait(&wfull[stage], phase, args.status, abort_flag)) {
+                if (!mbar_wait(&wfull[stage], phase, args.status, abort_flag, wlim)) {
                     ok = false;
                     break;
                 }
@@ -359,13 +361,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         uint32_t acc_phase = 0;
         bool issued = false;
         for (int tile = pair; tile < num_tiles; tile += npairs) {
-            if (!mbar_wait(&tempty[acc], acc_phase ^ 1, args.status, abort_flag)) break;
+            if (!mbar_wait(&tempty[acc], acc_phase ^ 1, args.status, abort_flag, wlim)) break;
             tc_fence_after();
             const uint32_t d = tmem_base + acc * BN;
             bool ok = true;
             for (int kb = 0; kb < kblocks; ++kb) {
-                if (!mbar_wait(&full[stage], phase, args.status, abort_flag) ||
-                    (W8 && !mbar_wait(&cfull[stage], phase, args.status, abort_flag))) {
+                if (!mbar_wait(&full[stage], phase, args.status, abort_flag, wlim) ||
+                    (W8 && !mbar_wait(&cfull[stage], phase, args.status, abort_flag, wlim))) {
                     ok = false;
                     break;
                 }
@@ -399,7 +401,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         if (issued) {
             umma_commit_pair(smem_u32(drain));
-            mbar_drain(drain, 0);
+            mbar_drain(drain, 0, wlim);
         }
     } else if (warp >= 4) {
         // ---------------- epilogue (both CTAs, own 128 rows) ----------------
@@ -457,7 +459,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     fnm = -st.x * st.y;
                 }
             }
-            if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag)) break;
+            if (!mbar_wait(&tfull[acc], acc_phase, args.status, abort_flag, wlim)) break;
             tc_fence_after();
             const uint32_t taddr =
                 tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + half * HALF;
@@ -601,7 +603,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     for (int i = 0; i < 32; i += 2) gelu_as2(v[i], v[i + 1]);
                 }
                 if constexpr (RES) {
-                    if (!mbar_wait(&rbar[b], (rphase >> b) & 1, args.status, abort_flag)) {
+                    if (!mbar_wait(&rbar[b], (rphase >> b) & 1, args.status, abort_flag, wlim)) {
                         ok = false;
                         break;
                     }
@@ -701,7 +703,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             bulk_wait_read<0>();
             for (int b = 0; b < 2; ++b)
-                if (rpending & (1u << b)) mbar_drain(&rbar[b], (rphase >> b) & 1);
+                if (rpending & (1u << b)) mbar_drain(&rbar[b], (rphase >> b) & 1, wlim);
         }
         __syncwarp();
     }

@@ -872,6 +872,11 @@ __global__ void __launch_bounds__(256) attention_f32_kernel(AttnF32Params p) {
         if (r >= nrow) continue;
         const float inv = l[i] > 0.f ? 1.0f / l[i] : 0.f;
         float* oh = p.out_hi + static_cast<int64_t>(s0 + q0 + r) * p.ldo + h * D;
+        if (!p.out_lo) {  // the unsplit fp32 result (kernel-level entry point)
+#pragma unroll
+            for (int c = 0; c < NC; ++c) oh[cg + 16 * c] = o[i][c] * inv;
+            continue;
+        }
         float* ol = p.out_lo + static_cast<int64_t>(s0 + q0 + r) * p.ldo + h * D;
 #pragma unroll
         for (int c = 0; c < NC; ++c) {

@@ -163,12 +163,16 @@ struct AttnF32Params {
     int rel_lo, rel_hi;
     const float* bias;
     int bias_off;
-    float *out_hi, *out_lo;
+    float *out_hi, *out_lo;  // out_lo nullptr: out_hi receives the unsplit fp32 result
     int ldo;
 };
 cudaError_t launch_attention_f32(const AttnF32Params& p, int nseq, int max_len, int heads, int head_dim,
                                  cudaStream_t st);
 
+
+// The status word the kernel-level C ABI entry points pass to their kernels
+// (one per device, allocated on first use; read by rg_kernel_status).
+cudaError_t kernel_status_word(int dev, int** out);
 
 // Pooling + L2 + Matryoshka truncation (bert.go:657-703, rembed.go:441-448):
 // out[nseq x dim].

@@ -1,12 +1,14 @@
 // noalloc.cu - rg_dense_residual_layernorm_bf16_noalloc: the dense +
 // residual + LayerNorm sublayer without any device allocation.
 //
-// Who needs it: callers that must not call cudaMalloc, for example code
-// that runs while a CUDA stream is being captured into a graph (an
-// allocation there fails the capture or synchronises the device), or a
-// host whose memory manager owns every device allocation and forbids
-// others.  rg_dense_residual_layernorm_bf16 allocates its scratch on first
-// use per device and grows it as needed; this variant never does.
+// Who needs it: callers that cannot call cudaMalloc.  A host whose memory
+// manager owns every byte of device memory (a serving runtime that carves
+// all of HBM into its own arena up front, or an allocator that must
+// account for each buffer) cannot let a library allocate behind its back,
+// and cudaMalloc may also synchronise the device, which a caller running a
+// latency-bound pipeline must avoid.  rg_dense_residual_layernorm_bf16
+// allocates its scratch on first use per device and grows it as needed;
+// this variant never does.
 //
 // Where the scratch lives: g_noalloc_scratch, a file-scope static device
 // array of RG_NOALLOC_SCRATCH_FLOATS floats plus a 256-byte header (one
@@ -18,11 +20,14 @@
 // to the kernels.
 //
 // Sharing: every call uses the same array and it keeps the last call's
-// contents.  The status word is cleared at the start of every call; the
-// fp32 sum region is fully overwritten by the GEMM before the LayerNorm
-// reads it.  Calls whose work overlaps on the GPU (different streams, or
-// different host threads, on one device) race on the array: order them on
-// one stream.
+// contents.  The fp32 sum region is fully overwritten by the GEMM before the
+// LayerNorm reads it, so it needs no clearing.  The status word starts at
+// zero when the module loads; a kernel that fails (a bounded pipeline wait
+// that gave up) sets a bit in it, and rg_kernel_status reads and clears it
+// (noalloc_status_take below, which copies through the symbol and so
+// allocates nothing either).  Calls whose work overlaps on the GPU
+// (different streams, or different host threads, on one device) race on the
+// array: order them on one stream.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -119,10 +124,8 @@ extern "C" int rg_dense_residual_layernorm_bf16_noalloc(const void* x, const voi
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return set_err(err, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    int* status = reinterpret_cast<int*>(base);
+    int* status = reinterpret_cast<int*>(base);  // sticky until rg_kernel_status clears it
     float* sum = base + kHeaderFloats;
-    e = cudaMemsetAsync(status, 0, sizeof(int), st);  // the only part that must start at zero
-    if (e != cudaSuccess) return set_err(err, "cudaMemsetAsync: %s", cudaGetErrorString(e));
 
     CUtensorMap ta, tb;
     const int bn = rg::gemm_block_n(M, N, sms);
@@ -139,7 +142,22 @@ extern "C" int rg_dense_residual_layernorm_bf16_noalloc(const void* x, const voi
     a.status = status;
     e = rg::gemm_launch(rg::GemmKind::kBF16, rg::kEpiBiasRes, bn, ta, tb, a, sms, st);
     if (e != cudaSuccess) return set_err(err, "gemm launch: %s", cudaGetErrorString(e));
-    e = rg::launch_ln(sum, gamma, beta, eps, M, N, out32, static_cast<uint16_t*>(outb), false, nullptr, nullptr, st);
+    e = rg::launch_ln(sum, gamma, beta, eps, M, N, out32, static_cast<uint16_t*>(outb), false, nullptr, nullptr, st,
+                      status);
     if (e != cudaSuccess) return set_err(err, "ln launch: %s", cudaGetErrorString(e));
     return 0;
 }
+
+namespace rg {
+
+// Read and clear the status word at the head of g_noalloc_scratch on the
+// current device (synchronous copies through the symbol; no allocation).
+cudaError_t noalloc_status_take(int* s) {
+    *s = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(s, g_noalloc_scratch, sizeof(int), 0, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess || *s == 0) return e;
+    const int zero = 0;
+    return cudaMemcpyToSymbol(g_noalloc_scratch, &zero, sizeof(int), 0, cudaMemcpyHostToDevice);
+}
+
+}  // namespace rg

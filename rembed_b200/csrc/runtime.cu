@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <array>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -156,8 +158,10 @@ struct Replica {
         size_t cap_ids = 0, cap_cu = 0, cap_out = 0;
         cudaEvent_t done = nullptr;  // recorded after the slot's D2H copies
         bool busy = false;           // submitted, not yet collected
-        float* user_out = nullptr;   // where rg_collect copies the slot's result
-        size_t nout = 0;
+        float* user_out = nullptr;   // the caller's output buffer
+        // where rg_collect copies the slot's result: (offset in user_out,
+        // offset in out, floats), one entry per run of consecutive sequences
+        std::vector<std::array<size_t, 3>> copies;
     };
     Staging stage[2];
     OpMaps tm_x, tm_ctx, tm_ffh;
@@ -215,9 +219,19 @@ struct rg_ctx {
     std::condition_variable tcv;  // a slot became free
     int64_t next_ticket = 0;
     int64_t pending[2] = {-1, -1};
+    // failure injection for tests (rg_test_inject): the next submission's
+    // host staging fails as an allocation failure would; replica
+    // inject_replica fails its next shard submission
+    bool inject_alloc = false;
+    int inject_replica = -1;
 };
 
 constexpr int64_t kSlotFree = -1, kSlotCollecting = -2;
+
+// rg_test_inject(RG_INJECT_GEMM_WAIT): the wait limit (cycles) of the next
+// kernel-level rg_dense_bf16 launch, which withholds one pipeline arrival
+// (0: none pending).
+std::atomic<long long> g_inject_gemm_wait{0};
 
 namespace {
 
@@ -1536,26 +1550,53 @@ void run_graphed(Replica& r, cudaStream_t st, const Replica::GraphKey& key, F&& 
     check(cudaGraphLaunch(ge, st), "cudaGraphLaunch");
 }
 
-// Stage sequences [s_lo, s_hi) of a host batch in staging slot `slot` of
-// replica r and enqueue pinned H2D -> forward -> D2H on its stream (a graph
-// per repeated shape); the result is copied to host_out at collect time.
-void submit_shard(rg_ctx* c, Replica& r, int slot, const int64_t* ids, const int32_t* cu, int s_lo, int s_hi,
+// Stage the sequences `seqs` (ascending indices into a host batch) in
+// staging slot `slot` of replica r, packed in that order, and enqueue pinned
+// H2D -> forward -> D2H on its stream (a graph per repeated shape); each
+// sequence's result is copied to its own place in host_out at collect time.
+void submit_shard(rg_ctx* c, Replica& r, int slot, const int64_t* ids, const int32_t* cu, const std::vector<int>& seqs,
                   int out_kind, int out_dim, float* host_out) {
     std::lock_guard<std::mutex> lk(r.mu);
     check(cudaSetDevice(r.device), "cudaSetDevice");
-    const int nseq = s_hi - s_lo;
+    const int nseq = static_cast<int>(seqs.size());
     if (nseq <= 0) return;
     Replica::Staging& sg = r.stage[slot];
     if (sg.busy) fail("rembed: staging slot %d is still in flight (collect the oldest submission first)", slot);
-    const int t0 = cu[s_lo], T = cu[s_hi] - t0;
+    int T = 0;
+    for (int s : seqs) T += cu[s + 1] - cu[s];
     const int H = c->d.hidden_size;
     const size_t nout = out_kind == RG_OUT_POOLED ? static_cast<size_t>(nseq) * out_dim : static_cast<size_t>(T) * H;
     ensure_workspace(c, r, T, nseq, nout);
+    if (c->inject_alloc) {
+        c->inject_alloc = false;
+        fail("cudaMallocHost: out of memory (injected failure of the host staging allocation)");
+    }
     ensure_host_staging(r, sg, T, nseq + 1, nout);
-    int max_len = 0;
-    for (int i = 0; i <= nseq; ++i) sg.cu[i] = cu[s_lo + i] - t0;
-    for (int i = 0; i < nseq; ++i) max_len = std::max(max_len, sg.cu[i + 1] - sg.cu[i]);
-    memcpy(sg.ids, ids + t0, sizeof(int64_t) * T);
+    // pack the sequences; runs of consecutive sequences copy in one piece
+    const size_t row = out_kind == RG_OUT_POOLED ? static_cast<size_t>(out_dim) : static_cast<size_t>(H);
+    sg.copies.clear();
+    int max_len = 0, t = 0;
+    sg.cu[0] = 0;
+    for (int i = 0; i < nseq;) {
+        int j = i + 1;
+        while (j < nseq && seqs[j] == seqs[j - 1] + 1) ++j;
+        const int a = seqs[i], b = seqs[j - 1] + 1;  // global sequences [a, b)
+        const int n_tok = cu[b] - cu[a];
+        memcpy(sg.ids + t, ids + cu[a], sizeof(int64_t) * n_tok);
+        for (int k = i; k < j; ++k) {
+            const int len = cu[seqs[k] + 1] - cu[seqs[k]];
+            sg.cu[k + 1] = sg.cu[k] + len;
+            max_len = std::max(max_len, len);
+        }
+        if (out_kind == RG_OUT_POOLED)
+            sg.copies.push_back({static_cast<size_t>(a) * row, static_cast<size_t>(i) * row,
+                                 static_cast<size_t>(j - i) * row});
+        else
+            sg.copies.push_back({static_cast<size_t>(cu[a]) * row, static_cast<size_t>(t) * row,
+                                 static_cast<size_t>(n_tok) * row});
+        t += n_tok;
+        i = j;
+    }
     cudaStream_t st = r.stream;
     r.h_cu_view = sg.cu;
     // pinned staging -> device, the forward, device -> pinned staging: one
@@ -1572,9 +1613,7 @@ void submit_shard(rg_ctx* c, Replica& r, int slot, const int64_t* ids, const int
     r.h_cu_view = nullptr;
     check(cudaEventRecord(sg.done, st), "cudaEventRecord");
     sg.busy = true;
-    sg.user_out = host_out + (out_kind == RG_OUT_POOLED ? static_cast<size_t>(s_lo) * out_dim
-                                                        : static_cast<size_t>(t0) * H);
-    sg.nout = nout;
+    sg.user_out = host_out;
 }
 
 // Wait for replica r's slot and copy its result out (no-op if idle).
@@ -1586,37 +1625,65 @@ void collect_shard(Replica& r, int slot) {
     sg.busy = false;
     check(cudaEventSynchronize(sg.done), "forward");
     if (*sg.status != 0) fail("rembed: %s", status_message(*sg.status).c_str());
-    memcpy(sg.user_out, sg.out, sizeof(float) * sg.nout);
+    for (const auto& cp : sg.copies) memcpy(sg.user_out + cp[0], sg.out + cp[1], sizeof(float) * cp[2]);
 }
 
-void run_host_shard(rg_ctx* c, Replica& r, int slot, const int64_t* ids, const int32_t* cu, int s_lo, int s_hi,
-                    int out_kind, int out_dim, float* host_out) {
-    submit_shard(c, r, slot, ids, cu, s_lo, s_hi, out_kind, out_dim, host_out);
-    collect_shard(r, slot);
+// Estimated FLOPs of one sequence of length L through the whole stack: the
+// dense projections of every layer (fused Q|K|V with grouped K/V heads, the
+// output projection, a gated FFN at twice its intermediate width) and each
+// layer's attention over the (query, key) pairs its mask allows (causal or
+// windowed layers see fewer), plus the Gemma Dense head.
+double seq_cost(const rg_model_desc& d, const std::vector<DevLayer>& layers, int L) {
+    const Dims m = dims(d);
+    const double H = m.H, I = m.I;
+    const double lin = 2.0 * L * (H * m.nqkv + m.qd * H + H * I * (is_glu(d.arch) ? 2.0 : 1.0) + I * H);
+    double cost = lin * d.num_hidden_layers;
+    const int32_t one[2] = {0, L};
+    for (const DevLayer& ly : layers) {
+        int lo, hi;
+        layer_window(d, ly, &lo, &hi);
+        cost += 4.0 * m.dh * m.nq * attn_pairs(one, 1, lo, hi);
+    }
+    if (d.arch == RG_ARCH_GEMMA3) cost += 4.0 * H * d.dense_hidden;
+    return cost;
 }
 
-// Contiguous shards with near-equal estimated cost (linear + quadratic
-// attention term), so outputs land in order in the caller's buffer.
-std::vector<int> shard_bounds(const rg_model_desc& d, const int32_t* cu, int nseq, int nrep) {
-    std::vector<double> cost(nseq + 1, 0.0);
-    const double H = d.hidden_size;
+// Sequences over replicas by the greedy longest-processing-time rule: in
+// order of decreasing estimated cost (ties: lower index first), each to the
+// replica with the smallest total so far (ties: lower replica).  Each
+// replica's list is returned in ascending sequence order.  Every sequence's
+// output is independent of which replica runs it and of its batch mates, so
+// any assignment gives the same embeddings bit for bit.
+std::vector<std::vector<int>> lpt_assign(const rg_model_desc& d, const std::vector<DevLayer>& layers,
+                                         const int32_t* cu, int nseq, int nrep) {
+    std::vector<std::vector<int>> out(nrep);
+    if (nrep == 1) {
+        out[0].resize(nseq);
+        for (int i = 0; i < nseq; ++i) out[0][i] = i;
+        return out;
+    }
+    std::vector<std::pair<double, int>> order(nseq);
+    std::map<int, double> by_len;  // cost of each distinct length, computed once
     for (int i = 0; i < nseq; ++i) {
-        const double L = cu[i + 1] - cu[i];
-        cost[i + 1] = cost[i] + L * (12.0 * H * H) + 2.0 * L * L * H;
+        const int L = cu[i + 1] - cu[i];
+        auto it = by_len.find(L);
+        if (it == by_len.end()) it = by_len.emplace(L, seq_cost(d, layers, L)).first;
+        order[i] = {it->second, i};
     }
-    std::vector<int> b(nrep + 1, nseq);
-    b[0] = 0;
-    int s = 0;
-    for (int k = 1; k < nrep; ++k) {
-        const double target = cost[nseq] * k / nrep;
-        while (s < nseq && cost[s] < target) ++s;
-        b[k] = s;
+    std::stable_sort(order.begin(), order.end(),
+                     [](const std::pair<double, int>& a, const std::pair<double, int>& b) { return a.first > b.first; });
+    std::vector<double> load(nrep, 0.0);
+    for (const auto& o : order) {
+        const int k = static_cast<int>(std::min_element(load.begin(), load.end()) - load.begin());
+        load[k] += o.first;
+        out[k].push_back(o.second);
     }
-    return b;
+    for (auto& v : out) std::sort(v.begin(), v.end());
+    return out;
 }
 
-// Submit a validated host batch: split over the replicas (contiguous,
-// cost-balanced shards) and staged in slot ticket % 2 of each.
+// Submit a validated host batch: split over the replicas (lpt_assign) and
+// staged in slot ticket % 2 of each.
 // wait_for_slot: the synchronous rg_forward waits for another thread to
 // collect the slot it needs; rg_submit (whose caller may hold both
 // outstanding tickets itself) reports the limit instead.
@@ -1635,10 +1702,16 @@ int64_t submit_batch(rg_ctx* c, const int64_t* ids, const int32_t* cu, int nseq,
     const int64_t t = c->next_ticket;
     const int slot = static_cast<int>(t & 1);
     const int nrep = static_cast<int>(c->reps.size());
-    const std::vector<int> b = nrep == 1 ? std::vector<int>{0, nseq} : shard_bounds(c->d, cu, nseq, nrep);
+    const std::vector<std::vector<int>> parts = lpt_assign(c->d, c->reps[0]->layers, cu, nseq, nrep);
     int k = 0;
     try {
-        for (; k < nrep; ++k) submit_shard(c, *c->reps[k], slot, ids, cu, b[k], b[k + 1], out_kind, out_dim, host_out);
+        for (; k < nrep; ++k) {
+            if (c->inject_replica == k) {
+                c->inject_replica = -1;
+                fail("rembed: the worker of device %d failed (injected)", c->reps[k]->device);
+            }
+            submit_shard(c, *c->reps[k], slot, ids, cu, parts[k], out_kind, out_dim, host_out);
+        }
     } catch (...) {
         for (int j = 0; j < k; ++j) {  // the shards already in flight finish before the slot is reused
             try {
@@ -1979,6 +2052,33 @@ int rg_profile_stats(rg_ctx* c, int dev_index, int kc, double* ms, int* launches
     return 0;
 }
 
+int rg_test_inject(rg_ctx* c, int what, long long arg, char** err) {
+    try {
+        if (what != RG_INJECT_GEMM_WAIT && what != RG_INJECT_HOST_ALLOC && what != RG_INJECT_REPLICA)
+            fail("rg_test_inject: unknown injection %d", what);
+        if (what == RG_INJECT_GEMM_WAIT) {
+            if (arg <= 0) fail("rg_test_inject: the wait limit must be positive");
+            g_inject_gemm_wait.store(arg);
+            return 0;
+        }
+        if (!c) fail("rg_test_inject: null context");
+        std::lock_guard<std::mutex> tl(c->tmu);
+        if (what == RG_INJECT_HOST_ALLOC) {
+            c->inject_alloc = true;
+        } else if (what == RG_INJECT_REPLICA) {
+            if (arg < 0 || arg >= static_cast<long long>(c->reps.size()))
+                fail("rg_test_inject: replica %lld out of range", arg);
+            c->inject_replica = static_cast<int>(arg);
+        } else {
+            fail("rg_test_inject: unknown injection %d", what);
+        }
+        return 0;
+    } catch (const Error& e) {
+        set_err(err, e.msg);
+        return -1;
+    }
+}
+
 int rg_hidden(const rg_ctx* c) { return c ? c->d.hidden_size : 0; }
 int rg_mode_active(const rg_ctx* c) { return c ? c->mode : -1; }
 int rg_last_launches(const rg_ctx* c, int dev_index) {
@@ -2020,14 +2120,14 @@ int rg_dense_residual_layernorm_bf16(const void* x, const void* w, const float* 
         int sms = 148;
         check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
         cudaStream_t st = static_cast<cudaStream_t>(stream);
-        // Per-device scratch: [status word | pad to 256 B | fp32 sum M x N].
+        // Per-device scratch: the fp32 sum M x N.
         struct Scratch {
             float* base = nullptr;
             size_t floats = 0;
         };
         static std::mutex smu;
         static std::map<int, Scratch> scratch;
-        const size_t need = static_cast<size_t>(M) * N + 64;
+        const size_t need = static_cast<size_t>(M) * N;
         float* base = nullptr;
         {
             std::lock_guard<std::mutex> lk(smu);
@@ -2042,9 +2142,11 @@ int rg_dense_residual_layernorm_bf16(const void* x, const void* w, const float* 
             }
             base = sc.base;
         }
-        int* status = reinterpret_cast<int*>(base);
-        float* sum = base + 64;
-        check(cudaMemsetAsync(status, 0, sizeof(int), st), "cudaMemsetAsync");
+        // in-kernel failures accumulate in the device's kernel-level status
+        // word until rg_kernel_status reads it
+        int* status = nullptr;
+        check(rg::kernel_status_word(dev, &status), "kernel status word");
+        float* sum = base;
         CUtensorMap ta, tb;
         const int bn = rg::gemm_block_n(M, N, sms);
         if (!rg::make_kmajor_tmap(&ta, x, 2, M, K, K, 128) || !rg::make_kmajor_tmap(&tb, w, 2, N, K, K, rg::gemm_w_box_rows(bn)))
@@ -2059,7 +2161,8 @@ int rg_dense_residual_layernorm_bf16(const void* x, const void* w, const float* 
         a.ld_out = N;
         a.status = status;
         check(rg::gemm_launch(rg::GemmKind::kBF16, rg::kEpiBiasRes, bn, ta, tb, a, sms, st), "gemm launch");
-        check(rg::launch_ln(sum, gamma, beta, eps, M, N, out32, static_cast<act16*>(outb), false, nullptr, nullptr, st),
+        check(rg::launch_ln(sum, gamma, beta, eps, M, N, out32, static_cast<act16*>(outb), false, nullptr, nullptr, st,
+                            status),
               "ln launch");
         return 0;
     } catch (const Error& e) {
@@ -2083,21 +2186,8 @@ int rg_dense_bf16(const void* x, const void* w, const float* bias, const float* 
         const int bn = rg::gemm_block_n(M, N, sms);
         if (!rg::make_kmajor_tmap(&ta, x, 2, M, K, K, 128) || !rg::make_kmajor_tmap(&tb, w, 2, N, K, K, rg::gemm_w_box_rows(bn)))
             fail("rg_dense_bf16: cuTensorMapEncodeTiled failed");
-        // One status word per device for this kernel-level entry point.
-        static std::mutex smu;
-        static std::map<int, int*> status_words;
         int* status = nullptr;
-        {
-            std::lock_guard<std::mutex> lk(smu);
-            auto it = status_words.find(dev);
-            if (it == status_words.end()) {
-                check(cudaMalloc(&status, sizeof(int)), "cudaMalloc");
-                check(cudaMemset(status, 0, sizeof(int)), "cudaMemset");
-                status_words[dev] = status;
-            } else {
-                status = it->second;
-            }
-        }
+        check(rg::kernel_status_word(dev, &status), "kernel status word");
         rg::GemmArgs a{};
         a.M = M;
         a.N = N;
@@ -2107,6 +2197,11 @@ int rg_dense_bf16(const void* x, const void* w, const float* bias, const float* 
         a.out = y;
         a.ld_out = N;
         a.status = status;
+        const long long inj = g_inject_gemm_wait.exchange(0);
+        if (inj > 0) {
+            a.wait_limit = inj;
+            a.inject_withhold = 1;
+        }
         check(rg::gemm_launch(rg::GemmKind::kBF16, epilogue, bn, ta, tb, a, sms, static_cast<cudaStream_t>(stream)),
               "gemm launch");
         return 0;

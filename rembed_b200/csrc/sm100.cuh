@@ -60,16 +60,17 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
 }
 
 // Wait for the phase of `parity` to complete.  Returns false (and raises
-// kStatusWaitTimeout in *status) if it does not complete within the limit
-// or if another role of the CTA has already aborted (*abort != 0).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, volatile int* abort) {
+// kStatusWaitTimeout in *status) if it does not complete within `limit`
+// cycles or if another role of the CTA has already aborted (*abort != 0).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, volatile int* abort,
+                                          long long limit = kWaitLimitCycles) {
     const uint32_t a = smem_u32(bar);
     if (mbar_test(a, parity)) return true;
     const long long t0 = clock64();
     while (true) {
         if (mbar_test(a, parity)) return true;
         if (*abort) return false;
-        if (clock64() - t0 > kWaitLimitCycles) {
+        if (clock64() - t0 > limit) {
             atomicOr(status, kStatusWaitTimeout);
             *abort = 1;
             return false;
@@ -78,11 +79,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
 }
 
 // Teardown variant: bounded, ignores the abort flag.
-__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity, long long limit = kWaitLimitCycles) {
     const uint32_t a = smem_u32(bar);
     const long long t0 = clock64();
     while (!mbar_test(a, parity)) {
-        if (clock64() - t0 > kWaitLimitCycles) return false;
+        if (clock64() - t0 > limit) return false;
     }
     return true;
 }

@@ -116,6 +116,15 @@ SIGNATURES = {
     "rg_dense_residual_layernorm_bf16_noalloc": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_float, _VP,
                                                                 _VP, ctypes.c_int, ctypes.c_int, ctypes.c_int, _VP,
                                                                 _ERR]),
+    "rg_kernel_status": (ctypes.c_int, [_VP, _ERR]),
+    "rg_test_inject": (ctypes.c_int, [_VP, ctypes.c_int, ctypes.c_longlong, _ERR]),
+    "rg_attention": (ctypes.c_int, [_VP, _VP, _VP, ctypes.c_int, ctypes.c_int, ctypes.c_int, _VP,
+                                    ctypes.POINTER(ctypes.c_int32), ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                    ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_int, _VP,
+                                    ctypes.c_int, _VP, _ERR]),
+    "rg_quantize_rows_s8": (ctypes.c_int, [_VP, ctypes.c_int, ctypes.c_int, _VP, _VP, _VP, _ERR]),
+    "rg_dense_s8": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_int, ctypes.c_int, ctypes.c_int, _VP,
+                                   _ERR]),
 }
 
 _lib = None

@@ -22,7 +22,7 @@ import numpy as np
 
 from .config import Config
 
-__all__ = ["PRESETS", "preset", "make_weights", "make_batch", "write_model_dir", "read_safetensors"]
+__all__ = ["PRESETS", "preset", "make_weights", "make_batch", "batch_of_lengths", "write_model_dir", "read_safetensors"]
 
 
 def _bert(name, H, L, heads, I, pooling, vocab=30522, max_pos=512):
@@ -99,6 +99,15 @@ PRESETS.update({
     # nomic-embed-text-v1.5: post-norm, RoPE 1000, SwiGLU fc11 * silu(fc12).
     "nomic-embed-v1.5": lambda: _nomic("synthetic/nomic-embed-text-v1.5", 768, 12, 12, 3072, 30528, 2048),
     "tiny-nomic": lambda: _nomic("synthetic/tiny-nomic", 128, 2, 2, 256, 2048, 512),
+    # Full-width, reduced-depth variants of three benchmark architectures for
+    # parity at the configurations' longest sequences, where a full-depth CPU
+    # forward would take hours: every layer kind stays present (ModernBERT:
+    # layer 0 global, 1-2 local; Gemma: layer 0 local, 1 global; Qwen3: two
+    # causal layers).
+    "modernbert-base-3l": lambda: _modernbert("synthetic/ModernBERT-base-3l", 768, 3, 12, 1152, 50368, 8192, 128),
+    "qwen3-0.6b-2l": lambda: _qwen3("synthetic/Qwen3-Embedding-0.6B-2l", 1024, 2, 16, 8, 128, 3072, 151669, 32768),
+    "embeddinggemma-300m-2l": lambda: _gemma3("synthetic/embeddinggemma-300m-2l", 768, 2, 3, 1, 256, 1152, 262144,
+                                              2048, 257, 2, 3072),
 })
 
 # Families whose token ids are not framed by CLS/SEP in the synthetic batches.
@@ -280,6 +289,25 @@ def make_batch(cfg: Config, nseq: int, lo: int, hi: int, seed: int = 1,
             ids[cu[i]] = cls_id
             if lens[i] > 1:
                 ids[cu[i + 1] - 1] = sep_id
+    return ids, cu
+
+
+def batch_of_lengths(cfg: Config, lens, seed: int = 1, id_lo: int = 0) -> tuple[np.ndarray, np.ndarray]:
+    """Packed batch with the given sequence lengths; ids uniform in
+    [id_lo, vocab) (framed by CLS/SEP for the BERT family, as make_batch)."""
+    framed = cfg.model_type not in UNFRAMED
+    if framed and id_lo == 0:
+        id_lo = 1000
+    rng = np.random.default_rng(seed)
+    lens = np.asarray(lens, dtype=np.int64)
+    cu = np.zeros(len(lens) + 1, dtype=np.int32)
+    cu[1:] = np.cumsum(lens)
+    ids = rng.integers(id_lo, cfg.vocab_size, size=int(cu[-1]), dtype=np.int64)
+    if framed:
+        for i in range(len(lens)):
+            ids[cu[i]] = 101
+            if lens[i] > 1:
+                ids[cu[i + 1] - 1] = 102
     return ids, cu
 
 

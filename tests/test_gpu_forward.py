@@ -215,9 +215,10 @@ def test_full_int8_parity_bge(cuda):
 
 
 def test_multi_device_context_matches_single_device(cuda):
-    """rg_forward over a context holding two devices splits the batch into
-    contiguous cost-balanced shards, one host thread per device, each
-    landing in its slice of the output; the result equals one device's."""
+    """rg_forward over a context holding two devices assigns the sequences
+    to the devices by estimated cost (longest first, each to the least
+    loaded device), each result landing in its own row of the output; the
+    result equals one device's bit for bit."""
     import torch
 
     if torch.cuda.device_count() < 2:

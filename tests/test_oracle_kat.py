@@ -198,3 +198,36 @@ def test_flash_semantics_of_oracle_attention_matmul():
         want = a.astype(np.float64) @ bT.astype(np.float64).T
         got = oracle.matmul_serial(a, bT, m, k, n)
         assert np.all(np.abs(got - want) <= 1e-5 * math.sqrt(k))
+
+
+def naive_causal_attention(q, k, v, scale):
+    """The naive float64 causal softmax of qwen3_test.go:15-43 (per query i,
+    softmax over keys [0, i] of (q_i . k_j) * scale, then the weighted sum of
+    v_j), vectorised."""
+    q, k, v = (np.asarray(a, dtype=np.float64) for a in (q, k, v))
+    seq = q.shape[0]
+    s = (q @ k.T) * float(scale)
+    s[np.triu_indices(seq, 1)] = -np.inf
+    s -= s.max(axis=1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(axis=1, keepdims=True)
+    return p @ v
+
+
+FLASH_SEQS = [1, 2, 5, 63, 64, 65, 120, 127, 128, 129, 200]
+
+
+@pytest.mark.parametrize("seq", FLASH_SEQS)
+def test_flash_attn_causal_head(seq):  # qwen3_test.go:45-80
+    """The oracle's flashAttnCausalHead against the naive softmax at sizes
+    below, at and across the 64-row block boundary, max-abs <= 1e-4 (the
+    reference test's bar).  Inputs uniform in [-1, 1) from a fixed seed (the
+    reference draws them from Go's math/rand with seed 7; any uniform draw
+    exercises the same block logic)."""
+    rng = np.random.default_rng(7 + seq)
+    dh = 64
+    q, k, v = (rng.uniform(-1, 1, size=(seq, dh)).astype(np.float32) for _ in range(3))
+    scale = np.float32(1 / math.sqrt(dh))
+    got = oracle.flash_attn_causal_head(q, k, v, scale)
+    want = naive_causal_attention(q, k, v, scale)
+    assert float(np.abs(got - want).max()) <= 1e-4

@@ -1,16 +1,21 @@
 """The allocation-free sublayer entry point against the allocating one.
 
-rg_dense_residual_layernorm_bf16_noalloc exists for callers that must not
-allocate device memory, such as code running while a stream is captured into
-a CUDA graph, or a host whose memory manager owns all device allocations.
-It keeps its scratch in a fixed 16 MiB static device array instead of the
-per-device buffer that rg_dense_residual_layernorm_bf16 allocates.
+rg_dense_residual_layernorm_bf16_noalloc exists for callers that cannot let a
+library call cudaMalloc: a host whose memory manager owns every byte of
+device memory (an arena carved out of HBM up front, or an allocator that
+accounts for each buffer), or a latency-bound caller that cannot afford the
+device synchronisation an allocation may bring.  It keeps its scratch in a
+fixed 16 MiB static device array instead of the per-device buffer that
+rg_dense_residual_layernorm_bf16 allocates.
 
 Both are called through the C ABI on the same inputs.  The outputs must agree
 within the tolerance the kernel tests use (test_gpu_gemm.py), on two calls in
 a row with different shapes, so the second call also proves that what the
-first call left in the shared array does not leak into the result.  The file
-is named to be collected last and must pass alone in a fresh process too.
+first call left in the shared array does not leak into the result; each is
+also checked against the plain fp32 torch reference of the sublayer, and
+rg_kernel_status (which reads the array's status word) must report no
+failure.  The file is named to be collected last and must pass alone in a
+fresh process too.
 """
 
 import ctypes
@@ -64,6 +69,26 @@ def test_noalloc_matches_allocating_entry_point_on_two_calls(cuda):
         assert not bool(torch.isnan(got32).any())
         assert float(((got32 - want32).abs() - tol).max()) <= 0, float((got32 - want32).abs().max())
         assert float((gotb.float() - wantb.float()).abs().max()) <= float((want32.abs() * 2.0 ** -7 + 1e-3).max())
+        ref = fp32_reference(*args, eps)
+        tol = 2e-4 * (1 + ref.abs()) * math.sqrt(K / 64)
+        assert float(((got32 - ref).abs() - tol).max()) <= 0, float((got32 - ref).abs().max())
+        kernel_status(torch)
+
+
+def fp32_reference(x, w, bias, res, gamma, beta, eps):
+    """Add then two-pass LayerNorm in fp32 (tensor.go:383-387, 433-452)."""
+    s = res + (x.float() @ w.float().t() + bias)
+    mean = s.mean(1, keepdim=True)
+    var = ((s - mean) ** 2).mean(1, keepdim=True)
+    return (s - mean) / (var + eps).sqrt() * gamma + beta
+
+
+def kernel_status(torch):
+    from rembed_b200.embedder import RembedError, library, take_error
+
+    err = ctypes.c_char_p()
+    if library().rg_kernel_status(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), ctypes.byref(err)) != 0:
+        raise RembedError(take_error(err))
 
 
 def test_noalloc_rejects_more_than_its_scratch(cuda):
