@@ -57,6 +57,9 @@ WORKLOADS = {
     "qwen3-0.6b-b128xU32-1024": dict(preset="qwen3-0.6b", nseq=128, lo=32, hi=1024),
     "modernbert-base-b64xU512-8192": dict(preset="modernbert-base", nseq=64, lo=512, hi=8192),
     "embeddinggemma-300m-b64xU16-2048": dict(preset="embeddinggemma-300m", nseq=64, lo=16, hi=2048),
+    # the configuration's whole 512-sequence batch (for --scaling strong over 8 GPUs)
+    "embeddinggemma-300m-b512xU16-2048": dict(preset="embeddinggemma-300m", nseq=512, lo=16, hi=2048),
+    "modernbert-base-b64xU512-8192-strong": dict(preset="modernbert-base", nseq=64, lo=512, hi=8192),
 }
 METRIC = "embeddings/sec at bge-base b256×L128 (fp & int8), 1–8 GPU; tensor-pipe util %"
 # mode -> (Embedder keyword arguments, oracle quantisation name, dtype the path computes in)
@@ -81,7 +84,12 @@ def parse():
                     help="further modes measured after --mode, each in a sub-object of the line: a comma list, "
                          "'none', or 'auto' (every other mode on the headline workload, none elsewhere)")
     ap.add_argument("--mode-steps", type=int, default=20, help="timed steps of each further mode (at most --steps)")
+    ap.add_argument("--ramp-seconds", type=float, default=0.5,
+                    help="untimed forwards before the warm-up steps (clock ramp)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target length of the CPU baseline sample")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
+                    help="weak: one process per GPU under torchrun, each with its own batch; strong: one process, "
+                         "one context over --gpus devices, one batch split across them by rg_forward")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -430,6 +438,14 @@ def measure_mode(args, mode, wl, cfg, weights, ids, cu, world, local_rank, dist,
         ranks.barrier(dist)
         torch.cuda.synchronize()
 
+    # clock ramp: the forward repeated for about half a second before the
+    # warm-up steps, so that the (short) timed region starts at the clock the
+    # workload settles to instead of an idle GPU's
+    t_ramp = time.perf_counter()
+    while time.perf_counter() - t_ramp < args.ramp_seconds:
+        for _ in range(4):
+            step()
+        torch.cuda.synchronize()
     for _ in range(max(args.warmup, 1)):
         step()
     emb.sync()
@@ -573,7 +589,8 @@ def ours(args, rank, world, local_rank):
         "config": {"workload": args.workload, "global_batch": world * nseq, "per_gpu_batch": nseq,
                    "seq_len": f"{wl['lo']}-{wl['hi']}", "tokens_per_gpu_step": T, "parallelism": f"dp{world}",
                    "mode": args.mode,
-                   "l2": "no flush: per-step working set (activations ~0.8 GB + weights) exceeds the 126 MB L2"},
+                   "l2": "no flush: per-step working set (activations ~0.8 GB + weights) exceeds the 126 MB L2",
+                   "clock_ramp_s": args.ramp_seconds},
         "roofline": main_r.roofline,
         "e2e": main_r.e2e,
         "clocks": main_r.clocks,
@@ -616,7 +633,77 @@ def main():
     if args.impl == "reference":
         reference_arm(args, rank, world)
         return
+    if args.scaling == "strong":
+        if world != 1:
+            raise SystemExit("--scaling strong runs as one process (no torchrun)")
+        strong(args)
+        return
     ours(args, rank, world, local_rank)
+
+
+def strong(args):
+    """One process, one context over --gpus devices: each step embeds the
+    workload's whole batch through the public host API (rg_submit /
+    rg_collect), which splits the sequences over the devices by estimated
+    cost (longest first to the least loaded device) and writes every result
+    into its row of the host output.  Host arrays in and out, so value and
+    e2e are the same measurement here."""
+    import torch
+
+    from rembed_b200 import ranks, synth
+    from rembed_b200.embedder import Embedder
+
+    wl = WORKLOADS[args.workload]
+    cfg = synth.preset(wl["preset"])
+    weights = synth.make_weights(cfg, seed=0)
+    _, ids, cu = make_inputs(wl, seed=ranks.batch_seed(0))
+    nseq = len(cu) - 1
+    devs = list(range(args.gpus))
+    emb = Embedder(cfg, weights, devices=devs, **MODES[args.mode][0])
+    del weights
+    outs = [np.empty((nseq, emb.dim), dtype=np.float32) for _ in range(2)]
+
+    def steps(n):
+        pending = None
+        for k in range(n):
+            nxt = emb.submit(ids, cu, out=outs[k % 2])
+            if pending is not None:
+                pending.result()
+            pending = nxt
+        pending.result()
+
+    t_ramp = time.perf_counter()
+    while time.perf_counter() - t_ramp < args.ramp_seconds:
+        steps(2)
+    steps(max(args.warmup, 1))
+    uuid = None
+    with clock_sampler(uuid) as clk:
+        t0 = time.perf_counter()
+        steps(args.steps)
+        wall = time.perf_counter() - t0
+    for d in devs:
+        torch.cuda.synchronize(d)
+    value = nseq * args.steps / wall
+    one = outs[(args.steps - 1) % 2].copy()
+    emb.close()
+    # the same batch on one device: the split must not change any embedding
+    with Embedder(cfg, synth.make_weights(cfg, seed=0), devices=[0], **MODES[args.mode][0]) as e1:
+        ref = e1.embed_packed(ids, cu)
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "embeddings/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * wall / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": MODES[args.mode][2],
+        "data": "synthetic (seeded random-init weights N(0,0.02) of the named architecture; seeded token ids)",
+        "config": {"workload": args.workload, "global_batch": nseq, "seq_len": f"{wl['lo']}-{wl['hi']}",
+                   "tokens_per_step": int(cu[-1]), "parallelism": f"one context over {args.gpus} GPUs, sequences "
+                   f"split by estimated cost (longest first)", "mode": args.mode, "clock_ramp_s": args.ramp_seconds},
+        "e2e": {"value": round(value, 2), "unit": "embeddings/s", "h2d_bytes_per_step": int(ids.nbytes + cu.nbytes),
+                "d2h_bytes_per_step": int(outs[0].nbytes),
+                "how": "rg_submit/rg_collect from host arrays, wall clock, two batches in flight"},
+        "identical_to_one_gpu": bool(np.array_equal(one, ref)),
+        "clocks_gpu0": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

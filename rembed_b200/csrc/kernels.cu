@@ -980,4 +980,204 @@ cudaError_t launch_pool(const float* x32, const int32_t* cu, int nseq, int H, in
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Pooling, Dense head, L2 and Matryoshka truncation as one kernel
+// (ForwardWorkers' pooling bert.go:670-703, the Gemma Dense head
+// gemma3.go:177-198, L2Normalize tensor.go:542-554, truncate
+// rembed.go:441-448).  A cluster of kHeadCtas CTAs serves kHeadSeqs
+// sequences and splits every stage between its CTAs through distributed
+// shared memory:
+//   1. pool: CTA r sums rows [r L / 8, (r+1) L / 8) of each sequence
+//      (mean) or takes its picked row (rank 0); the partial sums of all
+//      CTAs are added in rank order and scaled by 1/L;
+//   2. hid = pooled . W1^T: CTA r computes its D/8 hidden columns for the
+//      group's sequences, one warp per column (lanes split K, coalesced
+//      weight rows), and every CTA then gathers the whole hidden vector;
+//   3. y = hid . W2^T: CTA r computes its H/8 output columns the same way;
+//   4. L2 over H (float64 partial sums per CTA, added in rank order), then
+//      for dim < H the first dim columns re-normalised the same way;
+// each CTA writes its slice of the output.  The head weights stay fp32
+// (never quantised, as in the reference) and are read once per cluster.
+constexpr int kHeadCtas = 8, kHeadSeqs = 4, kHeadThreads = 256;
+
+__device__ __forceinline__ float ld_dsmem_f32(const float* local, uint32_t rank) {
+    const uint32_t a = mapa_shared(smem_u32(local), rank);
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ double ld_dsmem_f64(const double* local, uint32_t rank) {
+    const uint32_t a = mapa_shared(smem_u32(local), rank);
+    double v;
+    asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(a) : "memory");
+    return v;
+}
+
+// One column per warp: out[g][col] = sum_k x[g][k] * w[col][k] for the group's
+// kHeadSeqs rows of x (shared memory, row stride K); lanes split K.
+__device__ __forceinline__ void head_columns(const float* __restrict__ w, const float* x, int K, int col0, int ncols,
+                                             float* out, int out_stride, int warp, int lane) {
+    for (int c = warp; c < ncols; c += kHeadThreads / 32) {
+        const float* wr = w + static_cast<int64_t>(col0 + c) * K;
+        float acc[kHeadSeqs];
+#pragma unroll
+        for (int g = 0; g < kHeadSeqs; ++g) acc[g] = 0.f;
+        for (int k = lane; k < K; k += 32) {
+            const float wv = __ldg(wr + k);
+#pragma unroll
+            for (int g = 0; g < kHeadSeqs; ++g) acc[g] = fmaf(x[g * K + k], wv, acc[g]);
+        }
+#pragma unroll
+        for (int g = 0; g < kHeadSeqs; ++g) {
+            const float v = warp_sum(acc[g]);
+            if (lane == 0) out[g * out_stride + col0 + c] = v;
+        }
+    }
+}
+
+__global__ void __cluster_dims__(kHeadCtas, 1, 1) __launch_bounds__(kHeadThreads)
+    pool_head_kernel(const float* __restrict__ x32, const int32_t* __restrict__ cu, int nseq, int H, int D,
+                     int pooling, const float* __restrict__ w1, const float* __restrict__ w2, int normalize, int dim,
+                     float* __restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ float hsm[];
+    float* part = hsm;                        // [kHeadSeqs][H]: this CTA's pooling partial sums
+    float* pooled = part + kHeadSeqs * H;     // [kHeadSeqs][H]
+    float* hid = pooled + kHeadSeqs * H;      // [kHeadSeqs][D]: own slice written, others gathered
+    float* y = hid + kHeadSeqs * D;           // [kHeadSeqs][H]: own slice of the head output
+    __shared__ double ss[2][kHeadSeqs];       // this CTA's sums of squares (full row, first dim)
+    __shared__ double red[kHeadThreads / 32][kHeadSeqs];
+    __shared__ float scale[kHeadSeqs];
+    const uint32_t rank = cluster_ctarank();
+    const int grp = blockIdx.x / kHeadCtas;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+
+    // 1. pooling partial sums of this CTA's share of each sequence's rows
+    for (int g = 0; g < kHeadSeqs; ++g) {
+        const int s = grp * kHeadSeqs + g;
+        int r0 = 0, r1 = 0;
+        if (s < nseq) {
+            const int s0 = __ldg(cu + s), L = __ldg(cu + s + 1) - s0;
+            if (pooling == 0) {  // mean: rows split between the CTAs
+                r0 = s0 + static_cast<int>((static_cast<int64_t>(L) * rank) / kHeadCtas);
+                r1 = s0 + static_cast<int>((static_cast<int64_t>(L) * (rank + 1)) / kHeadCtas);
+            } else if (rank == 0) {  // cls (first) / last token: one row
+                r0 = pooling == 1 ? s0 : s0 + L - 1;
+                r1 = r0 + 1;
+            }
+        }
+        for (int j = t; j < H; j += kHeadThreads) {
+            float acc = 0.f;
+            int i = r0;
+            for (; i + 4 <= r1; i += 4) {
+                const float a0 = x32[static_cast<int64_t>(i) * H + j], a1 = x32[static_cast<int64_t>(i + 1) * H + j];
+                const float a2 = x32[static_cast<int64_t>(i + 2) * H + j], a3 = x32[static_cast<int64_t>(i + 3) * H + j];
+                acc = (((acc + a0) + a1) + a2) + a3;
+            }
+            for (; i < r1; ++i) acc += x32[static_cast<int64_t>(i) * H + j];
+            part[g * H + j] = acc;
+        }
+    }
+    cluster_sync();
+    for (int g = 0; g < kHeadSeqs; ++g) {
+        const int s = grp * kHeadSeqs + g;
+        float invL = 1.0f;
+        if (s < nseq && pooling == 0) invL = 1.0f / static_cast<float>(__ldg(cu + s + 1) - __ldg(cu + s));
+        for (int j = t; j < H; j += kHeadThreads) {
+            float v = 0.f;
+            for (int q = 0; q < kHeadCtas; ++q) v += ld_dsmem_f32(part + g * H + j, q);
+            pooled[g * H + j] = v * invL;
+        }
+    }
+    __syncthreads();
+    // 2. this CTA's hidden columns, then the whole hidden vector
+    const int dper = D / kHeadCtas, hper = H / kHeadCtas;
+    head_columns(w1, pooled, H, static_cast<int>(rank) * dper, dper, hid, D, warp, lane);
+    cluster_sync();
+    for (int q = 0; q < kHeadCtas; ++q) {
+        if (q == static_cast<int>(rank)) continue;
+        for (int i = t; i < kHeadSeqs * dper; i += kHeadThreads) {
+            const int g = i / dper, c = q * dper + i % dper;
+            hid[g * D + c] = ld_dsmem_f32(hid + g * D + c, q);
+        }
+    }
+    __syncthreads();
+    // 3. this CTA's output columns
+    head_columns(w2, hid, D, static_cast<int>(rank) * hper, hper, y, H, warp, lane);
+    __syncthreads();
+    // 4. L2 over H, then (dim < H) over the first dim columns
+    const int c0 = static_cast<int>(rank) * hper;
+    for (int pass = 0; pass < 2; ++pass) {
+        const bool trunc = pass == 1;
+        if (trunc && dim >= H) break;
+        if (!trunc && !normalize) continue;
+        const int lim = trunc ? dim : H;
+        double a[kHeadSeqs];
+#pragma unroll
+        for (int g = 0; g < kHeadSeqs; ++g) a[g] = 0.0;
+        for (int c = t; c < hper; c += kHeadThreads) {
+            if (c0 + c >= lim) continue;
+#pragma unroll
+            for (int g = 0; g < kHeadSeqs; ++g) {
+                const double v = y[g * H + c0 + c];
+                a[g] += v * v;
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < kHeadSeqs; ++g) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) a[g] += __shfl_xor_sync(0xffffffffu, a[g], o);
+            if (lane == 0) red[warp][g] = a[g];
+        }
+        __syncthreads();
+        if (t < kHeadSeqs) {
+            double v = 0.0;
+            for (int w = 0; w < kHeadThreads / 32; ++w) v += red[w][t];
+            ss[pass][t] = v;
+        }
+        cluster_sync();
+        if (t < kHeadSeqs) {
+            double v = 0.0;
+            for (int q = 0; q < kHeadCtas; ++q) v += ld_dsmem_f64(&ss[pass][t], q);
+            scale[t] = v != 0.0 ? static_cast<float>(1.0 / sqrt(v)) : 1.0f;
+        }
+        __syncthreads();
+        for (int c = t; c < hper; c += kHeadThreads)
+#pragma unroll
+            for (int g = 0; g < kHeadSeqs; ++g) y[g * H + c0 + c] *= scale[g];
+        __syncthreads();
+    }
+    for (int c = t; c < hper; c += kHeadThreads) {
+        if (c0 + c >= dim) continue;
+#pragma unroll
+        for (int g = 0; g < kHeadSeqs; ++g) {
+            const int s = grp * kHeadSeqs + g;
+            if (s < nseq) out[static_cast<int64_t>(s) * dim + c0 + c] = y[g * H + c0 + c];
+        }
+    }
+    // no CTA leaves while another may still read its shared memory
+    cluster_sync();
+}
+
+cudaError_t launch_pool_head(const float* x32, const int32_t* cu, int nseq, int H, int D, int pooling,
+                             const float* w1, const float* w2, int normalize, int dim, float* out, cudaStream_t st) {
+    if (nseq <= 0) return cudaSuccess;
+    if (H % kHeadCtas != 0 || D % kHeadCtas != 0 || dim < 1 || dim > H) return cudaErrorInvalidValue;
+    const size_t smem = sizeof(float) * (3 * kHeadSeqs * static_cast<size_t>(H) + kHeadSeqs * static_cast<size_t>(D));
+    static unsigned configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 32 || !(__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & (1u << dev))) {
+        cudaError_t e = cudaFuncSetAttribute(pool_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return e;
+        if (dev < 32) __atomic_fetch_or(&configured, 1u << dev, __ATOMIC_RELEASE);
+    }
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    const int groups = (nseq + kHeadSeqs - 1) / kHeadSeqs;
+    launch_pdl(pool_head_kernel, dim3(groups * kHeadCtas), dim3(kHeadThreads), smem, st, x32, cu, nseq, H, D, pooling,
+               w1, w2, normalize, dim, out);
+    return cudaGetLastError();
+}
+
 }  // namespace rg

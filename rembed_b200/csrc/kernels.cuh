@@ -178,5 +178,11 @@ cudaError_t kernel_status_word(int dev, int** out);
 // out[nseq x dim].
 cudaError_t launch_pool(const float* x32, const int32_t* cu, int nseq, int H, int pooling, int normalize, int dim,
                         float* out, cudaStream_t st);
+// The same with the Dense head between pooling and L2 (gemma3.go:177-198):
+// pooled -> W1 [D x H] -> W2 [H x D] -> L2 -> truncate, one launch (clusters
+// of 8 CTAs share each stage through distributed shared memory).  H and D
+// must be multiples of 8.
+cudaError_t launch_pool_head(const float* x32, const int32_t* cu, int nseq, int H, int D, int pooling,
+                             const float* w1, const float* w2, int normalize, int dim, float* out, cudaStream_t st);
 
 }  // namespace rg

@@ -1439,20 +1439,21 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
     }
     if (out_kind == RG_OUT_POOLED) {
         const double rows = d.pooling == 0 ? Td : double(nseq);
-        ProfScope ps(r, st, RG_KC_POOL, rows * Hd, 4.0 * (rows * Hd + double(nseq) * out_dim));
+        const double head_flops = r.dense1 ? 4.0 * double(nseq) * Hd * d.dense_hidden : 0.0;
+        const double head_bytes = r.dense1 ? 8.0 * Hd * d.dense_hidden : 0.0;
+        ProfScope ps(r, st, RG_KC_POOL, rows * Hd + head_flops, 4.0 * (rows * Hd + double(nseq) * out_dim) + head_bytes);
         // With the final norm applied to the pooled rows only (pick32), the
         // pool reads those rows as one-row sequences.
         const float* src = pick ? r.pick32 : r.x32;
         const int32_t* src_cu = pick ? r.iota : d_cu;
         const int pooling = pick ? 1 : d.pooling;
         if (r.dense1) {
-            // pool, Dense head H -> D -> H (fp32), then L2 and truncate (gemma3.go:177-198)
-            const int D = d.dense_hidden;
-            check(rg::launch_pool(src, src_cu, nseq, H, pooling, 0, H, r.pool32, st), "pool launch");
-            check(rg::launch_dense_f32(r.pool32, r.dense1, r.head_hid, nseq, D, H, st), "dense launch");
-            check(rg::launch_dense_f32(r.head_hid, r.dense2, r.head_out, nseq, H, D, st), "dense launch");
-            check(rg::launch_pool(r.head_out, r.iota, nseq, H, 1, d.normalize, out_dim, d_out, st), "l2 launch");
-            launches += 4;
+            // pool, Dense head H -> D -> H (fp32), L2 and truncate in one
+            // launch (gemma3.go:177-198)
+            check(rg::launch_pool_head(src, src_cu, nseq, H, d.dense_hidden, pooling, r.dense1, r.dense2, d.normalize,
+                                       out_dim, d_out, st),
+                  "pool/head launch");
+            ++launches;
         } else {
             check(rg::launch_pool(src, src_cu, nseq, H, pooling, d.normalize, out_dim, d_out, st), "pool launch");
             ++launches;
@@ -1778,6 +1779,8 @@ int rg_init(const rg_model_desc* desc, const int* devices, int ndev, int mode, r
         if (d.arch == RG_ARCH_GEMMA3 &&
             (d.sliding_window < 1 || d.sliding_window_pattern < 1 || d.query_pre_attn_scalar < 1 || d.dense_hidden < 1))
             fail("rg_init: gemma3 needs sliding_window, sliding_window_pattern, query_pre_attn_scalar, dense_hidden");
+        if (d.arch == RG_ARCH_GEMMA3 && d.dense_hidden % 8 != 0)
+            fail("rg_init: gemma3 dense_hidden must be a multiple of 8 (got %d)", d.dense_hidden);
         if (is_glu(d.arch) && (d.intermediate_size % 64 != 0))
             fail("rg_init: gated FFN needs intermediate_size %% 64 == 0 (got %d)", d.intermediate_size);
         if (dm.nqkv % 128 != 0 || dm.qd % 64 != 0)
