@@ -81,7 +81,7 @@ static bool make_epilogue_tmap(CUtensorMap* map, const void* base, bool f32, boo
     return r == CUDA_SUCCESS;
 }
 
-int gemm_block_n(int M, int N, int num_sms, bool glu) {
+int gemm_block_n(int M, int N, int num_sms, bool glu, int head_dim) {
     // Among the tile widths that divide N, the one with the fewest
     // (waves x per-tile cost), where a tile costs about BN + 32 columns of
     // work (the +32 models its fixed epilogue/pipeline overhead).
@@ -90,7 +90,7 @@ int gemm_block_n(int M, int N, int num_sms, bool glu) {
     int best = 0;
     long best_cost = 0;
     for (int bn : {256, 192, 128}) {
-        if (N % bn != 0 || (glu && bn == 192)) continue;
+        if (N % bn != 0 || (glu && bn == 192) || (head_dim > 0 && (bn / 2) % head_dim != 0)) continue;
         const long tiles = static_cast<long>(m_tiles) * (N / bn);
         const long waves = (tiles + pairs - 1) / pairs;
         const long cost = waves * (bn + 32);
@@ -119,8 +119,14 @@ static cudaError_t launch_impl(GemmKind kind, int epi, int block_n, GemmMaps& m,
     // outputs: 16-bit kinds only.
     const bool k16 = kind == GemmKind::kBF16 || kind == GemmKind::kF16;
     // (a gated epilogue adds no bias: its folded norm must have none either)
-    if (args.fold_stats && (!k16 || !args.fold_c1 ||
-                            (epi_is_glu(epi) ? false : (!args.bias || (epi != kEpiBias && epi != kEpiBiasGelu)))))
+    if (args.fold_stats &&
+        (!k16 || !args.fold_c1 ||
+         (epi_is_glu(epi) ? false : (!args.bias || (epi != kEpiBias && epi != kEpiBiasGelu && epi != kEpiQkRope)))))
+        return cudaErrorInvalidValue;
+    if (epi == kEpiQkRope &&
+        (f32out || args.rope_dh <= 0 || args.rope_dh % 64 != 0 || (block_n / 2) % args.rope_dh != 0 ||
+         args.rope_qd % args.rope_dh != 0 || args.rope_kvd % args.rope_dh != 0 ||
+         ((args.rope_cos || args.rope_sin) && (!args.rope_cos || !args.rope_sin || !args.positions))))
         return cudaErrorInvalidValue;
     if ((args.parts_out || args.out16) && (!k16 || !epi_has_residual(epi))) return cudaErrorInvalidValue;
     if (args.out16) {

@@ -452,7 +452,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             // folded LayerNorm of the A rows: rstd and -rstd * mean
             float fr = 1.f, fnm = 0.f;
-            if constexpr (EPI == kEpiBias || EPI == kEpiBiasGelu || (EPI >= kEpiGluSilu && EPI <= kEpiGluGeluTanh)) {
+            if constexpr (EPI == kEpiBias || EPI == kEpiBiasGelu || EPI == kEpiQkRope ||
+                          (EPI >= kEpiGluSilu && EPI <= kEpiGluGeluTanh)) {
                 if (args.fold_stats && row < args.M) {
                     const float2 st = args.fold_stats[row];
                     fr = st.y;
@@ -465,8 +466,118 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + half * HALF;
             constexpr bool GLU = EPI >= kEpiGluSilu && EPI <= kEpiGluGeluTanh;
             constexpr int STEP = GLU ? 2 : 1;  // accumulator chunks per output box
+            if constexpr (EPI == kEpiQkRope) {
+                // Heads of dh columns, whole inside this warp's HALF columns.
+                // The projection value of column col: dequantised (int8
+                // kinds), then the folded norm or + bias, exactly as kEpiBias.
+                auto value = [&](uint32_t raw, int col) -> float {
+                    float v = S8 ? static_cast<float>(static_cast<int32_t>(raw)) * rs : __uint_as_float(raw);
+                    if (args.col_scale) v *= __ldg(args.col_scale + col);
+                    if (args.fold_stats) v = fmaf(fr, v, fmaf(fnm, __ldg(args.fold_c1 + col), __ldg(args.bias + col)));
+                    else if (args.bias) v += __ldg(args.bias + col);
+                    return v;
+                };
+                const int dh = args.rope_dh, hd = dh / 2;
+                const int colw = n_blk * BN + half * HALF;
+                const int pos = (args.positions && row < args.M) ? __ldg(args.positions + row) : 0;
+                uint8_t* box0 = boxes;
+                uint8_t* box1 = boxes + kStageBytes;
+                float amax = 0.f;
 #pragma unroll 1
-            for (int c = 0; c < CHUNKS; c += STEP, ++k) {
+                for (int h0 = 0; h0 < HALF; h0 += dh) {
+                    const int gcol = colw + h0;  // first column of the head
+                    const bool is_q = gcol < args.rope_qd;
+                    const bool is_k = !is_q && gcol < args.rope_qd + args.rope_kvd;
+                    const float* g = is_q ? args.q_norm : (is_k ? args.k_norm : nullptr);
+                    const bool rot = (is_q || is_k) && args.rope_cos != nullptr;
+                    float inv = 1.0f;
+                    if (g) {  // the head's RMS over its dh values
+                        float ssq = 0.f;
+#pragma unroll 1
+                        for (int c = 0; c < dh; c += 32) {
+                            uint32_t r[32];
+                            tmem_ld32(taddr + h0 + c, r);
+                            tmem_ld_wait();
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) {
+                                const float v = value(r[i], gcol + c + i);
+                                ssq = fmaf(v, v, ssq);
+                            }
+                        }
+                        inv = 1.0f / sqrtf(ssq / static_cast<float>(dh) + args.rope_eps);
+                    }
+                    const float* cs = rot ? args.rope_cos + static_cast<int64_t>(pos) * hd : nullptr;
+                    const float* sn = rot ? args.rope_sin + static_cast<int64_t>(pos) * hd : nullptr;
+                    // columns d (first half) and d + dh/2 (second half) of the
+                    // head together, 32 at a time into the two staging boxes
+#pragma unroll 1
+                    for (int c = 0; c < hd; c += 32) {
+                        if (lane == 0) bulk_wait_read<0>();  // both boxes free
+                        __syncwarp();
+#pragma unroll 1
+                        for (int sub = 0; sub < 32; sub += 16) {
+                            const int d0 = c + sub;
+                            uint32_t ra[16], rb[16];
+                            tmem_ld16(taddr + h0 + d0, ra);
+                            tmem_ld16(taddr + h0 + hd + d0, rb);
+                            tmem_ld_wait();
+                            float x1[16], x2[16];
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                x1[i] = value(ra[i], gcol + d0 + i);
+                                x2[i] = value(rb[i], gcol + hd + d0 + i);
+                            }
+                            if (g) {
+#pragma unroll
+                                for (int i = 0; i < 16; ++i) {
+                                    x1[i] = x1[i] * inv * __ldg(g + d0 + i);
+                                    x2[i] = x2[i] * inv * __ldg(g + hd + d0 + i);
+                                }
+                            }
+                            if (rot) {
+#pragma unroll
+                                for (int i = 0; i < 16; i += 4) {
+                                    const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs + d0 + i));
+                                    const float4 s4 = __ldg(reinterpret_cast<const float4*>(sn + d0 + i));
+                                    const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+                                    for (int e = 0; e < 4; ++e) {
+                                        const float a = x1[i + e], b = x2[i + e];
+                                        x1[i + e] = __fsub_rn(__fmul_rn(a, cc[e]), __fmul_rn(b, ss[e]));
+                                        x2[i + e] = __fadd_rn(__fmul_rn(b, cc[e]), __fmul_rn(a, ss[e]));
+                                    }
+                                }
+                            }
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fmaxf(fabsf(x1[i]), fabsf(x2[i])));
+#pragma unroll
+                            for (int q = 0; q < 2; ++q) {
+                                const int ci = sub / 8 + q;  // 16-byte chunk of the 64-byte box row
+                                *reinterpret_cast<uint4*>(box0 + swz(lane, ci, 64)) =
+                                    make_uint4(pack2<F16>(x1[8 * q], x1[8 * q + 1]), pack2<F16>(x1[8 * q + 2], x1[8 * q + 3]),
+                                               pack2<F16>(x1[8 * q + 4], x1[8 * q + 5]),
+                                               pack2<F16>(x1[8 * q + 6], x1[8 * q + 7]));
+                                *reinterpret_cast<uint4*>(box1 + swz(lane, ci, 64)) =
+                                    make_uint4(pack2<F16>(x2[8 * q], x2[8 * q + 1]), pack2<F16>(x2[8 * q + 2], x2[8 * q + 3]),
+                                               pack2<F16>(x2[8 * q + 4], x2[8 * q + 5]),
+                                               pack2<F16>(x2[8 * q + 6], x2[8 * q + 7]));
+                            }
+                        }
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&tmOut, box0, gcol + c, row0);
+                            tma_store_2d(&tmOut, box1, gcol + hd + c, row0);
+                            bulk_commit();
+                        }
+                    }
+                }
+                // fp16 outputs fail loudly instead of turning into inf
+                if (F16 && __any_sync(0xffffffffu, !(amax <= 65504.0f)) && lane == 0)
+                    atomicOr(args.status, kStatusF16Overflow);
+            }
+#pragma unroll 1
+            for (int c = 0; c < (EPI == kEpiQkRope ? 0 : CHUNKS); c += STEP, ++k) {
                 const int b = k & 1;
                 uint8_t* box = boxes + b * kStageBytes;
                 const int col0 = n_blk * BN + half * HALF + c * kChunk;  // accumulator column
@@ -777,6 +888,9 @@ static cudaError_t dispatch_epi(int epi, const GemmMaps& m, const GemmArgs& args
     case kEpiGluGeluErf: return launch_one<BN, KIND, kEpiGluGeluErf>(m, args, num_sms, stream);
     case kEpiGluGeluTanh: return launch_one<BN, KIND, kEpiGluGeluTanh>(m, args, num_sms, stream);
     case kEpiBiasResLN: return launch_one<BN, KIND, kEpiBiasResLN>(m, args, num_sms, stream);
+    case kEpiQkRope:
+        if constexpr (KIND == static_cast<int>(GemmKind::kTF32x3)) return cudaErrorInvalidValue;
+        else return launch_one<BN, KIND, kEpiQkRope>(m, args, num_sms, stream);
     default: return cudaErrorInvalidValue;
     }
 }

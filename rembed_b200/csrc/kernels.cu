@@ -165,9 +165,11 @@ __global__ void __launch_bounds__(256) embed_kernel(EmbedParams p) {
     }
     const float* w = p.word + id * H;
     const float* pr = nullptr;
-    if (p.pos) {
+    if (p.pos || p.pos_out) {
         const int s = seq_of_token(p.cu, p.nseq, t);
-        pr = p.pos + static_cast<int64_t>(t - __ldg(p.cu + s) + p.pos_off) * H;
+        const int posn = t - __ldg(p.cu + s);
+        if (p.pos) pr = p.pos + static_cast<int64_t>(posn + p.pos_off) * H;
+        if (p.pos_out && lane == 0) p.pos_out[t] = posn;
     }
     float v[NV][4];
 #pragma unroll

@@ -30,6 +30,7 @@ struct EmbedParams {
     float* xq_scale;
     int* status;
     float *xhi, *xlo;  // strict fp32: the normalised row as tf32-exact hi + fp32 remainder
+    int32_t* pos_out;  // optional: each token's position in its sequence
 };
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t st);
 

@@ -130,6 +130,7 @@ struct Replica {
     int8_t *xq = nullptr, *ctxq = nullptr, *ffhq = nullptr;
     float *xs = nullptr, *ctxs = nullptr, *ffhs = nullptr;
     float2* lnst = nullptr;  // post-norm: the last LayerNorm's per-row (mean, rstd)
+    int32_t* pos32 = nullptr;  // [T]: each token's position in its sequence (RoPE in the QKV epilogue)
     // Folded norms (post-norm BERT family in the 16-bit modes; Qwen3 and
     // ModernBERT input norms in bf16): the residual GEMM writes its
     // output's 32-column chunk statistics (parts) and a 16-bit copy in xb, a
@@ -855,6 +856,7 @@ void ensure_workspace(rg_ctx* c, Replica& r, int T, int nseq, size_t nout) {
         r.x32 = ws_alloc<float>(r, t * H);
         r.y32 = ws_alloc<float>(r, t * H);
         r.lnst = ws_alloc<float2>(r, t);
+        r.pos32 = ws_alloc<int32_t>(r, t);
         if (r.fold) r.parts = ws_alloc<float2>(r, t * (H / 32));
         if (c->mode == RG_MODE_FP32) {
             r.xh = ws_alloc<float>(r, t * H);
@@ -1009,10 +1011,31 @@ struct LnFold {
     float2* parts_out = nullptr;
 };
 
+// QK-norm + RoPE applied by the QKV GEMM's epilogue (kEpiQkRope).
+struct QkRope {
+    const float *q_norm = nullptr, *k_norm = nullptr, *cos = nullptr, *sin = nullptr;
+    const int32_t* positions = nullptr;
+    int dh = 0, qd = 0, kvd = 0;
+    float eps = 0.f;
+};
+
 void gemm(Replica& r, int mode, const OpMaps& tmA, const DevDense& w, int M, int epi, const float* row_scale,
           const float* residual, void* out, cudaStream_t st, int& launches, const float2* ln_stats = nullptr,
-          const float* ln_g = nullptr, const float* ln_b = nullptr, const LnFold* lf = nullptr) {
+          const float* ln_g = nullptr, const float* ln_b = nullptr, const LnFold* lf = nullptr,
+          const QkRope* qr = nullptr) {
     rg::GemmArgs a{};
+    if (qr) {  // the bias epilogue with QK-norm + RoPE per head
+        epi = rg::kEpiQkRope;
+        a.q_norm = qr->q_norm;
+        a.k_norm = qr->k_norm;
+        a.rope_cos = qr->cos;
+        a.rope_sin = qr->sin;
+        a.positions = qr->positions;
+        a.rope_dh = qr->dh;
+        a.rope_qd = qr->qd;
+        a.rope_kvd = qr->kvd;
+        a.rope_eps = qr->eps;
+    }
     a.ln_stats = ln_stats;
     a.ln_g = ln_g;
     a.ln_b = ln_b;
@@ -1052,7 +1075,7 @@ void gemm(Replica& r, int mode, const OpMaps& tmA, const DevDense& w, int M, int
                       : (rg::epi_is_glu(epi) ? 1.0 : 2.0);
     const double bytes = eb * (double(M) * w.K + double(w.N) * w.K) + ob * double(M) * w.N +
                          (rg::epi_has_residual(epi) ? 4.0 * double(M) * w.N : 0.0) + fold_bytes;
-    const int bn = rg::gemm_block_n(M, w.N, r.num_sms, rg::epi_is_glu(epi));
+    const int bn = rg::gemm_block_n(M, w.N, r.num_sms, rg::epi_is_glu(epi), qr ? qr->dh : 0);
     if (bn == 0) fail("no GEMM tile width divides N=%d", w.N);
     if (kind == rg::GemmKind::kW8 && M >= kW8WidenRows) {
         {
@@ -1153,6 +1176,7 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         e.xq = (!pre && s8) ? r.xq : nullptr;
         e.xq_scale = (!pre && s8) ? r.xs : nullptr;
         e.status = r.d_status;
+        e.pos_out = has_rope(arch) ? r.pos32 : nullptr;
         check(rg::launch_embed(e, st), "embed launch");
         ++launches;
     }
@@ -1229,15 +1253,21 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         folded = true;
     };
     // A GEMM reading xb: LN(y) folded into it when the last norm was folded.
-    auto input_gemm = [&](const DevDense& w, const OpMaps& tmA, int epi, void* out) {
+    auto input_gemm = [&](const DevDense& w, const OpMaps& tmA, int epi, void* out, const QkRope* qr = nullptr) {
         if (folded) {
             LnFold lf;
             lf.fold_stats = r.lnst;
-            gemm(r, mode, tmA, w, T, epi, nullptr, nullptr, out, st, launches, nullptr, nullptr, nullptr, &lf);
+            gemm(r, mode, tmA, w, T, epi, nullptr, nullptr, out, st, launches, nullptr, nullptr, nullptr, &lf, qr);
         } else {
-            gemm(r, mode, tmA, w, T, epi, s8 ? r.xs : nullptr, nullptr, out, st, launches);
+            gemm(r, mode, tmA, w, T, epi, s8 ? r.xs : nullptr, nullptr, out, st, launches, nullptr, nullptr, nullptr,
+                 nullptr, qr);
         }
     };
+    // QK-norm + RoPE in the QKV projection's epilogue where the tile widths
+    // hold whole heads (head dims 64 and 128; 16-bit outputs); otherwise
+    // (Gemma's 256-wide heads, the strict fp32 mode) a separate kernel.
+    const bool rope_in_gemm = has_rope(arch) && !f32 && dh % 64 == 0 &&
+                              rg::gemm_block_n(T, m.nqkv, r.num_sms, false, dh) != 0;
     auto post_norm = [&](const float* g, const float* b, bool last) {
         ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * Hd * (4.0 + 2.0 + (s8 ? 1.0 : 0.0) + (last ? 4.0 : 0.0)));
         rg::NormParams p{};
@@ -1303,8 +1333,22 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
             norm_into_a(L.attn_norm, arch == RG_ARCH_MODERNBERT ? r.zero_beta : nullptr, arch != RG_ARCH_MODERNBERT);
             folded = false;
         }
-        input_gemm(L.qkv, r.tm_x, rg::kEpiBias, f32 ? static_cast<void*>(r.qkv32) : r.qkv);
-        if (has_rope(arch)) {
+        if (rope_in_gemm) {
+            QkRope qr;
+            qr.q_norm = L.q_norm;
+            qr.k_norm = L.k_norm;
+            qr.cos = L.global ? r.cos_g : r.cos_l;
+            qr.sin = L.global ? r.sin_g : r.sin_l;
+            qr.positions = r.pos32;
+            qr.dh = dh;
+            qr.qd = m.qd;
+            qr.kvd = m.kvd;
+            qr.eps = eps;
+            input_gemm(L.qkv, r.tm_x, rg::kEpiBias, r.qkv, &qr);
+        } else {
+            input_gemm(L.qkv, r.tm_x, rg::kEpiBias, f32 ? static_cast<void*>(r.qkv32) : r.qkv);
+        }
+        if (has_rope(arch) && !rope_in_gemm) {
             ProfScope ps(r, st, RG_KC_NORM, 0.0, Td * (m.qd + m.kvd) * 4.0);
             rg::QkRopeParams q{};
             q.qkv = r.qkv;
