@@ -57,6 +57,31 @@ __device__ __forceinline__ float ex2f(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
+// max(a, b, c) in one instruction (sm_100).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float y;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
+    return y;
+}
+// Two fp32 lanes per instruction (sm_100 f32x2 ALU ops).
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void unpk2(uint64_t r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
 
 // PLAIN: no window, no bias (only the sequence end masks keys); BIAS: the
 // MPNet relative-position bias (and any window); neither: a window / causal
@@ -252,14 +277,15 @@ __global__ void __launch_bounds__(192, AttnTc<D>::MIN_BLOCKS)
             float mx;
             float cs = 1.0f;  // factor applied inside the exponent
             if (fast) {
-                // 8 independent partial maxima (instruction-level parallelism)
+                // 8 independent partial maxima (instruction-level
+                // parallelism), each taking two scores per 3-input max
                 float pm[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) pm[e] = __uint_as_float(sr[e]);
 #pragma unroll
-                for (int c = 8; c < BKV; ++c) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(sr[c]));
-                mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                           fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) *
+                for (int c = 8; c < BKV; c += 2)
+                    pm[(c >> 1) & 7] = max3f(pm[(c >> 1) & 7], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+                mx = max3f(max3f(pm[0], pm[1], pm[2]), max3f(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7])) *
                      p.scale_log2;
                 cs = p.scale_log2;
             } else if constexpr (BIAS) {

@@ -468,20 +468,53 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             constexpr int STEP = GLU ? 2 : 1;  // accumulator chunks per output box
             if constexpr (EPI == kEpiQkRope) {
                 // Heads of dh columns, whole inside this warp's HALF columns.
-                // The projection value of column col: dequantised (int8
-                // kinds), then the folded norm or + bias, exactly as kEpiBias.
-                auto value = [&](uint32_t raw, int col) -> float {
-                    float v = S8 ? static_cast<float>(static_cast<int32_t>(raw)) * rs : __uint_as_float(raw);
-                    if (args.col_scale) v *= __ldg(args.col_scale + col);
-                    if (args.fold_stats) v = fmaf(fr, v, fmaf(fnm, __ldg(args.fold_c1 + col), __ldg(args.bias + col)));
-                    else if (args.bias) v += __ldg(args.bias + col);
-                    return v;
+                // The projection values of 16 columns from col on: dequantised
+                // (int8 kinds), then the folded norm or + bias, with the same
+                // vector loads and packed arithmetic as kEpiBias.
+                auto values16 = [&](const uint32_t (&r)[16], int col, float (&x)[16]) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        x[i] = S8 ? static_cast<float>(static_cast<int32_t>(r[i])) * rs : __uint_as_float(r[i]);
+                    if (args.col_scale) {
+                        const float4* cp = reinterpret_cast<const float4*>(args.col_scale + col);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float4 q = __ldg(cp + i);
+                            x[4 * i] *= q.x;
+                            x[4 * i + 1] *= q.y;
+                            x[4 * i + 2] *= q.z;
+                            x[4 * i + 3] *= q.w;
+                        }
+                    }
+                    if (args.fold_stats) {  // rstd * acc + (bias - rstd * mean * c1)
+                        const float4* c1 = reinterpret_cast<const float4*>(args.fold_c1 + col);
+                        const float4* bp = reinterpret_cast<const float4*>(args.bias + col);
+                        const uint64_t r2 = f2(fr, fr), nm2 = f2(fnm, fnm);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float4 q = __ldg(c1 + i), bb = __ldg(bp + i);
+                            const uint64_t u0 = fma2(nm2, f2(q.x, q.y), f2(bb.x, bb.y));
+                            const uint64_t u1 = fma2(nm2, f2(q.z, q.w), f2(bb.z, bb.w));
+                            f2split(fma2(r2, f2(x[4 * i], x[4 * i + 1]), u0), x[4 * i], x[4 * i + 1]);
+                            f2split(fma2(r2, f2(x[4 * i + 2], x[4 * i + 3]), u1), x[4 * i + 2], x[4 * i + 3]);
+                        }
+                    } else if (args.bias) {
+                        const float4* bp = reinterpret_cast<const float4*>(args.bias + col);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float4 q = __ldg(bp + i);
+                            f2split(add2(f2(x[4 * i], x[4 * i + 1]), f2(q.x, q.y)), x[4 * i], x[4 * i + 1]);
+                            f2split(add2(f2(x[4 * i + 2], x[4 * i + 3]), f2(q.z, q.w)), x[4 * i + 2], x[4 * i + 3]);
+                        }
+                    }
                 };
                 const int dh = args.rope_dh, hd = dh / 2;
                 const int colw = n_blk * BN + half * HALF;
                 const int pos = (args.positions && row < args.M) ? __ldg(args.positions + row) : 0;
-                uint8_t* box0 = boxes;
-                uint8_t* box1 = boxes + kStageBytes;
+                // four 2 KB 16-bit boxes in the warp's staging area: column
+                // pairs alternate between boxes {0, 1} and {2, 3} (k counts
+                // this warp's pairs across tiles), so one pair's stores read
+                // shared memory while the next is computed
                 float amax = 0.f;
 #pragma unroll 1
                 for (int h0 = 0; h0 < HALF; h0 += dh) {
@@ -490,29 +523,47 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     const bool is_k = !is_q && gcol < args.rope_qd + args.rope_kvd;
                     const float* g = is_q ? args.q_norm : (is_k ? args.k_norm : nullptr);
                     const bool rot = (is_q || is_k) && args.rope_cos != nullptr;
-                    float inv = 1.0f;
-                    if (g) {  // the head's RMS over its dh values
-                        float ssq = 0.f;
-#pragma unroll 1
-                        for (int c = 0; c < dh; c += 32) {
-                            uint32_t r[32];
-                            tmem_ld32(taddr + h0 + c, r);
-                            tmem_ld_wait();
-#pragma unroll
-                            for (int i = 0; i < 32; ++i) {
-                                const float v = value(r[i], gcol + c + i);
-                                ssq = fmaf(v, v, ssq);
-                            }
-                        }
-                        inv = 1.0f / sqrtf(ssq / static_cast<float>(dh) + args.rope_eps);
-                    }
                     const float* cs = rot ? args.rope_cos + static_cast<int64_t>(pos) * hd : nullptr;
                     const float* sn = rot ? args.rope_sin + static_cast<int64_t>(pos) * hd : nullptr;
+                    // the row's table entries come from L2 (one row per
+                    // lane): each 16-column step's are requested one step
+                    // ahead, the first ones before the norm pass
+                    float4 nc[4], ns[4];
+                    if (rot) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            nc[i] = __ldg(reinterpret_cast<const float4*>(cs) + i);
+                            ns[i] = __ldg(reinterpret_cast<const float4*>(sn) + i);
+                        }
+                    }
+                    float inv = 1.0f;
+                    if (g) {  // the head's RMS over its dh values
+                        float ssq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+                        for (int c = 0; c < dh; c += 32) {
+                            uint32_t ra[16], rb[16];
+                            tmem_ld16(taddr + h0 + c, ra);
+                            tmem_ld16(taddr + h0 + c + 16, rb);
+                            tmem_ld_wait();
+                            float xa[16], xb[16];
+                            values16(ra, gcol + c, xa);
+                            values16(rb, gcol + c + 16, xb);
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                ssq[i & 1] = fmaf(xa[i], xa[i], ssq[i & 1]);
+                                ssq[2 + (i & 1)] = fmaf(xb[i], xb[i], ssq[2 + (i & 1)]);
+                            }
+                        }
+                        inv = 1.0f / sqrtf(((ssq[0] + ssq[1]) + (ssq[2] + ssq[3])) / static_cast<float>(dh) +
+                                           args.rope_eps);
+                    }
                     // columns d (first half) and d + dh/2 (second half) of the
                     // head together, 32 at a time into the two staging boxes
 #pragma unroll 1
-                    for (int c = 0; c < hd; c += 32) {
-                        if (lane == 0) bulk_wait_read<0>();  // both boxes free
+                    for (int c = 0; c < hd; c += 32, ++k) {
+                        uint8_t* box0 = boxes + (k & 1) * 2 * kY16Bytes;
+                        uint8_t* box1 = box0 + kY16Bytes;
+                        if (lane == 0) bulk_wait_read<1>();  // the pair two back has read these boxes
                         __syncwarp();
 #pragma unroll 1
                         for (int sub = 0; sub < 32; sub += 16) {
@@ -522,23 +573,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             tmem_ld16(taddr + h0 + hd + d0, rb);
                             tmem_ld_wait();
                             float x1[16], x2[16];
-#pragma unroll
-                            for (int i = 0; i < 16; ++i) {
-                                x1[i] = value(ra[i], gcol + d0 + i);
-                                x2[i] = value(rb[i], gcol + hd + d0 + i);
-                            }
+                            values16(ra, gcol + d0, x1);
+                            values16(rb, gcol + hd + d0, x2);
                             if (g) {
 #pragma unroll
-                                for (int i = 0; i < 16; ++i) {
-                                    x1[i] = x1[i] * inv * __ldg(g + d0 + i);
-                                    x2[i] = x2[i] * inv * __ldg(g + hd + d0 + i);
+                                for (int i = 0; i < 16; i += 4) {
+                                    const float4 ga = __ldg(reinterpret_cast<const float4*>(g + d0 + i));
+                                    const float4 gb = __ldg(reinterpret_cast<const float4*>(g + hd + d0 + i));
+                                    const float gaa[4] = {ga.x, ga.y, ga.z, ga.w}, gbb[4] = {gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+                                    for (int e = 0; e < 4; ++e) {
+                                        x1[i + e] = x1[i + e] * inv * gaa[e];
+                                        x2[i + e] = x2[i + e] * inv * gbb[e];
+                                    }
                                 }
                             }
                             if (rot) {
+                                float4 c4v[4], s4v[4];
+#pragma unroll
+                                for (int i = 0; i < 4; ++i) {
+                                    c4v[i] = nc[i];
+                                    s4v[i] = ns[i];
+                                }
+                                if (d0 + 16 < hd) {  // the next step's entries
+#pragma unroll
+                                    for (int i = 0; i < 4; ++i) {
+                                        nc[i] = __ldg(reinterpret_cast<const float4*>(cs + d0 + 16) + i);
+                                        ns[i] = __ldg(reinterpret_cast<const float4*>(sn + d0 + 16) + i);
+                                    }
+                                }
 #pragma unroll
                                 for (int i = 0; i < 16; i += 4) {
-                                    const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs + d0 + i));
-                                    const float4 s4 = __ldg(reinterpret_cast<const float4*>(sn + d0 + i));
+                                    const float4 c4 = c4v[i / 4], s4 = s4v[i / 4];
                                     const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
                                     for (int e = 0; e < 4; ++e) {
@@ -548,8 +614,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                     }
                                 }
                             }
+                            if constexpr (F16) {
 #pragma unroll
-                            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fmaxf(fabsf(x1[i]), fabsf(x2[i])));
+                                for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fmaxf(fabsf(x1[i]), fabsf(x2[i])));
+                            }
 #pragma unroll
                             for (int q = 0; q < 2; ++q) {
                                 const int ci = sub / 8 + q;  // 16-byte chunk of the 64-byte box row
