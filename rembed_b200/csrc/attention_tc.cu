@@ -50,12 +50,40 @@ struct AttnTc {
     static constexpr int THREADS = 192;
     // CTAs per SM (shared memory, TMEM, registers)
     static constexpr int MIN_BLOCKS = D <= 64 ? 3 : (D == 128 ? 2 : 1);
+    // Which pairs of scores (bit j: pair index % 4 == j) take their
+    // exponentials on the FMA pipe (ex2_fma) instead of the transcendental
+    // unit, which also converts P to 16 bits.  Measured per head dim
+    // (rg_attention, B200): at 128 one pair in four lifts Qwen3's causal
+    // layers from 295 to 349 TFLOP/s (two in four: 285); at 64 (three CTAs
+    // per SM, 96 registers) every share was slower (682 -> 642 TFLOP/s at one
+    // in four on ModernBERT's global layers), and at 256 it made no
+    // difference.
+    static constexpr unsigned EXP_FMA_MASK = D == 128 ? 0x1u : 0x0u;
 };
 
 __device__ __forceinline__ float ex2f(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+// 2^x on the FMA pipe, for a share of the exponentials so that the
+// transcendental unit (which also converts P to 16 bits) is not the only
+// one computing them.  Range reduction with the round-to-nearest magic
+// constant 1.5 * 2^23: t = x + M holds n = round(x) in its low mantissa bits,
+// f = x - (t - M) in [-1/2, 1/2]; 2^f by a cubic fitted here to 2^f on
+// [-1/2, 1/2] for least relative error (max 7.5e-5, below the 16-bit rounding
+// of P that follows); 2^n enters by adding n to the exponent field, and
+// since M's low nine bits are zero, n << 23 = t_bits << 23 (mod 2^32).  x is
+// clamped at -125 so that the exponent stays normal (2^-125 is zero for P).
+__device__ __forceinline__ float ex2_fma(float x) {
+    x = fmaxf(x, -125.0f);
+    const float M = 12582912.0f;
+    const float t = x + M;
+    const float f = x - (t - M);
+    float p = fmaf(0.05517112836241722f, f, 0.24261008203029633f);
+    p = fmaf(p, f, 0.6932609677314758f);
+    p = fmaf(p, f, 0.9999281167984009f);
+    return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
 }
 // max(a, b, c) in one instruction (sm_100).
 __device__ __forceinline__ float max3f(float a, float b, float c) {
@@ -335,8 +363,12 @@ __global__ void __launch_bounds__(192, AttnTc<D>::MIN_BLOCKS)
             float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int c = 0; c < BKV / 2; ++c) {
-                const float a = ex2f(fmaf(__uint_as_float(sr[2 * c]), cs, xoff));
-                const float b = ex2f(fmaf(__uint_as_float(sr[2 * c + 1]), cs, xoff));
+                const float xa = fmaf(__uint_as_float(sr[2 * c]), cs, xoff);
+                const float xb = fmaf(__uint_as_float(sr[2 * c + 1]), cs, xoff);
+                // EXP_FMA_MASK pairs of every four on the FMA pipe
+                const bool fma_pipe = (S::EXP_FMA_MASK >> (c & 3)) & 1;
+                const float a = fma_pipe ? ex2_fma(xa) : ex2f(xa);
+                const float b = fma_pipe ? ex2_fma(xb) : ex2f(xb);
                 ls[c & 3] += a + b;
                 pk[c] = pack2<F16>(a, b);
             }

@@ -121,12 +121,12 @@ static cudaError_t launch_impl(GemmKind kind, int epi, int block_n, GemmMaps& m,
     // (a gated epilogue adds no bias: its folded norm must have none either)
     if (args.fold_stats &&
         (!k16 || !args.fold_c1 ||
-         (epi_is_glu(epi) ? false : (!args.bias || (epi != kEpiBias && epi != kEpiBiasGelu && epi != kEpiQkRope)))))
+         (epi_is_glu(epi) ? false : (!args.bias || (epi != kEpiBias && epi != kEpiBiasGelu && epi != kEpiRope)))))
         return cudaErrorInvalidValue;
-    if (epi == kEpiQkRope &&
+    if (epi == kEpiRope &&
         (f32out || args.rope_dh <= 0 || args.rope_dh % 64 != 0 || (block_n / 2) % args.rope_dh != 0 ||
-         args.rope_qd % args.rope_dh != 0 || args.rope_kvd % args.rope_dh != 0 ||
-         ((args.rope_cos || args.rope_sin) && (!args.rope_cos || !args.rope_sin || !args.positions))))
+         args.rope_qd % args.rope_dh != 0 || args.rope_kvd % args.rope_dh != 0 || !args.rope_cos ||
+         !args.rope_sin || !args.positions))
         return cudaErrorInvalidValue;
     if ((args.parts_out || args.out16) && (!k16 || !epi_has_residual(epi))) return cudaErrorInvalidValue;
     if (args.out16) {

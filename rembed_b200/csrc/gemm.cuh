@@ -24,13 +24,12 @@ enum Epilogue : int {
     // LayerNorm output of a post-norm stack that was never written out in
     // fp32 (bert.go:905-918)                                   -> fp32 (out may alias the residual)
     kEpiBiasResLN = 7,
-    // + bias (or the folded norm), then per head of rope_dh columns: Q heads
-    // (columns [0, rope_qd)) and K heads ([rope_qd, rope_qd + rope_kvd))
-    // RMS-normalised with q_norm / k_norm when those are set (QK-norm,
-    // qwen3.go:485-508) and rotated by the token's position (rotate-half
-    // RoPE, modernbert.go:125-143, products rounded before the add); V heads
-    // pass through                                              -> bf16 / fp16
-    kEpiQkRope = 8,
+    // + bias (or the folded norm), then per head of rope_dh columns the Q
+    // heads (columns [0, rope_qd)) and K heads ([rope_qd, rope_qd +
+    // rope_kvd)) rotated by the token's position (rotate-half RoPE,
+    // modernbert.go:125-143, products rounded before the add); V heads pass
+    // through                                                  -> bf16 / fp16
+    kEpiRope = 8,
 };
 inline bool epi_is_glu(int epi) { return epi >= kEpiGluSilu && epi <= kEpiGluGeluTanh; }
 inline bool epi_has_residual(int epi) { return epi == kEpiBiasRes || epi == kEpiBiasResLN; }
@@ -67,13 +66,11 @@ struct GemmArgs {
     // MMA issuer's wait runs out and the launch ends with kStatusWaitTimeout.
     long long wait_limit;
     int inject_withhold;
-    // kEpiQkRope: the QK-norm gains [rope_dh] (nullptr: no norm), the RoPE
-    // tables [positions x rope_dh / 2] (nullptr: no rotation), each row's
+    // kEpiRope: the RoPE tables [positions x rope_dh / 2], each row's
     // position in its sequence, and the head layout of the Q|K|V output.
-    const float *q_norm, *k_norm, *rope_cos, *rope_sin;
+    const float *rope_cos, *rope_sin;
     const int32_t* positions;
     int rope_dh, rope_qd, rope_kvd;
-    float rope_eps;
 };
 
 // Operand element kind of the GEMM.
@@ -106,7 +103,7 @@ bool make_w8_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t co
 // Output tile width (128, 192 or 256 columns) for an M x N GEMM on num_sms
 // SMs: the width dividing N with the least wave-quantised cost; 0 if none
 // divides N.  head_dim > 0: only widths whose per-warp half (block_n / 2)
-// holds whole heads of that many columns (kEpiQkRope).
+// holds whole heads of that many columns (kEpiRope).
 int gemm_block_n(int M, int N, int num_sms, bool glu = false, int head_dim = 0);
 
 // Rows of W one CTA loads per k-block: each CTA of the pair holds half of a

@@ -489,46 +489,6 @@ cudaError_t launch_qk_norm_rope(const QkRopeParams& p, int head_dim, cudaStream_
 }
 
 // ---------------------------------------------------------------------------
-// Small fp32 GEMM for the Dense head (gemma3.go:177-198, never quantised):
-// out[M x N] = x[M x K] . W[N x K]^T, 32 x 32 output tiles, K in steps of 32.
-__global__ void __launch_bounds__(256) dense_f32_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                       float* __restrict__ out, int M, int N, int K) {
-    pdl_trigger();
-    pdl_wait();
-    __shared__ float xs[32][33];
-    __shared__ float ws[32][33];
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
-    const int m0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int k0 = 0; k0 < K; k0 += 32) {
-        for (int r = ty; r < 32; r += 8) {
-            xs[r][tx] = (m0 + r < M && k0 + tx < K) ? x[static_cast<int64_t>(m0 + r) * K + k0 + tx] : 0.f;
-            ws[r][tx] = (n0 + r < N && k0 + tx < K) ? w[static_cast<int64_t>(n0 + r) * K + k0 + tx] : 0.f;
-        }
-        __syncthreads();
-#pragma unroll 8
-        for (int k = 0; k < 32; ++k) {
-            const float b = ws[tx][k];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc[i] = fmaf(xs[ty + 8 * i][k], b, acc[i]);
-        }
-        __syncthreads();
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int m = m0 + ty + 8 * i, n = n0 + tx;
-        if (m < M && n < N) out[static_cast<int64_t>(m) * N + n] = acc[i];
-    }
-}
-
-cudaError_t launch_dense_f32(const float* x, const float* w, float* out, int M, int N, int K, cudaStream_t st) {
-    if (M <= 0) return cudaSuccess;
-    const dim3 grid((N + 31) / 32, (M + 31) / 32);
-    launch_pdl(dense_f32_kernel, dim3(grid), dim3(256), 0, st, x, w, out, M, N, K);
-    return cudaGetLastError();
-}
-
-// ---------------------------------------------------------------------------
 // int8 -> fp16 widening, 16 weights per thread: (q + 128) placed in the low
 // mantissa byte of 1024.0 is exactly 1024 + q + 128; subtracting 1152 leaves q.
 __global__ void __launch_bounds__(256) widen_s8_f16_kernel(const uint4* __restrict__ w, size_t n16,

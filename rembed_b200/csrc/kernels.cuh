@@ -110,9 +110,6 @@ struct QkRopeParams {
 };
 cudaError_t launch_qk_norm_rope(const QkRopeParams& p, int head_dim, cudaStream_t st);
 
-// out[M x N] = x[M x K] . W[N x K]^T in fp32 (the Gemma Dense head).
-cudaError_t launch_dense_f32(const float* x, const float* w, float* out, int M, int N, int K, cudaStream_t st);
-
 // int8 -> fp16, exact (weight-only int8 at large batch: one layer's weight
 // widened just before its GEMM; the per-channel scale stays in the GEMM
 // epilogue).  n must be a multiple of 16, both pointers 16-byte aligned.

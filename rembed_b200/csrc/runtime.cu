@@ -139,7 +139,6 @@ struct Replica {
     bool fold = false;
     bool fold_rms = false;    // pre-norm stacks: the folded norms are RMSNorms (Qwen3)
     float2* parts = nullptr;  // [H / 32 x T]
-    float *pool32 = nullptr, *head_hid = nullptr, *head_out = nullptr;  // Gemma Dense head
     float* pick32 = nullptr;  // [sequences x H]: the final norm of each sequence's pooled row
     int32_t* iota = nullptr;                                            // [0, 1, ..., cap_seq]
     int64_t* d_ids = nullptr;
@@ -879,11 +878,6 @@ void ensure_workspace(rg_ctx* c, Replica& r, int T, int nseq, size_t nout) {
             for (int i = 0; i <= capS; ++i) io[i] = i;
             check(cudaMemcpy(r.iota, io.data(), sizeof(int32_t) * (capS + 1), cudaMemcpyHostToDevice), "cudaMemcpy");
         }
-        if (r.dense1) {
-            r.pool32 = ws_alloc<float>(r, static_cast<size_t>(capS) * H);
-            r.head_hid = ws_alloc<float>(r, static_cast<size_t>(capS) * d.dense_hidden);
-            r.head_out = ws_alloc<float>(r, static_cast<size_t>(capS) * H);
-        }
         if (c->mode == RG_MODE_INT8_FULL) {
             r.xq = ws_alloc<int8_t>(r, t * H);
             r.ctxq = ws_alloc<int8_t>(r, t * m.qd);
@@ -1011,12 +1005,11 @@ struct LnFold {
     float2* parts_out = nullptr;
 };
 
-// QK-norm + RoPE applied by the QKV GEMM's epilogue (kEpiQkRope).
+// RoPE applied by the QKV GEMM's epilogue (kEpiRope).
 struct QkRope {
-    const float *q_norm = nullptr, *k_norm = nullptr, *cos = nullptr, *sin = nullptr;
+    const float *cos = nullptr, *sin = nullptr;
     const int32_t* positions = nullptr;
     int dh = 0, qd = 0, kvd = 0;
-    float eps = 0.f;
 };
 
 void gemm(Replica& r, int mode, const OpMaps& tmA, const DevDense& w, int M, int epi, const float* row_scale,
@@ -1024,17 +1017,14 @@ void gemm(Replica& r, int mode, const OpMaps& tmA, const DevDense& w, int M, int
           const float* ln_g = nullptr, const float* ln_b = nullptr, const LnFold* lf = nullptr,
           const QkRope* qr = nullptr) {
     rg::GemmArgs a{};
-    if (qr) {  // the bias epilogue with QK-norm + RoPE per head
-        epi = rg::kEpiQkRope;
-        a.q_norm = qr->q_norm;
-        a.k_norm = qr->k_norm;
+    if (qr) {  // the bias epilogue with RoPE per head
+        epi = rg::kEpiRope;
         a.rope_cos = qr->cos;
         a.rope_sin = qr->sin;
         a.positions = qr->positions;
         a.rope_dh = qr->dh;
         a.rope_qd = qr->qd;
         a.rope_kvd = qr->kvd;
-        a.rope_eps = qr->eps;
     }
     a.ln_stats = ln_stats;
     a.ln_g = ln_g;
@@ -1263,10 +1253,14 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
                  nullptr, qr);
         }
     };
-    // QK-norm + RoPE in the QKV projection's epilogue where the tile widths
-    // hold whole heads (head dims 64 and 128; 16-bit outputs); otherwise
-    // (Gemma's 256-wide heads, the strict fp32 mode) a separate kernel.
-    const bool rope_in_gemm = has_rope(arch) && !f32 && dh % 64 == 0 &&
+    // RoPE in the QKV projection's epilogue where the tile widths hold whole
+    // heads (head dims 64 and 128; 16-bit outputs) and there is no QK-norm
+    // (ModernBERT, nomic): measured as fast as the separate pass and it saves
+    // the pass's HBM traffic.  A QK-norm in the epilogue (an extra pass over
+    // each head) cost more than the separate kernel (Qwen3 at
+    // 128 x U[32,1024]: 1,588 against 1,630 embeddings/s), so Qwen3, Gemma's
+    // 256-wide heads and the strict fp32 mode keep the separate kernel.
+    const bool rope_in_gemm = has_rope(arch) && !f32 && dh % 64 == 0 && !r.layers[0].q_norm &&
                               rg::gemm_block_n(T, m.nqkv, r.num_sms, false, dh) != 0;
     auto post_norm = [&](const float* g, const float* b, bool last) {
         ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * Hd * (4.0 + 2.0 + (s8 ? 1.0 : 0.0) + (last ? 4.0 : 0.0)));
@@ -1335,15 +1329,12 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         }
         if (rope_in_gemm) {
             QkRope qr;
-            qr.q_norm = L.q_norm;
-            qr.k_norm = L.k_norm;
             qr.cos = L.global ? r.cos_g : r.cos_l;
             qr.sin = L.global ? r.sin_g : r.sin_l;
             qr.positions = r.pos32;
             qr.dh = dh;
             qr.qd = m.qd;
             qr.kvd = m.kvd;
-            qr.eps = eps;
             input_gemm(L.qkv, r.tm_x, rg::kEpiBias, r.qkv, &qr);
         } else {
             input_gemm(L.qkv, r.tm_x, rg::kEpiBias, f32 ? static_cast<void*>(r.qkv32) : r.qkv);
