@@ -890,18 +890,42 @@ __global__ void __launch_bounds__(256) pool_kernel(const float* __restrict__ x32
     __shared__ double red[8];
     const int s = blockIdx.x;
     const int s0 = __ldg(cu + s), L = __ldg(cu + s + 1) - s0;
-    for (int j = threadIdx.x; j < H; j += blockDim.x) {
-        float v;
-        if (pooling == 1) {  // cls: first token
-            v = x32[static_cast<int64_t>(s0) * H + j];
-        } else if (pooling == 2) {  // lasttoken
-            v = x32[static_cast<int64_t>(s0 + L - 1) * H + j];
-        } else {  // mean, poolMean (bert.go:692-703): sequential sum, times 1/L
-            float acc = 0.f;
-            for (int i = 0; i < L; ++i) acc += x32[static_cast<int64_t>(s0 + i) * H + j];
-            v = acc * (1.0f / static_cast<float>(L));
+    if (pooling == 0) {
+        // mean, poolMean (bert.go:692-703): each column summed in row order,
+        // times 1/L; four columns per thread (16-byte loads) and eight rows'
+        // loads issued before they are added (H % 4 == 0)
+        const float invL = 1.0f / static_cast<float>(L);
+        for (int j = 4 * threadIdx.x; j < H; j += 4 * blockDim.x) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            const float* col = x32 + static_cast<int64_t>(s0) * H + j;
+            int i = 0;
+            for (; i + 8 <= L; i += 8) {
+                float4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = __ldg(reinterpret_cast<const float4*>(col + static_cast<int64_t>(i + u) * H));
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    acc.x += v[u].x;
+                    acc.y += v[u].y;
+                    acc.z += v[u].z;
+                    acc.w += v[u].w;
+                }
+            }
+            for (; i < L; ++i) {
+                const float4 v = __ldg(reinterpret_cast<const float4*>(col + static_cast<int64_t>(i) * H));
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
+            }
+            pooled[j] = acc.x * invL;
+            pooled[j + 1] = acc.y * invL;
+            pooled[j + 2] = acc.z * invL;
+            pooled[j + 3] = acc.w * invL;
         }
-        pooled[j] = v;
+    } else {
+        for (int j = threadIdx.x; j < H; j += blockDim.x)  // cls: first token; lasttoken: last
+            pooled[j] = x32[static_cast<int64_t>(pooling == 1 ? s0 : s0 + L - 1) * H + j];
     }
     __syncthreads();
     auto block_sumsq = [&](int n) -> double {
@@ -938,6 +962,7 @@ __global__ void __launch_bounds__(256) pool_kernel(const float* __restrict__ x32
 cudaError_t launch_pool(const float* x32, const int32_t* cu, int nseq, int H, int pooling, int normalize, int dim,
                         float* out, cudaStream_t st) {
     if (nseq <= 0) return cudaSuccess;
+    if (H % 4 != 0) return cudaErrorInvalidValue;
     launch_pdl(pool_kernel, dim3(nseq), dim3(256), H * sizeof(float), st, x32, cu, H, pooling, normalize, dim, out);
     return cudaGetLastError();
 }
@@ -1029,16 +1054,32 @@ __global__ void __cluster_dims__(kHeadCtas, 1, 1) __launch_bounds__(kHeadThreads
                 r1 = r0 + 1;
             }
         }
-        for (int j = t; j < H; j += kHeadThreads) {
-            float acc = 0.f;
+        // four columns per thread (16-byte loads, a warp reads 512
+        // contiguous bytes of a row) and eight rows' loads issued before
+        // they are added, in row order
+        for (int j = 4 * t; j < H; j += 4 * kHeadThreads) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             int i = r0;
-            for (; i + 4 <= r1; i += 4) {
-                const float a0 = x32[static_cast<int64_t>(i) * H + j], a1 = x32[static_cast<int64_t>(i + 1) * H + j];
-                const float a2 = x32[static_cast<int64_t>(i + 2) * H + j], a3 = x32[static_cast<int64_t>(i + 3) * H + j];
-                acc = (((acc + a0) + a1) + a2) + a3;
+            for (; i + 8 <= r1; i += 8) {
+                float4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = __ldg(reinterpret_cast<const float4*>(x32 + static_cast<int64_t>(i + u) * H + j));
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    acc.x += v[u].x;
+                    acc.y += v[u].y;
+                    acc.z += v[u].z;
+                    acc.w += v[u].w;
+                }
             }
-            for (; i < r1; ++i) acc += x32[static_cast<int64_t>(i) * H + j];
-            part[g * H + j] = acc;
+            for (; i < r1; ++i) {
+                const float4 v = __ldg(reinterpret_cast<const float4*>(x32 + static_cast<int64_t>(i) * H + j));
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
+            }
+            *reinterpret_cast<float4*>(part + g * H + j) = acc;
         }
     }
     cluster_sync();
@@ -1125,7 +1166,7 @@ __global__ void __cluster_dims__(kHeadCtas, 1, 1) __launch_bounds__(kHeadThreads
 cudaError_t launch_pool_head(const float* x32, const int32_t* cu, int nseq, int H, int D, int pooling,
                              const float* w1, const float* w2, int normalize, int dim, float* out, cudaStream_t st) {
     if (nseq <= 0) return cudaSuccess;
-    if (H % kHeadCtas != 0 || D % kHeadCtas != 0 || dim < 1 || dim > H) return cudaErrorInvalidValue;
+    if (H % kHeadCtas != 0 || H % 4 != 0 || D % kHeadCtas != 0 || dim < 1 || dim > H) return cudaErrorInvalidValue;
     const size_t smem = sizeof(float) * (3 * kHeadSeqs * static_cast<size_t>(H) + kHeadSeqs * static_cast<size_t>(D));
     static unsigned configured = 0;
     int dev = 0;
