@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(192, AttnTc<D>::MIN_BLOCKS)
     constexpr int BKV = S::BKV, QB = S::QB;
     pdl_trigger();
     pdl_wait();  // the previous kernel's outputs are complete from here on
-    const int s = blockIdx.z, h = blockIdx.y;
+    const int s = p.reverse ? gridDim.z - 1 - blockIdx.z : blockIdx.z, h = blockIdx.y;
     const int s0 = __ldg(p.cu + s), L = __ldg(p.cu + s + 1) - s0;
     const int q0 = blockIdx.x * 128;
     if (q0 >= L) return;

@@ -66,6 +66,9 @@ struct GemmArgs {
     // MMA issuer's wait runs out and the launch ends with kStatusWaitTimeout.
     long long wait_limit;
     int inject_withhold;
+    // Walk the row blocks from the last to the first (see the forward's
+    // L2-aware ordering): the output is the same, only the order of tiles.
+    int reverse_m;
     // kEpiRope: the RoPE tables [positions x rope_dh / 2], each row's
     // position in its sequence, and the head layout of the Q|K|V output.
     const float *rope_cos, *rope_sin;

@@ -202,6 +202,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int m_tiles = (args.M + 255) / 256;
     const int n_tiles = args.N / BN;
     const int num_tiles = m_tiles * n_tiles;
+    // Row block of a tile: m-major order, last row block first when
+    // args.reverse_m (so that the rows the previous kernel wrote last, still
+    // in L2, are read first).
+    auto m_of = [&](int t) { return args.reverse_m ? m_tiles - 1 - t / n_tiles : t / n_tiles; };
     const int kb_real = args.K / K_ELEMS;
     const int kblocks = X3 ? 3 * kb_real : kb_real;
     const long long wlim = args.wait_limit > 0 ? args.wait_limit : kWaitLimitCycles;
@@ -255,7 +259,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         uint32_t phase = 0;
         uint32_t issued_mask = 0, issued_parity = 0;
         for (int tile = pair; tile < num_tiles; tile += npairs) {
-            const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
+            const int m_blk = m_of(tile), n_blk = tile % n_tiles;
             bool ok = true;
             for (int kb = 0; kb < kblocks; ++kb) {
                 if (!mbar_wait(&empty[stage], phase ^ 1, args.status, abort_flag, wlim)) {
@@ -412,7 +416,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         auto load_residual = [&](int t, int c, int b) {
             if constexpr (RES) {
                 if (t >= num_tiles) return;
-                const int row0 = (t / n_tiles) * 256 + static_cast<int>(rank) * 128 + quarter * 32;
+                const int row0 = m_of(t) * 256 + static_cast<int>(rank) * 128 + quarter * 32;
                 const int col0 = (t % n_tiles) * BN + half * HALF + c * kChunk;
                 mbar_arrive_expect_tx(&rbar[b], kStageBytes);
                 tma_load_2d(boxes + b * kStageBytes, &tmRes, &rbar[b], col0, row0);
@@ -424,7 +428,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         uint32_t acc_phase = 0;
         bool ok = true;
         for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-            const int m_blk = tile / n_tiles, n_blk = tile % n_tiles;
+            const int m_blk = m_of(tile), n_blk = tile % n_tiles;
             const int row0 = m_blk * 256 + static_cast<int>(rank) * 128 + quarter * 32;
             const int row = row0 + lane;
             // Per-row operands of the epilogue, fetched while the tile's MMAs run.

@@ -987,6 +987,9 @@ cudaError_t launch_pool(const float* x32, const int32_t* cu, int nseq, int H, in
 // (never quantised, as in the reference) and are read once per cluster.
 constexpr int kHeadCtas = 8, kHeadSeqs = 4, kHeadThreads = 256;
 
+// Loads from another CTA's shared memory (distributed shared memory).
+// Callers issue several of them before using the results, so that their
+// latencies overlap.
 __device__ __forceinline__ float ld_dsmem_f32(const float* local, uint32_t rank) {
     const uint32_t a = mapa_shared(smem_u32(local), rank);
     float v;
@@ -1000,25 +1003,47 @@ __device__ __forceinline__ double ld_dsmem_f64(const double* local, uint32_t ran
     return v;
 }
 
-// One column per warp: out[g][col] = sum_k x[g][k] * w[col][k] for the group's
-// kHeadSeqs rows of x (shared memory, row stride K); lanes split K.
+// Columns [col0, col0 + ncols) of out[g][col] = sum_k x[g][k] * w[col][k]
+// for the group's kHeadSeqs rows of x (shared memory, row stride K): each
+// warp takes four columns at a time, lanes split K (coalesced weight rows),
+// and the k loop is unrolled so that sixteen weight loads are in flight per
+// lane (the weights come from L2: one column at a time would wait for them
+// one by one).
+constexpr int kHeadColsPerWarp = 4;
 __device__ __forceinline__ void head_columns(const float* __restrict__ w, const float* x, int K, int col0, int ncols,
                                              float* out, int out_stride, int warp, int lane) {
-    for (int c = warp; c < ncols; c += kHeadThreads / 32) {
-        const float* wr = w + static_cast<int64_t>(col0 + c) * K;
-        float acc[kHeadSeqs];
+    for (int c = warp * kHeadColsPerWarp; c < ncols; c += (kHeadThreads / 32) * kHeadColsPerWarp) {
+        const float* wr[kHeadColsPerWarp];
+        bool on[kHeadColsPerWarp];
 #pragma unroll
-        for (int g = 0; g < kHeadSeqs; ++g) acc[g] = 0.f;
+        for (int i = 0; i < kHeadColsPerWarp; ++i) {
+            on[i] = c + i < ncols;
+            wr[i] = w + static_cast<int64_t>(col0 + (on[i] ? c + i : c)) * K;
+        }
+        float acc[kHeadColsPerWarp][kHeadSeqs];
+#pragma unroll
+        for (int i = 0; i < kHeadColsPerWarp; ++i)
+#pragma unroll
+            for (int g = 0; g < kHeadSeqs; ++g) acc[i][g] = 0.f;
+#pragma unroll 4
         for (int k = lane; k < K; k += 32) {
-            const float wv = __ldg(wr + k);
+            float wv[kHeadColsPerWarp];
 #pragma unroll
-            for (int g = 0; g < kHeadSeqs; ++g) acc[g] = fmaf(x[g * K + k], wv, acc[g]);
+            for (int i = 0; i < kHeadColsPerWarp; ++i) wv[i] = __ldg(wr[i] + k);
+#pragma unroll
+            for (int g = 0; g < kHeadSeqs; ++g) {
+                const float xv = x[g * K + k];
+#pragma unroll
+                for (int i = 0; i < kHeadColsPerWarp; ++i) acc[i][g] = fmaf(xv, wv[i], acc[i][g]);
+            }
         }
 #pragma unroll
-        for (int g = 0; g < kHeadSeqs; ++g) {
-            const float v = warp_sum(acc[g]);
-            if (lane == 0) out[g * out_stride + col0 + c] = v;
-        }
+        for (int i = 0; i < kHeadColsPerWarp; ++i)
+#pragma unroll
+            for (int g = 0; g < kHeadSeqs; ++g) {
+                const float v = warp_sum(acc[i][g]);
+                if (lane == 0 && on[i]) out[g * out_stride + col0 + c + i] = v;
+            }
     }
 }
 
@@ -1055,17 +1080,17 @@ __global__ void __cluster_dims__(kHeadCtas, 1, 1) __launch_bounds__(kHeadThreads
             }
         }
         // four columns per thread (16-byte loads, a warp reads 512
-        // contiguous bytes of a row) and eight rows' loads issued before
+        // contiguous bytes of a row) and sixteen rows' loads issued before
         // they are added, in row order
         for (int j = 4 * t; j < H; j += 4 * kHeadThreads) {
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             int i = r0;
-            for (; i + 8 <= r1; i += 8) {
-                float4 v[8];
+            for (; i + 16 <= r1; i += 16) {
+                float4 v[16];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) v[u] = __ldg(reinterpret_cast<const float4*>(x32 + static_cast<int64_t>(i + u) * H + j));
+                for (int u = 0; u < 16; ++u) v[u] = __ldg(reinterpret_cast<const float4*>(x32 + static_cast<int64_t>(i + u) * H + j));
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
+                for (int u = 0; u < 16; ++u) {
                     acc.x += v[u].x;
                     acc.y += v[u].y;
                     acc.z += v[u].z;
@@ -1088,27 +1113,49 @@ __global__ void __cluster_dims__(kHeadCtas, 1, 1) __launch_bounds__(kHeadThreads
         float invL = 1.0f;
         if (s < nseq && pooling == 0) invL = 1.0f / static_cast<float>(__ldg(cu + s + 1) - __ldg(cu + s));
         for (int j = t; j < H; j += kHeadThreads) {
+            float pv[kHeadCtas];
+#pragma unroll
+            for (int q = 0; q < kHeadCtas; ++q) pv[q] = ld_dsmem_f32(part + g * H + j, q);
             float v = 0.f;
-            for (int q = 0; q < kHeadCtas; ++q) v += ld_dsmem_f32(part + g * H + j, q);
+#pragma unroll
+            for (int q = 0; q < kHeadCtas; ++q) v += pv[q];  // rank order
             pooled[g * H + j] = v * invL;
         }
     }
     __syncthreads();
-    // 2. this CTA's hidden columns, then the whole hidden vector
     const int dper = D / kHeadCtas, hper = H / kHeadCtas;
+    if (!w1) {
+        // no Dense head: the output slice is the pooled vector's
+        for (int i = t; i < kHeadSeqs * hper; i += kHeadThreads) {
+            const int g = i / hper, c = static_cast<int>(rank) * hper + i % hper;
+            y[g * H + c] = pooled[g * H + c];
+        }
+        __syncthreads();
+    } else {
+    // 2. this CTA's hidden columns, then the whole hidden vector
     head_columns(w1, pooled, H, static_cast<int>(rank) * dper, dper, hid, D, warp, lane);
     cluster_sync();
     for (int q = 0; q < kHeadCtas; ++q) {
         if (q == static_cast<int>(rank)) continue;
-        for (int i = t; i < kHeadSeqs * dper; i += kHeadThreads) {
-            const int g = i / dper, c = q * dper + i % dper;
-            hid[g * D + c] = ld_dsmem_f32(hid + g * D + c, q);
+        for (int i0 = t; i0 < kHeadSeqs * dper; i0 += 4 * kHeadThreads) {
+            float hv[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + u * kHeadThreads;
+                hv[u] = i < kHeadSeqs * dper ? ld_dsmem_f32(hid + (i / dper) * D + q * dper + i % dper, q) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + u * kHeadThreads;
+                if (i < kHeadSeqs * dper) hid[(i / dper) * D + q * dper + i % dper] = hv[u];
+            }
         }
     }
     __syncthreads();
     // 3. this CTA's output columns
     head_columns(w2, hid, D, static_cast<int>(rank) * hper, hper, y, H, warp, lane);
     __syncthreads();
+    }
     // 4. L2 over H, then (dim < H) over the first dim columns
     const int c0 = static_cast<int>(rank) * hper;
     for (int pass = 0; pass < 2; ++pass) {
@@ -1141,8 +1188,12 @@ __global__ void __cluster_dims__(kHeadCtas, 1, 1) __launch_bounds__(kHeadThreads
         }
         cluster_sync();
         if (t < kHeadSeqs) {
+            double sv[kHeadCtas];
+#pragma unroll
+            for (int q = 0; q < kHeadCtas; ++q) sv[q] = ld_dsmem_f64(&ss[pass][t], q);
             double v = 0.0;
-            for (int q = 0; q < kHeadCtas; ++q) v += ld_dsmem_f64(&ss[pass][t], q);
+#pragma unroll
+            for (int q = 0; q < kHeadCtas; ++q) v += sv[q];  // rank order
             scale[t] = v != 0.0 ? static_cast<float>(1.0 / sqrt(v)) : 1.0f;
         }
         __syncthreads();
@@ -1166,6 +1217,7 @@ __global__ void __cluster_dims__(kHeadCtas, 1, 1) __launch_bounds__(kHeadThreads
 cudaError_t launch_pool_head(const float* x32, const int32_t* cu, int nseq, int H, int D, int pooling,
                              const float* w1, const float* w2, int normalize, int dim, float* out, cudaStream_t st) {
     if (nseq <= 0) return cudaSuccess;
+    if (!w1 || !w2) D = 0;  // pooling, L2 and truncation only
     if (H % kHeadCtas != 0 || H % 4 != 0 || D % kHeadCtas != 0 || dim < 1 || dim > H) return cudaErrorInvalidValue;
     const size_t smem = sizeof(float) * (3 * kHeadSeqs * static_cast<size_t>(H) + kHeadSeqs * static_cast<size_t>(D));
     static unsigned configured = 0;

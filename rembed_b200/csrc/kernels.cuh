@@ -142,6 +142,7 @@ struct AttnParams {
     int T;         // rows of the packed buffers (tensor-map extent)
     int kv_heads;  // key/value heads (heads / group)
     int* status;   // device status word (bounded waits)
+    int reverse;   // visit the sequences from the last to the first (L2 reuse of the rows written last)
 };
 // Head dims 32, 64, 128 and 256 (the tcgen05 kernel, attention_tc.cu).
 cudaError_t launch_attention(const AttnParams& p, int nseq, int max_len, int heads, int head_dim, cudaStream_t st);
@@ -179,7 +180,10 @@ cudaError_t launch_pool(const float* x32, const int32_t* cu, int nseq, int H, in
 // The same with the Dense head between pooling and L2 (gemma3.go:177-198):
 // pooled -> W1 [D x H] -> W2 [H x D] -> L2 -> truncate, one launch (clusters
 // of 8 CTAs share each stage through distributed shared memory).  H and D
-// must be multiples of 8.
+// must be multiples of 8.  Without a head (w1 / w2 nullptr) the same kernel
+// pools, normalises and truncates: the mean pooling of long sequences is
+// then spread over eight CTAs per sequence group instead of one CTA per
+// sequence.
 cudaError_t launch_pool_head(const float* x32, const int32_t* cu, int nseq, int H, int D, int pooling,
                              const float* w1, const float* w2, int normalize, int dim, float* out, cudaStream_t st);
 

@@ -171,6 +171,7 @@ struct Replica {
     int tm_T = -1;
     int last_launches = 0;
     const int32_t* h_cu_view = nullptr;  // host copy of the current batch's offsets
+    int rev_m = 0;  // the next GEMMs walk their row blocks last to first (L2-aware order)
     // kernel timing (rg_profile)
     bool prof = false;
     // CUDA graphs of whole forwards, one per batch shape and buffer set (see
@@ -1053,6 +1054,7 @@ void gemm(Replica& r, int mode, const OpMaps& tmA, const DevDense& w, int M, int
     a.out = out;
     a.ld_out = rg::epi_is_glu(epi) ? w.N / 2 : w.N;
     a.status = r.d_status;
+    a.reverse_m = r.rev_m;
     const rg::GemmKind kind = mode == RG_MODE_INT8_FULL ? rg::GemmKind::kS8
                               : mode == RG_MODE_F16     ? rg::GemmKind::kF16
                               : mode == RG_MODE_INT8_W  ? rg::GemmKind::kW8
@@ -1403,6 +1405,9 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
                 ap.T = T;
                 ap.kv_heads = m.nkv;
                 ap.status = r.d_status;
+                // L2-aware order: the QKV GEMM wrote the last sequences'
+                // rows last, so they are the ones still in the 126 MB L2
+                ap.reverse = 1;
                 check(rg::launch_attention(ap, nseq, max_len, m.nq, dh, st), "attention launch");
             }
             ++launches;
@@ -1435,6 +1440,9 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         }
         if (s8) quantize(r.ffh, I, r.ffhq, r.ffhs);
         const bool last = li == d.num_hidden_layers - 1;
+        // FFN2 reads the FFN hidden state (4x the hidden width) that FFN1
+        // just wrote in row-block order: last block first finds it in L2
+        r.rev_m = 1;
         if (!pre && r.fold && !last) {
             residual_gemm(r.tm_ffh, L.ffn2, nullptr, true);
             fold_norm(L.ln2_g, L.ln2_b);
@@ -1456,6 +1464,7 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
                 gemm(r, mode, r.tm_ffh, L.ffn2, T, rg::kEpiBiasRes, s8 ? r.ffhs : nullptr, r.x32, r.x32, st,
                      launches);
         }
+        r.rev_m = 0;
     }
     if (r.final_norm && pick) {
         picked_norm(r.final_norm, arch == RG_ARCH_MODERNBERT ? r.zero_beta : nullptr, arch != RG_ARCH_MODERNBERT);
@@ -1488,6 +1497,11 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
             check(rg::launch_pool_head(src, src_cu, nseq, H, d.dense_hidden, pooling, r.dense1, r.dense2, d.normalize,
                                        out_dim, d_out, st),
                   "pool/head launch");
+            ++launches;
+        } else if (pooling == 0 && H % 8 == 0) {
+            // mean pooling over whole sequences: rows spread over clusters
+            check(rg::launch_pool_head(src, src_cu, nseq, H, 0, 0, nullptr, nullptr, d.normalize, out_dim, d_out, st),
+                  "pool launch");
             ++launches;
         } else {
             check(rg::launch_pool(src, src_cu, nseq, H, pooling, d.normalize, out_dim, d_out, st), "pool launch");
