@@ -244,7 +244,7 @@ def reference_arm(args, rank, world):
 
 # ---------------------------------------------------------------------------
 class NvmlClockSampler:
-    """SM clock, power and clock-event reasons read through NVML every 10 ms
+    """SM clock, power and clock-event reasons read through NVML every 2 ms
     by a background thread while the timed region runs (reads only)."""
 
     def __init__(self, uuid: str | None):
@@ -267,7 +267,7 @@ class NvmlClockSampler:
                                   "reasons": int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))})
             except nv.NVMLError:
                 pass
-            self.stop.wait(0.01)
+            self.stop.wait(0.002)
 
     def __enter__(self):
         self.thread = threading.Thread(target=self._run, daemon=True)
@@ -303,7 +303,8 @@ class NvmlClockSampler:
         sm = [r["sm"] for r in self.rows]
         return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": reasons, "other_reasons": others,
                 "sm_mhz_range": [min(sm), max(sm)], "samples": len(self.rows),
-                "source": "NVML every 10 ms during the timed region",
+                "source": "NVML every 2 ms during the timed region",
+                "samples_with_a_reason": sum(1 for r in self.rows if r["reasons"] & sum(bits.values())),
                 "power_w_max": round(max(r["power"] for r in self.rows), 1)}
 
 
