@@ -124,6 +124,14 @@ def test_attention_causal_kat(cuda, dtype, dh):
     ([16, 700, 257, 258], 3, 1, 256, -256, 256),
     ([1, 31, 32, 33, 128, 400], 4, 4, 32, -BIG, BIG),
     ([200, 384, 65], 2, 2, 128, -BIG, BIG),
+    # long batches (several query tiles per CTA on the 16-bit paths), with
+    # sequences shorter than one tile among them: bidirectional with GQA,
+    # causal, and a window
+    ([1, 700, 130, 1500, 257], 4, 2, 64, -BIG, BIG),
+    ([3, 1100, 640], 2, 1, 128, -BIG, 0),
+    ([900, 5, 1200], 2, 2, 64, -64, 64),
+    ([1500, 700, 33], 2, 2, 64, -600, 600),
+    ([2000, 130], 2, 1, 128, -700, 0),
 ])
 def test_attention_windows_and_heads(cuda, dtype, case):
     lens, heads, kv_heads, dh, lo, hi = case
