@@ -247,10 +247,16 @@ __global__ void __launch_bounds__(256) norm_kernel(NormParams p) {
 }
 
 // x32 += RMSNorm(o32; g): Gemma's post-attention / post-FFN norm of the
-// sublayer output before the residual add (gemma3.go:357-358, 376).
-template <int NV>
+// sublayer output before the residual add (gemma3.go:357-358, 376).  With
+// NEXT the kernel also applies the norm that reads the new residual stream
+// next (the pre-FFN norm, or the next layer's input norm: gemma3.go:359, 300)
+// to the row it holds in registers and writes that norm's outputs (the next
+// GEMM's A operand) as norm_kernel would from x32: the same values in the
+// same order, so the same bits, without reading x32 again.
+template <int NV, bool NEXT, bool F16>
 __global__ void __launch_bounds__(256) add_rmsnorm_kernel(float* __restrict__ x32, const float* __restrict__ o32,
-                                                         const float* __restrict__ g, float eps, int T, int H) {
+                                                         const float* __restrict__ g, float eps, int T, int H,
+                                                         NormParams nx) {
     pdl_trigger();
     pdl_wait();
     const int lane = threadIdx.x & 31;
@@ -280,6 +286,17 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(float* __restrict__ x3
         x.z += v[c][2] * inv * gg.z;
         x.w += v[c][3] * inv * gg.w;
         *xp = x;
+        v[c][0] = x.x;
+        v[c][1] = x.y;
+        v[c][2] = x.z;
+        v[c][3] = x.w;
+    }
+    if constexpr (NEXT) {
+        const bool overflow = norm_finish<NV, true, F16>(
+            v, nx.g, nullptr, nx.eps, H, nullptr, nx.outb ? nx.outb + off : nullptr, nx.outq ? nx.outq + off : nullptr,
+            nx.outqs ? nx.outqs + t : nullptr, lane, nullptr, nx.outhi ? nx.outhi + off : nullptr,
+            nx.outlo ? nx.outlo + off : nullptr);
+        if (overflow && nx.status && lane == 0) atomicOr(nx.status, kStatusF16Overflow);
     }
 }
 
@@ -342,11 +359,23 @@ cudaError_t launch_ln(const float* y32, const float* g, const float* b, float ep
     return launch_norm(p, false, st);
 }
 
-cudaError_t launch_add_rmsnorm(float* x32, const float* o32, const float* g, float eps, int T, int H, cudaStream_t st) {
+cudaError_t launch_add_rmsnorm(float* x32, const float* o32, const float* g, float eps, int T, int H, cudaStream_t st,
+                               const NormParams* next) {
     if (T <= 0) return cudaSuccess;
     if (H % 128 != 0) return cudaErrorInvalidValue;
     const int grid = (T + 7) / 8;
-    RG_NV_DISPATCH(H, (launch_pdl(add_rmsnorm_kernel<NV>, dim3(grid), dim3(256), 0, st, x32, o32, g, eps, T, H)));
+    NormParams nx{};
+    if (next) nx = *next;
+    if (!next) {
+        RG_NV_DISPATCH(H, (launch_pdl(add_rmsnorm_kernel<NV, false, false>, dim3(grid), dim3(256), 0, st, x32, o32, g,
+                                      eps, T, H, nx)));
+    } else if (next->f16) {
+        RG_NV_DISPATCH(H, (launch_pdl(add_rmsnorm_kernel<NV, true, true>, dim3(grid), dim3(256), 0, st, x32, o32, g,
+                                      eps, T, H, nx)));
+    } else {
+        RG_NV_DISPATCH(H, (launch_pdl(add_rmsnorm_kernel<NV, true, false>, dim3(grid), dim3(256), 0, st, x32, o32, g,
+                                      eps, T, H, nx)));
+    }
     return cudaGetLastError();
 }
 

@@ -91,7 +91,10 @@ cudaError_t launch_ln(const float* y32, const float* g, const float* b, float ep
                       uint16_t* xb, bool f16, int8_t* xq, float* xq_scale, cudaStream_t st,
                       int* status = nullptr);
 // x32 += RMSNorm(o32; g)  (Gemma's post-sublayer norms).
-cudaError_t launch_add_rmsnorm(float* x32, const float* o32, const float* g, float eps, int T, int H, cudaStream_t st);
+// x32 += RMSNorm(o32; g); with `next` (g, eps and the outputs of a NormParams)
+// also the RMSNorm of the new x32 into next's outputs, as launch_norm would.
+cudaError_t launch_add_rmsnorm(float* x32, const float* o32, const float* g, float eps, int T, int H, cudaStream_t st,
+                               const NormParams* next = nullptr);
 
 // QK-norm (optional) + RoPE (optional) in place on the q heads [0, nq) and
 // k heads of the fused qkv buffer [T x ld] (q at column 0, k at nq*dh).

@@ -1320,12 +1320,38 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
                         : arch == RG_ARCH_GEMMA3   ? rg::kEpiGluGeluTanh
                                                    : rg::kEpiGluSilu;
 
+    // Gemma: each post-norm residual add also applies the norm that reads
+    // the residual stream next (the pre-FFN norm; the next layer's input
+    // norm), writing the next GEMM's A operand as norm_into_a would.
+    const bool gemma = arch == RG_ARCH_GEMMA3;
+    auto add_post_norm = [&](const float* post_g, const float* next_g) {
+        const double out_b = next_g ? (f32 ? 8.0 : 2.0) + (s8 ? 1.0 : 0.0) : 0.0;
+        ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd * (next_g ? 2.0 : 1.0), Td * Hd * (12.0 + out_b));
+        rg::NormParams nx{};
+        if (next_g) {
+            nx.g = next_g;
+            nx.eps = eps;
+            nx.outb = f32 ? nullptr : r.xb;
+            nx.outhi = f32 ? r.xh : nullptr;
+            nx.outlo = f32 ? r.xl : nullptr;
+            nx.f16 = f16;
+            nx.status = r.d_status;
+            nx.outq = s8 ? r.xq : nullptr;
+            nx.outqs = s8 ? r.xs : nullptr;
+        }
+        check(rg::launch_add_rmsnorm(r.x32, r.y32, post_g, eps, T, H, st, next_g ? &nx : nullptr),
+              "add_rmsnorm launch");
+        ++launches;
+    };
+
     for (int li = 0; li < d.num_hidden_layers; ++li) {
         const DevLayer& L = r.layers[li];
         // ---- attention sublayer
         // (a folded pre-norm stack enters layers 1... with the norm's
-        // statistics already merged by the previous FFN's residual GEMM)
-        if (pre && !(r.fold && li > 0)) {
+        // statistics already merged by the previous FFN's residual GEMM;
+        // Gemma's layers 1... with the input norm applied by the previous
+        // layer's last residual add)
+        if (pre && !(r.fold && li > 0) && !(gemma && li > 0)) {
             norm_into_a(L.attn_norm, arch == RG_ARCH_MODERNBERT ? r.zero_beta : nullptr, arch != RG_ARCH_MODERNBERT);
             folded = false;
         }
@@ -1419,18 +1445,17 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         } else if (!pre) {
             residual_gemm(r.tm_ctx, L.o, s8 ? r.ctxs : nullptr, false);
             post_norm(L.ln1_g, L.ln1_b, false);
-        } else if (arch == RG_ARCH_GEMMA3) {
+        } else if (gemma) {
             gemm(r, mode, r.tm_ctx, L.o, T, rg::kEpiBiasF32, s8 ? r.ctxs : nullptr, nullptr, r.y32, st, launches);
-            ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * Hd * 12.0);
-            check(rg::launch_add_rmsnorm(r.x32, r.y32, L.post_attn, eps, T, H, st), "add_rmsnorm launch");
-            ++launches;
+            add_post_norm(L.post_attn, L.ffn_norm);
         } else if (r.fold) {  // residual in place + the folded FFN norm's statistics
             pre_residual_fold(r.tm_ctx, L.o);
         } else {  // residual added in place on x32
             gemm(r, mode, r.tm_ctx, L.o, T, rg::kEpiBiasRes, s8 ? r.ctxs : nullptr, r.x32, r.x32, st, launches);
         }
         // ---- FFN sublayer
-        if (pre && !r.fold) norm_into_a(L.ffn_norm, arch == RG_ARCH_MODERNBERT ? r.zero_beta : nullptr, arch != RG_ARCH_MODERNBERT);
+        if (pre && !r.fold && !gemma)
+            norm_into_a(L.ffn_norm, arch == RG_ARCH_MODERNBERT ? r.zero_beta : nullptr, arch != RG_ARCH_MODERNBERT);
         input_gemm(L.ffn1, r.tm_x, is_glu(arch) ? glu_epi : rg::kEpiBiasGelu,
                    f32 ? static_cast<void*>(r.ffhh) : r.ffh);
         if (f32) {  // the fp32 FFN hidden state -> tf32 hi (in place) + remainder
@@ -1452,11 +1477,9 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         } else if (!pre) {
             residual_gemm(r.tm_ffh, L.ffn2, s8 ? r.ffhs : nullptr, false);
             post_norm(L.ln2_g, L.ln2_b, last);
-        } else if (arch == RG_ARCH_GEMMA3) {
+        } else if (gemma) {
             gemm(r, mode, r.tm_ffh, L.ffn2, T, rg::kEpiBiasF32, s8 ? r.ffhs : nullptr, nullptr, r.y32, st, launches);
-            ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * Hd * 12.0);
-            check(rg::launch_add_rmsnorm(r.x32, r.y32, L.post_ffn, eps, T, H, st), "add_rmsnorm launch");
-            ++launches;
+            add_post_norm(L.post_ffn, last ? nullptr : r.layers[li + 1].attn_norm);
         } else {
             if (r.fold && !last)
                 pre_residual_fold(r.tm_ffh, L.ffn2);
