@@ -116,8 +116,9 @@ static cudaError_t launch_impl(GemmKind kind, int epi, int block_n, GemmMaps& m,
         return cudaErrorInvalidValue;
     if (epi == kEpiBiasResLN && (!args.ln_stats || !args.ln_g || !args.ln_b)) return cudaErrorInvalidValue;
     // Folded LayerNorm and the chunk statistics / 16-bit copy of residual
-    // outputs: 16-bit kinds only.
-    const bool k16 = kind == GemmKind::kBF16 || kind == GemmKind::kF16;
+    // outputs: the kinds with 16-bit activations only (kW8: fp16 activations,
+    // int8 weights widened in shared memory).
+    const bool k16 = kind == GemmKind::kBF16 || kind == GemmKind::kF16 || kind == GemmKind::kW8;
     // (a gated epilogue adds no bias: its folded norm must have none either)
     if (args.fold_stats &&
         (!k16 || !args.fold_c1 ||
@@ -129,8 +130,11 @@ static cudaError_t launch_impl(GemmKind kind, int epi, int block_n, GemmMaps& m,
          !args.rope_sin || !args.positions))
         return cudaErrorInvalidValue;
     if ((args.parts_out || args.out16) && (!k16 || !epi_has_residual(epi))) return cudaErrorInvalidValue;
+    if (args.copy_gain && (!args.out16 || (reinterpret_cast<uintptr_t>(args.copy_gain) & 15) != 0))
+        return cudaErrorInvalidValue;
     if (args.out16) {
-        if (!make_epilogue_tmap(&m.out16, args.out16, false, kind == GemmKind::kF16, args.M, args.N, args.ld16))
+        if (!make_epilogue_tmap(&m.out16, args.out16, false, kind == GemmKind::kF16 || kind == GemmKind::kW8, args.M,
+                                args.N, args.ld16))
             return cudaErrorInvalidValue;
     } else {
         m.out16 = m.out;  // unused

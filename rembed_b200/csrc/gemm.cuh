@@ -59,6 +59,10 @@ struct GemmArgs {
     uint16_t* out16;
     int ld16;
     float2* parts_out;
+    // optional with out16: the copy is round16(y[n] * copy_gain[n]) (a
+    // folded LayerNorm whose gain cannot go into the consumer's weight: the
+    // weight-only int8 mode keeps the reference's quantised weight)
+    const float* copy_gain;
     // Failure injection for tests (zero in production): wait_limit > 0
     // bounds every mbarrier wait of the launch at that many cycles instead of
     // about a second, and inject_withhold makes the even CTA of every pair

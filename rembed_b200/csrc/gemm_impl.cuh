@@ -123,12 +123,14 @@ template <int BN, int KIND, int EPI>
 struct GemmShape {
     static constexpr bool W8 = KIND == static_cast<int>(GemmKind::kW8);
     static constexpr bool Y16 = (EPI == kEpiBiasRes || EPI == kEpiBiasResLN) &&
-                                (KIND == static_cast<int>(GemmKind::kBF16) || KIND == static_cast<int>(GemmKind::kF16));
+                                (KIND == static_cast<int>(GemmKind::kBF16) || KIND == static_cast<int>(GemmKind::kF16) ||
+                                 KIND == static_cast<int>(GemmKind::kW8));
     static constexpr int A_BYTES = 128 * 128;
     static constexpr int B_BYTES = (BN / 2) * 128;
     static constexpr int B8_BYTES = W8 ? (BN / 2) * 64 : 0;
     static constexpr int Y16_BYTES = Y16 ? kEpiWarps * kY16Bytes : 0;
-    static constexpr int STAGES = W8 ? (BN == 128 ? 5 : 4) : (BN == 128 ? 6 : (Y16 && BN == 256 ? 4 : 5));
+    static constexpr int STAGES =
+        W8 ? (BN == 128 ? 5 : (Y16 && BN == 256 ? 3 : 4)) : (BN == 128 ? 6 : (Y16 && BN == 256 ? 4 : 5));
     static constexpr uint32_t TMEM_COLS = BN == 128 ? 256 : 512;  // 2 accumulators, power of two
     // mainloop ring + two staging boxes per epilogue warp (+ the 16-bit
     // copy's box) + barriers
@@ -771,10 +773,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         // box is free: every earlier store has read its box);
                         // an fp16 copy fails loudly instead of turning into inf
                         if (args.out16) {
+                            float y[32];
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) y[i] = v[i];
+                            if (args.copy_gain) {
+                                const float4* gp = reinterpret_cast<const float4*>(args.copy_gain + col0);
+#pragma unroll
+                                for (int i = 0; i < 8; ++i) {
+                                    const float4 q = __ldg(gp + i);
+                                    f2split(mul2(f2(y[4 * i], y[4 * i + 1]), f2(q.x, q.y)), y[4 * i], y[4 * i + 1]);
+                                    f2split(mul2(f2(y[4 * i + 2], y[4 * i + 3]), f2(q.z, q.w)), y[4 * i + 2],
+                                            y[4 * i + 3]);
+                                }
+                            }
                             if constexpr (F16) {
                                 float amax = 0.f;
 #pragma unroll
-                                for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+                                for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(y[i]));
                                 if (__any_sync(0xffffffffu, amax > 65504.0f) && lane == 0)
                                     atomicOr(args.status, kStatusF16Overflow);
                             }
@@ -782,8 +797,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                             for (int i = 0; i < 4; ++i)
                                 *reinterpret_cast<uint4*>(y16 + swz(lane, i, 64)) = make_uint4(
-                                    pack2<F16>(v[8 * i], v[8 * i + 1]), pack2<F16>(v[8 * i + 2], v[8 * i + 3]),
-                                    pack2<F16>(v[8 * i + 4], v[8 * i + 5]), pack2<F16>(v[8 * i + 6], v[8 * i + 7]));
+                                    pack2<F16>(y[8 * i], y[8 * i + 1]), pack2<F16>(y[8 * i + 2], y[8 * i + 3]),
+                                    pack2<F16>(y[8 * i + 4], y[8 * i + 5]), pack2<F16>(y[8 * i + 6], y[8 * i + 7]));
                         }
                     }
                 }

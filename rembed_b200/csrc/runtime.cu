@@ -76,6 +76,10 @@ struct DevDense {
     void* w_lo = nullptr;   // strict fp32: the fp32 remainder of the tf32-rounded weight in w
     CUtensorMap tmap_lo[3];
     float* fold_c1 = nullptr;  // folded LayerNorm: column sums of the 16-bit w (w = W * gain)
+    // weight-only int8 with a folded LayerNorm: w stays the quantised W, and
+    // fold_c1 / fold_bias are s[n] * sum_k g[k] q[n][k] and bias[n] +
+    // s[n] * sum_k b[k] q[n][k] (bias stays the unfolded one)
+    float* fold_bias = nullptr;
 };
 
 // A GEMM's A operand: the tensor map of the buffer the MMA reads and, in the
@@ -137,6 +141,7 @@ struct Replica {
     // small kernel merges the chunks into lnst, and the next GEMM reads the
     // copy with the norm's gain folded into its weight.
     bool fold = false;
+    bool fold_w8 = false;     // weight-only int8 folding (the gain through the activation copy)
     bool fold_rms = false;    // pre-norm stacks: the folded norms are RMSNorms (Qwen3)
     float2* parts = nullptr;  // [H / 32 x T]
     float* pick32 = nullptr;  // [sequences x H]: the final norm of each sequence's pooled row
@@ -521,6 +526,33 @@ DevDense make_dense_folded(Replica& r, int mode, const float* W, const float* bi
     return d;
 }
 
+// Weight-only int8 GEMM whose input is LN(y): the int8 weight is the
+// reference's quantisation of W itself (q, per-column s; make_dense), and the
+// gain reaches the product through the activation copy instead (the residual
+// GEMM that writes y writes round16(y * g)), so the epilogue's fold terms are
+// those of the dequantised weight q * s: c1[n] = s[n] * sum_k g[k] q[n][k],
+// bias'[n] = bias[n] + s[n] * sum_k b[k] q[n][k] (double sums).
+DevDense make_dense_w8_folded(Replica& r, const float* W, const float* bias, int N, int K, const float* g,
+                              const float* b) {
+    DevDense d = make_dense(r, RG_MODE_INT8_W, W, bias, N, K);
+    std::vector<int8_t> q(static_cast<size_t>(N) * K);
+    std::vector<float> s(N), c1(N), bf(N);
+    quant_packb8(W, N, K, q.data(), s.data());
+    for (int n = 0; n < N; ++n) {
+        const int8_t* row = q.data() + static_cast<size_t>(n) * K;
+        double cg = 0.0, cb = 0.0;
+        for (int k = 0; k < K; ++k) {
+            cg += static_cast<double>(g[k]) * row[k];
+            cb += static_cast<double>(b[k]) * row[k];
+        }
+        c1[n] = static_cast<float>(s[n] * cg);
+        bf[n] = static_cast<float>((bias ? bias[n] : 0.0) + s[n] * cb);
+    }
+    d.fold_c1 = dev_upload(r, c1.data(), N);
+    d.fold_bias = dev_upload(r, bf.data(), N);
+    return d;
+}
+
 void finalize_bert(rg_ctx* c, Replica& r) {
     const rg_model_desc& d = c->d;
     const int H = d.hidden_size, I = d.intermediate_size, V = d.vocab_size, P = d.max_position_embeddings;
@@ -621,8 +653,10 @@ void finalize_bert(rg_ctx* c, Replica& r) {
             w.b2 = T("output.LayerNorm.bias", {H});
         }
     }
-    // LayerNorm folding (16-bit modes; every folded weight in range)
-    r.fold = (c->mode == RG_MODE_BF16 || c->mode == RG_MODE_F16) && H % 32 == 0;
+    // LayerNorm folding (16-bit modes, every folded weight in range; the
+    // weight-only int8 mode, whose weights stay as quantised)
+    r.fold_w8 = c->mode == RG_MODE_INT8_W && H % 32 == 0;
+    r.fold = (c->mode == RG_MODE_BF16 || c->mode == RG_MODE_F16 || r.fold_w8) && H % 32 == 0;
     for (int li = 0; li < d.num_hidden_layers && r.fold; ++li) {
         const HostLayer& w = hl[li];
         r.fold = fold_ok(c->mode, w.f1W, w.g1, I, H);
@@ -645,12 +679,15 @@ void finalize_bert(rg_ctx* c, Replica& r) {
         memcpy(qkvB.data() + H, w.kB, sizeof(float) * H);
         memcpy(qkvB.data() + 2 * H, w.vB, sizeof(float) * H);
         // layer 0's QKV reads the embedding LayerNorm's output as is
-        L.qkv = r.fold && li > 0
+        L.qkv = r.fold_w8 && li > 0
+                    ? make_dense_w8_folded(r, qkvW.data(), qkvB.data(), 3 * H, H, hl[li - 1].g2, hl[li - 1].b2)
+                : r.fold && li > 0
                     ? make_dense_folded(r, c->mode, qkvW.data(), qkvB.data(), 3 * H, H, hl[li - 1].g2, hl[li - 1].b2)
                     : make_dense(r, c->mode, qkvW.data(), qkvB.data(), 3 * H, H);
         L.o = make_dense(r, c->mode, w.oW, w.oB, H, H);
-        L.ffn1 = r.fold ? make_dense_folded(r, c->mode, w.f1W, w.f1B, I, H, w.g1, w.b1)
-                        : make_dense(r, c->mode, w.f1W, w.f1B, I, H);
+        L.ffn1 = r.fold_w8 ? make_dense_w8_folded(r, w.f1W, w.f1B, I, H, w.g1, w.b1)
+                 : r.fold  ? make_dense_folded(r, c->mode, w.f1W, w.f1B, I, H, w.g1, w.b1)
+                           : make_dense(r, c->mode, w.f1W, w.f1B, I, H);
         L.ffn2 = make_dense(r, c->mode, w.f2W, w.f2B, H, I);
     }
 }
@@ -1004,6 +1041,7 @@ struct LnFold {
     const float2* fold_stats = nullptr;
     act16* out16 = nullptr;
     float2* parts_out = nullptr;
+    const float* copy_gain = nullptr;  // out16 = round16(y * copy_gain) (weight-only int8)
 };
 
 // RoPE applied by the QKV GEMM's epilogue (kEpiRope).
@@ -1039,6 +1077,7 @@ void gemm(Replica& r, int mode, const OpMaps& tmA, const DevDense& w, int M, int
             fold_bytes += 8.0 * M;
         }
         a.out16 = reinterpret_cast<uint16_t*>(lf->out16);
+        a.copy_gain = lf->copy_gain;
         a.ld16 = w.N;
         a.parts_out = lf->parts_out;
         if (lf->out16) fold_bytes += 2.0 * M * w.N;
@@ -1047,7 +1086,7 @@ void gemm(Replica& r, int mode, const OpMaps& tmA, const DevDense& w, int M, int
     a.M = M;
     a.N = w.N;
     a.K = w.K;
-    a.bias = w.bias;
+    a.bias = lf && lf->fold_stats && w.fold_bias ? w.fold_bias : w.bias;
     a.col_scale = w.scale;
     a.row_scale = row_scale;
     a.residual = residual;
@@ -1139,6 +1178,7 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
     const bool f16 = mode == RG_MODE_F16 || mode == RG_MODE_INT8_W;  // fp16 activations, else bf16
     const bool f32 = mode == RG_MODE_FP32;  // strict: fp32 activations, hi/lo GEMM operands
     const bool pre = is_prenorm(arch);
+    const bool fold_post = !pre && r.fold;  // post-norm stacks fold their inner LayerNorms (see below)
     int launches = 0;
     const double Td = T, Hd = H;
 
@@ -1207,10 +1247,13 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
     // and the next residual GEMM rebuilds LN(x32) from lnst as before.
     const float *res_g = nullptr, *res_b = nullptr;
     bool folded = false;  // xb holds the unnormalised rows of the pending (folded) norm
-    auto residual_gemm = [&](const OpMaps& tmA, const DevDense& w, const float* row_scale, bool fold_out) {
+    auto residual_gemm = [&](const OpMaps& tmA, const DevDense& w, const float* row_scale, bool fold_out,
+                             const float* next_g = nullptr) {
         LnFold lf;
         lf.out16 = fold_out ? r.xb : nullptr;
         lf.parts_out = fold_out ? r.parts : nullptr;
+        // weight-only int8: the next norm's gain goes into the copy
+        lf.copy_gain = fold_out && r.fold_w8 ? next_g : nullptr;
         const LnFold* lfp = fold_out ? &lf : nullptr;
         if (res_g)
             gemm(r, mode, tmA, w, T, rg::kEpiBiasResLN, row_scale, r.x32, r.x32, st, launches, r.lnst, res_g, res_b,
@@ -1439,8 +1482,8 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
             ++launches;
         }
         if (s8) quantize(r.ctx, m.qd, r.ctxq, r.ctxs);
-        if (!pre && r.fold) {
-            residual_gemm(r.tm_ctx, L.o, nullptr, true);
+        if (fold_post) {
+            residual_gemm(r.tm_ctx, L.o, nullptr, true, L.ln1_g);
             fold_norm(L.ln1_g, L.ln1_b);
         } else if (!pre) {
             residual_gemm(r.tm_ctx, L.o, s8 ? r.ctxs : nullptr, false);
@@ -1468,8 +1511,8 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         // FFN2 reads the FFN hidden state (4x the hidden width) that FFN1
         // just wrote in row-block order: last block first finds it in L2
         r.rev_m = 1;
-        if (!pre && r.fold && !last) {
-            residual_gemm(r.tm_ffh, L.ffn2, nullptr, true);
+        if (fold_post && !last) {
+            residual_gemm(r.tm_ffh, L.ffn2, nullptr, true, L.ln2_g);
             fold_norm(L.ln2_g, L.ln2_b);
         } else if (!pre && last && pick) {
             residual_gemm(r.tm_ffh, L.ffn2, s8 ? r.ffhs : nullptr, false);
