@@ -520,12 +520,25 @@ cudaError_t launch_qk_norm_rope(const QkRopeParams& p, int head_dim, cudaStream_
 // ---------------------------------------------------------------------------
 // int8 -> fp16 widening, 16 weights per thread: (q + 128) placed in the low
 // mantissa byte of 1024.0 is exactly 1024 + q + 128; subtracting 1152 leaves q.
-__global__ void __launch_bounds__(256) widen_s8_f16_kernel(const uint4* __restrict__ w, size_t n16,
-                                                          uint4* __restrict__ out) {
+// Several widenings (a layer's weights) in one launch: blocks are dealt over
+// the jobs in proportion to their sizes (job j takes blocks [first[j],
+// first[j + 1])).
+struct WidenJobs {
+    WidenJob job[4];
+    int first[5];
+};
+
+__global__ void __launch_bounds__(256) widen_s8_f16_multi_kernel(WidenJobs js) {
     pdl_trigger();
     pdl_wait();
-    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n16;
-         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    int j = 0;
+    while (j < 3 && static_cast<int>(blockIdx.x) >= js.first[j + 1]) ++j;
+    const uint4* w = reinterpret_cast<const uint4*>(js.job[j].src);
+    uint4* out = reinterpret_cast<uint4*>(js.job[j].dst);
+    const size_t n16 = js.job[j].n / 16;
+    const int nb = js.first[j + 1] - js.first[j];
+    for (size_t i = (blockIdx.x - js.first[j]) * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n16;
+         i += static_cast<size_t>(nb) * blockDim.x) {
         const uint4 u = __ldg(w + i);
         const uint32_t in[4] = {u.x, u.y, u.z, u.w};
         uint32_t o[8];
@@ -543,14 +556,30 @@ __global__ void __launch_bounds__(256) widen_s8_f16_kernel(const uint4* __restri
     }
 }
 
-cudaError_t launch_widen_s8_f16(const int8_t* w, size_t n, uint16_t* out, cudaStream_t st) {
-    if (n == 0) return cudaSuccess;
-    if (n % 16 != 0 || (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
-        return cudaErrorInvalidValue;
-    const size_t n16 = n / 16;
-    const int grid = static_cast<int>(std::min<size_t>((n16 + 255) / 256, 148 * 8));
-    launch_pdl(widen_s8_f16_kernel, dim3(grid), dim3(256), 0, st, reinterpret_cast<const uint4*>(w), n16,
-               reinterpret_cast<uint4*>(out));
+cudaError_t launch_widen_s8_f16_multi(const WidenJob* jobs, int count, cudaStream_t st) {
+    if (count <= 0 || count > 4) return cudaErrorInvalidValue;
+    WidenJobs js{};
+    size_t total = 0;
+    for (int j = 0; j < count; ++j) {
+        const WidenJob& b = jobs[j];
+        if (b.n == 0 || b.n % 16 != 0 || (reinterpret_cast<uintptr_t>(b.src) & 15) ||
+            (reinterpret_cast<uintptr_t>(b.dst) & 15))
+            return cudaErrorInvalidValue;
+        js.job[j] = b;
+        total += b.n / 16;
+    }
+    // about 4 blocks of 256 threads per SM in all, at least one per job
+    const int budget = 148 * 4;
+    js.first[0] = 0;
+    for (int j = 0; j < 4; ++j) {
+        int nb = 0;
+        if (j < count) {
+            const size_t n16 = js.job[j].n / 16;
+            nb = static_cast<int>(std::max<size_t>(1, std::min<size_t>((n16 + 255) / 256, budget * n16 / total)));
+        }
+        js.first[j + 1] = js.first[j] + nb;
+    }
+    launch_pdl(widen_s8_f16_multi_kernel, dim3(js.first[4]), dim3(256), 0, st, js);
     return cudaGetLastError();
 }
 

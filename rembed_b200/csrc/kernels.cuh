@@ -113,10 +113,16 @@ struct QkRopeParams {
 };
 cudaError_t launch_qk_norm_rope(const QkRopeParams& p, int head_dim, cudaStream_t st);
 
-// int8 -> fp16, exact (weight-only int8 at large batch: one layer's weight
-// widened just before its GEMM; the per-channel scale stays in the GEMM
-// epilogue).  n must be a multiple of 16, both pointers 16-byte aligned.
-cudaError_t launch_widen_s8_f16(const int8_t* w, size_t n, uint16_t* out, cudaStream_t st);
+// int8 -> fp16, exact (weight-only int8 at large batch: a layer's weights
+// widened just before its first GEMM; the per-channel scale stays in the
+// GEMM epilogue).  One launch over up to four (src, n, dst) widenings: n a
+// multiple of 16, both pointers 16-byte aligned.
+struct WidenJob {
+    const int8_t* src;
+    size_t n;
+    uint16_t* dst;
+};
+cudaError_t launch_widen_s8_f16_multi(const WidenJob* jobs, int count, cudaStream_t st);
 
 // Per-row symmetric int8 quantisation of a bf16 [T x K] matrix
 // (QuantizeRowU8 with the +128 offset removed: q in [-128, 127]).

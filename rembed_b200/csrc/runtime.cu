@@ -80,6 +80,7 @@ struct DevDense {
     // fold_c1 / fold_bias are s[n] * sum_k g[k] q[n][k] and bias[n] +
     // s[n] * sum_k b[k] q[n][k] (bias stays the unfolded one)
     float* fold_bias = nullptr;
+    size_t w16_off = 0;  // weight-only int8: element offset of the widened copy in the layer scratch
 };
 
 // A GEMM's A operand: the tensor map of the buffer the MMA reads and, in the
@@ -150,7 +151,7 @@ struct Replica {
     int32_t* d_cu = nullptr;
     float* d_out = nullptr;
     int* d_status = nullptr;
-    uint16_t* w16 = nullptr;  // weight-only int8: fp16 widening scratch (largest weight)
+    uint16_t* w16 = nullptr;  // weight-only int8: fp16 widening scratch (one layer's weights)
     size_t w16_elems = 0;
     // Pinned host staging, two slots so that one batch can be staged while
     // the previous one runs (rg_submit / rg_collect); the device buffers are
@@ -465,14 +466,6 @@ DevDense make_dense(Replica& r, int mode, const float* w, const float* bias, int
         d.scale = dev_upload(r, s.data(), N);
     }
     const int eb = mode == RG_MODE_FP32 ? 4 : ((mode == RG_MODE_BF16 || mode == RG_MODE_F16) ? 2 : 1);
-    if (mode == RG_MODE_INT8_W && n > r.w16_elems) {
-        // the widening scratch grows to the largest weight (sized before any
-        // tensor map over it is made: make_dense runs for every weight first)
-        if (r.w16) cudaFree(r.w16);
-        r.w16 = nullptr;
-        check(cudaMalloc(&r.w16, n * 2), "cudaMalloc");
-        r.w16_elems = n;
-    }
     for (int i = 0; i < 3; ++i) {
         if (N % kBlockWidths[i] != 0) continue;
         const uint32_t box_rows = rg::gemm_w_box_rows(kBlockWidths[i]);
@@ -851,15 +844,34 @@ void finalize_decoder(rg_ctx* c, Replica& r) {
 // Weight-only int8: tensor maps of each weight's shape over the fp16
 // widening scratch (made once the scratch has its final size).
 void make_widen_maps(Replica& r) {
+    // A layer's four weights side by side (the same offsets in every layer
+    // of the same shapes); the scratch holds the largest layer.
+    size_t need = 0;
+    for (DevLayer& L : r.layers) {
+        size_t off = 0;
+        for (DevDense* d : {&L.qkv, &L.o, &L.ffn1, &L.ffn2}) {
+            d->w16_off = off;
+            off += (static_cast<size_t>(d->N) * d->K + 63) / 64 * 64;
+        }
+        need = std::max(need, off);
+    }
+    if (need > r.w16_elems) {
+        if (r.w16) cudaFree(r.w16);
+        r.w16 = nullptr;
+        check(cudaMalloc(&r.w16, need * 2), "cudaMalloc");
+        r.w16_elems = need;
+    }
     for (DevLayer& L : r.layers)
         for (DevDense* d : {&L.qkv, &L.o, &L.ffn1, &L.ffn2})
             for (int i = 0; i < 3; ++i) {
                 if (d->N % kBlockWidths[i] != 0) continue;
-                if (!rg::make_kmajor_tmap(&d->tmap16[i], r.w16, 2, d->N, d->K, d->K,
+                if (!rg::make_kmajor_tmap(&d->tmap16[i], r.w16 + d->w16_off, 2, d->N, d->K, d->K,
                                           rg::gemm_w_box_rows(kBlockWidths[i])))
                     fail("cuTensorMapEncodeTiled failed for a [%d x %d] widened weight", d->N, d->K);
             }
 }
+
+
 
 void free_workspace(Replica& r) {
     for (void* p : r.ws) cudaFree(p);
@@ -1051,6 +1063,23 @@ struct QkRope {
     int dh = 0, qd = 0, kvd = 0;
 };
 
+// Weight-only int8 at >= kW8WidenRows rows: the layer's four int8 weights
+// widened to fp16 into the scratch in one launch before its first GEMM.
+void widen_layer(Replica& r, const DevLayer& L, cudaStream_t st, int& launches) {
+    const DevDense* ds[4] = {&L.qkv, &L.o, &L.ffn1, &L.ffn2};
+    rg::WidenJob jobs[4];
+    double bytes = 0.0;
+    for (int i = 0; i < 4; ++i) {
+        jobs[i].src = static_cast<const int8_t*>(ds[i]->w);
+        jobs[i].n = static_cast<size_t>(ds[i]->N) * ds[i]->K;
+        jobs[i].dst = r.w16 + ds[i]->w16_off;
+        bytes += 3.0 * jobs[i].n;
+    }
+    ProfScope pw(r, st, RG_KC_QUANT, 0.0, bytes);
+    check(rg::launch_widen_s8_f16_multi(jobs, 4, st), "widen launch");
+    ++launches;
+}
+
 void gemm(Replica& r, int mode, const OpMaps& tmA, const DevDense& w, int M, int epi, const float* row_scale,
           const float* residual, void* out, cudaStream_t st, int& launches, const float2* ln_stats = nullptr,
           const float* ln_g = nullptr, const float* ln_b = nullptr, const LnFold* lf = nullptr,
@@ -1109,12 +1138,7 @@ void gemm(Replica& r, int mode, const OpMaps& tmA, const DevDense& w, int M, int
     const int bn = rg::gemm_block_n(M, w.N, r.num_sms, rg::epi_is_glu(epi), qr ? qr->dh : 0);
     if (bn == 0) fail("no GEMM tile width divides N=%d", w.N);
     if (kind == rg::GemmKind::kW8 && M >= kW8WidenRows) {
-        {
-            ProfScope pw(r, st, RG_KC_QUANT, 0.0, 3.0 * double(w.N) * w.K);
-            check(rg::launch_widen_s8_f16(static_cast<const int8_t*>(w.w), static_cast<size_t>(w.N) * w.K, r.w16, st),
-                  "widen launch");
-            ++launches;
-        }
+        // the layer's weights were widened by widen_layer before its first GEMM
         ProfScope ps(r, st, RG_KC_GEMM, 2.0 * M * w.N * w.K, bytes);
         check(rg::gemm_launch(rg::GemmKind::kF16, epi, bn, tmA.m, w.tmap16[bn_index(bn)], a, r.num_sms, st),
               "gemm launch");
@@ -1389,6 +1413,7 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
 
     for (int li = 0; li < d.num_hidden_layers; ++li) {
         const DevLayer& L = r.layers[li];
+        if (mode == RG_MODE_INT8_W && T >= kW8WidenRows) widen_layer(r, L, st, launches);
         // ---- attention sublayer
         // (a folded pre-norm stack enters layers 1... with the norm's
         // statistics already merged by the previous FFN's residual GEMM;
