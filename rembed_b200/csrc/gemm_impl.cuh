@@ -99,12 +99,33 @@ __device__ __forceinline__ void gelu_as28x2(float& x0, float& x1) {
     x1 = x1 >= 0.f ? x1 - h1 : h1;
 }
 
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+// x * sigmoid(z) on a pair as x / (1 + 2^(-z log2 e)) with the hardware
+// exponential and reciprocal approximations (relative error about 1e-6,
+// against the gated output's 16-bit rounding of 2^-9 or 2^-12).  z -> -inf
+// gives 1/inf = 0.
+__device__ __forceinline__ void x_sigmoid_x2(float& x0, float& x1, float z0, float z1) {
+    float t0, t1;
+    f2split(mul2(f2(z0, z1), f2(-1.4426950408889634f, -1.4426950408889634f)), t0, t1);
+    float d0, d1;
+    f2split(add2(f2(ex2_approx(t0), ex2_approx(t1)), f2(1.0f, 1.0f)), d0, d1);
+    f2split(mul2(f2(x0, x1), f2(rcp_approx(d0), rcp_approx(d1))), x0, x1);
+}
 // SiLU x * sigmoid(x) (tensor.go:477-481 computes it through a float64 exp).
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
-// tanh-approximation GELU (tensor.go:490-497; HF gelu_pytorch_tanh).
-__device__ __forceinline__ float gelu_tanh_f(float x) {
-    const float inner = 0.7978845608028654f * (x + 0.044715f * x * x * x);
-    return 0.5f * x * (1.0f + tanhf(inner));
+__device__ __forceinline__ void silu_x2(float& x0, float& x1) { x_sigmoid_x2(x0, x1, x0, x1); }
+// tanh-approximation GELU (tensor.go:490-497; HF gelu_pytorch_tanh):
+// 0.5 x (1 + tanh(u)) = x * sigmoid(2u), u = sqrt(2/pi) (x + 0.044715 x^3).
+__device__ __forceinline__ void gelu_tanh_x2(float& x0, float& x1) {
+    constexpr float c0 = 2.0f * 0.7978845608028654f, c1 = 2.0f * 0.7978845608028654f * 0.044715f;
+    const uint64_t xs = f2(x0, x1);
+    const uint64_t p = fma2(mul2(xs, xs), f2(c1, c1), f2(c0, c0));  // c0 + c1 x^2
+    float z0, z1;
+    f2split(mul2(p, xs), z0, z1);
+    x_sigmoid_x2(x0, x1, z0, z1);
 }
 
 constexpr int kEpiWarps = 8;        // two epilogue warps per SM sub-partition
@@ -685,11 +706,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         }
                     } else {
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            float a = v[i];
-                            if constexpr (EPI == kEpiGluSilu) a = silu_f(a);
-                            else a = gelu_tanh_f(a);
-                            v[i] = a * w[i];
+                        for (int i = 0; i < 32; i += 2) {
+                            if constexpr (EPI == kEpiGluSilu) silu_x2(v[i], v[i + 1]);
+                            else gelu_tanh_x2(v[i], v[i + 1]);
+                            f2split(mul2(f2(v[i], v[i + 1]), f2(w[i], w[i + 1])), v[i], v[i + 1]);
                         }
                     }
                 }
