@@ -126,7 +126,9 @@ static cudaError_t launch_impl(GemmKind kind, int epi, int block_n, GemmMaps& m,
         return cudaErrorInvalidValue;
     if (epi == kEpiRope &&
         (f32out || args.rope_dh <= 0 || args.rope_dh % 64 != 0 || (block_n / 2) % args.rope_dh != 0 ||
-         args.rope_qd % args.rope_dh != 0 || args.rope_kvd % args.rope_dh != 0 || !args.rope_cos ||
+         args.rope_qd % args.rope_dh != 0 || args.rope_kvd % args.rope_dh != 0 || args.rope_npos <= 0 ||
+         (reinterpret_cast<uintptr_t>(args.rope_cos) & 15) != 0 || (reinterpret_cast<uintptr_t>(args.rope_sin) & 15) != 0 ||
+         !args.rope_cos ||
          !args.rope_sin || !args.positions))
         return cudaErrorInvalidValue;
     if ((args.parts_out || args.out16) && (!k16 || !epi_has_residual(epi))) return cudaErrorInvalidValue;

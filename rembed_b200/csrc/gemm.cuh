@@ -73,11 +73,13 @@ struct GemmArgs {
     // Walk the row blocks from the last to the first (see the forward's
     // L2-aware ordering): the output is the same, only the order of tiles.
     int reverse_m;
-    // kEpiRope: the RoPE tables [positions x rope_dh / 2], each row's
-    // position in its sequence, and the head layout of the Q|K|V output.
+    // kEpiRope: the RoPE tables laid out [rope_dh / 8][rope_npos][4] (entry
+    // (p, d) at ((d / 4) * rope_npos + p) * 4 + d % 4: lanes on consecutive
+    // positions read one contiguous run), each row's position in its
+    // sequence, and the head layout of the Q|K|V output.
     const float *rope_cos, *rope_sin;
     const int32_t* positions;
-    int rope_dh, rope_qd, rope_kvd;
+    int rope_dh, rope_qd, rope_kvd, rope_npos;
 };
 
 // Operand element kind of the GEMM.

@@ -533,17 +533,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 for (int h0 = 0; h0 < HALF; h0 += dh) {
                     const int gcol = colw + h0;  // first column of the head
                     const bool rot = gcol < args.rope_qd + args.rope_kvd;  // Q and K heads rotate
-                    const float* cs = rot ? args.rope_cos + static_cast<int64_t>(pos) * hd : nullptr;
-                    const float* sn = rot ? args.rope_sin + static_cast<int64_t>(pos) * hd : nullptr;
-                    // the row's table entries come from L2 (one row per
-                    // lane): each 16-column step's are requested one step
-                    // ahead
+                    // the row's table entries: entry group g (dims 4g .. 4g + 3)
+                    // of position pos at float4 g * npos + pos, so the
+                    // warp's lanes (mostly consecutive positions) read one
+                    // contiguous run; each 16-column step's are requested one
+                    // step ahead
+                    const int64_t npos = args.rope_npos;
+                    const float4* cs = reinterpret_cast<const float4*>(args.rope_cos) + pos;
+                    const float4* sn = reinterpret_cast<const float4*>(args.rope_sin) + pos;
                     float4 nc[4], ns[4];
                     if (rot) {
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
-                            nc[i] = __ldg(reinterpret_cast<const float4*>(cs) + i);
-                            ns[i] = __ldg(reinterpret_cast<const float4*>(sn) + i);
+                            nc[i] = __ldg(cs + i * npos);
+                            ns[i] = __ldg(sn + i * npos);
                         }
                     }
                     // columns d (first half) and d + dh/2 (second half) of the
@@ -574,8 +577,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                 if (d0 + 16 < hd) {  // the next step's entries
 #pragma unroll
                                     for (int i = 0; i < 4; ++i) {
-                                        nc[i] = __ldg(reinterpret_cast<const float4*>(cs + d0 + 16) + i);
-                                        ns[i] = __ldg(reinterpret_cast<const float4*>(sn + d0 + 16) + i);
+                                        nc[i] = __ldg(cs + ((d0 + 16) / 4 + i) * npos);
+                                        ns[i] = __ldg(sn + ((d0 + 16) / 4 + i) * npos);
                                     }
                                 }
 #pragma unroll

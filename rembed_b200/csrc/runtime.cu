@@ -125,6 +125,10 @@ struct Replica {
     float emb_scale = 1.0f;     // Gemma: sqrt(H)
     float *final_norm = nullptr, *zero_beta = nullptr;
     float *cos_g = nullptr, *sin_g = nullptr, *cos_l = nullptr, *sin_l = nullptr;  // RoPE [positions x dh/2]
+    // the same tables as [dh/8][positions][4] (the QKV epilogue's layout:
+    // one 16-byte load per lane, lanes on consecutive positions contiguous)
+    float *cos4_g = nullptr, *sin4_g = nullptr, *cos4_l = nullptr, *sin4_l = nullptr;
+    int rope_npos = 0;
     float *dense1 = nullptr, *dense2 = nullptr;  // Gemma Dense head, fp32
     std::vector<DevLayer> layers;
     // workspace
@@ -705,7 +709,8 @@ std::vector<float> concat_rows(std::initializer_list<std::pair<const float*, siz
 
 // ropeTable (modernbert.go:108-123): float64 inverse frequencies and trig,
 // rounded to float32, for positions [0, npos).
-void rope_tables(Replica& r, int npos, int dh, double theta, float** cosp, float** sinp) {
+void rope_tables(Replica& r, int npos, int dh, double theta, float** cosp, float** sinp, float** cos4p,
+                 float** sin4p) {
     const int half = dh / 2;
     std::vector<float> cs(static_cast<size_t>(npos) * half), sn(static_cast<size_t>(npos) * half);
     for (int d = 0; d < half; ++d) {
@@ -718,6 +723,18 @@ void rope_tables(Replica& r, int npos, int dh, double theta, float** cosp, float
     }
     *cosp = dev_upload(r, cs.data(), cs.size());
     *sinp = dev_upload(r, sn.data(), sn.size());
+    r.rope_npos = npos;
+    if (half % 4 == 0) {  // [half/4][npos][4]
+        std::vector<float> c4(cs.size()), s4(sn.size());
+        for (int p = 0; p < npos; ++p)
+            for (int d = 0; d < half; ++d) {
+                const size_t o = (static_cast<size_t>(d / 4) * npos + p) * 4 + d % 4;
+                c4[o] = cs[static_cast<size_t>(p) * half + d];
+                s4[o] = sn[static_cast<size_t>(p) * half + d];
+            }
+        *cos4p = dev_upload(r, c4.data(), c4.size());
+        *sin4p = dev_upload(r, s4.data(), s4.size());
+    }
 }
 
 std::vector<float> unit_offset(const float* v, int n) {  // gemma3.go:44-50
@@ -743,12 +760,12 @@ void finalize_decoder(rg_ctx* c, Replica& r) {
         r.word = up(G("embed_tokens.weight", {V, H}), static_cast<size_t>(V) * H);
         if (arch == RG_ARCH_QWEN3) {
             r.final_norm = up(G("norm.weight", {H}), H);
-            rope_tables(r, npos, dh, d.rope_theta, &r.cos_g, &r.sin_g);
+            rope_tables(r, npos, dh, d.rope_theta, &r.cos_g, &r.sin_g, &r.cos4_g, &r.sin4_g);
         } else {
             r.final_norm = up(unit_offset(G("norm.weight", {H}), H).data(), H);
             r.emb_scale = static_cast<float>(std::sqrt(static_cast<double>(H)));
-            rope_tables(r, npos, dh, d.global_rope_theta, &r.cos_g, &r.sin_g);
-            rope_tables(r, npos, dh, d.local_rope_theta, &r.cos_l, &r.sin_l);
+            rope_tables(r, npos, dh, d.global_rope_theta, &r.cos_g, &r.sin_g, &r.cos4_g, &r.sin4_g);
+            rope_tables(r, npos, dh, d.local_rope_theta, &r.cos_l, &r.sin_l, &r.cos4_l, &r.sin4_l);
             const int D = d.dense_hidden;
             r.dense1 = up(G("2_Dense.linear.weight", {D, H}), static_cast<size_t>(D) * H);
             r.dense2 = up(G("3_Dense.linear.weight", {H, D}), static_cast<size_t>(H) * D);
@@ -759,14 +776,14 @@ void finalize_decoder(rg_ctx* c, Replica& r) {
         r.final_norm = up(G("final_norm.weight", {H}), H);
         std::vector<float> z(H, 0.0f);
         r.zero_beta = up(z.data(), H);
-        rope_tables(r, npos, dh, d.global_rope_theta, &r.cos_g, &r.sin_g);
-        rope_tables(r, npos, dh, d.local_rope_theta, &r.cos_l, &r.sin_l);
+        rope_tables(r, npos, dh, d.global_rope_theta, &r.cos_g, &r.sin_g, &r.cos4_g, &r.sin4_g);
+        rope_tables(r, npos, dh, d.local_rope_theta, &r.cos_l, &r.sin_l, &r.cos4_l, &r.sin4_l);
     } else {  // nomic
         r.word = up(G("embeddings.word_embeddings.weight", {V, H}), static_cast<size_t>(V) * H);
         r.type0 = up(G("embeddings.token_type_embeddings.weight", {2, H}), H);
         r.emb_g = up(G("emb_ln.weight", {H}), H);
         r.emb_b = up(G("emb_ln.bias", {H}), H);
-        rope_tables(r, npos, dh, d.rope_theta, &r.cos_g, &r.sin_g);
+        rope_tables(r, npos, dh, d.rope_theta, &r.cos_g, &r.sin_g, &r.cos4_g, &r.sin4_g);
     }
     r.layers.resize(d.num_hidden_layers);
     // Pre-norm stacks whose input norms fold into the GEMMs (bf16 mode): the
@@ -1061,6 +1078,7 @@ struct QkRope {
     const float *cos = nullptr, *sin = nullptr;
     const int32_t* positions = nullptr;
     int dh = 0, qd = 0, kvd = 0;
+    int npos = 0;  // rows of the tables, laid out [dh/8][npos][4]
 };
 
 // Weight-only int8 at >= kW8WidenRows rows: the layer's four int8 weights
@@ -1089,6 +1107,7 @@ void gemm(Replica& r, int mode, const OpMaps& tmA, const DevDense& w, int M, int
         epi = rg::kEpiRope;
         a.rope_cos = qr->cos;
         a.rope_sin = qr->sin;
+        a.rope_npos = qr->npos;
         a.positions = qr->positions;
         a.rope_dh = qr->dh;
         a.rope_qd = qr->qd;
@@ -1425,8 +1444,9 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
         }
         if (rope_in_gemm) {
             QkRope qr;
-            qr.cos = L.global ? r.cos_g : r.cos_l;
-            qr.sin = L.global ? r.sin_g : r.sin_l;
+            qr.cos = L.global ? r.cos4_g : r.cos4_l;
+            qr.sin = L.global ? r.sin4_g : r.sin4_l;
+            qr.npos = r.rope_npos;
             qr.positions = r.pos32;
             qr.dh = dh;
             qr.qd = m.qd;
