@@ -80,6 +80,10 @@ struct GemmArgs {
     const float *rope_cos, *rope_sin;
     const int32_t* positions;
     int rope_dh, rope_qd, rope_kvd, rope_npos;
+    // kEpiRope, optional (Qwen3): an RMSNorm of each Q / K head over its dh
+    // values (gains q_norm / k_norm, eps rope_eps) before the rotation
+    const float *q_norm, *k_norm;
+    float rope_eps;
 };
 
 // Operand element kind of the GEMM.

@@ -533,6 +533,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 for (int h0 = 0; h0 < HALF; h0 += dh) {
                     const int gcol = colw + h0;  // first column of the head
                     const bool rot = gcol < args.rope_qd + args.rope_kvd;  // Q and K heads rotate
+                    const float* g = !rot ? nullptr : (gcol < args.rope_qd ? args.q_norm : args.k_norm);
                     // the row's table entries: entry group g (dims 4g .. 4g + 3)
                     // of position pos at float4 g * npos + pos, so the
                     // warp's lanes (mostly consecutive positions) read one
@@ -548,6 +549,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             nc[i] = __ldg(cs + i * npos);
                             ns[i] = __ldg(sn + i * npos);
                         }
+                    }
+                    // QK-norm: the head's RMS over its dh values, read from
+                    // TMEM in a first pass (the table entries above are
+                    // already on their way)
+                    float inv = 1.0f;
+                    if (g) {
+                        float ssq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+                        for (int c = 0; c < dh; c += 32) {
+                            uint32_t ra[16], rb[16];
+                            tmem_ld16(taddr + h0 + c, ra);
+                            tmem_ld16(taddr + h0 + c + 16, rb);
+                            tmem_ld_wait();
+                            float xa[16], xb[16];
+                            values16(ra, gcol + c, xa);
+                            values16(rb, gcol + c + 16, xb);
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                ssq[i & 1] = fmaf(xa[i], xa[i], ssq[i & 1]);
+                                ssq[2 + (i & 1)] = fmaf(xb[i], xb[i], ssq[2 + (i & 1)]);
+                            }
+                        }
+                        inv = 1.0f / sqrtf(((ssq[0] + ssq[1]) + (ssq[2] + ssq[3])) / static_cast<float>(dh) +
+                                           args.rope_eps);
                     }
                     // columns d (first half) and d + dh/2 (second half) of the
                     // head together, 32 at a time into a pair of staging boxes
@@ -567,6 +592,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             float x1[16], x2[16];
                             values16(ra, gcol + d0, x1);
                             values16(rb, gcol + hd + d0, x2);
+                            if (g) {  // x * rstd * gain (qwen3.go:485-508)
+#pragma unroll
+                                for (int i = 0; i < 16; i += 4) {
+                                    const float4 ga = __ldg(reinterpret_cast<const float4*>(g + d0 + i));
+                                    const float4 gb = __ldg(reinterpret_cast<const float4*>(g + hd + d0 + i));
+                                    const float gaa[4] = {ga.x, ga.y, ga.z, ga.w}, gbb[4] = {gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+                                    for (int e = 0; e < 4; ++e) {
+                                        x1[i + e] = x1[i + e] * inv * gaa[e];
+                                        x2[i + e] = x2[i + e] * inv * gbb[e];
+                                    }
+                                }
+                            }
                             if (rot) {
                                 float4 c4v[4], s4v[4];
 #pragma unroll

@@ -1079,6 +1079,8 @@ struct QkRope {
     const int32_t* positions = nullptr;
     int dh = 0, qd = 0, kvd = 0;
     int npos = 0;  // rows of the tables, laid out [dh/8][npos][4]
+    const float *q_norm = nullptr, *k_norm = nullptr;  // optional QK-norm before the rotation
+    float eps = 0.f;
 };
 
 // Weight-only int8 at >= kW8WidenRows rows: the layer's four int8 weights
@@ -1108,6 +1110,9 @@ void gemm(Replica& r, int mode, const OpMaps& tmA, const DevDense& w, int M, int
         a.rope_cos = qr->cos;
         a.rope_sin = qr->sin;
         a.rope_npos = qr->npos;
+        a.q_norm = qr->q_norm;
+        a.k_norm = qr->k_norm;
+        a.rope_eps = qr->eps;
         a.positions = qr->positions;
         a.rope_dh = qr->dh;
         a.rope_qd = qr->qd;
@@ -1341,14 +1346,11 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
                  nullptr, qr);
         }
     };
-    // RoPE in the QKV projection's epilogue where the tile widths hold whole
-    // heads (head dims 64 and 128; 16-bit outputs) and there is no QK-norm
-    // (ModernBERT, nomic): measured as fast as the separate pass and it saves
-    // the pass's HBM traffic.  A QK-norm in the epilogue (an extra pass over
-    // each head) cost more than the separate kernel (Qwen3 at
-    // 128 x U[32,1024]: 1,588 against 1,630 embeddings/s), so Qwen3, Gemma's
-    // 256-wide heads and the strict fp32 mode keep the separate kernel.
-    const bool rope_in_gemm = has_rope(arch) && !f32 && dh % 64 == 0 && !r.layers[0].q_norm &&
+    // RoPE (and Qwen3's QK-norm, as a first pass over each head) in the QKV
+    // projection's epilogue where the tile widths hold whole heads (head
+    // dims 64 and 128; 16-bit outputs); Gemma's 256-wide heads and the
+    // strict fp32 mode keep the separate kernel.
+    const bool rope_in_gemm = has_rope(arch) && !f32 && dh % 64 == 0 &&
                               rg::gemm_block_n(T, m.nqkv, r.num_sms, false, dh) != 0;
     auto post_norm = [&](const float* g, const float* b, bool last) {
         ProfScope ps(r, st, RG_KC_NORM, 8.0 * Td * Hd, Td * Hd * (4.0 + 2.0 + (s8 ? 1.0 : 0.0) + (last ? 4.0 : 0.0)));
@@ -1451,6 +1453,9 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
             qr.dh = dh;
             qr.qd = m.qd;
             qr.kvd = m.kvd;
+            qr.q_norm = L.q_norm;
+            qr.k_norm = L.k_norm;
+            qr.eps = eps;
             input_gemm(L.qkv, r.tm_x, rg::kEpiBias, r.qkv, &qr);
         } else {
             input_gemm(L.qkv, r.tm_x, rg::kEpiBias, f32 ? static_cast<void*>(r.qkv32) : r.qkv);
