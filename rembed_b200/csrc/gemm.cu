@@ -90,7 +90,10 @@ int gemm_block_n(int M, int N, int num_sms, bool glu, int head_dim) {
     int best = 0;
     long best_cost = 0;
     for (int bn : {256, 192, 128}) {
-        if (N % bn != 0 || (glu && bn == 192) || (head_dim > 0 && (bn / 2) % head_dim != 0)) continue;
+        // RoPE epilogue: whole heads in each half-warp's columns, or (head
+        // dim 256) one head per tile
+        const bool heads_fit = head_dim <= 0 || (bn / 2) % head_dim == 0 || (head_dim == 256 && bn == 256);
+        if (N % bn != 0 || (glu && bn == 192) || !heads_fit) continue;
         const long tiles = static_cast<long>(m_tiles) * (N / bn);
         const long waves = (tiles + pairs - 1) / pairs;
         const long cost = waves * (bn + 32);
@@ -125,7 +128,8 @@ static cudaError_t launch_impl(GemmKind kind, int epi, int block_n, GemmMaps& m,
          (epi_is_glu(epi) ? false : (!args.bias || (epi != kEpiBias && epi != kEpiBiasGelu && epi != kEpiRope)))))
         return cudaErrorInvalidValue;
     if (epi == kEpiRope &&
-        (f32out || args.rope_dh <= 0 || args.rope_dh % 64 != 0 || (block_n / 2) % args.rope_dh != 0 ||
+        (f32out || args.rope_dh <= 0 || args.rope_dh % 64 != 0 ||
+         ((block_n / 2) % args.rope_dh != 0 && !(args.rope_dh == 256 && block_n == 256)) ||
          args.rope_qd % args.rope_dh != 0 || args.rope_kvd % args.rope_dh != 0 || args.rope_npos <= 0 ||
          (reinterpret_cast<uintptr_t>(args.rope_cos) & 15) != 0 || (reinterpret_cast<uintptr_t>(args.rope_sin) & 15) != 0 ||
          !args.rope_cos ||

@@ -522,7 +522,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     }
                 };
                 const int dh = args.rope_dh, hd = dh / 2;
-                const int colw = n_blk * BN + half * HALF;
+                // A head as wide as the tile (Gemma's 256) spans both
+                // half-warps' columns: each half-warp then reads the whole
+                // head (its RMS) and rotates half of its pairs, d in
+                // [half hd/2, (half + 1) hd/2) with d + hd.
+                const bool wide = dh > HALF;
+                const uint32_t thead = wide ? taddr - half * HALF : taddr;
+                const int colw = wide ? n_blk * BN : n_blk * BN + half * HALF;
+                const int c_lo = wide ? half * (hd / 2) : 0, c_hi = wide ? c_lo + hd / 2 : hd;
                 const int pos = (args.positions && row < args.M) ? __ldg(args.positions + row) : 0;
                 // four 2 KB 16-bit boxes in the warp's staging area: column
                 // pairs alternate between boxes {0, 1} and {2, 3} (k counts
@@ -530,7 +537,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 // shared memory while the next is computed
                 float amax = 0.f;
 #pragma unroll 1
-                for (int h0 = 0; h0 < HALF; h0 += dh) {
+                for (int h0 = 0; h0 < (wide ? 1 : HALF); h0 += dh) {
                     const int gcol = colw + h0;  // first column of the head
                     const bool rot = gcol < args.rope_qd + args.rope_kvd;  // Q and K heads rotate
                     const float* g = !rot ? nullptr : (gcol < args.rope_qd ? args.q_norm : args.k_norm);
@@ -546,8 +553,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     if (rot) {
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
-                            nc[i] = __ldg(cs + i * npos);
-                            ns[i] = __ldg(sn + i * npos);
+                            nc[i] = __ldg(cs + (c_lo / 4 + i) * npos);
+                            ns[i] = __ldg(sn + (c_lo / 4 + i) * npos);
                         }
                     }
                     // QK-norm: the head's RMS over its dh values, read from
@@ -559,8 +566,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll 1
                         for (int c = 0; c < dh; c += 32) {
                             uint32_t ra[16], rb[16];
-                            tmem_ld16(taddr + h0 + c, ra);
-                            tmem_ld16(taddr + h0 + c + 16, rb);
+                            tmem_ld16(thead + h0 + c, ra);
+                            tmem_ld16(thead + h0 + c + 16, rb);
                             tmem_ld_wait();
                             float xa[16], xb[16];
                             values16(ra, gcol + c, xa);
@@ -577,7 +584,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     // columns d (first half) and d + dh/2 (second half) of the
                     // head together, 32 at a time into a pair of staging boxes
 #pragma unroll 1
-                    for (int c = 0; c < hd; c += 32, ++k) {
+                    for (int c = c_lo; c < c_hi; c += 32, ++k) {
                         uint8_t* box0 = boxes + (k & 1) * 2 * kY16Bytes;
                         uint8_t* box1 = box0 + kY16Bytes;
                         if (lane == 0) bulk_wait_read<1>();  // the pair two back has read these boxes
@@ -586,8 +593,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         for (int sub = 0; sub < 32; sub += 16) {
                             const int d0 = c + sub;
                             uint32_t ra[16], rb[16];
-                            tmem_ld16(taddr + h0 + d0, ra);
-                            tmem_ld16(taddr + h0 + hd + d0, rb);
+                            tmem_ld16(thead + h0 + d0, ra);
+                            tmem_ld16(thead + h0 + hd + d0, rb);
                             tmem_ld_wait();
                             float x1[16], x2[16];
                             values16(ra, gcol + d0, x1);
@@ -612,7 +619,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                     c4v[i] = nc[i];
                                     s4v[i] = ns[i];
                                 }
-                                if (d0 + 16 < hd) {  // the next step's entries
+                                if (d0 + 16 < c_hi) {  // the next step's entries
 #pragma unroll
                                     for (int i = 0; i < 4; ++i) {
                                         nc[i] = __ldg(cs + ((d0 + 16) / 4 + i) * npos);

@@ -1346,10 +1346,11 @@ void forward_on_device(rg_ctx* c, Replica& r, const int64_t* d_ids, const int32_
                  nullptr, qr);
         }
     };
-    // RoPE (and Qwen3's QK-norm, as a first pass over each head) in the QKV
-    // projection's epilogue where the tile widths hold whole heads (head
-    // dims 64 and 128; 16-bit outputs); Gemma's 256-wide heads and the
-    // strict fp32 mode keep the separate kernel.
+    // RoPE (and the QK-norm of Qwen3 and Gemma, as a first pass over each
+    // head) in the QKV projection's epilogue where a tile holds whole heads
+    // (head dims 64 and 128 in each half-warp's columns, 256 across the
+    // tile; 16-bit outputs); the strict fp32 mode keeps the separate
+    // kernel.
     const bool rope_in_gemm = has_rope(arch) && !f32 && dh % 64 == 0 &&
                               rg::gemm_block_n(T, m.nqkv, r.num_sms, false, dh) != 0;
     auto post_norm = [&](const float* g, const float* b, bool last) {
