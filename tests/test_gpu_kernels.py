@@ -132,6 +132,10 @@ def test_attention_causal_kat(cuda, dtype, dh):
     ([900, 5, 1200], 2, 2, 64, -64, 64),
     ([1500, 700, 33], 2, 2, 64, -600, 600),
     ([2000, 130], 2, 1, 128, -700, 0),
+    # head dim 128 with windows of at least 1024 keys (the two-tile kernel:
+    # each tile's key range differs, the tiles walk their union)
+    ([2500, 900, 64], 2, 1, 128, -600, 600),
+    ([1800, 5, 1300], 4, 2, 128, -1100, 0),
 ])
 def test_attention_windows_and_heads(cuda, dtype, case):
     lens, heads, kv_heads, dh, lo, hi = case
